@@ -1,0 +1,480 @@
+"""Benchmark: the 7B-shaped int8 decode matmul chain.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one pass of the chain: 32 layers x {wq, wk, wv, wo: 4096x4096; w1, w3:
+4096->11008; w2: 11008->4096} + the 4096->32000 classifier = 225 int8 weight x fp32
+activation products at m = 1, each on a fresh U(-1, 1) activation vector. Weights are
+N(0, 0.02^2), quantised per column as the reference's quant.cpp does. On N GPUs the
+column-parallel weights (wq, wk, wv, w1, w3, classifier) are split along n and the
+row-parallel ones (wo, w2) along k, followed by a sum all-reduce of the partial outputs.
+
+`value` is whole-job algorithmic bytes (int8 weights + scales + fp32 activations and
+outputs) per second with everything resident in HBM, timed with CUDA events around K graph
+replays, max over ranks. `e2e` is the same metric through the C ABI with the activations
+copied in from pinned host memory and every output copied back inside the timed region.
+The weights (6.6 GB / N per GPU) are far larger than L2, so no L2 flush is needed.
+`--impl reference` times the reference's own CPU matmul_parallel (compiled from its sources
+into oracle/_ref) on a bounded sample of the chain, on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "llm-engine_b200"))
+
+DIM, HIDDEN, VOCAB, LAYERS = 4096, 11008, 32000, 32
+METRIC = "int8 decode-GEMV HBM GB/s (7B-shaped chain, m=1)"
+UNIT = "GB/s"
+
+
+def chain_shapes():
+    """(name, k, n, row_parallel) for every product of one step, in order."""
+    out = []
+    for layer in range(LAYERS):
+        for name in ("wq", "wk", "wv"):
+            out.append((f"{name}{layer}", DIM, DIM, False))
+        out.append((f"wo{layer}", DIM, DIM, True))
+        out.append((f"w1{layer}", DIM, HIDDEN, False))
+        out.append((f"w3{layer}", DIM, HIDDEN, False))
+        out.append((f"w2{layer}", HIDDEN, DIM, True))
+    out.append(("cls", DIM, VOCAB, False))
+    return out
+
+
+def algorithmic_bytes(k, n, m=1):
+    # int8 weights + fp32 column scales + fp32 activations + fp32 outputs
+    return k * n + 4 * n + 4 * m * k + 4 * m * n
+
+
+# ---- clocks during the timed region (NVML, read-only) -------------------------------------
+
+class ClockSampler:
+    def __init__(self, device_index: int):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        nv = self.nv
+        names = {
+            "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+            "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+            "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+        }
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for k, bit in names.items():
+                    if r & bit and k != "gpu_idle":
+                        self.reasons.add(k)
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self):
+        if self.nv:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._thread:
+            self._stop.set()
+            self._thread.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
+                "reasons": sorted(self.reasons)}
+
+
+# ---- distributed plumbing -----------------------------------------------------------------
+
+def dist_setup(n_gpus: int):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---- the chain on the GPU -----------------------------------------------------------------
+
+def quantize_on_device(W):
+    """Synthetic-weight preparation (not timed): per-column symmetric int8 with the rule of the
+    reference's quant.cpp:6-28 (scale = max|col| / 127, round half away from zero, clamp)."""
+    import torch
+    scale = W.abs().amax(dim=0) / 127.0
+    inv = torch.where(scale > 0, 1.0 / scale, torch.zeros_like(scale))
+    x = W * inv
+    q = torch.sign(x) * torch.floor(x.abs() + 0.5)
+    return q.clamp_(-127, 127).to(torch.int8), scale.float()
+
+
+class Chain:
+    def __init__(self, world, rank, seed=3):
+        import torch
+        self.world, self.rank = world, rank
+        self.shapes = chain_shapes()
+        g = torch.Generator(device="cuda")
+        self.mats = []  # (q, scale, k_loc, n_loc, row_parallel)
+        for idx, (name, k, n, rowp) in enumerate(self.shapes):
+            g.manual_seed(seed * 100003 + idx)
+            W = torch.randn(k, n, generator=g, device="cuda") * 0.02
+            q, s = quantize_on_device(W)
+            del W
+            if world > 1:
+                if rowp:
+                    kk = k // world
+                    q = q[rank * kk:(rank + 1) * kk].contiguous()
+                    kl, nl = kk, n
+                else:
+                    nn = n // world
+                    q = q[:, rank * nn:(rank + 1) * nn].contiguous()
+                    s = s[rank * nn:(rank + 1) * nn].contiguous()
+                    kl, nl = k, nn
+            else:
+                kl, nl = k, n
+            self.mats.append((q, s, kl, nl, rowp))
+        torch.cuda.synchronize()
+        # Activations: fresh U(-1, 1) per product; outputs one slot each.
+        self.a_off, self.c_off = [], []
+        a_tot = c_tot = 0
+        for (_, _, kl, nl, _) in self.mats:
+            self.a_off.append(a_tot)
+            self.c_off.append(c_tot)
+            a_tot += (kl + 3) // 4 * 4   # keep every vector 16-byte aligned
+            c_tot += (nl + 3) // 4 * 4
+        ga = torch.Generator(device="cpu")
+        ga.manual_seed(seed * 7 + rank)
+        self.a_host = (torch.rand(a_tot, generator=ga) * 2 - 1).pin_memory()
+        self.c_host = torch.empty(c_tot, dtype=torch.float32).pin_memory()
+        self.a_dev = self.a_host.cuda()
+        self.c_dev = torch.empty(c_tot, dtype=torch.float32, device="cuda")
+        self.bytes_per_step = sum(algorithmic_bytes(kl, nl) for (_, _, kl, nl, _) in self.mats) \
+            * 1  # this rank's share
+        self.total_bytes = sum(algorithmic_bytes(k, n) for (_, k, n, _) in self.shapes)
+
+    def launch_all(self, stream_handle, comm=None):
+        import llme_b200 as L
+        for i, (q, s, kl, nl, rowp) in enumerate(self.mats):
+            a = self.a_dev.data_ptr() + 4 * self.a_off[i]
+            c = self.c_dev.data_ptr() + 4 * self.c_off[i]
+            L.matmul_cuda_q8(1, nl, kl, a, q.data_ptr(), s.data_ptr(), c, "automatic", False, 0,
+                             L.FLAG_WEIGHTS_STATIC, stream_handle)
+            if rowp and comm is not None:
+                comm(c, nl)
+
+    def n_launches(self):
+        return len(self.mats)
+
+
+def capture(fn, stream):
+    import torch
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        fn()  # warm (lazy module loading, tensor-map cache, scratch growth)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def time_graph(graph, steps, warmup, stream, world, sampler=None):
+    import torch
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx = sampler if sampler is not None else _Null()
+    with ctx:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / 1e3
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+def gemv_4096_probe(steps=200):
+    """Config 0 in isolation: m = 1, 4096 x 4096 int8, back to back over 16 weight copies
+    (268 MB > 2 x L2), with and without programmatic dependent launch."""
+    import torch
+    import llme_b200 as L
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    copies = 16
+    qs, ss = [], []
+    for i in range(copies):
+        W = torch.randn(DIM, DIM, generator=g, device="cuda") * 0.02
+        q, s = quantize_on_device(W)
+        qs.append(q)
+        ss.append(s)
+    A = torch.rand(DIM, generator=g, device="cuda") * 2 - 1
+    C = torch.empty(copies, DIM, device="cuda")
+    stream = torch.cuda.Stream()
+    h = stream.cuda_stream
+    res = {}
+    for label, flags in (("pdl", L.FLAG_WEIGHTS_STATIC), ("serial", 0)):
+        def fn():
+            for i in range(copies):
+                L.matmul_cuda_q8(1, DIM, DIM, A.data_ptr(), qs[i].data_ptr(), ss[i].data_ptr(),
+                                 C[i].data_ptr(), "automatic", False, 0, flags, h)
+        graph = capture(fn, stream)
+        secs = time_graph(graph, steps, 5, stream, 1)
+        us = secs / (steps * copies) * 1e6
+        res[label] = {"us_per_gemv": round(us, 3),
+                      "GB_s": round(algorithmic_bytes(DIM, DIM) / (us * 1e-6) / 1e9, 1)}
+        del graph
+    return res
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def cpu_baseline_sample(chain, budget_s=8.0):
+    """The reference's matmul_parallel on layer 0's seven products + the classifier (the same
+    int8 bytes the GPU uses), on all host cores; GB/s of algorithmic bytes."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle  # the CPU baseline leg only
+    kind = "reference" if oracle.Reference.available(fast=True) else "port"
+    idx = list(range(7)) + [len(chain.mats) - 1]
+    mats = [(chain.mats[i][0].cpu().numpy(), chain.mats[i][1].cpu().numpy()) for i in idx]
+    rng = np.random.default_rng(1)
+    acts = [rng.uniform(-1, 1, (1, q.shape[0])).astype(np.float32) for q, _ in mats]
+    nbytes = sum(algorithmic_bytes(q.shape[0], q.shape[1]) for q, _ in mats)
+    if kind == "reference":
+        ref = oracle.Reference(fast=True)
+        hs = [ref.qtensor(q, s) for q, s in mats]
+        cores = ref.threads()
+
+        def one():
+            for a, h in zip(acts, hs):
+                ref.matmul_parallel_q8(a, h)
+    else:
+        cores = oracle.default_threads()
+
+        def one():
+            for a, (q, s) in zip(acts, mats):
+                oracle.matmul_parallel(a, q=q, scale=s)
+    one()
+    times, t_end = [], time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": round(nbytes / med / 1e9, 2), "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"layer 0 (7 products) + classifier, m=1, {nbytes / 1e6:.0f} MB of "
+                      f"algorithmic bytes per pass, median of {len(times)} passes"}
+
+
+def run_ours(args):
+    import torch
+    import llme_b200 as L
+    world, rank, local = dist_setup(args.gpus)
+    L.load()
+    if not L.device_supported():
+        raise SystemExit("this benchmark needs an sm_100 (B200) GPU")
+    chain = Chain(world, rank)
+    comm = None
+    if world > 1:
+        import torch.distributed as dist
+        comm_stream = torch.cuda.Stream()
+
+        def comm(c_ptr, n):  # noqa: F811
+            raise NotImplementedError("multi-GPU exchange")
+    stream = torch.cuda.Stream()
+    h = stream.cuda_stream
+    graph = capture(lambda: chain.launch_all(h, comm), stream)
+    sampler = ClockSampler(local)
+    secs = time_graph(graph, args.steps, args.warmup, stream, world, sampler)
+    secs = max_over_ranks(secs, world)
+    value = chain.total_bytes * args.steps / secs / 1e9
+    ms_per_step = secs / args.steps * 1e3
+
+    # e2e: the same chain through the C ABI with host buffers, copies in the timed region.
+    def e2e_fn():
+        chain.a_dev.copy_(chain.a_host, non_blocking=True)
+        chain.launch_all(h, comm)
+        chain.c_host.copy_(chain.c_dev, non_blocking=True)
+    e2e_graph = capture(e2e_fn, stream)
+    e2e_secs = max_over_ranks(time_graph(e2e_graph, args.steps, args.warmup, stream, world), world)
+    e2e = {"value": round(chain.total_bytes * args.steps / e2e_secs / 1e9, 1), "unit": UNIT,
+           "h2d_bytes_per_step": int(chain.a_host.numel() * 4),
+           "d2h_bytes_per_step": int(chain.c_host.numel() * 4),
+           "ms_per_step": round(e2e_secs / args.steps * 1e3, 4)}
+
+    peak, peak_kind = peaks()
+    launches = chain.n_launches()
+    per_launch_bytes = chain.bytes_per_step / launches
+    per_launch_s = (secs / args.steps) / launches
+    achieved = per_launch_bytes / per_launch_s / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                "kernel": "gemv_tma_kernel<1,int8>",
+                "traffic": None}
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: N(0,0.02^2) weights quantised per column to int8, U(-1,1) activations",
+        "config": {"workload": "7B-shaped int8 decode matmul chain, m=1 (BASELINE configs[3])",
+                   "products_per_step": launches, "dim": DIM, "hidden": HIDDEN, "vocab": VOCAB,
+                   "layers": LAYERS, "weight_bytes_per_step": int(chain.total_bytes),
+                   "parallelism": f"tp{world}" if world > 1 else "single",
+                   "l2": "no flush: 6.6 GB of weights per step (>> 126 MB L2)",
+                   "launch": "one CUDA graph per step, programmatic dependent launch"},
+        "roofline": roofline, "e2e": e2e, "gpu_launches": launches * args.steps,
+        "clocks": sampler.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_extras:
+        line["gemv_4096x4096"] = gemv_4096_probe()
+        for v in line["gemv_4096x4096"].values():
+            v["frac"] = round(v["GB_s"] / peak, 4)
+        line["cpu_baseline"] = cpu_baseline_sample(chain)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph, e2e_graph
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle  # the reference arm: the reference's own CPU code
+    kind = "reference" if oracle.Reference.available(fast=True) else "port"
+    rng = np.random.default_rng(3)
+    shapes = chain_shapes()
+    sample = shapes[:7] + shapes[-1:]
+    mats = []
+    for _, k, n, _ in sample:
+        W = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
+        mats.append(oracle.Reference(fast=True).quantize_q8(W) if kind == "reference"
+                    else oracle.quantize_q8(W))
+    acts = [rng.uniform(-1, 1, (1, q.shape[0])).astype(np.float32) for q, _ in mats]
+    nbytes = sum(algorithmic_bytes(q.shape[0], q.shape[1]) for q, _ in mats)
+    if kind == "reference":
+        ref = oracle.Reference(fast=True)
+        hs = [ref.qtensor(q, s) for q, s in mats]
+        cores = ref.threads()
+
+        def step():
+            for a, hq in zip(acts, hs):
+                ref.matmul_parallel_q8(a, hq)
+    else:
+        cores = oracle.default_threads()
+
+        def step():
+            for a, (q, s) in zip(acts, mats):
+                oracle.matmul_parallel(a, q=q, scale=s)
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    secs = time.perf_counter() - t0
+    value = nbytes * args.steps / secs / 1e9
+    sample_desc = (f"layer 0 (7 products) + classifier of the chain, m=1, "
+                   f"{nbytes / 1e6:.0f} MB of algorithmic bytes per step")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(secs / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "7B-shaped int8 decode matmul chain, m=1 (BASELINE configs[3])",
+                       "sample": sample_desc},
+            "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores,
+                             "kind": kind, "sample": sample_desc},
+            "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the isolated 4096^2 GEMV probe and the CPU baseline")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,155 @@
+/*
+ * llme_b200.h -- the C ABI of the B200 (sm_100a) matmul library.
+ *
+ * This is the thin extern "C" layer under the drop-in C++ API
+ * (include/cuda_matmul.h, the same surface as the reference engine's
+ * src/cuda_matmul.h). Plain pointers, sizes and int status codes only: a C
+ * caller, a ctypes/cffi binding, or the C++ shim call these directly.
+ *
+ * Layouts (as the reference, cuda_matmul.h:94-107): A is m x k fp32 row-major
+ * activations, B is k x n row-major weights ("in x out"), fp32 or int8 with one
+ * fp32 scale per column (quant.h:4-9), C is m x n fp32 row-major. Every
+ * pointer is device memory unless said otherwise.
+ *
+ * Streams: `stream` is a cudaStream_t. NULL means the calling thread's
+ * per-thread default stream, which is where the reference launches (it is
+ * built with --default-stream=per-thread, cuda_matmul.h:7-12). Calls are
+ * asynchronous: they return before the GPU finishes.
+ *
+ * Errors: a nonzero status; llme_last_error() then holds a message for the
+ * calling thread (the text the reference puts in its exceptions).
+ */
+#ifndef LLME_B200_H
+#define LLME_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LLME_ABI_VERSION 1
+
+/* ---- status codes ------------------------------------------------------------------- */
+enum {
+    LLME_OK = 0,
+    LLME_E_INVALID = 1,     /* bad shape/argument: std::invalid_argument in the reference */
+    LLME_E_CUDA = 2,        /* CUDA error: std::runtime_error("cuda: <what>: <msg>") */
+    LLME_E_TIMEOUT = 3,     /* a bounded device-side wait gave up (see llme_device_status) */
+    LLME_E_UNSUPPORTED = 4, /* no usable sm_100 device, or a feature this build lacks */
+    LLME_E_NCCL = 5         /* NCCL error in a sharded call */
+};
+
+/* ---- kernel choice: GpuKernel, cuda_matmul.h:66-72 ---------------------------------- */
+enum {
+    LLME_KERNEL_AUTOMATIC = 0,   /* weight-streaming GEMV for m <= 8, split-K tiles up to m = 127,
+                                    tcgen05 tensor-core GEMM from m = 128 */
+    LLME_KERNEL_NAIVE = 1,       /* one thread per element of C, the reference's summation order */
+    LLME_KERNEL_TILED = 2,       /* whole-k tiles (tcgen05 GEMM where the shape allows it) */
+    LLME_KERNEL_TILED_SPLIT = 3, /* tiles with k split across CTAs, deterministic reduction */
+    LLME_KERNEL_SKINNY = 4       /* m <= 8 only: the weight-streaming GEMV */
+};
+
+/* ---- arithmetic of the tensor-core path ------------------------------------------------ */
+enum {
+    /* The tensor-core GEMM multiplies in TF32 (fp32 B) or bf16 (int8 B, exact; A rounded
+       to bf16), accumulating in fp32. Error bound: 5e-3 of the row's L2 norm. Default. */
+    LLME_MATH_TENSOR = 0,
+    /* fp32-faithful: every kernel keeps fp32 products (the tensor-core GEMM splits each
+       operand into high and low parts and runs three products), as the reference's SIMT
+       kernels do. Selected at load time by LLME_B200_MATH=fp32 in the environment. */
+    LLME_MATH_FP32 = 1
+};
+
+/* ---- call flags ------------------------------------------------------------------------ */
+enum {
+    /* B and scale are not written by the launch that precedes this one on the stream, so the
+       kernel may start streaming them before that launch finishes (programmatic dependent
+       launch). True for model weights; not assumed by default. */
+    LLME_FLAG_WEIGHTS_STATIC = 1u << 0
+};
+
+/* matmul_cuda(m, n, k, A, const float* B, C, kernel, fusion): cuda_matmul.h:97-99.
+ * C (+)= [rmsnorm(A) * rms_weight] x B. accumulate != 0 adds into C (MatmulFusion::accumulate,
+ * cuda_matmul.h:85-92); rms_weight != NULL (k floats, device) normalises each row of A first,
+ * eps 1e-5. m == 0 or n == 0 does nothing; k == 0 zeroes C unless accumulating. */
+int llme_matmul_f32(size_t m, size_t n, size_t k, const float* A, const float* B, float* C,
+                    int kernel, int accumulate, const float* rms_weight, unsigned flags,
+                    void* stream);
+
+/* matmul_cuda(m, n, k, A, const int8_t* B, scale, C, kernel, fusion): cuda_matmul.h:105-107.
+ * C (+)= [rmsnorm(A) * rms_weight] x (B * scale), B int8 k x n, scale n floats. */
+int llme_matmul_q8(size_t m, size_t n, size_t k, const float* A, const int8_t* B,
+                   const float* scale, float* C, int kernel, int accumulate,
+                   const float* rms_weight, unsigned flags, void* stream);
+
+/* Message for the last failed call on this thread ("" if none). Never NULL. */
+const char* llme_last_error(void);
+
+/* cuda_scratch_generation(), cuda_matmul.h:109-112: bumped whenever an internal scratch buffer
+ * is reallocated; a CUDA graph captured before the bump must be captured again. */
+size_t llme_scratch_generation(void);
+
+/* cuda_synchronize(), cuda_matmul.h:118-119: waits for all queued work on the device, then
+ * reports a failed launch (LLME_E_CUDA) or a device-side wait that gave up (LLME_E_TIMEOUT). */
+int llme_synchronize(void);
+
+/* cuda_available(), cuda_matmul.h:121-122: 1 if a CUDA device is usable, else 0. */
+int llme_device_available(void);
+
+/* 1 if device 0 (or the current device) is sm_100 (B200 class) and this build's kernels can run. */
+int llme_device_supported(void);
+
+/* Reads and clears the device-side error word (LLME_OK or LLME_E_TIMEOUT) of the current device.
+ * Synchronises the device. */
+int llme_device_status(void);
+
+/* Process-wide arithmetic of the tensor-core path (LLME_MATH_*). Returns the previous value,
+ * or -1 (message in llme_last_error) for an unknown mode. */
+int llme_set_math(int math);
+int llme_get_math(void);
+
+/* ---- memory helpers for callers without a CUDA runtime of their own (the C++ shim) ------- */
+int llme_alloc(void** ptr, size_t bytes);      /* cudaMalloc */
+int llme_free(void* ptr);                      /* cudaFree; NULL is fine */
+int llme_copy_to_device(void* dst, const void* src, size_t bytes);   /* waits */
+int llme_copy_to_host(void* dst, const void* src, size_t bytes);     /* waits */
+
+/* ---- host-side planning, exposed so the dispatch logic can be tested without a GPU -------- */
+enum {
+    LLME_PATH_NONE = 0,        /* nothing to launch (m == 0 or n == 0) */
+    LLME_PATH_ZERO = 1,        /* k == 0: memset of C */
+    LLME_PATH_NAIVE = 2,
+    LLME_PATH_GEMV_TMA = 3,    /* weight-streaming GEMV, TMA ring (aligned B, m <= 8) */
+    LLME_PATH_GEMV_LDG = 4,    /* weight-streaming GEMV, plain loads (ragged B) */
+    LLME_PATH_TILED_SIMT = 5,  /* fp32 SIMT tiles, k split across CTAs */
+    LLME_PATH_TCGEN05 = 6      /* tcgen05/TMEM tensor-core GEMM */
+};
+
+typedef struct {
+    int path;             /* LLME_PATH_* */
+    int kernel;           /* the kernel choice after resolving LLME_KERNEL_AUTOMATIC */
+    int rms_prepass;      /* 1 if rms_weight is applied by a separate pass over A */
+    int grid_x, grid_y;   /* launch grid of the main kernel */
+    int slices;           /* k slices reduced deterministically across CTAs (1 = none) */
+    int span;             /* rows of k per slice */
+    int tile_m, tile_n;   /* rows and columns of C per CTA */
+    size_t split_bytes;   /* split-K scratch: partial sums (0 when slices == 1) */
+    size_t counter_slots; /* split-K tickets needed (one per output tile) */
+    size_t norm_bytes;    /* scratch for the normalised copy of A (rms_prepass) */
+} llme_plan_t;
+
+/* The plan llme_matmul_f32 (is_q8 == 0) or llme_matmul_q8 (is_q8 == 1) would follow on a
+ * device with `sm_count` SMs, for A, B and the RMSNorm weight at the given device addresses
+ * (rms_addr 0 = no RMSNorm). No GPU is touched. Returns LLME_E_INVALID (with the same
+ * message) where the call would. */
+int llme_plan(size_t m, size_t n, size_t k, int is_q8, int kernel, int accumulate,
+              uintptr_t a_addr, uintptr_t b_addr, uintptr_t rms_addr, int sm_count, int math,
+              llme_plan_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLME_B200_H */

@@ -1,0 +1,541 @@
+// The C ABI (include/llme_b200.h): argument checks and kernel choice, device
+// scratch, the TMA descriptor cache, and the launches. Mirrors the reference's
+// matmul_impl (src/cuda_matmul.cu:399-448) for validation, error text and the
+// empty/k == 0 cases; the plan itself (llme_plan) is a pure function so the
+// dispatch logic can be tested without a GPU.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+using namespace llme;
+
+thread_local std::string g_error;
+
+int fail(int code, std::string msg) {
+    g_error = std::move(msg);
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(LLME_E_CUDA, std::string("cuda: ") + what + ": " + cudaGetErrorString(e));
+}
+
+std::string shapes(size_t m, size_t n, size_t k) {
+    return "(A is " + std::to_string(m) + "x" + std::to_string(k) + ", B is " + std::to_string(k) +
+           "x" + std::to_string(n) + ")";
+}
+
+size_t ceil_div(size_t x, size_t d) { return (x + d - 1) / d; }
+size_t round_up(size_t x, size_t to) { return ceil_div(x, to) * to; }
+
+// ---- math mode -------------------------------------------------------------------------
+
+std::atomic<int> g_math{-1};
+
+int math_mode() {
+    int v = g_math.load(std::memory_order_relaxed);
+    if (v < 0) {
+        const char* env = std::getenv("LLME_B200_MATH");
+        v = (env && std::strcmp(env, "fp32") == 0) ? LLME_MATH_FP32 : LLME_MATH_TENSOR;
+        int expected = -1;
+        g_math.compare_exchange_strong(expected, v);
+        v = g_math.load();
+    }
+    return v;
+}
+
+// ---- planning ----------------------------------------------------------------------------
+
+constexpr size_t kMaxElems = size_t{1} << 31;  // kernels index with int
+constexpr int kSkinnyMaxRows = 8;
+constexpr int kSplitMaxRows = 127;             // automatic: tiled_split below 128 rows
+
+struct PlanIn {
+    size_t m, n, k;
+    bool q8;
+    int kernel;
+    bool accumulate;
+    uintptr_t a_addr, b_addr, rms_addr;
+    int sms;
+    int math;
+};
+
+int make_plan(const PlanIn& in, llme_plan_t* p) {
+    std::memset(p, 0, sizeof(*p));
+    const size_t m = in.m, n = in.n, k = in.k;
+    int kernel = in.kernel;
+    if (kernel < LLME_KERNEL_AUTOMATIC || kernel > LLME_KERNEL_SKINNY)
+        return fail(LLME_E_INVALID, "matmul_cuda: unknown kernel " + std::to_string(kernel));
+    if (kernel == LLME_KERNEL_AUTOMATIC) {
+        kernel = m <= kSkinnyMaxRows ? LLME_KERNEL_SKINNY
+                 : m <= kSplitMaxRows ? LLME_KERNEL_TILED_SPLIT
+                                      : LLME_KERNEL_TILED;
+    }
+    p->kernel = kernel;
+    if (kernel == LLME_KERNEL_SKINNY && m > kSkinnyMaxRows)
+        return fail(LLME_E_INVALID,
+                    "matmul_cuda: skinny kernel takes at most 8 rows " + shapes(m, n, k));
+    if (m * k >= kMaxElems || k * n >= kMaxElems || m * n >= kMaxElems)
+        return fail(LLME_E_INVALID, "matmul_cuda: more than 2^31 elements " + shapes(m, n, k));
+    if (m == 0 || n == 0) {
+        p->path = LLME_PATH_NONE;
+        return LLME_OK;
+    }
+    if (k == 0) {
+        p->path = in.accumulate ? LLME_PATH_NONE : LLME_PATH_ZERO;
+        return LLME_OK;
+    }
+    const bool has_rms = in.rms_addr != 0;
+    const int sms = in.sms > 0 ? in.sms : 148;
+
+    if (kernel == LLME_KERNEL_SKINNY) {
+        const size_t esz = in.q8 ? 1 : 4;
+        const bool tma = in.b_addr % 16 == 0 && (n * esz) % 16 == 0 && in.a_addr % 16 == 0 &&
+                         k % 4 == 0 && (!has_rms || in.rms_addr % 16 == 0);
+        p->tile_m = static_cast<int>(m);
+        size_t strips, slices, span;
+        if (tma) {
+            p->path = LLME_PATH_GEMV_TMA;
+            p->tile_n = gemv_tma_cols(in.q8);
+            strips = ceil_div(n, p->tile_n);
+            // Two CTAs per SM; each slice at least two boxes deep.
+            const size_t target = 2 * static_cast<size_t>(sms);
+            slices = std::max<size_t>(1, std::min(target / strips, ceil_div(k, 2 * kGemvBoxRows)));
+            span = round_up(ceil_div(k, slices), kGemvBoxRows);
+        } else {
+            p->path = LLME_PATH_GEMV_LDG;
+            p->tile_n = kGemvLdgCols;
+            strips = ceil_div(n, p->tile_n);
+            const size_t target = 8 * static_cast<size_t>(sms);
+            slices = std::max<size_t>(1, std::min(target / strips, ceil_div(k, 256)));
+            span = ceil_div(k, slices);
+        }
+        slices = ceil_div(k, span);
+        p->grid_x = static_cast<int>(strips);
+        p->grid_y = static_cast<int>(slices);
+        p->slices = static_cast<int>(slices);
+        p->span = static_cast<int>(span);
+        if (slices > 1) {
+            p->counter_slots = strips;
+            p->split_bytes = strips * slices * (m * p->tile_n + m) * sizeof(float);
+        }
+        return LLME_OK;
+    }
+
+    // naive / tiled / tiled_split: A is normalised by a separate pass first.
+    p->rms_prepass = has_rms ? 1 : 0;
+    if (has_rms) p->norm_bytes = m * k * sizeof(float);
+    if (kernel == LLME_KERNEL_NAIVE) {
+        p->path = LLME_PATH_NAIVE;
+        p->tile_m = p->tile_n = 16;
+        p->grid_x = static_cast<int>(ceil_div(n, 16));
+        p->grid_y = static_cast<int>(ceil_div(m, 16));
+        p->slices = 1;
+        p->span = static_cast<int>(k);
+        return LLME_OK;
+    }
+    p->path = LLME_PATH_TILED_SIMT;
+    p->tile_m = kTiledBM;
+    p->tile_n = kTiledBN;
+    const size_t tiles = ceil_div(n, kTiledBN) * ceil_div(m, kTiledBM);
+    size_t slices = 1;
+    if (kernel == LLME_KERNEL_TILED_SPLIT) {
+        // Split k until about 4 CTAs per SM, each slice at least 256 deep.
+        const size_t target = 4 * static_cast<size_t>(sms);
+        slices = std::max<size_t>(1, std::min(ceil_div(target, tiles), ceil_div(k, 256)));
+    }
+    const size_t span = round_up(ceil_div(k, slices), kTiledBK);
+    slices = ceil_div(k, span);
+    p->grid_x = static_cast<int>(ceil_div(n, kTiledBN));
+    p->grid_y = static_cast<int>(ceil_div(m, kTiledBM));
+    p->slices = static_cast<int>(slices);
+    p->span = static_cast<int>(span);
+    if (slices > 1) {
+        p->counter_slots = tiles;
+        p->split_bytes = tiles * slices * kTiledBM * kTiledBN * sizeof(float);
+    }
+    return LLME_OK;
+}
+
+// ---- per-device state ------------------------------------------------------------------
+
+constexpr int kMaxDevices = 64;
+std::atomic<size_t> g_generation{0};
+
+struct Scratch {
+    void* ptr = nullptr;
+    size_t cap = 0;
+};
+
+struct DeviceState {
+    int sms = 0;
+    // Split-K buffer: [counters: counter_cap x u32, zeroed][partial sums ...].
+    Scratch split;
+    size_t counter_cap = 0;
+    Scratch norm;
+};
+
+std::mutex g_dev_mu;
+DeviceState g_dev[kMaxDevices];
+
+int current_device(int* dev) {
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return cuda_fail(e, "get device");
+    if (*dev < 0 || *dev >= kMaxDevices) return fail(LLME_E_UNSUPPORTED, "device index too large");
+    return LLME_OK;
+}
+
+int device_sms(int dev, int* sms) {
+    DeviceState& d = g_dev[dev];
+    if (d.sms == 0) {
+        int n = 0;
+        cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "get SMs");
+        d.sms = n;
+    }
+    *sms = d.sms;
+    return LLME_OK;
+}
+
+// Grow-only; every growth bumps the generation (a captured graph must be re-captured).
+int ensure_split(int dev, size_t counters, size_t bytes, cudaStream_t stream, SplitScratch* out,
+                 size_t partial_floats) {
+    DeviceState& d = g_dev[dev];
+    const size_t want_counters = std::max<size_t>(counters, d.counter_cap);
+    const size_t counter_bytes = round_up(want_counters * sizeof(unsigned), 256);
+    const size_t need = counter_bytes + round_up(bytes, 256);
+    if (need > d.split.cap || want_counters > d.counter_cap) {
+        const size_t cap = std::max(need, d.split.cap);
+        if (d.split.ptr) {
+            cudaError_t e = cudaFree(d.split.ptr);
+            if (e != cudaSuccess) return cuda_fail(e, "free scratch");
+            d.split.ptr = nullptr;
+            d.split.cap = 0;
+        }
+        cudaError_t e = cudaMalloc(&d.split.ptr, cap);
+        if (e != cudaSuccess) return cuda_fail(e, "alloc scratch");
+        d.split.cap = cap;
+        d.counter_cap = counter_bytes / sizeof(unsigned);
+        e = cudaMemsetAsync(d.split.ptr, 0, counter_bytes, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "zero scratch");
+        g_generation.fetch_add(1);
+    }
+    const size_t cbytes = round_up(d.counter_cap * sizeof(unsigned), 256);
+    out->counters = static_cast<unsigned*>(d.split.ptr);
+    out->partial = reinterpret_cast<float*>(static_cast<char*>(d.split.ptr) + cbytes);
+    out->partial_ss = out->partial + partial_floats;
+    return LLME_OK;
+}
+
+int ensure_norm(int dev, size_t bytes, float** out) {
+    DeviceState& d = g_dev[dev];
+    if (bytes > d.norm.cap) {
+        if (d.norm.ptr) {
+            cudaError_t e = cudaFree(d.norm.ptr);
+            if (e != cudaSuccess) return cuda_fail(e, "free scratch");
+            d.norm.ptr = nullptr;
+            d.norm.cap = 0;
+        }
+        cudaError_t e = cudaMalloc(&d.norm.ptr, bytes);
+        if (e != cudaSuccess) return cuda_fail(e, "alloc scratch");
+        d.norm.cap = bytes;
+        g_generation.fetch_add(1);
+    }
+    *out = static_cast<float*>(d.norm.ptr);
+    return LLME_OK;
+}
+
+// ---- TMA descriptors -------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+struct MapKey {
+    uintptr_t ptr;
+    int dtype, rank;
+    uint64_t d0, d1;
+    uint32_t b0, b1;
+    bool operator==(const MapKey& o) const {
+        return ptr == o.ptr && dtype == o.dtype && rank == o.rank && d0 == o.d0 && d1 == o.d1 &&
+               b0 == o.b0 && b1 == o.b1;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey& k) const {
+        size_t h = std::hash<uintptr_t>()(k.ptr);
+        auto mix = [&h](uint64_t v) { h ^= std::hash<uint64_t>()(v) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2); };
+        mix(static_cast<uint64_t>(k.dtype) << 8 | static_cast<uint64_t>(k.rank));
+        mix(k.d0);
+        mix(k.d1);
+        mix(static_cast<uint64_t>(k.b0) << 32 | k.b1);
+        return h;
+    }
+};
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+// Row-major matrix of `rows` x `cols` elements (rank 2), or a vector (rows == 0, rank 1),
+// tiled into boxes of box_cols x box_rows.
+int tensor_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t rows, uint64_t cols,
+               uint32_t box_cols, uint32_t box_rows, CUtensorMap* out) {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                             &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!g_encode) return fail(LLME_E_UNSUPPORTED, "cuda: cuTensorMapEncodeTiled is unavailable");
+    const int rank = rows ? 2 : 1;
+    const MapKey key{reinterpret_cast<uintptr_t>(ptr), static_cast<int>(dtype), rank, cols, rows,
+                     box_cols, box_rows};
+    {
+        std::lock_guard<std::mutex> lk(g_map_mu);
+        auto it = g_maps.find(key);
+        if (it != g_maps.end()) {
+            *out = it->second;
+            return LLME_OK;
+        }
+    }
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * esz};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(out, dtype, rank, const_cast<void*>(ptr), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(LLME_E_CUDA, "cuda: encode tensor map: CUresult " + std::to_string(int(r)));
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    if (g_maps.size() > 8192) g_maps.clear();
+    g_maps.emplace(key, *out);
+    return LLME_OK;
+}
+
+// ---- the call --------------------------------------------------------------------------
+
+int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float* scale, float* C,
+        bool q8, int kernel, bool accumulate, const float* rms, unsigned flags, void* stream_ptr) {
+    g_error.clear();
+    cudaStream_t stream = stream_ptr ? static_cast<cudaStream_t>(stream_ptr) : cudaStreamPerThread;
+    int dev = 0, sms = 0;
+    int st = current_device(&dev);
+    if (st) return st;
+    st = device_sms(dev, &sms);
+    if (st) return st;
+    PlanIn in{m,
+              n,
+              k,
+              q8,
+              kernel,
+              accumulate,
+              reinterpret_cast<uintptr_t>(A),
+              reinterpret_cast<uintptr_t>(B),
+              reinterpret_cast<uintptr_t>(rms),
+              sms,
+              math_mode()};
+    llme_plan_t p;
+    st = make_plan(in, &p);
+    if (st) return st;
+    if (p.path == LLME_PATH_NONE) return LLME_OK;
+    if (p.path == LLME_PATH_ZERO) {
+        cudaError_t e = cudaMemsetAsync(C, 0, m * n * sizeof(float), stream);
+        return e == cudaSuccess ? LLME_OK : cuda_fail(e, "memset");
+    }
+
+    std::lock_guard<std::mutex> lk(g_dev_mu);  // scratch is shared per device
+    SplitScratch split;
+    if (p.slices > 1) {
+        // Partial sums first, then (GEMV with RMSNorm) the per-slice sums of squares.
+        const size_t partial_floats =
+            p.path == LLME_PATH_TILED_SIMT
+                ? static_cast<size_t>(p.counter_slots) * p.slices * kTiledBM * kTiledBN
+                : static_cast<size_t>(p.grid_x) * p.slices * m * p.tile_n;
+        st = ensure_split(dev, p.counter_slots, p.split_bytes, stream, &split, partial_floats);
+        if (st) return st;
+    }
+    const float* a_in = A;
+    if (p.rms_prepass) {
+        float* normed = nullptr;
+        st = ensure_norm(dev, p.norm_bytes, &normed);
+        if (st) return st;
+        cudaError_t e = launch_rmsnorm_rows(static_cast<int>(m), static_cast<int>(k), A, rms,
+                                            normed, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "launch");
+        a_in = normed;
+    }
+
+    cudaError_t e = cudaSuccess;
+    if (p.path == LLME_PATH_GEMV_TMA || p.path == LLME_PATH_GEMV_LDG) {
+        GemvArgs g;
+        g.m = static_cast<int>(m);
+        g.n = static_cast<int>(n);
+        g.k = static_cast<int>(k);
+        g.A = A;
+        g.B = B;
+        g.scale = scale;
+        g.rms = rms;
+        g.C = C;
+        g.q8 = q8;
+        g.accumulate = accumulate;
+        g.slices = p.slices;
+        g.span = p.span;
+        g.strips = p.grid_x;
+        g.split = split;
+        g.stream = stream;
+        g.pdl = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
+        if (p.path == LLME_PATH_GEMV_TMA) {
+            CUtensorMap tmB, tmA, tmW;
+            st = q8 ? tensor_map(B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, kGemvRowBytes,
+                                 kGemvBoxRows, &tmB)
+                    : tensor_map(B, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k, n, kGemvRowBytes / 4,
+                                 kGemvBoxRows, &tmB);
+            if (st) return st;
+            st = tensor_map(A, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, k, kGemvBoxRows,
+                            static_cast<uint32_t>(m), &tmA);
+            if (st) return st;
+            if (rms) {
+                st = tensor_map(rms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 0, k, kGemvBoxRows, 1,
+                                &tmW);
+                if (st) return st;
+            } else {
+                tmW = tmA;  // unused
+            }
+            e = launch_gemv_tma(g, tmB, tmA, tmW);
+        } else {
+            e = launch_gemv_ldg(g);
+        }
+    } else {
+        TiledArgs t;
+        t.m = static_cast<int>(m);
+        t.n = static_cast<int>(n);
+        t.k = static_cast<int>(k);
+        t.A = a_in;
+        t.B = B;
+        t.scale = scale;
+        t.C = C;
+        t.q8 = q8;
+        t.accumulate = accumulate;
+        t.slices = p.slices;
+        t.span = p.span;
+        t.split = split;
+        t.stream = stream;
+        e = p.path == LLME_PATH_NAIVE ? launch_naive(t) : launch_tiled_simt(t);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "launch");
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "launch");
+    return LLME_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int llme_matmul_f32(size_t m, size_t n, size_t k, const float* A, const float* B, float* C,
+                    int kernel, int accumulate, const float* rms_weight, unsigned flags,
+                    void* stream) {
+    return run(m, n, k, A, B, nullptr, C, false, kernel, accumulate != 0, rms_weight, flags,
+               stream);
+}
+
+int llme_matmul_q8(size_t m, size_t n, size_t k, const float* A, const int8_t* B,
+                   const float* scale, float* C, int kernel, int accumulate,
+                   const float* rms_weight, unsigned flags, void* stream) {
+    return run(m, n, k, A, B, scale, C, true, kernel, accumulate != 0, rms_weight, flags, stream);
+}
+
+const char* llme_last_error(void) { return g_error.c_str(); }
+
+size_t llme_scratch_generation(void) { return g_generation.load(); }
+
+int llme_synchronize(void) {
+    g_error.clear();
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "synchronize");
+    const unsigned dev_err = read_and_clear_gemv_error() | read_and_clear_tiled_error();
+    if (dev_err) return fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up");
+    return LLME_OK;
+}
+
+int llme_device_available(void) {
+    int count = 0;
+    return cudaGetDeviceCount(&count) == cudaSuccess && count > 0;
+}
+
+int llme_device_supported(void) {
+    int dev = 0, major = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+        return 0;
+    return major == 10;
+}
+
+int llme_device_status(void) {
+    g_error.clear();
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "synchronize");
+    const unsigned dev_err = read_and_clear_gemv_error() | read_and_clear_tiled_error();
+    return dev_err ? fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up") : LLME_OK;
+}
+
+int llme_set_math(int math) {
+    const int prev = math_mode();
+    if (math != LLME_MATH_TENSOR && math != LLME_MATH_FP32) {
+        fail(LLME_E_INVALID, "llme_set_math: unknown mode " + std::to_string(math));
+        return -1;
+    }
+    g_math.store(math);
+    return prev;
+}
+
+int llme_get_math(void) { return math_mode(); }
+
+int llme_alloc(void** ptr, size_t bytes) {
+    *ptr = nullptr;
+    if (bytes == 0) return LLME_OK;
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "alloc");
+}
+
+int llme_free(void* ptr) {
+    if (!ptr) return LLME_OK;
+    cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "free");
+}
+
+int llme_copy_to_device(void* dst, const void* src, size_t bytes) {
+    if (!bytes) return LLME_OK;
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, cudaStreamPerThread);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamPerThread);
+    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "upload");
+}
+
+int llme_copy_to_host(void* dst, const void* src, size_t bytes) {
+    if (!bytes) return LLME_OK;
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, cudaStreamPerThread);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamPerThread);
+    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "download");
+}
+
+int llme_plan(size_t m, size_t n, size_t k, int is_q8, int kernel, int accumulate,
+              uintptr_t a_addr, uintptr_t b_addr, uintptr_t rms_addr, int sm_count, int math,
+              llme_plan_t* out) {
+    g_error.clear();
+    PlanIn in{m, n, k, is_q8 != 0, kernel, accumulate != 0, a_addr, b_addr, rms_addr, sm_count, math};
+    return make_plan(in, out);
+}
+
+}  // extern "C"

@@ -1,0 +1,76 @@
+// Host-side launchers of the sm_100a kernels, shared between the .cu files
+// and the C ABI (capi.cu). Internal to the library.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace llme {
+
+// Deterministic split-K across CTAs: a CTA that owns slice s of a tile writes
+// its partial sums to partial[(tile * slices + s) * tile_elems + e], bumps
+// counters[tile], and the CTA that brings the count to `slices` adds the
+// slices in order s = 0, 1, ... and writes C, then resets the counter to 0
+// (so counters are all zero between launches).
+struct SplitScratch {
+    float* partial = nullptr;     // tiles * slices * tile_elems floats
+    float* partial_ss = nullptr;  // tiles * slices * rows floats (RMSNorm sums of squares)
+    unsigned* counters = nullptr; // one per tile, zero between launches
+};
+
+struct GemvArgs {
+    int m = 0, n = 0, k = 0;
+    const float* A = nullptr;
+    const void* B = nullptr;        // int8 or fp32, k x n
+    const float* scale = nullptr;   // int8 only
+    const float* rms = nullptr;     // k floats or null
+    float* C = nullptr;
+    bool q8 = false;
+    bool accumulate = false;
+    int slices = 1;                 // k slices per column strip (grid y)
+    int span = 0;                   // rows of k per slice (multiple of the box depth)
+    int strips = 0;                 // column strips (grid x)
+    SplitScratch split;
+    cudaStream_t stream = nullptr;
+    bool pdl = false;               // launch with programmatic stream serialization
+};
+
+// Columns of C per CTA and rows per TMA box of the TMA GEMV.
+constexpr int kGemvRowBytes = 256;
+constexpr int kGemvBoxRows = 64;
+inline int gemv_tma_cols(bool q8) { return q8 ? kGemvRowBytes : kGemvRowBytes / 4; }
+constexpr int kGemvLdgCols = 32;
+
+// TMA GEMV: B, A (and rms weight) read through the given tensor maps.
+cudaError_t launch_gemv_tma(const GemvArgs& a, const CUtensorMap& tmB, const CUtensorMap& tmA,
+                            const CUtensorMap& tmW);
+// Plain-load GEMV for shapes the TMA path cannot take (ragged rows, unaligned pointers).
+cudaError_t launch_gemv_ldg(const GemvArgs& a);
+
+struct TiledArgs {
+    int m = 0, n = 0, k = 0;
+    const float* A = nullptr;
+    const void* B = nullptr;
+    const float* scale = nullptr;
+    float* C = nullptr;
+    bool q8 = false;
+    bool accumulate = false;
+    int slices = 1, span = 0;
+    SplitScratch split;
+    cudaStream_t stream = nullptr;
+};
+constexpr int kTiledBM = 64, kTiledBN = 64, kTiledBK = 16;
+cudaError_t launch_tiled_simt(const TiledArgs& a);
+cudaError_t launch_naive(const TiledArgs& a);
+
+// out = rmsnorm(A) * w per row (eps 1e-5), m rows of k.
+cudaError_t launch_rmsnorm_rows(int m, int k, const float* A, const float* w, float* out,
+                                cudaStream_t stream);
+
+// Reads and clears the device error words of the kernels in each file.
+unsigned read_and_clear_gemv_error();
+unsigned read_and_clear_tiled_error();
+
+}  // namespace llme

@@ -1,0 +1,217 @@
+"""Python binding of the B200 matmul library's C ABI (include/llme_b200.h).
+
+A thin ctypes layer with the reference's operator interface for this path
+(src/cuda_matmul.h:94-107): matmul_cuda on raw device pointers for fp32 or int8
+weights, with the MatmulFusion fields (accumulate, rms_weight), the GpuKernel
+names, cuda_scratch_generation, cuda_synchronize and cuda_available. Errors
+follow the reference's exception split: InvalidArgument (a ValueError, for the
+reference's std::invalid_argument) and CudaError (a RuntimeError, for its
+std::runtime_error "cuda: ..." messages).
+
+PyTorch is used only to hand over device memory and streams (the `matmul`
+helper); the arithmetic is entirely in libllme_b200.so. There is no fallback:
+if the library is missing, loading raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "lib", "libllme_b200.so")
+
+KERNELS = {"automatic": 0, "naive": 1, "tiled": 2, "tiled_split": 3, "skinny": 4}
+PATHS = {0: "none", 1: "zero", 2: "naive", 3: "gemv_tma", 4: "gemv_ldg", 5: "tiled_simt",
+         6: "tcgen05"}
+MATH_TENSOR, MATH_FP32 = 0, 1
+FLAG_WEIGHTS_STATIC = 1
+
+OK, E_INVALID, E_CUDA, E_TIMEOUT, E_UNSUPPORTED, E_NCCL = range(6)
+
+# cudaStreamLegacy: torch's default stream has handle 0, which the C ABI would read as
+# "per-thread default stream"; pass the legacy handle instead so both sides agree.
+_STREAM_LEGACY = 1
+
+
+class InvalidArgument(ValueError):
+    """std::invalid_argument in the reference (shape mismatch, skinny with m > 8, 2^31)."""
+
+
+class CudaError(RuntimeError):
+    """std::runtime_error("cuda: <what>: <message>") in the reference."""
+
+
+class DeviceTimeout(RuntimeError):
+    """A bounded device-side wait gave up (LLME_E_TIMEOUT)."""
+
+
+class Plan(ctypes.Structure):
+    _fields_ = [
+        ("path", ctypes.c_int), ("kernel", ctypes.c_int), ("rms_prepass", ctypes.c_int),
+        ("grid_x", ctypes.c_int), ("grid_y", ctypes.c_int), ("slices", ctypes.c_int),
+        ("span", ctypes.c_int), ("tile_m", ctypes.c_int), ("tile_n", ctypes.c_int),
+        ("split_bytes", ctypes.c_size_t), ("counter_slots", ctypes.c_size_t),
+        ("norm_bytes", ctypes.c_size_t),
+    ]
+
+    def as_dict(self) -> dict:
+        d = {name: getattr(self, name) for name, _ in self._fields_}
+        d["path_name"] = PATHS.get(self.path, "?")
+        return d
+
+
+_lib = None
+
+
+def library_path() -> str:
+    return LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Loads libllme_b200.so (built by llm-engine_b200/build.py); raises if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python llm-engine_b200/build.py` "
+            "(there is no CPU fallback)")
+    lib = ctypes.CDLL(LIB_PATH)
+    sz, vp, i, u = ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int, ctypes.c_uint
+    lib.llme_matmul_f32.argtypes = [sz, sz, sz, vp, vp, vp, i, i, vp, u, vp]
+    lib.llme_matmul_q8.argtypes = [sz, sz, sz, vp, vp, vp, vp, i, i, vp, u, vp]
+    lib.llme_matmul_f32.restype = lib.llme_matmul_q8.restype = i
+    lib.llme_last_error.restype = ctypes.c_char_p
+    lib.llme_scratch_generation.restype = sz
+    for f in ("llme_synchronize", "llme_device_available", "llme_device_supported",
+              "llme_device_status", "llme_get_math"):
+        getattr(lib, f).restype = i
+        getattr(lib, f).argtypes = []
+    lib.llme_set_math.argtypes = [i]
+    lib.llme_set_math.restype = i
+    lib.llme_plan.argtypes = [sz, sz, sz, i, i, i, ctypes.c_size_t, ctypes.c_size_t,
+                              ctypes.c_size_t, i, i, ctypes.POINTER(Plan)]
+    lib.llme_plan.restype = i
+    lib.llme_alloc.argtypes = [ctypes.POINTER(vp), sz]
+    lib.llme_free.argtypes = [vp]
+    lib.llme_copy_to_device.argtypes = [vp, vp, sz]
+    lib.llme_copy_to_host.argtypes = [vp, vp, sz]
+    for f in ("llme_alloc", "llme_free", "llme_copy_to_device", "llme_copy_to_host"):
+        getattr(lib, f).restype = i
+    _lib = lib
+    return lib
+
+
+def last_error() -> str:
+    return load().llme_last_error().decode()
+
+
+def _check(status: int) -> None:
+    if status == OK:
+        return
+    msg = last_error()
+    if status == E_INVALID:
+        raise InvalidArgument(msg)
+    if status == E_TIMEOUT:
+        raise DeviceTimeout(msg)
+    raise CudaError(msg or f"cuda: error {status}")
+
+
+def _kernel_id(kernel) -> int:
+    if isinstance(kernel, int):
+        return kernel
+    return KERNELS[kernel]
+
+
+def matmul_cuda_f32(m: int, n: int, k: int, A: int, B: int, C: int, kernel="automatic",
+                    accumulate: bool = False, rms_weight: int = 0, flags: int = 0,
+                    stream: int | None = None) -> None:
+    """C (+)= [rmsnorm(A)] x B on device pointers (cuda_matmul.h:97-99)."""
+    _check(load().llme_matmul_f32(m, n, k, A, B, C, _kernel_id(kernel), int(bool(accumulate)),
+                                  rms_weight or None, flags, stream or None))
+
+
+def matmul_cuda_q8(m: int, n: int, k: int, A: int, B: int, scale: int, C: int,
+                   kernel="automatic", accumulate: bool = False, rms_weight: int = 0,
+                   flags: int = 0, stream: int | None = None) -> None:
+    """C (+)= [rmsnorm(A)] x (B * scale) with int8 B on device pointers (cuda_matmul.h:105-107)."""
+    _check(load().llme_matmul_q8(m, n, k, A, B, scale, C, _kernel_id(kernel),
+                                 int(bool(accumulate)), rms_weight or None, flags, stream or None))
+
+
+def plan(m: int, n: int, k: int, q8: bool, kernel="automatic", accumulate: bool = False,
+         a_addr: int = 256, b_addr: int = 256, rms_addr: int = 0, sm_count: int = 148,
+         math: int = MATH_TENSOR) -> dict:
+    """The dispatch decision for a call, computed on the host only (no GPU needed)."""
+    p = Plan()
+    _check(load().llme_plan(m, n, k, int(bool(q8)), _kernel_id(kernel), int(bool(accumulate)),
+                            a_addr, b_addr, rms_addr, sm_count, math, ctypes.byref(p)))
+    return p.as_dict()
+
+
+def scratch_generation() -> int:
+    return load().llme_scratch_generation()
+
+
+def synchronize() -> None:
+    _check(load().llme_synchronize())
+
+
+def device_status() -> None:
+    _check(load().llme_device_status())
+
+
+def available() -> bool:
+    return bool(load().llme_device_available())
+
+
+def device_supported() -> bool:
+    return bool(load().llme_device_supported())
+
+
+def set_math(mode: int) -> int:
+    prev = load().llme_set_math(mode)
+    if prev < 0:
+        _check(E_INVALID)
+    return prev
+
+
+def get_math() -> int:
+    return load().llme_get_math()
+
+
+def torch_stream_handle(stream=None) -> int:
+    """The cudaStream_t of a torch stream (default: current), mapped for the C ABI."""
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    h = s.cuda_stream
+    return h if h else _STREAM_LEGACY
+
+
+def matmul(A, B, scale=None, C=None, kernel="automatic", accumulate: bool = False,
+           rms_weight=None, weights_static: bool = False, stream=None):
+    """Convenience over torch CUDA tensors: A (m x k fp32), B (k x n fp32 or int8), scale
+    (n fp32, int8 only), C (m x n fp32, allocated if None). Returns C. Runs on the current
+    torch stream unless `stream` is given."""
+    import torch
+    m, k = A.shape
+    kb, n = B.shape
+    if kb != k:
+        raise InvalidArgument(f"matmul_cuda: inner dimensions differ (A is {m}x{k}, B is {kb}x{n})")
+    for t in (A, B, C, scale, rms_weight):
+        if t is not None and not t.is_contiguous():
+            raise InvalidArgument("matmul: tensors must be contiguous row-major")
+    if C is None:
+        C = torch.empty((m, n), dtype=torch.float32, device=A.device)
+    flags = FLAG_WEIGHTS_STATIC if weights_static else 0
+    h = torch_stream_handle(stream)
+    rms = rms_weight.data_ptr() if rms_weight is not None else 0
+    if B.dtype == torch.int8:
+        if scale is None:
+            raise InvalidArgument("matmul: int8 B needs a scale vector")
+        matmul_cuda_q8(m, n, k, A.data_ptr(), B.data_ptr(), scale.data_ptr(), C.data_ptr(),
+                       kernel, accumulate, rms, flags, h)
+    else:
+        matmul_cuda_f32(m, n, k, A.data_ptr(), B.data_ptr(), C.data_ptr(), kernel, accumulate,
+                        rms, flags, h)
+    return C

@@ -1,0 +1,227 @@
+"""TEST INFRASTRUCTURE ONLY: numpy bindings of the CPU oracle.
+
+Two libraries, both built by oracle/Makefile:
+  * liboracle.so      -- the plain-C restatement of the reference's CPU matmul path
+                         (oracle.c; each function cites the reference file:line it follows);
+  * _ref/libllme_ref*.so -- the reference's own matmul.cpp / quant.cpp / ops.cpp /
+                         thread_pool.cpp compiled from its sources (present only where the
+                         reference tree was available at build time).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs import this module,
+and only as the checker or the timed CPU baseline; the product never does.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libllme_ref.so")
+REF_FAST_SO = os.path.join(HERE, "_ref", "libllme_ref_fast.so")
+
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_i8p = np.ctypeslib.ndpointer(dtype=np.int8, flags="C_CONTIGUOUS")
+_sz = ctypes.c_size_t
+
+
+def build() -> None:
+    """Builds liboracle.so (and oracle/_ref when the reference sources are present)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    if os.path.isdir("/root/reference/src"):
+        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+
+
+_oracle = None
+
+
+def oracle_lib() -> ctypes.CDLL:
+    global _oracle
+    if _oracle is None:
+        if not os.path.exists(ORACLE_SO):
+            build()
+        lib = ctypes.CDLL(ORACLE_SO)
+        lib.orc_quantize_q8.argtypes = [_sz, _sz, _f32p, _i8p, _f32p]
+        lib.orc_dequantize.argtypes = [_sz, _sz, _i8p, _f32p, _f32p]
+        lib.orc_matmul_naive.argtypes = [_sz, _sz, _sz, _f32p, _f32p, _f32p]
+        lib.orc_matmul_naive_q8.argtypes = [_sz, _sz, _sz, _f32p, _i8p, _f32p, _f32p]
+        lib.orc_rmsnorm.argtypes = [_sz, _sz, _f32p, _f32p, ctypes.c_float, _f32p]
+        vp = ctypes.c_void_p
+        lib.orc_matmul_parallel.argtypes = [_sz, _sz, _sz, vp, vp, vp, vp, vp, ctypes.c_uint]
+        lib.orc_default_threads.restype = ctypes.c_uint
+        _oracle = lib
+    return _oracle
+
+
+def _c(a, dtype):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+def quantize_q8(B: np.ndarray):
+    """quant.cpp:6-28 -> (q int8 [rows, cols], scale fp32 [cols])."""
+    B = _c(B, np.float32)
+    rows, cols = B.shape
+    q = np.empty((rows, cols), np.int8)
+    s = np.empty(cols, np.float32)
+    oracle_lib().orc_quantize_q8(rows, cols, B, q, s)
+    return q, s
+
+
+def dequantize(q: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    q = _c(q, np.int8)
+    rows, cols = q.shape
+    out = np.empty((rows, cols), np.float32)
+    oracle_lib().orc_dequantize(rows, cols, q, _c(scale, np.float32), out)
+    return out
+
+
+def matmul_naive(A: np.ndarray, B: np.ndarray) -> np.ndarray:
+    """matmul.cpp:205-217 (fp32, i-k-j order)."""
+    A, B = _c(A, np.float32), _c(B, np.float32)
+    m, k = A.shape
+    n = B.shape[1]
+    C = np.empty((m, n), np.float32)
+    oracle_lib().orc_matmul_naive(m, n, k, A, B, C)
+    return C
+
+
+def matmul_naive_q8(A: np.ndarray, q: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    """matmul_naive(A, dequantize(q)) without materialising the fp32 weights."""
+    A, q = _c(A, np.float32), _c(q, np.int8)
+    m, k = A.shape
+    n = q.shape[1]
+    C = np.empty((m, n), np.float32)
+    oracle_lib().orc_matmul_naive_q8(m, n, k, A, q, _c(scale, np.float32), C)
+    return C
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float = 1e-5) -> np.ndarray:
+    """ops.cpp:8-26 (double accumulation)."""
+    x = _c(x, np.float32)
+    rows, cols = x.shape
+    y = np.empty_like(x)
+    oracle_lib().orc_rmsnorm(rows, cols, x, _c(w, np.float32), eps, y)
+    return y
+
+
+def matmul_parallel(A: np.ndarray, B=None, q=None, scale=None, threads: int = 0) -> np.ndarray:
+    """The CPU-baseline port of matmul.cpp:240-306 (pthreads)."""
+    A = _c(A, np.float32)
+    m, k = A.shape
+    if q is not None:
+        q, scale = _c(q, np.int8), _c(scale, np.float32)
+        n = q.shape[1]
+        args = (None, q.ctypes.data, scale.ctypes.data)
+    else:
+        B = _c(B, np.float32)
+        n = B.shape[1]
+        args = (B.ctypes.data, None, None)
+    C = np.empty((m, n), np.float32)
+    oracle_lib().orc_matmul_parallel(m, n, k, A.ctypes.data, *args, C.ctypes.data, threads)
+    return C
+
+
+def default_threads() -> int:
+    return int(oracle_lib().orc_default_threads())
+
+
+# ---- the reference's own code (oracle/_ref) --------------------------------------------------
+
+class Reference:
+    """The reference engine's CPU matmul / quant / rmsnorm, compiled from its sources."""
+
+    def __init__(self, fast: bool = False):
+        path = REF_FAST_SO if fast else REF_SO
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        lib = ctypes.CDLL(path)
+        lib.ref_last_error.restype = ctypes.c_char_p
+        lib.ref_pool_threads.restype = ctypes.c_uint
+        lib.ref_matmul_naive.argtypes = [_sz, _sz, _sz, _sz, _f32p, _f32p, _f32p]
+        lib.ref_matmul_parallel_f32.argtypes = [_sz, _sz, _sz, _f32p, _f32p, _f32p, ctypes.c_uint]
+        lib.ref_quantize_q8.argtypes = [_sz, _sz, _f32p, _i8p, _f32p]
+        lib.ref_dequantize.argtypes = [_sz, _sz, _i8p, _f32p, _f32p]
+        lib.ref_rmsnorm.argtypes = [_sz, _sz, _f32p, _f32p, _f32p]
+        lib.ref_qtensor_new.argtypes = [_sz, _sz, _i8p, _f32p]
+        lib.ref_qtensor_new.restype = ctypes.c_void_p
+        lib.ref_qtensor_free.argtypes = [ctypes.c_void_p]
+        lib.ref_matmul_parallel_q8.argtypes = [ctypes.c_void_p, _sz, _sz, _f32p, _f32p,
+                                               ctypes.c_uint]
+        self.lib = lib
+
+    @staticmethod
+    def available(fast: bool = False) -> bool:
+        return os.path.exists(REF_FAST_SO if fast else REF_SO)
+
+    def _check(self, st: int) -> None:
+        if st == 1:
+            raise ValueError(self.lib.ref_last_error().decode())
+        if st:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+
+    def threads(self) -> int:
+        return int(self.lib.ref_pool_threads())
+
+    def matmul_naive(self, A, B, b_rows=None):
+        A, B = _c(A, np.float32), _c(B, np.float32)
+        m, k = A.shape
+        n = B.shape[1]
+        C = np.empty((m, n), np.float32)
+        self._check(self.lib.ref_matmul_naive(m, n, k, B.shape[0] if b_rows is None else b_rows,
+                                              A, B, C))
+        return C
+
+    def matmul_parallel(self, A, B, threads: int = 0):
+        A, B = _c(A, np.float32), _c(B, np.float32)
+        m, k = A.shape
+        n = B.shape[1]
+        C = np.empty((m, n), np.float32)
+        self._check(self.lib.ref_matmul_parallel_f32(m, n, k, A, B, C, threads))
+        return C
+
+    def quantize_q8(self, B):
+        B = _c(B, np.float32)
+        rows, cols = B.shape
+        q = np.empty((rows, cols), np.int8)
+        s = np.empty(cols, np.float32)
+        self._check(self.lib.ref_quantize_q8(rows, cols, B, q, s))
+        return q, s
+
+    def dequantize(self, q, scale):
+        q = _c(q, np.int8)
+        out = np.empty(q.shape, np.float32)
+        self._check(self.lib.ref_dequantize(q.shape[0], q.shape[1], q, _c(scale, np.float32), out))
+        return out
+
+    def rmsnorm(self, x, w):
+        x = _c(x, np.float32)
+        y = np.empty_like(x)
+        self._check(self.lib.ref_rmsnorm(x.shape[0], x.shape[1], x, _c(w, np.float32), y))
+        return y
+
+    def qtensor(self, q, scale):
+        """A QTensor kept alive on the reference side; pass to matmul_parallel_q8."""
+        q, scale = _c(q, np.int8), _c(scale, np.float32)
+        h = self.lib.ref_qtensor_new(q.shape[0], q.shape[1], q, scale)
+        return _QHandle(self, h, q.shape)
+
+    def matmul_parallel_q8(self, A, qh: "_QHandle", threads: int = 0, out=None):
+        A = _c(A, np.float32)
+        m, k = A.shape
+        C = out if out is not None else np.empty((m, qh.shape[1]), np.float32)
+        self._check(self.lib.ref_matmul_parallel_q8(qh.handle, m, k, A, C, threads))
+        return C
+
+
+class _QHandle:
+    def __init__(self, ref: Reference, handle, shape):
+        self.ref, self.handle, self.shape = ref, handle, shape
+
+    def __del__(self):
+        try:
+            self.ref.lib.ref_qtensor_free(self.handle)
+        except Exception:
+            pass

@@ -1,0 +1,151 @@
+"""The C ABI boundary and the host-side dispatch logic (no GPU).
+
+Checks that libllme_b200.so loads and exports every entry point include/llme_b200.h
+declares, that libllme_b200_cxx.so exports the reference's C++ API (cuda_matmul.h), and
+the plan the dispatcher makes: kernel choice (cuda_matmul.cu:406-410), the argument
+errors and their messages (:411-417, test_cuda.cpp:277-287), empty and k == 0 handling
+(:418-422), the TMA / plain-load choice and the split-K sizing.
+"""
+from __future__ import annotations
+
+import os
+import re
+import subprocess
+
+import pytest
+
+import llme_b200 as L
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "llme_b200.h")
+CXX_LIB = os.path.join(REPO, "llm-engine_b200", "lib", "libllme_b200_cxx.so")
+
+
+def declared_functions() -> list[str]:
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(llme_\w+)\s*\(", text)))
+
+
+def exported(path: str, demangle: bool = False) -> str:
+    args = ["nm", "-D", "--defined-only"] + (["-C"] if demangle else []) + [path]
+    return subprocess.run(args, check=True, stdout=subprocess.PIPE, text=True).stdout
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    L.load()
+    names = declared_functions()
+    assert "llme_matmul_q8" in names and "llme_matmul_f32" in names
+    syms = exported(L.library_path())
+    for name in names:
+        assert re.search(rf"\bT {name}$", syms, re.M), name
+        assert hasattr(L.load(), name)
+
+
+def test_cxx_shim_exports_reference_api():
+    syms = exported(CXX_LIB, demangle=True)
+    for sig in ["matmul_cuda(DeviceTensor const&, DeviceTensor const&, DeviceTensor&, GpuKernel)",
+                "matmul_cuda(unsigned long, unsigned long, unsigned long, float const*, float const*, float*, GpuKernel, MatmulFusion const&)",
+                "matmul_cuda(unsigned long, unsigned long, unsigned long, float const*, signed char const*, float const*, float*, GpuKernel, MatmulFusion const&)",
+                "matmul_cuda(Tensor const&, Tensor const&, GpuKernel)",
+                "matmul_cuda(Tensor const&, QTensor const&, GpuKernel)",
+                "cuda_scratch_generation()", "cuda_synchronize()", "cuda_available()",
+                "DeviceTensor::upload(Tensor const&)", "DeviceTensor::download() const",
+                "DeviceQTensor::DeviceQTensor(QTensor const&)"]:
+        assert sig in syms, sig
+
+
+@pytest.mark.parametrize("m,kernel", [(1, "skinny"), (8, "skinny"), (9, "tiled_split"),
+                                      (64, "tiled_split"), (127, "tiled_split"), (128, "tiled"),
+                                      (512, "tiled")])
+def test_automatic_kernel_choice(m, kernel):
+    p = L.plan(m, 4096, 4096, q8=True)
+    assert p["kernel"] == L.KERNELS[kernel]
+
+
+def test_skinny_rejects_more_than_8_rows():
+    with pytest.raises(L.InvalidArgument) as e:
+        L.plan(9, 2, 2, q8=False, kernel="skinny")
+    assert "at most 8 rows" in str(e.value)
+    assert "9x2" in str(e.value)
+
+
+def test_rejects_2_pow_31_elements():
+    with pytest.raises(L.InvalidArgument) as e:
+        L.plan(1, 1 << 16, 1 << 15, q8=True)
+    assert "2^31" in str(e.value)
+    L.plan(1, (1 << 16) - 1, 1 << 15, q8=True)  # just below the limit
+
+
+def test_unknown_kernel_is_invalid():
+    with pytest.raises(L.InvalidArgument):
+        L.plan(1, 4, 4, q8=False, kernel=7)
+
+
+@pytest.mark.parametrize("m,n,k,acc,path", [(0, 5, 5, False, "none"), (3, 0, 5, False, "none"),
+                                            (1, 5, 0, False, "zero"), (12, 3, 0, True, "none"),
+                                            (12, 3, 0, False, "zero")])
+def test_empty_and_zero_k(m, n, k, acc, path):
+    assert L.plan(m, n, k, q8=False, accumulate=acc)["path_name"] == path
+
+
+def test_tma_path_needs_aligned_rows_and_pointers():
+    assert L.plan(1, 4096, 4096, q8=True)["path_name"] == "gemv_tma"
+    assert L.plan(1, 4100, 4096, q8=True)["path_name"] == "gemv_ldg"      # 4100 B rows
+    assert L.plan(1, 4112, 4096, q8=True)["path_name"] == "gemv_tma"
+    assert L.plan(1, 1028, 96, q8=False)["path_name"] == "gemv_tma"       # 4112 B rows
+    assert L.plan(1, 1027, 96, q8=False)["path_name"] == "gemv_ldg"
+    assert L.plan(1, 4096, 4096, q8=True, b_addr=257)["path_name"] == "gemv_ldg"
+    assert L.plan(1, 4096, 4097, q8=True)["path_name"] == "gemv_ldg"      # k % 4 (A rows)
+    assert L.plan(1, 4096, 4096, q8=True, rms_addr=260)["path_name"] == "gemv_ldg"
+    assert L.plan(1, 4096, 4096, q8=True, rms_addr=272)["path_name"] == "gemv_tma"
+
+
+@pytest.mark.parametrize("n,k", [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096),
+                                 (288, 4096), (4, 4096), (4100, 1000), (1, 17)])
+@pytest.mark.parametrize("q8", [True, False])
+@pytest.mark.parametrize("sms", [148, 132, 20])
+def test_split_k_plan_covers_k_exactly_once(n, k, q8, sms):
+    p = L.plan(1, n, k, q8=q8, sm_count=sms)
+    s, span = p["slices"], p["span"]
+    assert s >= 1 and span >= 1
+    assert (s - 1) * span < k <= s * span           # every row in exactly one slice
+    assert p["grid_y"] == s
+    assert p["grid_x"] * p["tile_n"] >= n
+    if p["path_name"] == "gemv_tma":
+        assert span % 64 == 0                       # boxes never straddle two slices
+        assert p["grid_x"] * p["grid_y"] <= max(2 * sms, p["grid_x"])
+    if s > 1:
+        assert p["split_bytes"] > 0 and p["counter_slots"] == p["grid_x"]
+    else:
+        assert p["split_bytes"] == 0
+
+
+def test_decode_shapes_fill_the_gpu():
+    # The BASELINE decode shapes launch close to two CTAs per SM on 148 SMs.
+    for n, k in [(4096, 4096), (11008, 4096), (4096, 11008)]:
+        p = L.plan(1, n, k, q8=True)
+        assert 0.8 * 296 <= p["grid_x"] * p["grid_y"] <= 296, (n, k, p)
+
+
+def test_rms_prepass_only_outside_the_gemv():
+    assert L.plan(4, 300, 288, q8=False, rms_addr=256)["rms_prepass"] == 0
+    p = L.plan(70, 130, 40, q8=False, rms_addr=256)
+    assert p["rms_prepass"] == 1 and p["norm_bytes"] == 70 * 40 * 4
+
+
+def test_tiled_split_sizes():
+    p = L.plan(16, 4096, 4096, q8=True, kernel="tiled_split")
+    assert p["path_name"] == "tiled_simt" and p["slices"] > 1
+    assert (p["slices"] - 1) * p["span"] < 4096 <= p["slices"] * p["span"]
+    p = L.plan(200, 33, 513, q8=False, kernel="tiled")
+    assert p["slices"] == 1
+
+
+def test_math_mode_roundtrip():
+    prev = L.get_math()
+    assert L.set_math(L.MATH_FP32) == prev
+    assert L.get_math() == L.MATH_FP32
+    L.set_math(prev)
+    with pytest.raises(L.InvalidArgument):
+        L.set_math(5)
