@@ -34,6 +34,14 @@ sys.path.insert(0, os.path.join(REPO, "llm-engine_b200"))
 
 DIM, HIDDEN, VOCAB, LAYERS = 4096, 11008, 32000, 32
 METRIC = "int8 decode-GEMV HBM GB/s (7B-shaped chain, m=1)"
+WORKLOAD_CONFIG = {
+    "chain": {"workload": "7B-shaped int8 decode matmul chain, m=1 (BASELINE configs[3])",
+              "dim": DIM, "hidden": HIDDEN, "vocab": VOCAB, "layers": LAYERS,
+              "l2": "no flush: 6.6 GB of weights per step (>> 126 MB L2)"},
+    "gemv": {"workload": "decode GEMV m=1, 4096x4096 int8 (BASELINE configs[0]), 16 weight "
+                         "copies per step",
+             "l2": "no flush: 16 distinct 16.8 MB weights per step (268 MB > 2 x L2)"},
+}
 UNIT = "GB/s"
 
 
@@ -155,11 +163,17 @@ def quantize_on_device(W):
     return q.clamp_(-127, 127).to(torch.int8), scale.float()
 
 
+def gemv_shapes(copies=16):
+    """Config 0: m = 1, 4096 x 4096 int8, over `copies` distinct weight matrices per step
+    (16 x 16.8 MB = 268 MB > 2 x L2, so every product streams from HBM)."""
+    return [(f"gemv{i}", DIM, DIM, False) for i in range(copies)]
+
+
 class Chain:
-    def __init__(self, world, rank, seed=3):
+    def __init__(self, world, rank, shapes, seed=3):
         import torch
         self.world, self.rank = world, rank
-        self.shapes = chain_shapes()
+        self.shapes = shapes
         g = torch.Generator(device="cuda")
         self.mats = []  # (q, scale, k_loc, n_loc, row_parallel)
         for idx, (name, k, n, rowp) in enumerate(self.shapes):
@@ -341,7 +355,10 @@ def run_ours(args):
     L.load()
     if not L.device_supported():
         raise SystemExit("this benchmark needs an sm_100 (B200) GPU")
-    chain = Chain(world, rank)
+    if args.workload == "chain":
+        chain = Chain(world, rank, chain_shapes(), seed=3)
+    else:
+        chain = Chain(world, rank, gemv_shapes(), seed=0)
     comm = None
     if world > 1:
         import torch.distributed as dist
@@ -384,16 +401,15 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: N(0,0.02^2) weights quantised per column to int8, U(-1,1) activations",
-        "config": {"workload": "7B-shaped int8 decode matmul chain, m=1 (BASELINE configs[3])",
-                   "products_per_step": launches, "dim": DIM, "hidden": HIDDEN, "vocab": VOCAB,
-                   "layers": LAYERS, "weight_bytes_per_step": int(chain.total_bytes),
+        "config": WORKLOAD_CONFIG[args.workload] | {
+                   "products_per_step": launches,
+                   "algorithmic_bytes_per_step": int(chain.total_bytes),
                    "parallelism": f"tp{world}" if world > 1 else "single",
-                   "l2": "no flush: 6.6 GB of weights per step (>> 126 MB L2)",
                    "launch": "one CUDA graph per step, programmatic dependent launch"},
         "roofline": roofline, "e2e": e2e, "gpu_launches": launches * args.steps,
         "clocks": sampler.summary(),
     }
-    if rank == 0 and world == 1 and not args.no_extras:
+    if rank == 0 and world == 1 and not args.no_extras and args.workload == "chain":
         line["gemv_4096x4096"] = gemv_4096_probe()
         for v in line["gemv_4096x4096"].values():
             v["frac"] = round(v["GB_s"] / peak, 4)
@@ -465,6 +481,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["chain", "gemv"], default="chain",
+                    help="chain: BASELINE configs[3] (default); gemv: configs[0] alone")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the isolated 4096^2 GEMV probe and the CPU baseline")
     args = ap.parse_args()

@@ -180,9 +180,12 @@ struct Scratch {
 
 struct DeviceState {
     int sms = 0;
-    // Split-K buffer: [counters: counter_cap x u32, zeroed][partial sums ...].
+    // Split-K buffer: [counters: counter_cap x u32, zeroed][partial sums: partial_cap bytes].
+    // The two regions grow independently to the largest size seen, so a fixed sequence of
+    // calls stops reallocating after its first pass.
     Scratch split;
     size_t counter_cap = 0;
+    size_t partial_cap = 0;
     Scratch norm;
 };
 
@@ -212,21 +215,23 @@ int device_sms(int dev, int* sms) {
 int ensure_split(int dev, size_t counters, size_t bytes, cudaStream_t stream, SplitScratch* out,
                  size_t partial_floats) {
     DeviceState& d = g_dev[dev];
-    const size_t want_counters = std::max<size_t>(counters, d.counter_cap);
-    const size_t counter_bytes = round_up(want_counters * sizeof(unsigned), 256);
-    const size_t need = counter_bytes + round_up(bytes, 256);
-    if (need > d.split.cap || want_counters > d.counter_cap) {
-        const size_t cap = std::max(need, d.split.cap);
+    const size_t want_counters =
+        round_up(std::max<size_t>(counters, d.counter_cap) * sizeof(unsigned), 256) /
+        sizeof(unsigned);
+    const size_t want_partial = std::max(round_up(bytes, 256), d.partial_cap);
+    if (want_counters > d.counter_cap || want_partial > d.partial_cap) {
+        const size_t counter_bytes = want_counters * sizeof(unsigned);
         if (d.split.ptr) {
             cudaError_t e = cudaFree(d.split.ptr);
             if (e != cudaSuccess) return cuda_fail(e, "free scratch");
             d.split.ptr = nullptr;
-            d.split.cap = 0;
+            d.split.cap = d.counter_cap = d.partial_cap = 0;
         }
-        cudaError_t e = cudaMalloc(&d.split.ptr, cap);
+        cudaError_t e = cudaMalloc(&d.split.ptr, counter_bytes + want_partial);
         if (e != cudaSuccess) return cuda_fail(e, "alloc scratch");
-        d.split.cap = cap;
-        d.counter_cap = counter_bytes / sizeof(unsigned);
+        d.split.cap = counter_bytes + want_partial;
+        d.counter_cap = want_counters;
+        d.partial_cap = want_partial;
         e = cudaMemsetAsync(d.split.ptr, 0, counter_bytes, stream);
         if (e != cudaSuccess) return cuda_fail(e, "zero scratch");
         g_generation.fetch_add(1);

@@ -173,6 +173,29 @@ def test_split_k_queue_is_deterministic():
                 np.testing.assert_array_equal(got, outs[i - 1].cpu().numpy())
 
 
+def test_scratch_settles_after_one_pass():
+    # cuda_scratch_generation() contract (cuda_matmul.h:109-112): once a fixed sequence of
+    # calls has run, repeating it allocates nothing, so it can be captured in a CUDA graph.
+    rng = np.random.default_rng(17)
+    shapes = [(1, 4096, 4096), (1, 4096, 11008), (1, 11008, 4096), (1, 4096, 32000),
+              (16, 4096, 300), (3, 288, 4100)]
+    ops = []
+    for m, k, n in shapes:
+        q, s = oracle.quantize_q8(uni(rng, k, n))
+        ops.append((dev(uni(rng, m, k)), dev(q), dev(s), torch.empty(m, n, device="cuda")))
+
+    def one_pass():
+        for dA, dq, ds, dC in ops:
+            L.matmul(dA, dq, scale=ds, C=dC, weights_static=True)
+    one_pass()
+    torch.cuda.synchronize()
+    gen = L.scratch_generation()
+    one_pass()
+    one_pass()
+    torch.cuda.synchronize()
+    assert L.scratch_generation() == gen
+
+
 def test_programmatic_launch_gives_identical_bits():
     rng = np.random.default_rng(21)
     A = uni(rng, 2, 4096)
