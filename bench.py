@@ -248,13 +248,20 @@ def time_graph(graph, steps, warmup, stream, world, sampler=None):
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ctx = sampler if sampler is not None else _Null()
+    # LLME_PROFILE_REGION=1 brackets the timed replays with cudaProfilerStart/Stop, so
+    # `ncu --profile-from-start off` sees exactly the timed launches.
+    profile = os.environ.get("LLME_PROFILE_REGION") == "1"
     with ctx:
+        if profile:
+            torch.cuda.cudart().cudaProfilerStart()
         with torch.cuda.stream(stream):
             start.record(stream)
             for _ in range(steps):
                 graph.replay()
             end.record(stream)
         torch.cuda.synchronize()
+        if profile:
+            torch.cuda.cudart().cudaProfilerStop()
     barrier(world)
     torch.cuda.synchronize()
     return start.elapsed_time(end) / 1e3

@@ -133,6 +133,7 @@ typedef struct {
     int rms_prepass;      /* 1 if rms_weight is applied by a separate pass over A */
     int grid_x, grid_y;   /* launch grid of the main kernel */
     int slices;           /* k slices reduced deterministically across CTAs (1 = none) */
+    int cluster;          /* CTAs per thread-block cluster (slices reduced through DSMEM) */
     int span;             /* rows of k per slice */
     int tile_m, tile_n;   /* rows and columns of C per CTA */
     size_t split_bytes;   /* split-K scratch: partial sums (0 when slices == 1) */

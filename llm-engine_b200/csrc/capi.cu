@@ -5,6 +5,7 @@
 // dispatch logic can be tested without a GPU.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
@@ -109,9 +110,11 @@ int make_plan(const PlanIn& in, llme_plan_t* p) {
             p->path = LLME_PATH_GEMV_TMA;
             p->tile_n = gemv_tma_cols(in.q8);
             strips = ceil_div(n, p->tile_n);
-            // Two CTAs per SM; each slice at least two boxes deep.
+            // Two CTAs per SM; slices form one cluster (at most 8), each at least two boxes deep.
             const size_t target = 2 * static_cast<size_t>(sms);
-            slices = std::max<size_t>(1, std::min(target / strips, ceil_div(k, 2 * kGemvBoxRows)));
+            slices = std::max<size_t>(
+                1, std::min({target / strips, ceil_div(k, 2 * kGemvBoxRows),
+                             static_cast<size_t>(kGemvMaxCluster)}));
             span = round_up(ceil_div(k, slices), kGemvBoxRows);
         } else {
             p->path = LLME_PATH_GEMV_LDG;
@@ -126,7 +129,9 @@ int make_plan(const PlanIn& in, llme_plan_t* p) {
         p->grid_y = static_cast<int>(slices);
         p->slices = static_cast<int>(slices);
         p->span = static_cast<int>(span);
-        if (slices > 1) {
+        p->cluster = p->path == LLME_PATH_GEMV_TMA ? static_cast<int>(slices) : 1;
+        if (slices > 1 && p->path == LLME_PATH_GEMV_LDG) {
+            // The plain-load kernel reduces its slices through global scratch.
             p->counter_slots = strips;
             p->split_bytes = strips * slices * (m * p->tile_n + m) * sizeof(float);
         }
@@ -141,6 +146,20 @@ int make_plan(const PlanIn& in, llme_plan_t* p) {
         p->tile_m = p->tile_n = 16;
         p->grid_x = static_cast<int>(ceil_div(n, 16));
         p->grid_y = static_cast<int>(ceil_div(m, 16));
+        p->slices = 1;
+        p->span = static_cast<int>(k);
+        return LLME_OK;
+    }
+    // The tcgen05 GEMM: TF32 multiplies, so only in LLME_MATH_TENSOR; rows of A and B must
+    // be TMA-addressable (16-byte aligned starts and pitches).
+    const bool a_ok = has_rms || in.a_addr % 16 == 0;
+    if (kernel == LLME_KERNEL_TILED && in.math == LLME_MATH_TENSOR && !in.q8 && m >= 128 &&
+        k % 4 == 0 && n % 4 == 0 && a_ok && in.b_addr % 16 == 0) {
+        p->path = LLME_PATH_TCGEN05;
+        p->tile_m = tc_tile_m();
+        p->tile_n = tc_tile_n();
+        p->grid_x = static_cast<int>(ceil_div(m, p->tile_m) * ceil_div(n, p->tile_n));
+        p->grid_y = 1;
         p->slices = 1;
         p->span = static_cast<int>(k);
         return LLME_OK;
@@ -293,7 +312,8 @@ std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 // Row-major matrix of `rows` x `cols` elements (rank 2), or a vector (rows == 0, rank 1),
 // tiled into boxes of box_cols x box_rows.
 int tensor_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t rows, uint64_t cols,
-               uint32_t box_cols, uint32_t box_rows, CUtensorMap* out) {
+               uint32_t box_cols, uint32_t box_rows, CUtensorMap* out,
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
     std::call_once(g_encode_once, [] {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -304,8 +324,8 @@ int tensor_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t 
     });
     if (!g_encode) return fail(LLME_E_UNSUPPORTED, "cuda: cuTensorMapEncodeTiled is unavailable");
     const int rank = rows ? 2 : 1;
-    const MapKey key{reinterpret_cast<uintptr_t>(ptr), static_cast<int>(dtype), rank, cols, rows,
-                     box_cols, box_rows};
+    const MapKey key{reinterpret_cast<uintptr_t>(ptr), static_cast<int>(dtype) | (static_cast<int>(swizzle) << 8),
+                     rank, cols, rows, box_cols, box_rows};
     {
         std::lock_guard<std::mutex> lk(g_map_mu);
         auto it = g_maps.find(key);
@@ -319,7 +339,7 @@ int tensor_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t 
     cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = g_encode(out, dtype, rank, const_cast<void*>(ptr), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return fail(LLME_E_CUDA, "cuda: encode tensor map: CUresult " + std::to_string(int(r)));
@@ -362,7 +382,7 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
 
     std::lock_guard<std::mutex> lk(g_dev_mu);  // scratch is shared per device
     SplitScratch split;
-    if (p.slices > 1) {
+    if (p.split_bytes > 0) {
         // Partial sums first, then (GEMV with RMSNorm) the per-slice sums of squares.
         const size_t partial_floats =
             p.path == LLME_PATH_TILED_SIMT
@@ -422,6 +442,25 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
         } else {
             e = launch_gemv_ldg(g);
         }
+    } else if (p.path == LLME_PATH_TCGEN05) {
+        CUtensorMap tmA, tmB;
+        st = tensor_map(a_in, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, k, 32, 128, &tmA,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+        if (st) return st;
+        st = tensor_map(B, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k, n, 32, 32, &tmB,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+        if (st) return st;
+        TcArgs t;
+        t.m = static_cast<int>(m);
+        t.n = static_cast<int>(n);
+        t.k = static_cast<int>(k);
+        t.C = C;
+        t.accumulate = accumulate;
+        t.tiles_m = static_cast<int>(ceil_div(m, p.tile_m));
+        t.tiles_n = static_cast<int>(ceil_div(n, p.tile_n));
+        t.stream = stream;
+        t.pdl = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
+        e = launch_gemm_tf32(t, tmA, tmB);
     } else {
         TiledArgs t;
         t.m = static_cast<int>(m);
@@ -470,7 +509,8 @@ int llme_synchronize(void) {
     g_error.clear();
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return cuda_fail(e, "synchronize");
-    const unsigned dev_err = read_and_clear_gemv_error() | read_and_clear_tiled_error();
+    const unsigned dev_err =
+        read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error();
     if (dev_err) return fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up");
     return LLME_OK;
 }
@@ -492,7 +532,8 @@ int llme_device_status(void) {
     g_error.clear();
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return cuda_fail(e, "synchronize");
-    const unsigned dev_err = read_and_clear_gemv_error() | read_and_clear_tiled_error();
+    const unsigned dev_err =
+        read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error();
     return dev_err ? fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up") : LLME_OK;
 }
 

@@ -5,26 +5,28 @@
 // (src/cuda_matmul.cu:189-254, launched by run_skinny :365-397). This design
 // is B200-first rather than a translation:
 //
-//  * B is streamed by TMA (cp.async.bulk.tensor.2d) in 64-row x 256-byte
-//    boxes into a 5-stage shared-memory ring per CTA; one producer thread
-//    keeps every stage in flight, so with two CTAs per SM ~160 KB of weights
-//    are outstanding per SM from the first cycle. A (and the RMSNorm weight)
-//    ride in the same stage as small boxes, so the consumers never touch
-//    global memory in the hot loop. Weights use an L2 evict-first policy.
+//  * B is streamed by TMA (cp.async.bulk.tensor.2d) in 128-row x 128-byte
+//    boxes into a 4-stage shared-memory ring per CTA; one producer thread
+//    keeps every stage in flight (a 512-row slice is requested whole at
+//    launch). A (and the RMSNorm weight) ride in the same stage as small
+//    boxes, so the consumers never touch global memory in the hot loop.
+//    Weights use an L2 evict-first policy.
+//  * k is split across the CTAs of a thread-block cluster (up to 8, grid.y):
+//    each CTA reduces its slice in shared memory, then cluster rank 0 adds
+//    the slices through distributed shared memory in rank order. No global
+//    scratch, fence or atomic sits on the critical path, and repeats are
+//    bit-identical.
 //  * With programmatic dependent launch the producer issues the first stages
 //    of weights before griddepcontrol.wait, overlapping the previous kernel's
 //    tail; A and C are touched only after the wait.
 //  * int8 is widened without I2F: a PRMT builds 2^23 + (q + 128) as a float
-//    and one FADD removes the bias (exact), then the raw int8 values are
+//    and a packed f32x2 add removes the bias (exact); products accumulate with
+//    packed fma.rn.f32x2 (bitwise the same as two fmaf). Raw int8 values are
 //    summed and each column scaled once at the end, as the reference does.
 //  * RMSNorm is applied as an epilogue scale: each CTA sums a*a over its own
 //    k rows while it streams, multiplies A by the norm weight in the loop, and
 //    the final per-row 1/sqrt(mean + eps) multiplies the reduced sums -- no
 //    pre-pass and no second read of A.
-//  * k is split across CTAs (grid.y) when the columns alone cannot fill 148
-//    SMs. Slices are reduced deterministically: partials to scratch, a ticket
-//    per column strip, and the last CTA to arrive adds the slices in index
-//    order. Repeats are bit-identical (no float atomics).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -36,19 +38,21 @@ __device__ unsigned int g_gemv_error;
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kTmaThreads = kConsumers + 32;  // + one producer warp
-constexpr int kStages = 5;
+constexpr int kStages = 4;
 constexpr int kBoxBytesB = kGemvRowBytes * kGemvBoxRows;  // 16 KB
 
-// Per-thread work split of one 256-byte row segment of B.
+// Per-thread work split of one 128-byte row segment of B.
 template <int M, bool Q8>
 struct Shape {
     static constexpr int ESZ = Q8 ? 1 : 4;
-    static constexpr int V = Q8 ? (M <= 4 ? 16 : 8) : 4;  // columns per thread
+    // Columns per thread: fewer as M grows, so M x V accumulators fit 2 CTAs per SM.
+    static constexpr int V = Q8 ? (M <= 2 ? 16 : (M <= 4 ? 8 : 4)) : 4;
     static constexpr int NT = kGemvRowBytes / ESZ;         // columns per CTA
     static constexpr int TPR = NT / V;                     // threads per row
     static constexpr int RG = kConsumers / TPR;            // row groups
     static constexpr int RPT = kGemvBoxRows / RG;          // rows per thread per box
-    static_assert(TPR == 16 || TPR == 32, "row split");
+    static_assert(TPR == 8 || TPR == 16 || TPR == 32, "row split");
+    static_assert(V % 4 == 0, "packed pairs");
 };
 
 template <int M, bool Q8, bool Norm>
@@ -67,90 +71,113 @@ struct Layout {
     static_assert((kConsumerWarps + 1) * M * 4 <= kStages * kABox, "ss reduction fits");
 };
 
+// ---- packed f32x2 arithmetic (sm_100) ---------------------------------------------------
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// Four signed bytes -> two exact f32x2 pairs (see s8x4_to_f32 in common.cuh).
+__device__ __forceinline__ void s8x4_to_f32x2(uint32_t w, uint64_t& p01, uint64_t& p23) {
+    const uint32_t u = w ^ 0x80808080u;
+    constexpr float kBias = -8388736.0f;  // -(2^23 + 128)
+    const uint64_t bias = pack2(kBias, kBias);
+    p01 = add2(pack2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)),
+                     __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541))),
+               bias);
+    p23 = add2(pack2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)),
+                     __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543))),
+               bias);
+}
+
+// V columns of one row of B (at p, shared memory) as V/2 f32x2 pairs.
 template <bool Q8, int V>
-__device__ __forceinline__ void load_cols(const uint8_t* p, float (&x)[V]) {
+__device__ __forceinline__ void load_pairs(const uint8_t* p, uint64_t (&x)[V / 2]) {
     if constexpr (Q8) {
         if constexpr (V == 16) {
             const uint4 q = *reinterpret_cast<const uint4*>(p);
-            float t[4];
-            s8x4_to_f32(q.x, t);
-            x[0] = t[0]; x[1] = t[1]; x[2] = t[2]; x[3] = t[3];
-            s8x4_to_f32(q.y, t);
-            x[4] = t[0]; x[5] = t[1]; x[6] = t[2]; x[7] = t[3];
-            s8x4_to_f32(q.z, t);
-            x[8] = t[0]; x[9] = t[1]; x[10] = t[2]; x[11] = t[3];
-            s8x4_to_f32(q.w, t);
-            x[12] = t[0]; x[13] = t[1]; x[14] = t[2]; x[15] = t[3];
-        } else {
-            static_assert(V == 8, "int8 columns per thread");
+            s8x4_to_f32x2(q.x, x[0], x[1]);
+            s8x4_to_f32x2(q.y, x[2], x[3]);
+            s8x4_to_f32x2(q.z, x[4], x[5]);
+            s8x4_to_f32x2(q.w, x[6], x[7]);
+        } else if constexpr (V == 8) {
             const uint2 q = *reinterpret_cast<const uint2*>(p);
-            float t[4];
-            s8x4_to_f32(q.x, t);
-            x[0] = t[0]; x[1] = t[1]; x[2] = t[2]; x[3] = t[3];
-            s8x4_to_f32(q.y, t);
-            x[4] = t[0]; x[5] = t[1]; x[6] = t[2]; x[7] = t[3];
+            s8x4_to_f32x2(q.x, x[0], x[1]);
+            s8x4_to_f32x2(q.y, x[2], x[3]);
+        } else {
+            static_assert(V == 4, "int8 columns per thread");
+            s8x4_to_f32x2(*reinterpret_cast<const uint32_t*>(p), x[0], x[1]);
         }
     } else {
         static_assert(V == 4, "fp32 columns per thread");
-        const float4 f = *reinterpret_cast<const float4*>(p);
-        x[0] = f.x; x[1] = f.y; x[2] = f.z; x[3] = f.w;
+        const ulonglong2 f = *reinterpret_cast<const ulonglong2*>(p);
+        x[0] = f.x;
+        x[1] = f.y;
     }
 }
 
-// Writes the CTA's M x NT sums (tot, in shared memory) to C, through the
-// deterministic cross-CTA slice reduction when k is split. Called by the
-// kConsumers consumer threads only (named barrier 1).
+// ---- thread-block cluster helpers ---------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Every thread of every CTA in the cluster; release/acquire orders shared-memory writes.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(const float* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(remote)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ float ld_dsmem_f(const float* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+// Writes C for a CTA's column strip from M x NT sums that are already complete
+// (tot, shared memory) -- the kernels' common epilogue.
 template <int M, int NT, bool Q8, bool Norm>
-__device__ void finish_strip(const float* tot, const float* tot_ss, const GemvArgs& a, int strip,
-                             int slice, int tid, int* flag) {
-    constexpr int E = M * NT;
-    const int col0 = strip * NT;
-    const bool split = a.slices > 1;
-    if (split) {
-        float* part = a.split.partial + (static_cast<size_t>(strip) * a.slices + slice) * E;
-        for (int e = tid; e < E; e += kConsumers) __stcg(part + e, tot[e]);
-        if (Norm && tid < M)
-            __stcg(a.split.partial_ss + (static_cast<size_t>(strip) * a.slices + slice) * M + tid,
-                   tot_ss[tid]);
-        __threadfence();
-        named_barrier(1, kConsumers);
-        if (tid == 0)
-            *flag = atomicAdd(a.split.counters + strip, 1u) == static_cast<unsigned>(a.slices - 1);
-        named_barrier(1, kConsumers);
-        if (!*flag) return;
-        __threadfence();
-    }
+__device__ __forceinline__ void store_strip(const float* tot, const float* tot_ss, const GemvArgs& a,
+                                            int col0, int tid, int nthreads) {
     float rs[M];
     if constexpr (Norm) {
 #pragma unroll
-        for (int r = 0; r < M; ++r) {
-            float s2 = 0.0f;
-            if (split) {
-                const float* ps = a.split.partial_ss + static_cast<size_t>(strip) * a.slices * M + r;
-                for (int s = 0; s < a.slices; ++s) s2 += __ldcg(ps + static_cast<size_t>(s) * M);
-            } else {
-                s2 = tot_ss[r];
-            }
-            rs[r] = 1.0f / sqrtf(s2 / static_cast<float>(a.k) + kRmsEps);
-        }
+        for (int r = 0; r < M; ++r) rs[r] = 1.0f / sqrtf(tot_ss[r] / static_cast<float>(a.k) + kRmsEps);
     }
-    const float* base = a.split.partial + static_cast<size_t>(strip) * a.slices * E;
-    for (int e = tid; e < E; e += kConsumers) {
+    for (int e = tid; e < M * NT; e += nthreads) {
         const int r = e / NT, col = col0 + e % NT;
         if (col >= a.n) continue;
-        float v;
-        if (split) {
-            v = 0.0f;
-            for (int s = 0; s < a.slices; ++s) v += __ldcg(base + static_cast<size_t>(s) * E + e);
-        } else {
-            v = tot[e];
-        }
+        float v = tot[e];
         if constexpr (Q8) v *= __ldg(a.scale + col);
         if constexpr (Norm) v *= rs[r];
         float* out = a.C + static_cast<size_t>(r) * a.n + col;
         *out = a.accumulate ? *out + v : v;
     }
-    if (split && tid == 0) atomicExch(a.split.counters + strip, 0u);
 }
 
 template <int M, bool Q8, bool Norm>
@@ -162,10 +189,9 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
     uint64_t* empty = full + kStages;
-    int* flag = reinterpret_cast<int*>(empty + kStages);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int strip = blockIdx.x, slice = blockIdx.y;
+    const int strip = blockIdx.x, slice = blockIdx.y;  // grid.y = slices = cluster size
     const int col0 = strip * S::NT;
     const int k0 = slice * a.span;
     const int k1 = min(a.k, k0 + a.span);
@@ -183,6 +209,11 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
     }
     __syncthreads();
     if (tid == 0) pdl_launch_dependents();
+
+    float* red = reinterpret_cast<float*>(smem);
+    float* tot = red + L::kRedFloats;
+    float* red_ss = reinterpret_cast<float*>(smem + L::kOffA);
+    float* tot_ss = red_ss + kConsumerWarps * M;
 
     if (warp == kConsumerWarps) {
         // Producer. Weights first (they do not depend on the previous launch),
@@ -212,95 +243,181 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
                 if (Norm) tma_load_1d(smem + L::kOffW + s * L::kWBox, &tmW, y, &full[s]);
             }
         }
-        return;
-    }
-
-    // Consumers: C and the split scratch are touched after this.
-    pdl_wait();
-    const int cg = tid % S::TPR, rg = tid / S::TPR;
-    float acc[M][S::V];
-    float ss[M];
+        __syncwarp();
+    } else {
+        // Consumers: C is touched only after this.
+        pdl_wait();
+        const int cg = tid % S::TPR, rg = tid / S::TPR;
+        uint64_t acc[M][S::V / 2];
+        float ss[M];
 #pragma unroll
-    for (int r = 0; r < M; ++r) {
-        ss[r] = 0.0f;
+        for (int r = 0; r < M; ++r) {
+            ss[r] = 0.0f;
 #pragma unroll
-        for (int j = 0; j < S::V; ++j) acc[r][j] = 0.0f;
-    }
-    for (int b = 0; b < nb; ++b) {
-        const int s = b % kStages;
-        if (!mbar_wait(&full[s], (b / kStages) & 1, &g_gemv_error)) break;
-        const uint8_t* sb = smem + s * kBoxBytesB + cg * (S::V * S::ESZ);
-        const float* sa = reinterpret_cast<const float*>(smem + L::kOffA + s * L::kABox);
-        const float* sw = reinterpret_cast<const float*>(smem + L::kOffW + s * L::kWBox);
+            for (int j = 0; j < S::V / 2; ++j) acc[r][j] = 0ull;
+        }
+        for (int b = 0; b < nb; ++b) {
+            const int s = b % kStages;
+            if (!mbar_wait(&full[s], (b / kStages) & 1, &g_gemv_error)) break;
+            const uint8_t* sb = smem + s * kBoxBytesB + cg * (S::V * S::ESZ);
+            const float* sa = reinterpret_cast<const float*>(smem + L::kOffA + s * L::kABox);
+            const float* sw = reinterpret_cast<const float*>(smem + L::kOffW + s * L::kWBox);
 #pragma unroll
-        for (int i = 0; i < S::RPT; ++i) {
-            const int row = rg + i * S::RG;
-            float av[M];
+            for (int i = 0; i < S::RPT; ++i) {
+                const int row = rg + i * S::RG;
+                float av[M];
 #pragma unroll
-            for (int r = 0; r < M; ++r) av[r] = sa[r * kGemvBoxRows + row];
-            if constexpr (Norm) {
-                const float w = sw[row];
+                for (int r = 0; r < M; ++r) av[r] = sa[r * kGemvBoxRows + row];
+                if constexpr (Norm) {
+                    const float w = sw[row];
+#pragma unroll
+                    for (int r = 0; r < M; ++r) {
+                        ss[r] = fmaf(av[r], av[r], ss[r]);
+                        av[r] *= w;
+                    }
+                }
+                uint64_t x[S::V / 2];
+                load_pairs<Q8, S::V>(sb + row * kGemvRowBytes, x);
 #pragma unroll
                 for (int r = 0; r < M; ++r) {
-                    ss[r] = fmaf(av[r], av[r], ss[r]);
-                    av[r] *= w;
+                    const uint64_t a2 = pack2(av[r], av[r]);
+#pragma unroll
+                    for (int j = 0; j < S::V / 2; ++j) acc[r][j] = fma2(a2, x[j], acc[r][j]);
                 }
             }
-            float x[S::V];
-            load_cols<Q8, S::V>(sb + row * kGemvRowBytes, x);
-#pragma unroll
-            for (int r = 0; r < M; ++r)
-#pragma unroll
-                for (int j = 0; j < S::V; ++j) acc[r][j] = fmaf(av[r], x[j], acc[r][j]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-    }
 
-    // Reduce the row groups: pairs inside a warp by shuffle, then the 8 warps
-    // through shared memory (the drained ring), always in the same order.
-    named_barrier(1, kConsumers);
-    float* red = reinterpret_cast<float*>(smem);
-    float* tot = red + L::kRedFloats;
-    float* red_ss = reinterpret_cast<float*>(smem + L::kOffA);
-    float* tot_ss = red_ss + kConsumerWarps * M;
-    if constexpr (S::TPR == 16) {
+        // Reduce the row groups: inside a warp by shuffle, then the 8 warps
+        // through shared memory (the drained ring), always in the same order.
+        named_barrier(1, kConsumers);
+        float accf[M][S::V];
 #pragma unroll
-        for (int r = 0; r < M; ++r) {
-            ss[r] += __shfl_xor_sync(0xffffffffu, ss[r], 16);
+        for (int r = 0; r < M; ++r)
 #pragma unroll
-            for (int j = 0; j < S::V; ++j) acc[r][j] += __shfl_xor_sync(0xffffffffu, acc[r][j], 16);
+            for (int j = 0; j < S::V / 2; ++j) unpack2(acc[r][j], accf[r][2 * j], accf[r][2 * j + 1]);
+#pragma unroll
+        for (int off = S::TPR; off < 32; off <<= 1) {
+#pragma unroll
+            for (int r = 0; r < M; ++r) {
+                ss[r] += __shfl_xor_sync(0xffffffffu, ss[r], off);
+#pragma unroll
+                for (int j = 0; j < S::V; ++j) accf[r][j] += __shfl_xor_sync(0xffffffffu, accf[r][j], off);
+            }
+        }
+        if (lane < S::TPR) {
+#pragma unroll
+            for (int r = 0; r < M; ++r) {
+                float4* dst = reinterpret_cast<float4*>(red + (warp * M + r) * S::NT + cg * S::V);
+#pragma unroll
+                for (int j = 0; j < S::V / 4; ++j)
+                    dst[j] = make_float4(accf[r][4 * j], accf[r][4 * j + 1], accf[r][4 * j + 2],
+                                         accf[r][4 * j + 3]);
+            }
+            if (Norm && cg == 0) {
+#pragma unroll
+                for (int r = 0; r < M; ++r) red_ss[warp * M + r] = ss[r];
+            }
+        }
+        named_barrier(1, kConsumers);
+        for (int e = tid; e < M * S::NT; e += kConsumers) {
+            float v = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) v += red[w * M * S::NT + e];
+            tot[e] = v;
+        }
+        if (Norm && tid < M) {
+            float v = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) v += red_ss[w * M + tid];
+            tot_ss[tid] = v;
+        }
+        if (a.slices == 1) {
+            named_barrier(1, kConsumers);
+            store_strip<M, S::NT, Q8, Norm>(tot, tot_ss, a, col0, tid, kConsumers);
         }
     }
-    if (S::TPR == 32 || lane < 16) {
-#pragma unroll
-        for (int r = 0; r < M; ++r) {
-            float4* dst = reinterpret_cast<float4*>(red + (warp * M + r) * S::NT + cg * S::V);
-#pragma unroll
-            for (int j = 0; j < S::V / 4; ++j)
-                dst[j] = make_float4(acc[r][4 * j], acc[r][4 * j + 1], acc[r][4 * j + 2],
-                                     acc[r][4 * j + 3]);
+    if (a.slices == 1) return;
+    __syncwarp();
+
+    // k split across the cluster: rank 0 adds the slices' sums, read from each
+    // CTA's shared memory, in rank order; the second barrier keeps every CTA's
+    // shared memory alive until rank 0 has read it.
+    cluster_sync();
+    if (cluster_rank() == 0 && tid < kConsumers) {
+        constexpr int E4 = M * S::NT / 4;
+        for (int e4 = tid; e4 < E4; e4 += kConsumers) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = 0; r < a.slices; ++r) {
+                const float4 t = ld_dsmem_f4(tot + 4 * e4, r);
+                v.x += t.x;
+                v.y += t.y;
+                v.z += t.z;
+                v.w += t.w;
+            }
+            // Rank 0's own tot is read before it is overwritten by this thread only.
+            *reinterpret_cast<float4*>(red + 4 * e4) = v;
         }
-        if (Norm && cg == 0) {
-#pragma unroll
-            for (int r = 0; r < M; ++r) red_ss[warp * M + r] = ss[r];
+        if (Norm && tid < M) {
+            float v = 0.0f;
+            for (int r = 0; r < a.slices; ++r) v += ld_dsmem_f(tot_ss + tid, r);
+            red_ss[tid] = v;
         }
+        named_barrier(1, kConsumers);
+        store_strip<M, S::NT, Q8, Norm>(red, red_ss, a, col0, tid, kConsumers);
     }
-    named_barrier(1, kConsumers);
-    for (int e = tid; e < M * S::NT; e += kConsumers) {
+    cluster_sync();
+}
+
+// The plain-load kernel's k split: partials to scratch, a ticket per column
+// strip, and the CTA that brings the count to `slices` adds the slices in index
+// order (loads issued eight at a time so their latencies overlap), writes C and
+// resets the ticket.
+template <int M, int NT, bool Q8, bool Norm>
+__device__ void finish_strip(const float* tot, const float* tot_ss, const GemvArgs& a, int strip,
+                             int slice, int tid, int* flag, float* red, float* red_ss) {
+    constexpr int E = M * NT;
+    const int col0 = strip * NT;
+    if (a.slices == 1) {
+        store_strip<M, NT, Q8, Norm>(tot, tot_ss, a, col0, tid, kConsumers);
+        return;
+    }
+    float* part = a.split.partial + (static_cast<size_t>(strip) * a.slices + slice) * E;
+    for (int e = tid; e < E; e += kConsumers) __stcg(part + e, tot[e]);
+    if (Norm && tid < M)
+        __stcg(a.split.partial_ss + (static_cast<size_t>(strip) * a.slices + slice) * M + tid,
+               tot_ss[tid]);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0)
+        *flag = atomicAdd(a.split.counters + strip, 1u) == static_cast<unsigned>(a.slices - 1);
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+    const float* base = a.split.partial + static_cast<size_t>(strip) * a.slices * E;
+    for (int e = tid; e < E; e += kConsumers) {
         float v = 0.0f;
+        for (int s0 = 0; s0 < a.slices; s0 += 8) {
+            float t[8];
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) v += red[w * M * S::NT + e];
-        tot[e] = v;
+            for (int i = 0; i < 8; ++i)
+                t[i] = s0 + i < a.slices ? __ldcg(base + static_cast<size_t>(s0 + i) * E + e) : 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (s0 + i < a.slices) v += t[i];
+        }
+        red[e] = v;
     }
     if (Norm && tid < M) {
         float v = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) v += red_ss[w * M + tid];
-        tot_ss[tid] = v;
+        const float* ps = a.split.partial_ss + static_cast<size_t>(strip) * a.slices * M + tid;
+        for (int s = 0; s < a.slices; ++s) v += __ldcg(ps + static_cast<size_t>(s) * M);
+        red_ss[tid] = v;
     }
-    named_barrier(1, kConsumers);
-    finish_strip<M, S::NT, Q8, Norm>(tot, tot_ss, a, strip, slice, tid, flag);
+    __syncthreads();
+    store_strip<M, NT, Q8, Norm>(red, red_ss, a, col0, tid, kConsumers);
+    if (tid == 0) atomicExch(a.split.counters + strip, 0u);
 }
 
 // Fallback for B rows that are not 16-byte multiples or pointers TMA cannot
@@ -363,7 +480,7 @@ __global__ void __launch_bounds__(kConsumers) gemv_ldg_kernel(const GemvArgs a) 
         tot_ss[tid] = v;
     }
     __syncthreads();
-    finish_strip<M, NT, Q8, Norm>(tot, tot_ss, a, strip, slice, tid, &flag);
+    finish_strip<M, NT, Q8, Norm>(tot, tot_ss, a, strip, slice, tid, &flag, red, red_ss);
 }
 
 cudaLaunchConfig_t make_config(dim3 grid, int threads, size_t smem, cudaStream_t stream, bool pdl,
@@ -398,9 +515,18 @@ cudaError_t launch_tma_m(const GemvArgs& a, const CUtensorMap& tmB, const CUtens
         if (e != cudaSuccess) return e;
         configured |= 1u << dev;
     }
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     cudaLaunchConfig_t cfg =
         make_config(dim3(a.strips, a.slices), kTmaThreads, L::kBytes, a.stream, a.pdl, attr);
+    if (a.slices > 1) {
+        // The k slices of a column strip form one cluster (reduced through DSMEM).
+        attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+        attr[cfg.numAttrs].val.clusterDim.x = 1;
+        attr[cfg.numAttrs].val.clusterDim.y = static_cast<unsigned>(a.slices);
+        attr[cfg.numAttrs].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        ++cfg.numAttrs;
+    }
     return cudaLaunchKernelEx(&cfg, kern, tmB, tmA, tmW, a);
 }
 

@@ -37,9 +37,11 @@ struct GemvArgs {
     bool pdl = false;               // launch with programmatic stream serialization
 };
 
-// Columns of C per CTA and rows per TMA box of the TMA GEMV.
-constexpr int kGemvRowBytes = 256;
-constexpr int kGemvBoxRows = 64;
+// TMA GEMV: each CTA streams 128-byte row segments of B (128 int8 or 32 fp32 columns) in
+// boxes of 128 rows; k is split across at most kGemvMaxCluster CTAs of one cluster.
+constexpr int kGemvRowBytes = 128;
+constexpr int kGemvBoxRows = 128;
+constexpr int kGemvMaxCluster = 8;
 inline int gemv_tma_cols(bool q8) { return q8 ? kGemvRowBytes : kGemvRowBytes / 4; }
 constexpr int kGemvLdgCols = 32;
 
@@ -64,6 +66,21 @@ struct TiledArgs {
 constexpr int kTiledBM = 64, kTiledBN = 64, kTiledBK = 16;
 cudaError_t launch_tiled_simt(const TiledArgs& a);
 cudaError_t launch_naive(const TiledArgs& a);
+
+// tcgen05 tensor-core GEMM (gemm_tc.cu): 128 x 256 output tiles, TF32 operands read by
+// TMA with 128-byte swizzle (A: K-major box 32 x 128; B: MN-major boxes 32 x 32).
+struct TcArgs {
+    int m = 0, n = 0, k = 0;
+    float* C = nullptr;
+    bool accumulate = false;
+    int tiles_m = 0, tiles_n = 0;
+    cudaStream_t stream = nullptr;
+    bool pdl = false;
+};
+int tc_tile_m();
+int tc_tile_n();
+cudaError_t launch_gemm_tf32(const TcArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB);
+unsigned read_and_clear_tc_error();
 
 // out = rmsnorm(A) * w per row (eps 1e-5), m rows of k.
 cudaError_t launch_rmsnorm_rows(int m, int k, const float* A, const float* w, float* out,

@@ -49,6 +49,7 @@ class Plan(ctypes.Structure):
     _fields_ = [
         ("path", ctypes.c_int), ("kernel", ctypes.c_int), ("rms_prepass", ctypes.c_int),
         ("grid_x", ctypes.c_int), ("grid_y", ctypes.c_int), ("slices", ctypes.c_int),
+        ("cluster", ctypes.c_int),
         ("span", ctypes.c_int), ("tile_m", ctypes.c_int), ("tile_n", ctypes.c_int),
         ("split_bytes", ctypes.c_size_t), ("counter_slots", ctypes.c_size_t),
         ("norm_bytes", ctypes.c_size_t),

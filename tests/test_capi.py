@@ -113,9 +113,11 @@ def test_split_k_plan_covers_k_exactly_once(n, k, q8, sms):
     assert p["grid_y"] == s
     assert p["grid_x"] * p["tile_n"] >= n
     if p["path_name"] == "gemv_tma":
-        assert span % 64 == 0                       # boxes never straddle two slices
+        assert span % 128 == 0                      # boxes never straddle two slices
+        assert s <= 8 and p["cluster"] == s         # the slices of a strip are one cluster
         assert p["grid_x"] * p["grid_y"] <= max(2 * sms, p["grid_x"])
-    if s > 1:
+        assert p["split_bytes"] == 0                # reduced through DSMEM, no scratch
+    elif s > 1:
         assert p["split_bytes"] > 0 and p["counter_slots"] == p["grid_x"]
     else:
         assert p["split_bytes"] == 0
@@ -126,6 +128,18 @@ def test_decode_shapes_fill_the_gpu():
     for n, k in [(4096, 4096), (11008, 4096), (4096, 11008)]:
         p = L.plan(1, n, k, q8=True)
         assert 0.8 * 296 <= p["grid_x"] * p["grid_y"] <= 296, (n, k, p)
+
+
+def test_tcgen05_path_choice():
+    # TF32 tensor cores for m >= 128 with TMA-addressable fp32 operands, in tensor math only.
+    assert L.plan(128, 4096, 4096, q8=False)["path_name"] == "tcgen05"
+    assert L.plan(8192, 8192, 8192, q8=False)["grid_x"] == 64 * 32
+    assert L.plan(127, 4096, 4096, q8=False)["path_name"] == "tiled_simt"
+    assert L.plan(128, 4096, 4096, q8=False, math=L.MATH_FP32)["path_name"] == "tiled_simt"
+    assert L.plan(128, 1030, 4096, q8=False)["path_name"] == "tiled_simt"   # n % 4
+    assert L.plan(128, 1028, 513, q8=False)["path_name"] == "tiled_simt"    # k % 4
+    assert L.plan(128, 1028, 512, q8=False, a_addr=260)["path_name"] == "tiled_simt"
+    assert L.plan(128, 1028, 512, q8=False, a_addr=260, rms_addr=256)["path_name"] == "tcgen05"
 
 
 def test_rms_prepass_only_outside_the_gemv():
