@@ -308,6 +308,51 @@ def gemv_4096_probe(steps=200):
     return res
 
 
+def run_sgemm(args, world, rank, local):
+    """C = A x B, fp32 N x N, A and B ~ U(-1, 1) (seed 2), through the
+    C ABI on the tcgen05 TF32 path (including its B^T re-layout pass). Inputs 768 MB > L2."""
+    import torch
+    import llme_b200 as L
+    n = args.size
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2)
+    A = torch.rand(n, n, generator=g, device="cuda") * 2 - 1
+    B = torch.rand(n, n, generator=g, device="cuda") * 2 - 1
+    C = torch.empty(n, n, device="cuda")
+    plan = L.plan(n, n, n, q8=False, a_addr=A.data_ptr(), b_addr=B.data_ptr())
+    stream = torch.cuda.Stream()
+    h = stream.cuda_stream
+    graph = capture(lambda: L.matmul_cuda_f32(n, n, n, A.data_ptr(), B.data_ptr(), C.data_ptr(),
+                                              "automatic", False, 0, L.FLAG_WEIGHTS_STATIC, h),
+                    stream)
+    sampler = ClockSampler(local)
+    secs = max_over_ranks(time_graph(graph, args.steps, args.warmup, stream, world, sampler), world)
+    flops = 2.0 * n ** 3
+    tflops = flops * args.steps * world / secs / 1e12
+    bf16 = None
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            bf16 = float(json.load(f)["bf16_tflops"])
+        peak, kind = bf16 / 2, "half of measured bf16 (TF32 runs at half the bf16 rate)"
+    except Exception:
+        peak, kind = 1590.0 / 2, "half of fallback bf16"
+    line = {"metric": f"TF32 GEMM TFLOP/s ({n}^3, fp32 in/out)", "value": round(tflops, 1),
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "tf32",
+            "data": "synthetic U(-1,1)",
+            "config": {"workload": "square fp32 SGEMM on the TF32 tcgen05 path (BASELINE configs[2])",
+                       "N": n, "path": plan["path_name"],
+                       "l2": "no flush: 768 MB of operands (> 126 MB L2)"},
+            "roofline": {"bound": "tensor", "achieved": round(tflops / world, 1), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(tflops / world / peak, 4),
+                         "peak_kind": kind, "kernel": "gemm_tf32_kernel (+ transpose)",
+                         "traffic": None},
+            "gpu_launches": 2 * args.steps, "clocks": sampler.summary()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def peaks():
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
@@ -362,6 +407,8 @@ def run_ours(args):
     L.load()
     if not L.device_supported():
         raise SystemExit("this benchmark needs an sm_100 (B200) GPU")
+    if args.workload == "sgemm":
+        return run_sgemm(args, world, rank, local)
     if args.workload == "chain":
         chain = Chain(world, rank, chain_shapes(), seed=3)
     else:
@@ -488,8 +535,10 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["chain", "gemv"], default="chain",
-                    help="chain: BASELINE configs[3] (default); gemv: configs[0] alone")
+    ap.add_argument("--workload", choices=["chain", "gemv", "sgemm"], default="chain",
+                    help="chain: BASELINE configs[3] (default); gemv: configs[0] alone; "
+                         "sgemm: configs[2] (square TF32 GEMM, --size)")
+    ap.add_argument("--size", type=int, default=8192, help="N for --workload sgemm")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the isolated 4096^2 GEMV probe and the CPU baseline")
     args = ap.parse_args()

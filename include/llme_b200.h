@@ -139,6 +139,7 @@ typedef struct {
     size_t split_bytes;   /* split-K scratch: partial sums (0 when slices == 1) */
     size_t counter_slots; /* split-K tickets needed (one per output tile) */
     size_t norm_bytes;    /* scratch for the normalised copy of A (rms_prepass) */
+    size_t operand_bytes; /* scratch for a re-laid-out copy of B (the tensor-core GEMM's B^T) */
 } llme_plan_t;
 
 /* The plan llme_matmul_f32 (is_q8 == 0) or llme_matmul_q8 (is_q8 == 1) would follow on a

@@ -158,6 +158,7 @@ int make_plan(const PlanIn& in, llme_plan_t* p) {
         p->path = LLME_PATH_TCGEN05;
         p->tile_m = tc_tile_m();
         p->tile_n = tc_tile_n();
+        p->operand_bytes = k * n * sizeof(float);  // B^T for the K-major MMA operand
         p->grid_x = static_cast<int>(ceil_div(m, p->tile_m) * ceil_div(n, p->tile_n));
         p->grid_y = 1;
         p->slices = 1;
@@ -206,6 +207,7 @@ struct DeviceState {
     size_t counter_cap = 0;
     size_t partial_cap = 0;
     Scratch norm;
+    Scratch operand;  // transposed weights for the tensor-core GEMM
 };
 
 std::mutex g_dev_mu;
@@ -262,23 +264,25 @@ int ensure_split(int dev, size_t counters, size_t bytes, cudaStream_t stream, Sp
     return LLME_OK;
 }
 
-int ensure_norm(int dev, size_t bytes, float** out) {
-    DeviceState& d = g_dev[dev];
-    if (bytes > d.norm.cap) {
-        if (d.norm.ptr) {
-            cudaError_t e = cudaFree(d.norm.ptr);
+// Grow-only buffer; growth bumps the generation.
+int ensure_buffer(Scratch& b, size_t bytes, float** out) {
+    if (bytes > b.cap) {
+        if (b.ptr) {
+            cudaError_t e = cudaFree(b.ptr);
             if (e != cudaSuccess) return cuda_fail(e, "free scratch");
-            d.norm.ptr = nullptr;
-            d.norm.cap = 0;
+            b.ptr = nullptr;
+            b.cap = 0;
         }
-        cudaError_t e = cudaMalloc(&d.norm.ptr, bytes);
+        cudaError_t e = cudaMalloc(&b.ptr, bytes);
         if (e != cudaSuccess) return cuda_fail(e, "alloc scratch");
-        d.norm.cap = bytes;
+        b.cap = bytes;
         g_generation.fetch_add(1);
     }
-    *out = static_cast<float*>(d.norm.ptr);
+    *out = static_cast<float*>(b.ptr);
     return LLME_OK;
 }
+
+int ensure_norm(int dev, size_t bytes, float** out) { return ensure_buffer(g_dev[dev].norm, bytes, out); }
 
 // ---- TMA descriptors -------------------------------------------------------------------
 
@@ -443,11 +447,17 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
             e = launch_gemv_ldg(g);
         }
     } else if (p.path == LLME_PATH_TCGEN05) {
+        float* bt = nullptr;
+        st = ensure_buffer(g_dev[dev].operand, p.operand_bytes, &bt);
+        if (st) return st;
+        e = launch_transpose(static_cast<const float*>(B), bt, static_cast<int>(k),
+                             static_cast<int>(n), stream);
+        if (e != cudaSuccess) return cuda_fail(e, "launch");
         CUtensorMap tmA, tmB;
         st = tensor_map(a_in, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, k, 32, 128, &tmA,
                         CU_TENSOR_MAP_SWIZZLE_128B);
         if (st) return st;
-        st = tensor_map(B, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k, n, 32, 32, &tmB,
+        st = tensor_map(bt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, n, k, 32, 256, &tmB,
                         CU_TENSOR_MAP_SWIZZLE_128B);
         if (st) return st;
         TcArgs t;

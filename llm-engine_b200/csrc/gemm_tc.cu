@@ -4,9 +4,11 @@
 //
 // The reference runs these shapes on its SIMT sgemm_tiled<128,8>
 // (src/cuda_matmul.cu:71-125). Here one CTA per SM computes a 128 x 256 tile:
-//   warp 0      one thread issues TMA loads of A (K-major) and B (MN-major, B
-//               is stored k x n, so n is contiguous), 128-byte swizzled, into
-//               a 4-stage ring guarded by mbarriers;
+//   warp 0      one thread issues TMA loads of A and B, both K-major and
+//               128-byte swizzled, into a 4-stage ring guarded by mbarriers
+//               (B is stored k x n, n contiguous; a transpose pass first
+//               writes B^T, n x k, into scratch -- the TF32 MMA is run with
+//               both operands K-major);
 //   warp 1      allocates 256 TMEM columns; one thread issues
 //               tcgen05.mma.kind::tf32 (M=128, N=256, K=8) four times per
 //               32-deep stage and releases each stage with tcgen05.commit;
@@ -27,9 +29,7 @@ constexpr int TBM = 128, TBN = 256, TBK = 32;  // 32 fp32 = 128 bytes along K
 constexpr int kStages = 4;
 constexpr int kThreads = 192;
 constexpr int kABytes = TBM * TBK * 4;        // 16 KB
-constexpr int kBBoxCols = 32;                  // 128-byte swizzle span of fp32
-constexpr int kBBoxBytes = kBBoxCols * TBK * 4;  // 4 KB: 32 columns x 32 k-rows
-constexpr int kBBytes = TBK * TBN * 4;        // 32 KB
+constexpr int kBBytes = TBK * TBN * 4;        // 32 KB: B^T box of 256 rows (n) x 32 (k)
 constexpr int kRingBytes = kStages * (kABytes + kBBytes);
 constexpr int kSmemBytes = kRingBytes + 256 + 1024;  // barriers + alignment slack
 constexpr int kGroupM = 8;
@@ -85,15 +85,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
                 tma_load_2d_nohint(sA + s * kABytes, &tmA, kb * TBK, m0, &full[s]);
-#pragma unroll
-                for (int j = 0; j < TBN / kBBoxCols; ++j)
-                    tma_load_2d_nohint(sB + s * kBBytes + j * kBBoxBytes, &tmB, n0 + j * kBBoxCols,
-                                       kb * TBK, &full[s]);
+                tma_load_2d_nohint(sB + s * kBBytes, &tmB, kb * TBK, n0, &full[s]);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::instr_desc(tc::kFmtTF32, tc::kFmtTF32, false, true, TBM, TBN);
+            constexpr uint32_t idesc = tc::instr_desc(tc::kFmtTF32, tc::kFmtTF32, false, false, TBM, TBN);
             for (int kb = 0; kb < nk; ++kb) {
                 const int s = kb % kStages;
                 if (!mbar_wait(&full[s], (kb / kStages) & 1, &g_tc_error)) break;
@@ -102,10 +99,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t bbase = smem_u32(sB + s * kBBytes);
 #pragma unroll
                 for (int kk = 0; kk < TBK / 8; ++kk) {
-                    // A: K-major rows of 128 B; the 8-deep K step is 32 B into each row.
+                    // K-major rows of 128 B (8-row groups 1 KB apart); the 8-deep K step is
+                    // 32 B into each row.
                     const uint64_t ad = tc::smem_desc_sw128(abase + kk * 32, 16, 1024);
-                    // B: MN-major; the K step is one 8-row (1 KB) group; 32-column boxes 4 KB apart.
-                    const uint64_t bd = tc::smem_desc_sw128(bbase + kk * 1024, kBBoxBytes, 1024);
+                    const uint64_t bd = tc::smem_desc_sw128(bbase + kk * 32, 16, 1024);
                     tc::mma_tf32(tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
                 }
                 tc::commit(&empty[s]);
@@ -163,7 +160,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// out (n x k) = B^T for B k x n, fp32, through 32 x 32 shared-memory tiles so both the
+// reads and the writes are coalesced.
+__global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict__ B,
+                                                         float* __restrict__ out, int k, int n) {
+    __shared__ float tile[32][33];
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+    for (int i = ty; i < 32; i += 8) {
+        const int r = r0 + i, c = c0 + tx;
+        if (r < k && c < n) tile[i][tx] = B[static_cast<size_t>(r) * n + c];
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+        const int c = c0 + i, r = r0 + tx;  // out row c (a column of B), column r
+        if (c < n && r < k) out[static_cast<size_t>(c) * k + r] = tile[tx][i];
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_transpose(const float* B, float* out, int k, int n, cudaStream_t stream) {
+    const dim3 grid((n + 31) / 32, (k + 31) / 32);
+    transpose_kernel<<<grid, 256, 0, stream>>>(B, out, k, n);
+    return cudaGetLastError();
+}
 
 int tc_tile_m() { return TBM; }
 int tc_tile_n() { return TBN; }

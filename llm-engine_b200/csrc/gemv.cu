@@ -68,7 +68,7 @@ struct Layout {
     // Reduction buffers reuse the drained ring.
     static constexpr int kRedFloats = kConsumerWarps * M * Shape<M, Q8>::NT;
     static_assert((kRedFloats + M * Shape<M, Q8>::NT) * 4 <= kB, "reduction fits in the ring");
-    static_assert((kConsumerWarps + 1) * M * 4 <= kStages * kABox, "ss reduction fits");
+    static_assert((kConsumerWarps + 2) * M * 4 <= kStages * kABox, "ss reduction fits");
 };
 
 // ---- packed f32x2 arithmetic (sm_100) ---------------------------------------------------
@@ -341,32 +341,65 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
     if (a.slices == 1) return;
     __syncwarp();
 
-    // k split across the cluster: rank 0 adds the slices' sums, read from each
-    // CTA's shared memory, in rank order; the second barrier keeps every CTA's
-    // shared memory alive until rank 0 has read it.
+    // k split across the cluster: every CTA finishes 1/slices of the strip's
+    // columns, adding the slices' sums (read from each CTA's shared memory)
+    // in rank order; all remote loads are issued before the first add. The
+    // second barrier keeps every CTA's shared memory alive until all reads are
+    // done.
     cluster_sync();
-    if (cluster_rank() == 0 && tid < kConsumers) {
-        constexpr int E4 = M * S::NT / 4;
-        for (int e4 = tid; e4 < E4; e4 += kConsumers) {
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int r = 0; r < a.slices; ++r) {
-                const float4 t = ld_dsmem_f4(tot + 4 * e4, r);
-                v.x += t.x;
-                v.y += t.y;
-                v.z += t.z;
-                v.w += t.w;
-            }
-            // Rank 0's own tot is read before it is overwritten by this thread only.
-            *reinterpret_cast<float4*>(red + 4 * e4) = v;
+    if (tid < kConsumers) {
+        const uint32_t me = cluster_rank();
+        constexpr int E4 = M * S::NT / 4;  // float4 chunks of the strip's sums
+        const int per = (E4 + a.slices - 1) / a.slices;
+        const int e4_begin = static_cast<int>(me) * per;
+        const int e4_end = min(E4, e4_begin + per);
+        float* out4 = red;  // this CTA's drained ring: finished sums of its chunks
+        for (int e4 = e4_begin + tid; e4 < e4_end; e4 += kConsumers) {
+            float4 t[kGemvMaxCluster];
+#pragma unroll
+            for (int r = 0; r < kGemvMaxCluster; ++r)
+                if (r < a.slices) t[r] = ld_dsmem_f4(tot + 4 * e4, r);
+            float4 v = t[0];
+#pragma unroll
+            for (int r = 1; r < kGemvMaxCluster; ++r)
+                if (r < a.slices) {
+                    v.x += t[r].x;
+                    v.y += t[r].y;
+                    v.z += t[r].z;
+                    v.w += t[r].w;
+                }
+            *reinterpret_cast<float4*>(out4 + 4 * (e4 - e4_begin)) = v;
         }
+        float* ss_all = red_ss + kConsumerWarps * M + M;  // past tot_ss
         if (Norm && tid < M) {
-            float v = 0.0f;
-            for (int r = 0; r < a.slices; ++r) v += ld_dsmem_f(tot_ss + tid, r);
-            red_ss[tid] = v;
+            float t[kGemvMaxCluster];
+#pragma unroll
+            for (int r = 0; r < kGemvMaxCluster; ++r)
+                if (r < a.slices) t[r] = ld_dsmem_f(tot_ss + tid, r);
+            float v = t[0];
+#pragma unroll
+            for (int r = 1; r < kGemvMaxCluster; ++r)
+                if (r < a.slices) v += t[r];
+            ss_all[tid] = v;
         }
         named_barrier(1, kConsumers);
-        store_strip<M, S::NT, Q8, Norm>(red, red_ss, a, col0, tid, kConsumers);
+        float rs[M];
+        if constexpr (Norm) {
+#pragma unroll
+            for (int r = 0; r < M; ++r)
+                rs[r] = 1.0f / sqrtf(ss_all[r] / static_cast<float>(a.k) + kRmsEps);
+        }
+        for (int e = 4 * e4_begin + tid; e < 4 * e4_end; e += kConsumers) {
+            const int r = e / S::NT, col = col0 + e % S::NT;
+            if (col >= a.n) continue;
+            float v = out4[e - 4 * e4_begin];
+            if constexpr (Q8) v *= __ldg(a.scale + col);
+            if constexpr (Norm) v *= rs[r];
+            float* o = a.C + static_cast<size_t>(r) * a.n + col;
+            *o = a.accumulate ? *o + v : v;
+        }
     }
+    __syncwarp();
     cluster_sync();
 }
 

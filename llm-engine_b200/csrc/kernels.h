@@ -68,7 +68,7 @@ cudaError_t launch_tiled_simt(const TiledArgs& a);
 cudaError_t launch_naive(const TiledArgs& a);
 
 // tcgen05 tensor-core GEMM (gemm_tc.cu): 128 x 256 output tiles, TF32 operands read by
-// TMA with 128-byte swizzle (A: K-major box 32 x 128; B: MN-major boxes 32 x 32).
+// TMA with 128-byte swizzle, both K-major (A: box 32 x 128 of A; B: box 32 x 256 of B^T).
 struct TcArgs {
     int m = 0, n = 0, k = 0;
     float* C = nullptr;
@@ -79,7 +79,9 @@ struct TcArgs {
 };
 int tc_tile_m();
 int tc_tile_n();
-cudaError_t launch_gemm_tf32(const TcArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB);
+cudaError_t launch_gemm_tf32(const TcArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmBt);
+// out (n x k) = B^T for fp32 B (k x n).
+cudaError_t launch_transpose(const float* B, float* out, int k, int n, cudaStream_t stream);
 unsigned read_and_clear_tc_error();
 
 // out = rmsnorm(A) * w per row (eps 1e-5), m rows of k.

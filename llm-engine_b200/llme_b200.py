@@ -52,7 +52,7 @@ class Plan(ctypes.Structure):
         ("cluster", ctypes.c_int),
         ("span", ctypes.c_int), ("tile_m", ctypes.c_int), ("tile_n", ctypes.c_int),
         ("split_bytes", ctypes.c_size_t), ("counter_slots", ctypes.c_size_t),
-        ("norm_bytes", ctypes.c_size_t),
+        ("norm_bytes", ctypes.c_size_t), ("operand_bytes", ctypes.c_size_t),
     ]
 
     def as_dict(self) -> dict:
