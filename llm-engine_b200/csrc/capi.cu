@@ -494,9 +494,97 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
     return LLME_OK;
 }
 
+// ---- allocation-free entry point ------------------------------------------------------------
+//
+// llme_matmul_q8_noalloc runs the split-K tile kernel (the tiled_split plan) with its
+// partial sums and tickets in one fixed device array defined here, instead of the grow-only
+// scratch the other entry points cudaMalloc. Layout: [tickets: kNoAllocTickets x u32]
+// [partial sums: the rest]. The tickets must be zero when a launch starts; set-up clears them
+// once and every launch leaves them at zero again (the last CTA of a tile resets its ticket).
+// Partial sums are always written before they are read. Every call on a device shares this
+// one array, so two calls that overlap on the GPU (different streams, or concurrent graphs)
+// race on it.
+constexpr size_t kNoAllocBytes = LLME_NOALLOC_SCRATCH_BYTES;
+constexpr size_t kNoAllocTickets = 4096;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_base[kMaxDevices] = {};
+
+// Once per device, with that device current: the array's device address (the host-side
+// symbol is only a stand-in, never a device pointer) and cleared tickets.
+int noalloc_setup(int dev, cudaStream_t stream, unsigned char** base) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_base[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "scratch symbol address");
+        e = cudaMemsetAsync(p, 0, kNoAllocTickets * sizeof(unsigned), stream);
+        if (e != cudaSuccess) return cuda_fail(e, "clear scratch tickets");
+        g_noalloc_base[dev] = static_cast<unsigned char*>(p);
+    }
+    *base = g_noalloc_base[dev];
+    return LLME_OK;
+}
+
+int run_noalloc(size_t m, size_t n, size_t k, const float* A, const int8_t* B, const float* scale,
+                float* C, bool accumulate, void* stream_ptr) {
+    g_error.clear();
+    cudaStream_t stream = stream_ptr ? static_cast<cudaStream_t>(stream_ptr) : cudaStreamPerThread;
+    int dev = 0, sms = 0;
+    int st = current_device(&dev);
+    if (st) return st;
+    st = device_sms(dev, &sms);
+    if (st) return st;
+    PlanIn in{m, n, k, true, LLME_KERNEL_TILED_SPLIT, accumulate, reinterpret_cast<uintptr_t>(A),
+              reinterpret_cast<uintptr_t>(B), 0, sms, math_mode()};
+    llme_plan_t p;
+    st = make_plan(in, &p);
+    if (st) return st;
+    if (p.path == LLME_PATH_NONE) return LLME_OK;
+    if (p.path == LLME_PATH_ZERO) {
+        cudaError_t e = cudaMemsetAsync(C, 0, m * n * sizeof(float), stream);
+        return e == cudaSuccess ? LLME_OK : cuda_fail(e, "memset");
+    }
+    const size_t ticket_bytes = kNoAllocTickets * sizeof(unsigned);
+    if (p.counter_slots > kNoAllocTickets || p.split_bytes > kNoAllocBytes - ticket_bytes)
+        return fail(LLME_E_INVALID,
+                    "llme_matmul_q8_noalloc: this product needs " + std::to_string(p.split_bytes) +
+                        " bytes of split-K scratch and " + std::to_string(p.counter_slots) +
+                        " tickets; the fixed scratch holds " +
+                        std::to_string(kNoAllocBytes - ticket_bytes) + " bytes and " +
+                        std::to_string(kNoAllocTickets) + " tickets " + shapes(m, n, k));
+    unsigned char* base = nullptr;
+    st = noalloc_setup(dev, stream, &base);
+    if (st) return st;
+    TiledArgs t;
+    t.m = static_cast<int>(m);
+    t.n = static_cast<int>(n);
+    t.k = static_cast<int>(k);
+    t.A = A;
+    t.B = B;
+    t.scale = scale;
+    t.C = C;
+    t.q8 = true;
+    t.accumulate = accumulate;
+    t.slices = p.slices;
+    t.span = p.span;
+    t.split.counters = reinterpret_cast<unsigned*>(base);
+    t.split.partial = reinterpret_cast<float*>(base + ticket_bytes);
+    t.stream = stream;
+    cudaError_t e = launch_tiled_simt(t);
+    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "launch");
+}
+
 }  // namespace
 
 extern "C" {
+
+int llme_matmul_q8_noalloc(size_t m, size_t n, size_t k, const float* A, const int8_t* B,
+                           const float* scale, float* C, int accumulate, void* stream) {
+    return run_noalloc(m, n, k, A, B, scale, C, accumulate != 0, stream);
+}
+
 
 int llme_matmul_f32(size_t m, size_t n, size_t k, const float* A, const float* B, float* C,
                     int kernel, int accumulate, const float* rms_weight, unsigned flags,

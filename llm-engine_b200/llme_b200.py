@@ -82,6 +82,8 @@ def load() -> ctypes.CDLL:
     lib.llme_matmul_f32.argtypes = [sz, sz, sz, vp, vp, vp, i, i, vp, u, vp]
     lib.llme_matmul_q8.argtypes = [sz, sz, sz, vp, vp, vp, vp, i, i, vp, u, vp]
     lib.llme_matmul_f32.restype = lib.llme_matmul_q8.restype = i
+    lib.llme_matmul_q8_noalloc.argtypes = [sz, sz, sz, vp, vp, vp, vp, i, vp]
+    lib.llme_matmul_q8_noalloc.restype = i
     lib.llme_last_error.restype = ctypes.c_char_p
     lib.llme_scratch_generation.restype = sz
     for f in ("llme_synchronize", "llme_device_available", "llme_device_supported",
@@ -138,6 +140,14 @@ def matmul_cuda_q8(m: int, n: int, k: int, A: int, B: int, scale: int, C: int,
     """C (+)= [rmsnorm(A)] x (B * scale) with int8 B on device pointers (cuda_matmul.h:105-107)."""
     _check(load().llme_matmul_q8(m, n, k, A, B, scale, C, _kernel_id(kernel),
                                  int(bool(accumulate)), rms_weight or None, flags, stream or None))
+
+
+def matmul_cuda_q8_noalloc(m: int, n: int, k: int, A: int, B: int, scale: int, C: int,
+                           accumulate: bool = False, stream: int | None = None) -> None:
+    """The allocation-free split-K product (llme_matmul_q8_noalloc): its scratch is a fixed
+    device array inside the library, so the call never allocates device memory."""
+    _check(load().llme_matmul_q8_noalloc(m, n, k, A, B, scale, C, int(bool(accumulate)),
+                                         stream or None))
 
 
 def plan(m: int, n: int, k: int, q8: bool, kernel="automatic", accumulate: bool = False,
