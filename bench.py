@@ -182,20 +182,21 @@ class Chain:
             q, s = quantize_on_device(W)
             del W
             if world > 1:
+                import shard
                 if rowp:
-                    kk = k // world
-                    q = q[rank * kk:(rank + 1) * kk].contiguous()
-                    kl, nl = kk, n
+                    q = shard.row_shard(q, world, rank).contiguous()
+                    kl, nl = q.shape[0], n
                 else:
-                    nn = n // world
-                    q = q[:, rank * nn:(rank + 1) * nn].contiguous()
-                    s = s[rank * nn:(rank + 1) * nn].contiguous()
-                    kl, nl = k, nn
+                    q, s = shard.column_shard(q, s, world, rank)
+                    s = s.contiguous()
+                    kl, nl = k, q.shape[1]
             else:
                 kl, nl = k, n
             self.mats.append((q, s, kl, nl, rowp))
         torch.cuda.synchronize()
-        # Activations: fresh U(-1, 1) per product; outputs one slot each.
+        # Activations: a fresh U(-1, 1) row per product, the same on every rank (a row shard
+        # takes its slice of it); outputs one slot each.
+        import shard
         self.a_off, self.c_off = [], []
         a_tot = c_tot = 0
         for (_, _, kl, nl, _) in self.mats:
@@ -204,8 +205,14 @@ class Chain:
             a_tot += (kl + 3) // 4 * 4   # keep every vector 16-byte aligned
             c_tot += (nl + 3) // 4 * 4
         ga = torch.Generator(device="cpu")
-        ga.manual_seed(seed * 7 + rank)
-        self.a_host = (torch.rand(a_tot, generator=ga) * 2 - 1).pin_memory()
+        ga.manual_seed(seed * 7)
+        a_host = torch.empty(a_tot)
+        for i, (_, k, n, rowp) in enumerate(self.shapes):
+            full = torch.rand(k, generator=ga) * 2 - 1
+            kl = self.mats[i][2]
+            s0 = shard.shard_range(k, world, rank)[0] if (rowp and world > 1) else 0
+            a_host[self.a_off[i]:self.a_off[i] + kl] = full[s0:s0 + kl]
+        self.a_host = a_host.pin_memory()
         self.c_host = torch.empty(c_tot, dtype=torch.float32).pin_memory()
         self.a_dev = self.a_host.cuda()
         self.c_dev = torch.empty(c_tot, dtype=torch.float32, device="cuda")
@@ -213,7 +220,7 @@ class Chain:
             * 1  # this rank's share
         self.total_bytes = sum(algorithmic_bytes(k, n) for (_, k, n, _) in self.shapes)
 
-    def launch_all(self, stream_handle, comm=None):
+    def launch_all(self, stream_handle, comm=None, join=None):
         import llme_b200 as L
         for i, (q, s, kl, nl, rowp) in enumerate(self.mats):
             a = self.a_dev.data_ptr() + 4 * self.a_off[i]
@@ -222,6 +229,8 @@ class Chain:
                              L.FLAG_WEIGHTS_STATIC, stream_handle)
             if rowp and comm is not None:
                 comm(c, nl)
+        if join is not None:
+            join()
 
     def n_launches(self):
         return len(self.mats)
@@ -413,16 +422,23 @@ def run_ours(args):
         chain = Chain(world, rank, chain_shapes(), seed=3)
     else:
         chain = Chain(world, rank, gemv_shapes(), seed=0)
-    comm = None
+    comm = tp = None
+    stream = torch.cuda.Stream()
+    h = stream.cuda_stream
     if world > 1:
+        # The library's own NCCL communicator; each row-parallel all-reduce runs on a side
+        # stream so it overlaps the products that follow, and the step joins it at the end.
         import torch.distributed as dist
+        uid = [L.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        tp = L.Comm(world, rank, uid[0], timeout_s=60.0)
         comm_stream = torch.cuda.Stream()
 
         def comm(c_ptr, n):  # noqa: F811
-            raise NotImplementedError("multi-GPU exchange")
-    stream = torch.cuda.Stream()
-    h = stream.cuda_stream
-    graph = capture(lambda: chain.launch_all(h, comm), stream)
+            comm_stream.wait_stream(torch.cuda.current_stream())
+            tp.allreduce_sum_f32(c_ptr, n, comm_stream.cuda_stream)
+    join = (lambda: torch.cuda.current_stream().wait_stream(comm_stream)) if world > 1 else None
+    graph = capture(lambda: chain.launch_all(h, comm, join), stream)
     sampler = ClockSampler(local)
     secs = time_graph(graph, args.steps, args.warmup, stream, world, sampler)
     secs = max_over_ranks(secs, world)
@@ -432,7 +448,7 @@ def run_ours(args):
     # e2e: the same chain through the C ABI with host buffers, copies in the timed region.
     def e2e_fn():
         chain.a_dev.copy_(chain.a_host, non_blocking=True)
-        chain.launch_all(h, comm)
+        chain.launch_all(h, comm, join)
         chain.c_host.copy_(chain.c_dev, non_blocking=True)
     e2e_graph = capture(e2e_fn, stream)
     e2e_secs = max_over_ranks(time_graph(e2e_graph, args.steps, args.warmup, stream, world), world)
@@ -455,6 +471,8 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: N(0,0.02^2) weights quantised per column to int8, U(-1,1) activations",
+        "exchange": ("NCCL sum all-reduce of wo/w2 partial outputs (library communicator, side "
+                     "stream)") if world > 1 else None,
         "config": WORKLOAD_CONFIG[args.workload] | {
                    "products_per_step": launches,
                    "algorithmic_bytes_per_step": int(chain.total_bytes),
@@ -470,7 +488,11 @@ def run_ours(args):
         line["cpu_baseline"] = cpu_baseline_sample(chain)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    # Graphs holding NCCL calls go first, then the communicator, then the process group.
     del graph, e2e_graph
+    torch.cuda.synchronize()
+    if tp is not None:
+        tp.destroy()
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

@@ -141,6 +141,45 @@ int llme_free(void* ptr);                      /* cudaFree; NULL is fine */
 int llme_copy_to_device(void* dst, const void* src, size_t bytes);   /* waits */
 int llme_copy_to_host(void* dst, const void* src, size_t bytes);     /* waits */
 
+/* ---- multi-GPU: tensor-parallel products over NCCL --------------------------------------- *
+ * One process per GPU. The reference has no multi-GPU code (single CudaTransformer); these
+ * entry points are additive. Column-parallel weights (wq, wk, wv, w1, w3, classifier) need no
+ * new call: each rank runs llme_matmul_* on its contiguous k x (n/ranks) slice of B (and the
+ * matching slice of scale) and owns those columns of C. Row-parallel weights (wo, w2) are
+ * split along k: each rank holds rows [r*k/ranks, (r+1)*k/ranks) of B, the matching columns
+ * of A, and the whole scale vector (the column scale is linear, so it applies to each partial
+ * sum), and the m x n partial products are summed with an NCCL all-reduce over NVLink. NCCL
+ * (libnccl.so.2) is loaded on first use. */
+#define LLME_COMM_ID_BYTES 128
+typedef struct llme_comm llme_comm_t;
+
+/* A fresh communicator id (LLME_COMM_ID_BYTES bytes) on one rank, to be shared with all ranks. */
+int llme_comm_unique_id(void* id);
+
+/* Joins the communicator of `nranks` ranks with the shared id, on the current device.
+ * Initialisation is non-blocking and polled: if it has not finished after timeout_s seconds
+ * (a rank that never joins), it is aborted and LLME_E_TIMEOUT returned. */
+int llme_comm_init(llme_comm_t** comm, int nranks, int rank, const void* id, double timeout_s);
+int llme_comm_destroy(llme_comm_t* comm);   /* after all work on it has finished */
+int llme_comm_abort(llme_comm_t* comm);     /* from an error path: frees without waiting */
+int llme_comm_size(const llme_comm_t* comm);
+int llme_comm_rank(const llme_comm_t* comm);
+
+/* In-place sum all-reduce of `count` fp32 values on `stream` (capturable in a CUDA graph). */
+int llme_allreduce_sum_f32(float* buf, size_t count, llme_comm_t* comm, void* stream);
+
+/* Row-parallel product: C = A_local x (B_local * scale) summed over ranks (C += ... with
+ * accumulate, the residual add: only rank 0 adds its C, so the sum counts it once). A_local
+ * is m x k_local (this rank's columns of A), B_local k_local x n, scale n (the full vector).
+ * Same kernels as llme_matmul_q8 on the shard, then llme_allreduce_sum_f32 on C, both on
+ * `stream`. No RMSNorm fusion here: a row norm needs the whole row of A. */
+int llme_matmul_q8_rowpar(size_t m, size_t n, size_t k_local, const float* A_local,
+                          const int8_t* B_local, const float* scale, float* C, int kernel,
+                          int accumulate, unsigned flags, llme_comm_t* comm, void* stream);
+int llme_matmul_f32_rowpar(size_t m, size_t n, size_t k_local, const float* A_local,
+                           const float* B_local, float* C, int kernel, int accumulate,
+                           unsigned flags, llme_comm_t* comm, void* stream);
+
 /* ---- host-side planning, exposed so the dispatch logic can be tested without a GPU -------- */
 enum {
     LLME_PATH_NONE = 0,        /* nothing to launch (m == 0 or n == 0) */

@@ -27,7 +27,7 @@ INCLUDE = os.path.join(REPO, "include")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "lib")
 
-CUDA_SOURCES = ["capi.cu", "gemv.cu", "gemm_simt.cu", "gemm_tc.cu"]
+CUDA_SOURCES = ["capi.cu", "gemv.cu", "gemm_simt.cu", "gemm_tc.cu", "comm.cu"]
 CXX_SHIM = "cuda_matmul.cpp"
 LIB_NAME = "libllme_b200.so"
 CXX_LIB_NAME = "libllme_b200_cxx.so"
@@ -89,7 +89,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
                     print(out)
     lib = os.path.join(LIB, LIB_NAME)
     if force or _stale(lib, objs):
-        _run([nv] + ARCH + ["-shared", "-o", lib] + objs, verbose)
+        _run([nv] + ARCH + ["-shared", "-o", lib] + objs + ["-ldl"], verbose)
     cxx = os.path.join(LIB, CXX_LIB_NAME)
     shim = os.path.join(CSRC, CXX_SHIM)
     if force or _stale(cxx, [shim, lib] + headers):

@@ -578,6 +578,16 @@ int run_noalloc(size_t m, size_t n, size_t k, const float* A, const int8_t* B, c
 
 }  // namespace
 
+namespace llme {
+int set_error(int code, const std::string& msg) { return fail(code, msg); }
+int set_cuda_error(cudaError_t e, const char* what) { return cuda_fail(e, what); }
+int run_product(size_t m, size_t n, size_t k, const float* A, const void* B, const float* scale,
+                float* C, bool q8, int kernel, bool accumulate, const float* rms, unsigned flags,
+                void* stream) {
+    return run(m, n, k, A, B, scale, C, q8, kernel, accumulate, rms, flags, stream);
+}
+}  // namespace llme
+
 extern "C" {
 
 int llme_matmul_q8_noalloc(size_t m, size_t n, size_t k, const float* A, const int8_t* B,

@@ -35,6 +35,13 @@ namespace {
 
 __device__ unsigned int g_gemv_error;
 
+#ifdef LLME_GEMV_TRACE
+#define GEMV_TRACE(a, point) \
+    (a).trace[(static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x) * 8 + (point)] = global_timer_ns()
+#else
+#define GEMV_TRACE(a, point) ((void)0)
+#endif
+
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kTmaThreads = kConsumers + 32;  // + one producer warp
@@ -62,7 +69,8 @@ struct Layout {
     static constexpr int kWBox = kGemvBoxRows * 4;
     static constexpr int kOffA = kB;
     static constexpr int kOffW = kOffA + kStages * kABox;
-    static constexpr int kOffBar = kOffW + (Norm ? kStages * kWBox : 0);
+    static constexpr int kOffScale = kOffW + (Norm ? kStages * kWBox : 0);  // NT floats (int8)
+    static constexpr int kOffBar = kOffScale + (Q8 ? Shape<M, Q8>::NT * 4 : 0);
     static constexpr int kBytes = kOffBar + 2 * kStages * 8 + 16;
     static constexpr uint32_t kTx = kBoxBytesB + kABox + (Norm ? kWBox : 0);
     // Reduction buffers reuse the drained ring.
@@ -161,20 +169,18 @@ __device__ __forceinline__ float ld_dsmem_f(const float* local, uint32_t rank) {
 
 // Writes C for a CTA's column strip from M x NT sums that are already complete
 // (tot, shared memory) -- the kernels' common epilogue.
+// sscale: the strip's column scales already in shared memory (int8 TMA kernel), or null to
+// read them from global memory.
 template <int M, int NT, bool Q8, bool Norm>
 __device__ __forceinline__ void store_strip(const float* tot, const float* tot_ss, const GemvArgs& a,
-                                            int col0, int tid, int nthreads) {
-    float rs[M];
-    if constexpr (Norm) {
-#pragma unroll
-        for (int r = 0; r < M; ++r) rs[r] = 1.0f / sqrtf(tot_ss[r] / static_cast<float>(a.k) + kRmsEps);
-    }
+                                            int col0, int tid, int nthreads,
+                                            const float* sscale = nullptr) {
     for (int e = tid; e < M * NT; e += nthreads) {
         const int r = e / NT, col = col0 + e % NT;
         if (col >= a.n) continue;
         float v = tot[e];
-        if constexpr (Q8) v *= __ldg(a.scale + col);
-        if constexpr (Norm) v *= rs[r];
+        if constexpr (Q8) v *= sscale ? sscale[e % NT] : __ldg(a.scale + col);
+        if constexpr (Norm) v *= 1.0f / sqrtf(tot_ss[r] / static_cast<float>(a.k) + kRmsEps);
         float* out = a.C + static_cast<size_t>(r) * a.n + col;
         *out = a.accumulate ? *out + v : v;
     }
@@ -197,6 +203,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
     const int k1 = min(a.k, k0 + a.span);
     const int nb = (k1 - k0 + kGemvBoxRows - 1) / kGemvBoxRows;
 
+    if (tid == 0) GEMV_TRACE(a, 0);
     if (tid == kConsumers) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
@@ -208,7 +215,10 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
         if (Norm) prefetch_tensormap(&tmW);
     }
     __syncthreads();
-    if (tid == 0) pdl_launch_dependents();
+    if (tid == 0) {
+        pdl_launch_dependents();
+        GEMV_TRACE(a, 1);
+    }
 
     float* red = reinterpret_cast<float*>(smem);
     float* tot = red + L::kRedFloats;
@@ -225,6 +235,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
                 mbar_arrive_expect_tx(&full[b], L::kTx);
                 tma_load_2d(smem + b * kBoxBytesB, &tmB, col0, k0 + b * kGemvBoxRows, &full[b], pol);
             }
+            GEMV_TRACE(a, 2);
             pdl_wait();
             for (int b = 0; b < pro; ++b) {
                 tma_load_2d_nohint(smem + L::kOffA + b * L::kABox, &tmA, k0 + b * kGemvBoxRows, 0,
@@ -233,6 +244,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
                     tma_load_1d(smem + L::kOffW + b * L::kWBox, &tmW, k0 + b * kGemvBoxRows,
                                 &full[b]);
             }
+            GEMV_TRACE(a, 3);
             for (int b = pro; b < nb; ++b) {
                 const int s = b % kStages;
                 if (!mbar_wait(&empty[s], ((b / kStages) - 1) & 1, &g_gemv_error)) break;
@@ -245,6 +257,12 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
         }
         __syncwarp();
     } else {
+        // The strip's column scales are weights too: fetch them before waiting for the
+        // previous launch, so the epilogue never waits on DRAM for them.
+        if constexpr (Q8) {
+            float* sscale = reinterpret_cast<float*>(smem + L::kOffScale);
+            if (tid < S::NT) sscale[tid] = col0 + tid < a.n ? __ldg(a.scale + col0 + tid) : 0.0f;
+        }
         // Consumers: C is touched only after this.
         pdl_wait();
         const int cg = tid % S::TPR, rg = tid / S::TPR;
@@ -259,6 +277,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
         for (int b = 0; b < nb; ++b) {
             const int s = b % kStages;
             if (!mbar_wait(&full[s], (b / kStages) & 1, &g_gemv_error)) break;
+            if (tid == 0 && b == 0) GEMV_TRACE(a, 4);
             const uint8_t* sb = smem + s * kBoxBytesB + cg * (S::V * S::ESZ);
             const float* sa = reinterpret_cast<const float*>(smem + L::kOffA + s * L::kABox);
             const float* sw = reinterpret_cast<const float*>(smem + L::kOffW + s * L::kWBox);
@@ -291,6 +310,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
 
         // Reduce the row groups: inside a warp by shuffle, then the 8 warps
         // through shared memory (the drained ring), always in the same order.
+        if (tid == 0) GEMV_TRACE(a, 5);
         named_barrier(1, kConsumers);
         float accf[M][S::V];
 #pragma unroll
@@ -333,9 +353,12 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
             for (int w = 0; w < kConsumerWarps; ++w) v += red_ss[w * M + tid];
             tot_ss[tid] = v;
         }
+        if (tid == 0) GEMV_TRACE(a, 6);
         if (a.slices == 1) {
             named_barrier(1, kConsumers);
-            store_strip<M, S::NT, Q8, Norm>(tot, tot_ss, a, col0, tid, kConsumers);
+            store_strip<M, S::NT, Q8, Norm>(tot, tot_ss, a, col0, tid, kConsumers,
+                                            reinterpret_cast<const float*>(smem + L::kOffScale));
+            if (tid == 0) GEMV_TRACE(a, 7);
         }
     }
     if (a.slices == 1) return;
@@ -383,24 +406,19 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
             ss_all[tid] = v;
         }
         named_barrier(1, kConsumers);
-        float rs[M];
-        if constexpr (Norm) {
-#pragma unroll
-            for (int r = 0; r < M; ++r)
-                rs[r] = 1.0f / sqrtf(ss_all[r] / static_cast<float>(a.k) + kRmsEps);
-        }
         for (int e = 4 * e4_begin + tid; e < 4 * e4_end; e += kConsumers) {
             const int r = e / S::NT, col = col0 + e % S::NT;
             if (col >= a.n) continue;
             float v = out4[e - 4 * e4_begin];
-            if constexpr (Q8) v *= __ldg(a.scale + col);
-            if constexpr (Norm) v *= rs[r];
+            if constexpr (Q8) v *= reinterpret_cast<const float*>(smem + L::kOffScale)[e % S::NT];
+            if constexpr (Norm) v *= 1.0f / sqrtf(ss_all[r] / static_cast<float>(a.k) + kRmsEps);
             float* o = a.C + static_cast<size_t>(r) * a.n + col;
             *o = a.accumulate ? *o + v : v;
         }
     }
     __syncwarp();
     cluster_sync();
+    if (tid == 0) GEMV_TRACE(a, 7);
 }
 
 // The plain-load kernel's k split: partials to scratch, a ticket per column

@@ -6,8 +6,17 @@
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
+#include <string>
 
 namespace llme {
+
+// The calling thread's llme_last_error message (defined in capi.cu); return `code`.
+int set_error(int code, const std::string& msg);
+int set_cuda_error(cudaError_t e, const char* what);
+// The C ABI's products without the public wrapper (capi.cu), for the sharded entry points.
+int run_product(size_t m, size_t n, size_t k, const float* A, const void* B, const float* scale,
+                float* C, bool q8, int kernel, bool accumulate, const float* rms, unsigned flags,
+                void* stream);
 
 // Deterministic split-K across CTAs: a CTA that owns slice s of a tile writes
 // its partial sums to partial[(tile * slices + s) * tile_elems + e], bumps
@@ -35,6 +44,10 @@ struct GemvArgs {
     SplitScratch split;
     cudaStream_t stream = nullptr;
     bool pdl = false;               // launch with programmatic stream serialization
+    // Timeline tracing, used only when gemv.cu is compiled with LLME_GEMV_TRACE: 8 global
+    // timer stamps per CTA (entry, init, weights issued, activations issued, first data, loop
+    // done, CTA sums ready, end). Null and unused in normal builds.
+    unsigned long long* trace = nullptr;
 };
 
 // TMA GEMV: each CTA streams 128-byte row segments of B (128 int8 or 32 fp32 columns) in

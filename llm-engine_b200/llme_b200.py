@@ -84,6 +84,17 @@ def load() -> ctypes.CDLL:
     lib.llme_matmul_f32.restype = lib.llme_matmul_q8.restype = i
     lib.llme_matmul_q8_noalloc.argtypes = [sz, sz, sz, vp, vp, vp, vp, i, vp]
     lib.llme_matmul_q8_noalloc.restype = i
+    lib.llme_comm_unique_id.argtypes = [ctypes.c_char_p]
+    lib.llme_comm_init.argtypes = [ctypes.POINTER(vp), i, i, ctypes.c_char_p, ctypes.c_double]
+    lib.llme_comm_destroy.argtypes = lib.llme_comm_abort.argtypes = [vp]
+    lib.llme_comm_size.argtypes = lib.llme_comm_rank.argtypes = [vp]
+    lib.llme_allreduce_sum_f32.argtypes = [vp, sz, vp, vp]
+    lib.llme_matmul_q8_rowpar.argtypes = [sz, sz, sz, vp, vp, vp, vp, i, i, u, vp, vp]
+    lib.llme_matmul_f32_rowpar.argtypes = [sz, sz, sz, vp, vp, vp, i, i, u, vp, vp]
+    for f in ("llme_comm_unique_id", "llme_comm_init", "llme_comm_destroy", "llme_comm_abort",
+              "llme_comm_size", "llme_comm_rank", "llme_allreduce_sum_f32",
+              "llme_matmul_q8_rowpar", "llme_matmul_f32_rowpar"):
+        getattr(lib, f).restype = i
     lib.llme_last_error.restype = ctypes.c_char_p
     lib.llme_scratch_generation.restype = sz
     for f in ("llme_synchronize", "llme_device_available", "llme_device_supported",
@@ -148,6 +159,52 @@ def matmul_cuda_q8_noalloc(m: int, n: int, k: int, A: int, B: int, scale: int, C
     device array inside the library, so the call never allocates device memory."""
     _check(load().llme_matmul_q8_noalloc(m, n, k, A, B, scale, C, int(bool(accumulate)),
                                          stream or None))
+
+
+COMM_ID_BYTES = 128
+
+
+class Comm:
+    """An NCCL communicator owned by the library (one per GPU, one process per GPU)."""
+
+    def __init__(self, nranks: int, rank: int, unique_id: bytes, timeout_s: float = 60.0):
+        if len(unique_id) != COMM_ID_BYTES:
+            raise InvalidArgument("communicator id must be 128 bytes")
+        h = ctypes.c_void_p()
+        _check(load().llme_comm_init(ctypes.byref(h), nranks, rank, unique_id, timeout_s))
+        self.handle = h.value
+        self.nranks, self.rank = nranks, rank
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(COMM_ID_BYTES)
+        _check(load().llme_comm_unique_id(buf))
+        return buf.raw
+
+    def allreduce_sum_f32(self, ptr: int, count: int, stream: int | None = None) -> None:
+        _check(load().llme_allreduce_sum_f32(ptr, count, self.handle, stream or None))
+
+    def matmul_q8_rowpar(self, m, n, k_local, A, B, scale, C, kernel="automatic",
+                         accumulate=False, flags=0, stream=None) -> None:
+        _check(load().llme_matmul_q8_rowpar(m, n, k_local, A, B, scale, C, _kernel_id(kernel),
+                                            int(bool(accumulate)), flags, self.handle,
+                                            stream or None))
+
+    def matmul_f32_rowpar(self, m, n, k_local, A, B, C, kernel="automatic", accumulate=False,
+                          flags=0, stream=None) -> None:
+        _check(load().llme_matmul_f32_rowpar(m, n, k_local, A, B, C, _kernel_id(kernel),
+                                             int(bool(accumulate)), flags, self.handle,
+                                             stream or None))
+
+    def destroy(self) -> None:
+        if self.handle:
+            h, self.handle = self.handle, None
+            _check(load().llme_comm_destroy(h))
+
+    def abort(self) -> None:
+        if self.handle:
+            h, self.handle = self.handle, None
+            _check(load().llme_comm_abort(h))
 
 
 def plan(m: int, n: int, k: int, q8: bool, kernel="automatic", accumulate: bool = False,

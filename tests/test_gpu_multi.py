@@ -1,0 +1,111 @@
+"""Tensor-parallel products through the library's NCCL communicator.
+
+* A communicator whose second rank never joins must end in LLME_E_TIMEOUT within its
+  deadline, not hang (host-side failure: nothing runs on the GPU; one GPU is enough).
+* On two GPUs (skipped with fewer): column-parallel products on n-shards and row-parallel
+  products on k-shards (llme_matmul_q8_rowpar, all-reduce inside, residual added once), both
+  through the C ABI, against the oracle on the unsharded weights.
+Child processes keep NVLS off (NCCL_NVLS_ENABLE=0), as failure tests on this pool require.
+"""
+from __future__ import annotations
+
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import close_to
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ENV = dict(os.environ, NCCL_NVLS_ENABLE="0")
+
+NEVER_JOINS = r"""
+import sys, time
+sys.path.insert(0, "llm-engine_b200")
+import llme_b200 as L
+uid = L.Comm.unique_id()
+t0 = time.time()
+try:
+    L.Comm(2, 0, uid, timeout_s=3.0)
+    print("JOINED")
+except L.DeviceTimeout as e:
+    print("TIMEOUT", round(time.time() - t0, 1), e)
+"""
+
+
+def test_comm_init_times_out_when_a_rank_never_joins():
+    r = subprocess.run([sys.executable, "-c", NEVER_JOINS], cwd=REPO, env=ENV, timeout=120,
+                       stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+    assert r.returncode == 0, r.stdout[-2000:]
+    assert "TIMEOUT" in r.stdout, r.stdout[-2000:]
+
+
+TP_WORKER = r"""
+import os, sys, datetime
+import numpy as np
+sys.path.insert(0, "llm-engine_b200"); sys.path.insert(0, "oracle")
+import torch, torch.distributed as dist
+import llme_b200 as L, shard, oracle
+rank, world, port, out = int(sys.argv[1]), int(sys.argv[2]), int(sys.argv[3]), sys.argv[4]
+torch.cuda.set_device(rank)
+dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                        world_size=world, timeout=datetime.timedelta(seconds=60))
+uid = [L.Comm.unique_id() if rank == 0 else None]
+dist.broadcast_object_list(uid, src=0)
+comm = L.Comm(world, rank, uid[0], timeout_s=60.0)
+rng = np.random.default_rng(31)
+for (m, k, n) in [(1, 4096, 4096), (4, 11008, 4096), (8, 1024, 2048), (130, 512, 1024)]:
+    A = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    q, s = oracle.quantize_q8((rng.standard_normal((k, n)) * 0.02).astype(np.float32))
+    C0 = rng.uniform(-1, 1, (m, n)).astype(np.float32)
+    dev = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    # column-parallel: this rank's columns
+    qc, sc = shard.column_shard(q, s, world, rank)
+    Cc = torch.empty(m, qc.shape[1], device="cuda")
+    L.matmul(dev(A), dev(qc), scale=dev(sc), C=Cc)
+    # row-parallel with the residual add
+    Ar, qr = shard.activation_columns(A, world, rank), shard.row_shard(q, world, rank)
+    Cr = dev(C0)
+    comm.matmul_q8_rowpar(m, n, Ar.shape[1], dev(Ar).data_ptr(), dev(qr).data_ptr(),
+                          dev(s).data_ptr(), Cr.data_ptr(), accumulate=True,
+                          stream=L.torch_stream_handle())
+    torch.cuda.synchronize()
+    np.save(f"{out}/col_{m}_{rank}.npy", Cc.cpu().numpy())
+    np.save(f"{out}/row_{m}_{rank}.npy", Cr.cpu().numpy())
+L.synchronize()
+comm.destroy()
+dist.destroy_process_group()
+print("OK", rank)
+"""
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tensor_parallel_products_on_two_gpus(tmp_path):
+    world = 2
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    procs = [subprocess.Popen([sys.executable, "-c", TP_WORKER, str(r), str(world), str(port),
+                               str(tmp_path)], cwd=REPO, env=ENV, stdout=subprocess.PIPE,
+                              stderr=subprocess.STDOUT, text=True) for r in range(world)]
+    outs = [p.communicate(timeout=300)[0] for p in procs]
+    for p, o in zip(procs, outs):
+        assert p.returncode == 0 and "OK" in o, o[-3000:]
+    import shard
+    rng = np.random.default_rng(31)
+    for (m, k, n) in [(1, 4096, 4096), (4, 11008, 4096), (8, 1024, 2048), (130, 512, 1024)]:
+        A = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+        q, s = oracle.quantize_q8((rng.standard_normal((k, n)) * 0.02).astype(np.float32))
+        C0 = rng.uniform(-1, 1, (m, n)).astype(np.float32)
+        full = oracle.matmul_naive_q8(A, q, s)
+        cols = np.concatenate([np.load(tmp_path / f"col_{m}_{r}.npy") for r in range(world)], axis=1)
+        assert close_to(cols, full, k), m
+        for r in range(world):
+            assert close_to(np.load(tmp_path / f"row_{m}_{r}.npy"), C0 + full, k, 2.0), (m, r)
