@@ -73,9 +73,9 @@ for (m, k, n) in [(1, 4096, 4096), (4, 11008, 4096), (8, 1024, 2048), (130, 512,
     # row-parallel with the residual add
     Ar, qr = shard.activation_columns(A, world, rank), shard.row_shard(q, world, rank)
     Cr = dev(C0)
-    comm.matmul_q8_rowpar(m, n, Ar.shape[1], dev(Ar).data_ptr(), dev(qr).data_ptr(),
-                          dev(s).data_ptr(), Cr.data_ptr(), accumulate=True,
-                          stream=L.torch_stream_handle())
+    dAr, dqr, ds = dev(Ar), dev(qr), dev(s)  # kept alive until the async product has run
+    comm.matmul_q8_rowpar(m, n, Ar.shape[1], dAr.data_ptr(), dqr.data_ptr(), ds.data_ptr(),
+                          Cr.data_ptr(), accumulate=True, stream=L.torch_stream_handle())
     torch.cuda.synchronize()
     np.save(f"{out}/col_{m}_{rank}.npy", Cc.cpu().numpy())
     np.save(f"{out}/row_{m}_{rank}.npy", Cr.cpu().numpy())
