@@ -37,7 +37,7 @@ __device__ unsigned int g_gemv_error;
 
 #ifdef LLME_GEMV_TRACE
 #define GEMV_TRACE(a, point) \
-    (a).trace[(static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x) * 8 + (point)] = global_timer_ns()
+    (a).trace[(static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x) * 16 + (point)] = global_timer_ns()
 #else
 #define GEMV_TRACE(a, point) ((void)0)
 #endif
@@ -147,6 +147,12 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 // Every thread of every CTA in the cluster; release/acquire orders shared-memory writes.
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+// The same rendezvous with no memory ordering: only "nobody leaves yet". A release arrive
+// would first wait for this CTA's global stores to be acknowledged (~1 us here).
+__device__ __forceinline__ void cluster_sync_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::
                      : "memory");
 }
 __device__ __forceinline__ float4 ld_dsmem_f4(const float* local, uint32_t rank) {
@@ -370,6 +376,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
     // second barrier keeps every CTA's shared memory alive until all reads are
     // done.
     cluster_sync();
+    if (tid == 0) GEMV_TRACE(a, 8);
     if (tid < kConsumers) {
         const uint32_t me = cluster_rank();
         constexpr int E4 = M * S::NT / 4;  // float4 chunks of the strip's sums
@@ -406,6 +413,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
             ss_all[tid] = v;
         }
         named_barrier(1, kConsumers);
+        if (tid == 0) GEMV_TRACE(a, 9);
         for (int e = 4 * e4_begin + tid; e < 4 * e4_end; e += kConsumers) {
             const int r = e / S::NT, col = col0 + e % S::NT;
             if (col >= a.n) continue;
@@ -415,9 +423,10 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
             float* o = a.C + static_cast<size_t>(r) * a.n + col;
             *o = a.accumulate ? *o + v : v;
         }
+        if (tid == 0) GEMV_TRACE(a, 10);
     }
     __syncwarp();
-    cluster_sync();
+    cluster_sync_relaxed();
     if (tid == 0) GEMV_TRACE(a, 7);
 }
 

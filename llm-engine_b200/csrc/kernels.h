@@ -44,9 +44,10 @@ struct GemvArgs {
     SplitScratch split;
     cudaStream_t stream = nullptr;
     bool pdl = false;               // launch with programmatic stream serialization
-    // Timeline tracing, used only when gemv.cu is compiled with LLME_GEMV_TRACE: 8 global
-    // timer stamps per CTA (entry, init, weights issued, activations issued, first data, loop
-    // done, CTA sums ready, end). Null and unused in normal builds.
+    // Timeline tracing, used only when gemv.cu is compiled with LLME_GEMV_TRACE: 16 global
+    // timer slots per CTA (entry, init, weights issued, activations issued, first data, loop
+    // done, CTA sums ready, end, then the cluster reduction's steps). Null and unused in
+    // normal builds.
     unsigned long long* trace = nullptr;
 };
 
