@@ -195,15 +195,22 @@ class Chain:
             self.mats.append((q, s, kl, nl, rowp))
         torch.cuda.synchronize()
         # Activations: a fresh U(-1, 1) row per product, the same on every rank (a row shard
-        # takes its slice of it); outputs one slot each.
+        # takes its slice of it). Outputs: one slot each, the row-parallel ones contiguous at
+        # the end so one all-reduce covers them all.
         import shard
-        self.a_off, self.c_off = [], []
+        self.a_off, self.c_off = [None] * len(self.mats), [None] * len(self.mats)
         a_tot = c_tot = 0
-        for (_, _, kl, nl, _) in self.mats:
-            self.a_off.append(a_tot)
-            self.c_off.append(c_tot)
+        for i, (_, _, kl, nl, _) in enumerate(self.mats):
+            self.a_off[i] = a_tot
             a_tot += (kl + 3) // 4 * 4   # keep every vector 16-byte aligned
-            c_tot += (nl + 3) // 4 * 4
+        for rowp_pass in (False, True):
+            if rowp_pass:
+                self.rp_off = c_tot
+            for i, (_, _, kl, nl, rowp) in enumerate(self.mats):
+                if rowp == rowp_pass:
+                    self.c_off[i] = c_tot
+                    c_tot += (nl + 3) // 4 * 4
+        self.rp_count = c_tot - self.rp_off
         ga = torch.Generator(device="cpu")
         ga.manual_seed(seed * 7)
         a_host = torch.empty(a_tot)
@@ -219,6 +226,22 @@ class Chain:
         self.bytes_per_step = sum(algorithmic_bytes(kl, nl) for (_, _, kl, nl, _) in self.mats) \
             * 1  # this rank's share
         self.total_bytes = sum(algorithmic_bytes(k, n) for (_, k, n, _) in self.shapes)
+
+    def make_batch(self):
+        """All products of the step as one grouped launch (they are independent)."""
+        import llme_b200 as L
+        prods = []
+        for i, (q, s, kl, nl, rowp) in enumerate(self.mats):
+            prods.append((nl, kl, self.a_dev.data_ptr() + 4 * self.a_off[i], q.data_ptr(),
+                          s.data_ptr(), self.c_dev.data_ptr() + 4 * self.c_off[i], 0))
+        self.batch = L.Batch(1, prods)
+
+    def launch_grouped(self, stream_handle, tp=None):
+        import llme_b200 as L
+        self.batch.run(L.FLAG_WEIGHTS_STATIC, stream_handle)
+        if tp is not None and self.rp_count:
+            tp.allreduce_sum_f32(self.c_dev.data_ptr() + 4 * self.rp_off, self.rp_count,
+                                 stream_handle)
 
     def launch_all(self, stream_handle, comm=None, join=None):
         import llme_b200 as L
@@ -438,17 +461,32 @@ def run_ours(args):
             comm_stream.wait_stream(torch.cuda.current_stream())
             tp.allreduce_sum_f32(c_ptr, n, comm_stream.cuda_stream)
     join = (lambda: torch.cuda.current_stream().wait_stream(comm_stream)) if world > 1 else None
-    graph = capture(lambda: chain.launch_all(h, comm, join), stream)
+    grouped = args.launch == "grouped"
+    if grouped:
+        chain.make_batch()
+        step_fn = lambda: chain.launch_grouped(h, tp)  # noqa: E731
+    else:
+        step_fn = lambda: chain.launch_all(h, comm, join)  # noqa: E731
+    graph = capture(step_fn, stream)
     sampler = ClockSampler(local)
     secs = time_graph(graph, args.steps, args.warmup, stream, world, sampler)
     secs = max_over_ranks(secs, world)
     value = chain.total_bytes * args.steps / secs / 1e9
     ms_per_step = secs / args.steps * 1e3
+    # The same step as one C-ABI call per product (the reference's call pattern), for comparison.
+    per_call = None
+    if grouped:
+        pc_graph = capture(lambda: chain.launch_all(h, comm, join), stream)
+        pc_secs = max_over_ranks(time_graph(pc_graph, args.steps, args.warmup, stream, world), world)
+        per_call = {"value": round(chain.total_bytes * args.steps / pc_secs / 1e9, 1),
+                    "unit": UNIT, "ms_per_step": round(pc_secs / args.steps * 1e3, 4),
+                    "launches_per_step": chain.n_launches()}
+        del pc_graph
 
-    # e2e: the same chain through the C ABI with host buffers, copies in the timed region.
+    # e2e: the same step through the C ABI with host buffers, copies in the timed region.
     def e2e_fn():
         chain.a_dev.copy_(chain.a_host, non_blocking=True)
-        chain.launch_all(h, comm, join)
+        step_fn()
         chain.c_host.copy_(chain.c_dev, non_blocking=True)
     e2e_graph = capture(e2e_fn, stream)
     e2e_secs = max_over_ranks(time_graph(e2e_graph, args.steps, args.warmup, stream, world), world)
@@ -458,14 +496,14 @@ def run_ours(args):
            "ms_per_step": round(e2e_secs / args.steps * 1e3, 4)}
 
     peak, peak_kind = peaks()
-    launches = chain.n_launches()
+    launches = 1 if grouped else chain.n_launches()
     per_launch_bytes = chain.bytes_per_step / launches
     per_launch_s = (secs / args.steps) / launches
     achieved = per_launch_bytes / per_launch_s / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                "kernel": "gemv_tma_kernel<1,int8>",
-                "traffic": None}
+                "kernel": "gemv_batch_kernel<1> (int8)" if grouped else "gemv_tma_kernel<1,int8>",
+                "bytes_per_launch": int(per_launch_bytes), "traffic": None}
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
@@ -477,8 +515,11 @@ def run_ours(args):
                    "products_per_step": launches,
                    "algorithmic_bytes_per_step": int(chain.total_bytes),
                    "parallelism": f"tp{world}" if world > 1 else "single",
-                   "launch": "one CUDA graph per step, programmatic dependent launch"},
+                   "launch": ("one grouped launch of all products per step (llme_batch_run; the "
+                              "products are independent), in a CUDA graph with PDL") if grouped
+                             else "one C-ABI call per product, one CUDA graph per step, PDL"},
         "roofline": roofline, "e2e": e2e, "gpu_launches": launches * args.steps,
+        "per_call": per_call,
         "clocks": sampler.summary(),
     }
     if rank == 0 and world == 1 and not args.no_extras and args.workload == "chain":
@@ -491,6 +532,8 @@ def run_ours(args):
     # Graphs holding NCCL calls go first, then the communicator, then the process group.
     del graph, e2e_graph
     torch.cuda.synchronize()
+    if grouped:
+        chain.batch.destroy()
     if tp is not None:
         tp.destroy()
     if world > 1:
@@ -561,6 +604,9 @@ def main():
                     help="chain: BASELINE configs[3] (default); gemv: configs[0] alone; "
                          "sgemm: configs[2] (square TF32 GEMM, --size)")
     ap.add_argument("--size", type=int, default=8192, help="N for --workload sgemm")
+    ap.add_argument("--launch", choices=["grouped", "per_call"], default="grouped",
+                    help="grouped: one llme_batch_run per step (default); per_call: one "
+                         "llme_matmul_q8 per product (also reported as per_call)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the isolated 4096^2 GEMV probe and the CPU baseline")
     args = ap.parse_args()

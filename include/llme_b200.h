@@ -141,6 +141,34 @@ int llme_free(void* ptr);                      /* cudaFree; NULL is fine */
 int llme_copy_to_device(void* dst, const void* src, size_t bytes);   /* waits */
 int llme_copy_to_host(void* dst, const void* src, size_t bytes);     /* waits */
 
+/* ---- grouped products ------------------------------------------------------------------------ *
+ * Many independent int8 products of the same m (1..8) in ONE persistent launch. The reference
+ * issues one matmul_cuda per projection; products that do not read each other's outputs (a
+ * decode layer's q/k/v, w1/w3, or the benchmark's chain of fresh activations) can instead be
+ * grouped: every CTA walks a list of (product, 128-column strip) units over the product's whole
+ * k, streaming weights by TMA without a pause between products, and writes C directly (no
+ * cross-CTA reduction). Requirements per product: n % 16 == 0, k % 4 == 0, A and B 16-byte
+ * aligned, no product's C overlapping another product's A. */
+typedef struct {
+    size_t n, k;          /* B is k x n int8, C is m x n */
+    const float* A;       /* m x k */
+    const int8_t* B;
+    const float* scale;   /* n */
+    float* C;
+    int accumulate;       /* C += instead of C = */
+} llme_q8_product;
+typedef struct llme_batch llme_batch_t;
+
+/* Validates the products and uploads their descriptors (TMA maps, a unit table) to device
+ * memory once; the pointers are captured, so the buffers must stay valid while the batch
+ * lives. Allocates (cudaMalloc) -- call before capturing graphs. */
+int llme_batch_q8_create(llme_batch_t** batch, size_t m, size_t count,
+                         const llme_q8_product* products);
+/* Runs every product of the batch in one launch on `stream` (no allocation; capturable).
+ * flags: LLME_FLAG_WEIGHTS_STATIC as for llme_matmul_q8. */
+int llme_batch_run(llme_batch_t* batch, unsigned flags, void* stream);
+int llme_batch_destroy(llme_batch_t* batch);
+
 /* ---- multi-GPU: tensor-parallel products over NCCL --------------------------------------- *
  * One process per GPU. The reference has no multi-GPU code (single CudaTransformer); these
  * entry points are additive. Column-parallel weights (wq, wk, wv, w1, w3, classifier) need no

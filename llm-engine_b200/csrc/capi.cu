@@ -13,6 +13,7 @@
 #include <mutex>
 #include <string>
 #include <unordered_map>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -313,6 +314,11 @@ struct MapKeyHash {
 std::mutex g_map_mu;
 std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 
+// Encodes without the cache (rank 2, or rank 1 when rows == 0).
+int encode_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t rows, uint64_t cols,
+               uint32_t box_cols, uint32_t box_rows, CUtensorMap* out,
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
+
 // Row-major matrix of `rows` x `cols` elements (rank 2), or a vector (rows == 0, rank 1),
 // tiled into boxes of box_cols x box_rows.
 int tensor_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t rows, uint64_t cols,
@@ -338,6 +344,26 @@ int tensor_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t 
             return LLME_OK;
         }
     }
+    const int st = encode_map(ptr, dtype, esz, rows, cols, box_cols, box_rows, out, swizzle);
+    if (st) return st;
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    if (g_maps.size() > 8192) g_maps.clear();
+    g_maps.emplace(key, *out);
+    return LLME_OK;
+}
+
+int encode_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t rows, uint64_t cols,
+               uint32_t box_cols, uint32_t box_rows, CUtensorMap* out, CUtensorMapSwizzle swizzle) {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                             &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!g_encode) return fail(LLME_E_UNSUPPORTED, "cuda: cuTensorMapEncodeTiled is unavailable");
+    const int rank = rows ? 2 : 1;
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {cols * esz};
     cuuint32_t box[2] = {box_cols, box_rows};
@@ -347,9 +373,6 @@ int tensor_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t 
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return fail(LLME_E_CUDA, "cuda: encode tensor map: CUresult " + std::to_string(int(r)));
-    std::lock_guard<std::mutex> lk(g_map_mu);
-    if (g_maps.size() > 8192) g_maps.clear();
-    g_maps.emplace(key, *out);
     return LLME_OK;
 }
 
@@ -578,6 +601,92 @@ int run_noalloc(size_t m, size_t n, size_t k, const float* A, const int8_t* B, c
 
 }  // namespace
 
+struct llme_batch {
+    int dev = 0;
+    void* dmem = nullptr;
+    llme::BatchArgs args;
+};
+
+namespace {
+
+int batch_create(llme_batch_t** out, size_t m, size_t count, const llme_q8_product* p) {
+    g_error.clear();
+    *out = nullptr;
+    if (m < 1 || m > 8)
+        return fail(LLME_E_INVALID, "llme_batch_q8_create: m must be 1..8, got " + std::to_string(m));
+    if (count < 1 || count > 65535)
+        return fail(LLME_E_INVALID, "llme_batch_q8_create: 1..65535 products, got " +
+                                        std::to_string(count));
+    std::vector<BatchItem> items(count);
+    std::vector<CUtensorMap> mb(count), ma(count);
+    std::vector<unsigned> table;
+    for (size_t i = 0; i < count; ++i) {
+        const llme_q8_product& q = p[i];
+        const std::string where = "llme_batch_q8_create: product " + std::to_string(i) + " " +
+                                  shapes(m, q.n, q.k);
+        if (q.n == 0 || q.k == 0 || q.n % 16 || q.k % 4)
+            return fail(LLME_E_INVALID, where + ": needs n % 16 == 0, k % 4 == 0, both nonzero");
+        if (m * q.k >= kMaxElems || q.k * q.n >= kMaxElems || m * q.n >= kMaxElems)
+            return fail(LLME_E_INVALID, where + ": more than 2^31 elements");
+        if (reinterpret_cast<uintptr_t>(q.A) % 16 || reinterpret_cast<uintptr_t>(q.B) % 16)
+            return fail(LLME_E_INVALID, where + ": A and B must be 16-byte aligned");
+        const size_t strips = ceil_div(q.n, gemv_tma_cols(true));
+        if (strips > 65535) return fail(LLME_E_INVALID, where + ": too many columns");
+        items[i] = BatchItem{q.A, q.C, q.scale, static_cast<int>(q.n), static_cast<int>(q.k),
+                             q.accumulate ? 1 : 0, 0};
+        int st = encode_map(q.B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q.k, q.n, kGemvRowBytes,
+                            kGemvBoxRows, &mb[i]);
+        if (st) return st;
+        st = encode_map(q.A, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, q.k, kGemvBoxRows,
+                        static_cast<uint32_t>(m), &ma[i]);
+        if (st) return st;
+        for (size_t sidx = 0; sidx < strips; ++sidx)
+            table.push_back(static_cast<unsigned>(i << 16 | sidx));
+    }
+    int dev = 0, sms = 0;
+    int st = current_device(&dev);
+    if (st) return st;
+    st = device_sms(dev, &sms);
+    if (st) return st;
+    // [maps B][maps A][items][unit table], each part 128-byte aligned.
+    const size_t maps_bytes = count * sizeof(CUtensorMap);
+    const size_t items_off = 2 * maps_bytes;
+    const size_t table_off = round_up(items_off + count * sizeof(BatchItem), 128);
+    const size_t bytes = table_off + table.size() * sizeof(unsigned);
+    auto* b = new llme_batch;
+    b->dev = dev;
+    cudaError_t e = cudaMalloc(&b->dmem, bytes);
+    if (e != cudaSuccess) {
+        delete b;
+        return cuda_fail(e, "alloc batch");
+    }
+    char* base = static_cast<char*>(b->dmem);
+    e = cudaMemcpy(base, mb.data(), maps_bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(base + maps_bytes, ma.data(), maps_bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(base + items_off, items.data(), count * sizeof(BatchItem), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(base + table_off, table.data(), table.size() * sizeof(unsigned),
+                       cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(b->dmem);
+        delete b;
+        return cuda_fail(e, "upload batch");
+    }
+    BatchArgs& a = b->args;
+    a.m = static_cast<int>(m);
+    a.units = static_cast<int>(table.size());
+    a.tmB = reinterpret_cast<const CUtensorMap*>(base);
+    a.tmA = reinterpret_cast<const CUtensorMap*>(base + maps_bytes);
+    a.items = reinterpret_cast<const BatchItem*>(base + items_off);
+    a.unit_table = reinterpret_cast<const unsigned*>(base + table_off);
+    a.grid = std::min(a.units, gemv_batch_ctas_per_sm() * sms);
+    *out = b;
+    return LLME_OK;
+}
+
+}  // namespace
+
 namespace llme {
 int set_error(int code, const std::string& msg) { return fail(code, msg); }
 int set_cuda_error(cudaError_t e, const char* what) { return cuda_fail(e, what); }
@@ -593,6 +702,32 @@ extern "C" {
 int llme_matmul_q8_noalloc(size_t m, size_t n, size_t k, const float* A, const int8_t* B,
                            const float* scale, float* C, int accumulate, void* stream) {
     return run_noalloc(m, n, k, A, B, scale, C, accumulate != 0, stream);
+}
+
+int llme_batch_q8_create(llme_batch_t** batch, size_t m, size_t count,
+                         const llme_q8_product* products) {
+    return batch_create(batch, m, count, products);
+}
+
+int llme_batch_run(llme_batch_t* b, unsigned flags, void* stream) {
+    g_error.clear();
+    if (!b) return fail(LLME_E_INVALID, "llme_batch_run: null batch");
+    int dev = 0;
+    int st = current_device(&dev);
+    if (st) return st;
+    if (dev != b->dev) return fail(LLME_E_INVALID, "llme_batch_run: batch belongs to another device");
+    BatchArgs a = b->args;
+    a.stream = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
+    a.pdl = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
+    cudaError_t e = launch_gemv_batch(a);
+    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "launch");
+}
+
+int llme_batch_destroy(llme_batch_t* b) {
+    if (!b) return LLME_OK;
+    cudaError_t e = cudaFree(b->dmem);
+    delete b;
+    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "free batch");
 }
 
 

@@ -543,6 +543,190 @@ __global__ void __launch_bounds__(kConsumers) gemv_ldg_kernel(const GemvArgs a) 
     finish_strip<M, NT, Q8, Norm>(tot, tot_ss, a, strip, slice, tid, &flag, red, red_ss);
 }
 
+// ---- grouped GEMV: independent products in one persistent launch ---------------------------
+//
+// Every CTA walks its list of (product, 128-column strip) units over the whole k of each
+// product, so there is no cross-CTA reduction at all; its producer thread streams the boxes of
+// one unit after another through the same ring, so the ring never drains between products
+// (the per-call kernel pays launch, griddepcontrol release and a cluster rendezvous per
+// product). The reduction buffers therefore get their own shared memory. Used for products
+// that do not read each other's outputs (a decode layer's independent projections; the
+// benchmark's chain of fresh activations).
+template <int M>
+struct BatchLayout {
+    using S = Shape<M, true>;
+    static constexpr int kB = kStages * kBoxBytesB;
+    static constexpr int kABox = M * kGemvBoxRows * 4;
+    static constexpr int kOffA = kB;
+    static constexpr int kOffRed = kOffA + kStages * kABox;
+    static constexpr int kRedFloats = kConsumerWarps * M * S::NT;
+    static constexpr int kOffTot = kOffRed + kRedFloats * 4;
+    static constexpr int kOffBar = kOffTot + M * S::NT * 4;
+    static constexpr int kBytes = kOffBar + 2 * kStages * 8 + 16;
+    static constexpr uint32_t kTx = kBoxBytesB + kABox;
+};
+
+template <int M>
+__global__ void __launch_bounds__(kTmaThreads, 2) gemv_batch_kernel(const BatchArgs a) {
+    using S = Shape<M, true>;
+    using L = BatchLayout<M>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+    uint64_t* empty = full + kStages;
+    float* red = reinterpret_cast<float*>(smem + L::kOffRed);
+    float* tot = reinterpret_cast<float*>(smem + L::kOffTot);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = gridDim.x;
+
+    if (tid == kConsumers) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) pdl_launch_dependents();
+
+    if (warp == kConsumerWarps) {
+        if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
+            // Box cursor over this CTA's units; the first kStages weight boxes are requested
+            // before griddepcontrol.wait, their activation boxes after it.
+            int u = blockIdx.x, item = 0, strip = 0, j = 0, nb = 0;
+            auto load_unit = [&]() {
+                const unsigned code = __ldg(a.unit_table + u);
+                item = static_cast<int>(code >> 16);
+                strip = static_cast<int>(code & 0xFFFFu);
+                nb = (__ldg(&a.items[item].k) + kGemvBoxRows - 1) / kGemvBoxRows;
+                j = 0;
+            };
+            if (u < a.units) load_unit();
+            int pend_item[kStages], pend_j[kStages];
+            int b = 0;
+            bool waited = false;
+            while (u < a.units) {
+                const int s = b % kStages;
+                if (b >= kStages) {
+                    if (!waited) {
+                        pdl_wait();
+                        for (int t = 0; t < kStages; ++t)
+                            tma_load_2d_nohint(smem + L::kOffA + t * L::kABox, &a.tmA[pend_item[t]],
+                                               pend_j[t] * kGemvBoxRows, 0, &full[t]);
+                        waited = true;
+                    }
+                    if (!mbar_wait(&empty[s], ((b / kStages) - 1) & 1, &g_gemv_error)) break;
+                }
+                mbar_arrive_expect_tx(&full[s], L::kTx);
+                tma_load_2d(smem + s * kBoxBytesB, &a.tmB[item], strip * S::NT, j * kGemvBoxRows,
+                            &full[s], pol);
+                if (waited) {
+                    tma_load_2d_nohint(smem + L::kOffA + s * L::kABox, &a.tmA[item],
+                                       j * kGemvBoxRows, 0, &full[s]);
+                } else {
+                    pend_item[s] = item;
+                    pend_j[s] = j;
+                }
+                ++b;
+                if (++j == nb) {
+                    u += G;
+                    if (u < a.units) load_unit();
+                }
+            }
+            if (!waited) {  // fewer boxes than stages in total
+                pdl_wait();
+                for (int t = 0; t < min(b, kStages); ++t)
+                    tma_load_2d_nohint(smem + L::kOffA + t * L::kABox, &a.tmA[pend_item[t]],
+                                       pend_j[t] * kGemvBoxRows, 0, &full[t]);
+            }
+        }
+        return;
+    }
+
+    pdl_wait();
+    const int cg = tid % S::TPR, rg = tid / S::TPR;
+    int b = 0;
+    for (int u = blockIdx.x; u < a.units; u += G) {
+        const unsigned code = __ldg(a.unit_table + u);
+        const int item = static_cast<int>(code >> 16), strip = static_cast<int>(code & 0xFFFFu);
+        const BatchItem it = a.items[item];
+        const int col0 = strip * S::NT;
+        const int nb = (it.k + kGemvBoxRows - 1) / kGemvBoxRows;
+        // This thread's output column (the same for all M rows) and its scale, fetched now so
+        // the store at the end of the unit does not wait on memory.
+        const int my_col = col0 + tid % S::NT;
+        const float sc = my_col < it.n ? __ldg(it.scale + my_col) : 0.0f;
+        uint64_t acc[M][S::V / 2];
+#pragma unroll
+        for (int r = 0; r < M; ++r)
+#pragma unroll
+            for (int jj = 0; jj < S::V / 2; ++jj) acc[r][jj] = 0ull;
+        bool ok = true;
+        for (int j = 0; j < nb; ++j, ++b) {
+            const int s = b % kStages;
+            if (!mbar_wait(&full[s], (b / kStages) & 1, &g_gemv_error)) {
+                ok = false;
+                break;
+            }
+            const uint8_t* sb = smem + s * kBoxBytesB + cg * S::V;
+            const float* sa = reinterpret_cast<const float*>(smem + L::kOffA + s * L::kABox);
+#pragma unroll
+            for (int i = 0; i < S::RPT; ++i) {
+                const int row = rg + i * S::RG;
+                uint64_t x[S::V / 2];
+                load_pairs<true, S::V>(sb + row * kGemvRowBytes, x);
+#pragma unroll
+                for (int r = 0; r < M; ++r) {
+                    const float av = sa[r * kGemvBoxRows + row];
+                    const uint64_t a2 = pack2(av, av);
+#pragma unroll
+                    for (int jj = 0; jj < S::V / 2; ++jj) acc[r][jj] = fma2(a2, x[jj], acc[r][jj]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        if (!ok) break;
+        // Reduce the row groups (shuffle, then the 8 warps in order) and store.
+        float accf[M][S::V];
+#pragma unroll
+        for (int r = 0; r < M; ++r)
+#pragma unroll
+            for (int jj = 0; jj < S::V / 2; ++jj) unpack2(acc[r][jj], accf[r][2 * jj], accf[r][2 * jj + 1]);
+#pragma unroll
+        for (int off = S::TPR; off < 32; off <<= 1) {
+#pragma unroll
+            for (int r = 0; r < M; ++r)
+#pragma unroll
+                for (int jj = 0; jj < S::V; ++jj)
+                    accf[r][jj] += __shfl_xor_sync(0xffffffffu, accf[r][jj], off);
+        }
+        if (lane < S::TPR) {
+#pragma unroll
+            for (int r = 0; r < M; ++r) {
+                float4* dst = reinterpret_cast<float4*>(red + (warp * M + r) * S::NT + cg * S::V);
+#pragma unroll
+                for (int jj = 0; jj < S::V / 4; ++jj)
+                    dst[jj] = make_float4(accf[r][4 * jj], accf[r][4 * jj + 1], accf[r][4 * jj + 2],
+                                          accf[r][4 * jj + 3]);
+            }
+        }
+        named_barrier(1, kConsumers);
+        for (int e = tid; e < M * S::NT; e += kConsumers) {
+            float v = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) v += red[w * M * S::NT + e];
+            const int r = e / S::NT, col = col0 + e % S::NT;
+            if (col < it.n) {
+                v *= sc;
+                float* o = it.C + static_cast<size_t>(r) * it.n + col;
+                *o = it.accumulate ? *o + v : v;
+            }
+        }
+        named_barrier(1, kConsumers);  // red is rewritten by the next unit
+    }
+}
+
 cudaLaunchConfig_t make_config(dim3 grid, int threads, size_t smem, cudaStream_t stream, bool pdl,
                                cudaLaunchAttribute* attr) {
     cudaLaunchConfig_t cfg = {};
@@ -629,7 +813,41 @@ cudaError_t launch_ldg_rows(const GemvArgs& a) {
     }
 }
 
+template <int M>
+cudaError_t launch_batch_m(const BatchArgs& a) {
+    using L = BatchLayout<M>;
+    auto kern = gemv_batch_kernel<M>;
+    static unsigned configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 32 && !(configured & (1u << dev))) {
+        cudaError_t e =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+        if (e != cudaSuccess) return e;
+        configured |= 1u << dev;
+    }
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = make_config(dim3(a.grid), kTmaThreads, L::kBytes, a.stream, a.pdl, attr);
+    return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
 }  // namespace
+
+int gemv_batch_ctas_per_sm() { return 2; }
+
+cudaError_t launch_gemv_batch(const BatchArgs& a) {
+    switch (a.m) {
+        case 1: return launch_batch_m<1>(a);
+        case 2: return launch_batch_m<2>(a);
+        case 3: return launch_batch_m<3>(a);
+        case 4: return launch_batch_m<4>(a);
+        case 5: return launch_batch_m<5>(a);
+        case 6: return launch_batch_m<6>(a);
+        case 7: return launch_batch_m<7>(a);
+        case 8: return launch_batch_m<8>(a);
+        default: return cudaErrorInvalidValue;
+    }
+}
 
 cudaError_t launch_gemv_tma(const GemvArgs& a, const CUtensorMap& tmB, const CUtensorMap& tmA,
                             const CUtensorMap& tmW) {

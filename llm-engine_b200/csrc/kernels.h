@@ -59,6 +59,32 @@ constexpr int kGemvMaxCluster = 8;
 inline int gemv_tma_cols(bool q8) { return q8 ? kGemvRowBytes : kGemvRowBytes / 4; }
 constexpr int kGemvLdgCols = 32;
 
+// Grouped GEMV: many independent int8 products of the same m (<= 8) in one persistent
+// launch. Work unit = (product, 128-column strip) over the product's whole k; CTA c takes
+// units c, c + grid, ... . Everything below lives in device memory, written once by
+// llme_batch_q8_create.
+struct BatchItem {
+    const float* A;      // m x k, 16-byte aligned, k % 4 == 0
+    float* C;            // m x n
+    const float* scale;  // n
+    int n, k;
+    int accumulate;
+    int pad;
+};
+struct BatchArgs {
+    int m = 0;
+    int units = 0;
+    const BatchItem* items = nullptr;
+    const CUtensorMap* tmB = nullptr;  // per product: B (k x n int8), box 128 x 128
+    const CUtensorMap* tmA = nullptr;  // per product: A (m x k fp32), box 128 x m
+    const unsigned* unit_table = nullptr;  // unit -> (product << 16) | strip
+    int grid = 0;
+    cudaStream_t stream = nullptr;
+    bool pdl = false;
+};
+cudaError_t launch_gemv_batch(const BatchArgs& a);
+int gemv_batch_ctas_per_sm();
+
 // TMA GEMV: B, A (and rms weight) read through the given tensor maps.
 cudaError_t launch_gemv_tma(const GemvArgs& a, const CUtensorMap& tmB, const CUtensorMap& tmA,
                             const CUtensorMap& tmW);

@@ -61,6 +61,13 @@ class Plan(ctypes.Structure):
         return d
 
 
+class Q8Product(ctypes.Structure):
+    """llme_q8_product: one product of a grouped launch (device pointers)."""
+    _fields_ = [("n", ctypes.c_size_t), ("k", ctypes.c_size_t), ("A", ctypes.c_void_p),
+                ("B", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("C", ctypes.c_void_p),
+                ("accumulate", ctypes.c_int)]
+
+
 _lib = None
 
 
@@ -84,6 +91,11 @@ def load() -> ctypes.CDLL:
     lib.llme_matmul_f32.restype = lib.llme_matmul_q8.restype = i
     lib.llme_matmul_q8_noalloc.argtypes = [sz, sz, sz, vp, vp, vp, vp, i, vp]
     lib.llme_matmul_q8_noalloc.restype = i
+    lib.llme_batch_q8_create.argtypes = [ctypes.POINTER(vp), sz, sz, ctypes.POINTER(Q8Product)]
+    lib.llme_batch_run.argtypes = [vp, u, vp]
+    lib.llme_batch_destroy.argtypes = [vp]
+    for f in ("llme_batch_q8_create", "llme_batch_run", "llme_batch_destroy"):
+        getattr(lib, f).restype = i
     lib.llme_comm_unique_id.argtypes = [ctypes.c_char_p]
     lib.llme_comm_init.argtypes = [ctypes.POINTER(vp), i, i, ctypes.c_char_p, ctypes.c_double]
     lib.llme_comm_destroy.argtypes = lib.llme_comm_abort.argtypes = [vp]
@@ -159,6 +171,26 @@ def matmul_cuda_q8_noalloc(m: int, n: int, k: int, A: int, B: int, scale: int, C
     device array inside the library, so the call never allocates device memory."""
     _check(load().llme_matmul_q8_noalloc(m, n, k, A, B, scale, C, int(bool(accumulate)),
                                          stream or None))
+
+
+class Batch:
+    """Independent int8 products of the same m run in one persistent launch
+    (llme_batch_q8_create / llme_batch_run). products: (n, k, A, B, scale, C, accumulate)
+    tuples of device pointers that stay valid for the batch's lifetime."""
+
+    def __init__(self, m: int, products):
+        arr = (Q8Product * len(products))(*[Q8Product(*p) for p in products])
+        h = ctypes.c_void_p()
+        _check(load().llme_batch_q8_create(ctypes.byref(h), m, len(products), arr))
+        self.handle = h.value
+
+    def run(self, flags: int = 0, stream: int | None = None) -> None:
+        _check(load().llme_batch_run(self.handle, flags, stream or None))
+
+    def destroy(self) -> None:
+        if self.handle:
+            h, self.handle = self.handle, None
+            _check(load().llme_batch_destroy(h))
 
 
 COMM_ID_BYTES = 128
