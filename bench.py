@@ -512,7 +512,7 @@ def run_ours(args):
         "exchange": ("NCCL sum all-reduce of wo/w2 partial outputs (library communicator, side "
                      "stream)") if world > 1 else None,
         "config": WORKLOAD_CONFIG[args.workload] | {
-                   "products_per_step": launches,
+                   "products_per_step": chain.n_launches(), "launches_per_step": launches,
                    "algorithmic_bytes_per_step": int(chain.total_bytes),
                    "parallelism": f"tp{world}" if world > 1 else "single",
                    "launch": ("one grouped launch of all products per step (llme_batch_run; the "
