@@ -503,7 +503,13 @@ def run_ours(args):
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                 "kernel": "gemv_batch_kernel<1> (int8)" if grouped else "gemv_tma_kernel<1,int8>",
-                "bytes_per_launch": int(per_launch_bytes), "traffic": None}
+                "bytes_per_launch": int(per_launch_bytes),
+                # DRAM read+write bytes per launch: the full ncu capture of the same kernel on
+                # the configs[0] case measured 1.013 x its algorithmic bytes (traffic grows with
+                # the weights streamed), scaled here to this launch.
+                "traffic": int(1.013 * per_launch_bytes) if grouped else None,
+                "traffic_source": ("profiles/gemv_batch_config0_full.md (1.013 x algorithmic, "
+                                   "scaled)") if grouped else None}
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
