@@ -228,20 +228,36 @@ class Chain:
         self.total_bytes = sum(algorithmic_bytes(k, n) for (_, k, n, _) in self.shapes)
 
     def make_batch(self):
-        """All products of the step as one grouped launch (they are independent)."""
+        """The step's products as grouped launches (they are independent): one batch on one
+        GPU; on several, the row-parallel products first (their partial outputs are summed
+        while the column-parallel batch runs) and the column-parallel ones second."""
         import llme_b200 as L
-        prods = []
+        prods = {False: [], True: []}
         for i, (q, s, kl, nl, rowp) in enumerate(self.mats):
-            prods.append((nl, kl, self.a_dev.data_ptr() + 4 * self.a_off[i], q.data_ptr(),
-                          s.data_ptr(), self.c_dev.data_ptr() + 4 * self.c_off[i], 0))
-        self.batch = L.Batch(1, prods)
+            prods[rowp and self.world > 1].append(
+                (nl, kl, self.a_dev.data_ptr() + 4 * self.a_off[i], q.data_ptr(), s.data_ptr(),
+                 self.c_dev.data_ptr() + 4 * self.c_off[i], 0))
+        self.batches = [L.Batch(1, prods[True])] if prods[True] else []
+        self.batches.append(L.Batch(1, prods[False]))
 
-    def launch_grouped(self, stream_handle, tp=None):
+    def launch_grouped(self, stream_handle, tp=None, comm_stream=None):
+        import torch
         import llme_b200 as L
-        self.batch.run(L.FLAG_WEIGHTS_STATIC, stream_handle)
-        if tp is not None and self.rp_count:
-            tp.allreduce_sum_f32(self.c_dev.data_ptr() + 4 * self.rp_off, self.rp_count,
-                                 stream_handle)
+        if tp is None or len(self.batches) == 1:
+            for b in self.batches:
+                b.run(L.FLAG_WEIGHTS_STATIC, stream_handle)
+            return
+        row, col = self.batches
+        row.run(L.FLAG_WEIGHTS_STATIC, stream_handle)
+        comm_stream.wait_stream(torch.cuda.current_stream())
+        tp.allreduce_sum_f32(self.c_dev.data_ptr() + 4 * self.rp_off, self.rp_count,
+                             comm_stream.cuda_stream)
+        col.run(L.FLAG_WEIGHTS_STATIC, stream_handle)
+        torch.cuda.current_stream().wait_stream(comm_stream)
+
+    def destroy_batches(self):
+        for b in getattr(self, "batches", []):
+            b.destroy()
 
     def launch_all(self, stream_handle, comm=None, join=None):
         import llme_b200 as L
@@ -464,7 +480,7 @@ def run_ours(args):
     grouped = args.launch == "grouped"
     if grouped:
         chain.make_batch()
-        step_fn = lambda: chain.launch_grouped(h, tp)  # noqa: E731
+        step_fn = lambda: chain.launch_grouped(h, tp, comm_stream if world > 1 else None)  # noqa: E731
     else:
         step_fn = lambda: chain.launch_all(h, comm, join)  # noqa: E731
     graph = capture(step_fn, stream)
@@ -496,7 +512,7 @@ def run_ours(args):
            "ms_per_step": round(e2e_secs / args.steps * 1e3, 4)}
 
     peak, peak_kind = peaks()
-    launches = 1 if grouped else chain.n_launches()
+    launches = len(chain.batches) if grouped else chain.n_launches()
     per_launch_bytes = chain.bytes_per_step / launches
     per_launch_s = (secs / args.steps) / launches
     achieved = per_launch_bytes / per_launch_s / 1e9
@@ -539,7 +555,7 @@ def run_ours(args):
     del graph, e2e_graph
     torch.cuda.synchronize()
     if grouped:
-        chain.batch.destroy()
+        chain.destroy_batches()
     if tp is not None:
         tp.destroy()
     if world > 1:

@@ -12,6 +12,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <queue>
 #include <unordered_map>
 #include <vector>
 
@@ -619,7 +620,8 @@ int batch_create(llme_batch_t** out, size_t m, size_t count, const llme_q8_produ
                                         std::to_string(count));
     std::vector<BatchItem> items(count);
     std::vector<CUtensorMap> mb(count), ma(count);
-    std::vector<unsigned> table;
+    std::vector<unsigned> units;
+    std::vector<size_t> unit_bytes;
     for (size_t i = 0; i < count; ++i) {
         const llme_q8_product& q = p[i];
         const std::string where = "llme_batch_q8_create: product " + std::to_string(i) + " " +
@@ -640,19 +642,51 @@ int batch_create(llme_batch_t** out, size_t m, size_t count, const llme_q8_produ
         st = encode_map(q.A, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, q.k, kGemvBoxRows,
                         static_cast<uint32_t>(m), &ma[i]);
         if (st) return st;
-        for (size_t sidx = 0; sidx < strips; ++sidx)
-            table.push_back(static_cast<unsigned>(i << 16 | sidx));
+        for (size_t sidx = 0; sidx < strips; ++sidx) {
+            units.push_back(static_cast<unsigned>(i << 16 | sidx));
+            // Work of a unit: its weight bytes plus a fixed cost for the per-unit reduction.
+            unit_bytes.push_back(q.k * static_cast<size_t>(gemv_tma_cols(true)) + 16384);
+        }
     }
     int dev = 0, sms = 0;
     int st = current_device(&dev);
     if (st) return st;
     st = device_sms(dev, &sms);
     if (st) return st;
+    // Longest-processing-time-first: units by decreasing work, each to the CTA with the least
+    // work so far (ties to the lower index). Deterministic, and within a few percent of the
+    // best possible makespan; each CTA then runs its units in their original order.
+    const int grid = static_cast<int>(std::min<size_t>(units.size(), gemv_batch_ctas_per_sm() * sms));
+    std::vector<size_t> order(units.size());
+    for (size_t u = 0; u < order.size(); ++u) order[u] = u;
+    std::stable_sort(order.begin(), order.end(),
+                     [&](size_t x, size_t y) { return unit_bytes[x] > unit_bytes[y]; });
+    std::vector<std::vector<size_t>> per_cta(grid);
+    {
+        using Load = std::pair<size_t, int>;  // (work, cta)
+        std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+        for (int c = 0; c < grid; ++c) heap.push({0, c});
+        for (size_t u : order) {
+            Load l = heap.top();
+            heap.pop();
+            per_cta[l.second].push_back(u);
+            heap.push({l.first + unit_bytes[u], l.second});
+        }
+    }
+    std::vector<unsigned> table;
+    std::vector<int> cta_begin(grid + 1, 0);
+    for (int c = 0; c < grid; ++c) {
+        std::sort(per_cta[c].begin(), per_cta[c].end());
+        cta_begin[c] = static_cast<int>(table.size());
+        for (size_t u : per_cta[c]) table.push_back(units[u]);
+    }
+    cta_begin[grid] = static_cast<int>(table.size());
     // [maps B][maps A][items][unit table], each part 128-byte aligned.
     const size_t maps_bytes = count * sizeof(CUtensorMap);
     const size_t items_off = 2 * maps_bytes;
     const size_t table_off = round_up(items_off + count * sizeof(BatchItem), 128);
-    const size_t bytes = table_off + table.size() * sizeof(unsigned);
+    const size_t begin_off = round_up(table_off + table.size() * sizeof(unsigned), 128);
+    const size_t bytes = begin_off + cta_begin.size() * sizeof(int);
     auto* b = new llme_batch;
     b->dev = dev;
     cudaError_t e = cudaMalloc(&b->dmem, bytes);
@@ -668,6 +702,9 @@ int batch_create(llme_batch_t** out, size_t m, size_t count, const llme_q8_produ
     if (e == cudaSuccess)
         e = cudaMemcpy(base + table_off, table.data(), table.size() * sizeof(unsigned),
                        cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(base + begin_off, cta_begin.data(), cta_begin.size() * sizeof(int),
+                       cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         cudaFree(b->dmem);
         delete b;
@@ -680,7 +717,8 @@ int batch_create(llme_batch_t** out, size_t m, size_t count, const llme_q8_produ
     a.tmA = reinterpret_cast<const CUtensorMap*>(base + maps_bytes);
     a.items = reinterpret_cast<const BatchItem*>(base + items_off);
     a.unit_table = reinterpret_cast<const unsigned*>(base + table_off);
-    a.grid = std::min(a.units, gemv_batch_ctas_per_sm() * sms);
+    a.cta_begin = reinterpret_cast<const int*>(base + begin_off);
+    a.grid = grid;
     *out = b;
     return LLME_OK;
 }

@@ -545,8 +545,9 @@ __global__ void __launch_bounds__(kConsumers) gemv_ldg_kernel(const GemvArgs a) 
 
 // ---- grouped GEMV: independent products in one persistent launch ---------------------------
 //
-// Every CTA walks its list of (product, 128-column strip) units over the whole k of each
-// product, so there is no cross-CTA reduction at all; its producer thread streams the boxes of
+// Every CTA walks its own list of (product, 128-column strip) units -- balanced by bytes
+// when the batch is created -- over the whole k of each product, so there is no cross-CTA
+// reduction at all; its producer thread streams the boxes of
 // one unit after another through the same ring, so the ring never drains between products
 // (the per-call kernel pays launch, griddepcontrol release and a cluster rendezvous per
 // product). The reduction buffers therefore get their own shared memory. Used for products
@@ -576,7 +577,6 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_batch_kernel(const BatchA
     float* red = reinterpret_cast<float*>(smem + L::kOffRed);
     float* tot = reinterpret_cast<float*>(smem + L::kOffTot);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int G = gridDim.x;
 
     if (tid == kConsumers) {
         for (int s = 0; s < kStages; ++s) {
@@ -593,7 +593,8 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_batch_kernel(const BatchA
             const uint64_t pol = l2_evict_first_policy();
             // Box cursor over this CTA's units; the first kStages weight boxes are requested
             // before griddepcontrol.wait, their activation boxes after it.
-            int u = blockIdx.x, item = 0, strip = 0, j = 0, nb = 0;
+            const int u_end = __ldg(a.cta_begin + blockIdx.x + 1);
+            int u = __ldg(a.cta_begin + blockIdx.x), item = 0, strip = 0, j = 0, nb = 0;
             auto load_unit = [&]() {
                 const unsigned code = __ldg(a.unit_table + u);
                 item = static_cast<int>(code >> 16);
@@ -601,11 +602,11 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_batch_kernel(const BatchA
                 nb = (__ldg(&a.items[item].k) + kGemvBoxRows - 1) / kGemvBoxRows;
                 j = 0;
             };
-            if (u < a.units) load_unit();
+            if (u < u_end) load_unit();
             int pend_item[kStages], pend_j[kStages];
             int b = 0;
             bool waited = false;
-            while (u < a.units) {
+            while (u < u_end) {
                 const int s = b % kStages;
                 if (b >= kStages) {
                     if (!waited) {
@@ -629,8 +630,8 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_batch_kernel(const BatchA
                 }
                 ++b;
                 if (++j == nb) {
-                    u += G;
-                    if (u < a.units) load_unit();
+                    ++u;
+                    if (u < u_end) load_unit();
                 }
             }
             if (!waited) {  // fewer boxes than stages in total
@@ -646,7 +647,8 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_batch_kernel(const BatchA
     pdl_wait();
     const int cg = tid % S::TPR, rg = tid / S::TPR;
     int b = 0;
-    for (int u = blockIdx.x; u < a.units; u += G) {
+    const int u_end = __ldg(a.cta_begin + blockIdx.x + 1);
+    for (int u = __ldg(a.cta_begin + blockIdx.x); u < u_end; ++u) {
         const unsigned code = __ldg(a.unit_table + u);
         const int item = static_cast<int>(code >> 16), strip = static_cast<int>(code & 0xFFFFu);
         const BatchItem it = a.items[item];

@@ -60,9 +60,9 @@ inline int gemv_tma_cols(bool q8) { return q8 ? kGemvRowBytes : kGemvRowBytes / 
 constexpr int kGemvLdgCols = 32;
 
 // Grouped GEMV: many independent int8 products of the same m (<= 8) in one persistent
-// launch. Work unit = (product, 128-column strip) over the product's whole k; CTA c takes
-// units c, c + grid, ... . Everything below lives in device memory, written once by
-// llme_batch_q8_create.
+// launch. Work unit = (product, 128-column strip) over the product's whole k; each CTA runs
+// its own list of units, balanced by bytes when the batch is created. Everything below lives
+// in device memory, written once by llme_batch_q8_create.
 struct BatchItem {
     const float* A;      // m x k, 16-byte aligned, k % 4 == 0
     float* C;            // m x n
@@ -77,7 +77,8 @@ struct BatchArgs {
     const BatchItem* items = nullptr;
     const CUtensorMap* tmB = nullptr;  // per product: B (k x n int8), box 128 x 128
     const CUtensorMap* tmA = nullptr;  // per product: A (m x k fp32), box 128 x m
-    const unsigned* unit_table = nullptr;  // unit -> (product << 16) | strip
+    const unsigned* unit_table = nullptr;  // units, grouped by CTA: (product << 16) | strip
+    const int* cta_begin = nullptr;        // CTA c runs unit_table[cta_begin[c], cta_begin[c+1])
     int grid = 0;
     cudaStream_t stream = nullptr;
     bool pdl = false;
