@@ -471,6 +471,8 @@ def run_ours(args):
         uid = [L.Comm.unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         tp = L.Comm(world, rank, uid[0], timeout_s=60.0)
+        if args.allreduce == "peer":
+            tp.enable_peer(chain.rp_count)  # the library's NVLink peer all-reduce
         comm_stream = torch.cuda.Stream()
 
         def comm(c_ptr, n):  # noqa: F811
@@ -531,8 +533,10 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: N(0,0.02^2) weights quantised per column to int8, U(-1,1) activations",
-        "exchange": ("NCCL sum all-reduce of wo/w2 partial outputs (library communicator, side "
-                     "stream)") if world > 1 else None,
+        "exchange": ((("one-shot all-reduce over NVLink peer memory (library kernel)"
+                       if args.allreduce == "peer" else "NCCL all-reduce (library communicator)")
+                      + " of the wo/w2 partial outputs, on a side stream overlapping the "
+                        "column-parallel products") if world > 1 else None),
         "config": WORKLOAD_CONFIG[args.workload] | {
                    "products_per_step": chain.n_launches(), "launches_per_step": launches,
                    "algorithmic_bytes_per_step": int(chain.total_bytes),
@@ -626,6 +630,8 @@ def main():
                     help="chain: BASELINE configs[3] (default); gemv: configs[0] alone; "
                          "sgemm: configs[2] (square TF32 GEMM, --size)")
     ap.add_argument("--size", type=int, default=8192, help="N for --workload sgemm")
+    ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
+                    help="N>1: the library's NVLink peer all-reduce (default) or NCCL")
     ap.add_argument("--launch", choices=["grouped", "per_call"], default="grouped",
                     help="grouped: one llme_batch_run per step (default); per_call: one "
                          "llme_matmul_q8 per product (also reported as per_call)")

@@ -193,6 +193,17 @@ int llme_comm_abort(llme_comm_t* comm);     /* from an error path: frees without
 int llme_comm_size(const llme_comm_t* comm);
 int llme_comm_rank(const llme_comm_t* comm);
 
+/* Switches llme_allreduce_sum_f32 (up to max_floats values) from NCCL to the library's own
+ * one-shot all-reduce over NVLink peer memory: a symmetric buffer per rank shared through CUDA
+ * IPC (handles exchanged once over this communicator; collective: every rank calls it), per-CTA
+ * arrival flags with bounded waits, and sums taken in rank order, so every rank gets the same
+ * bits. Plain peer loads and stores only. Call before capturing graphs. */
+int llme_comm_enable_peer(llme_comm_t* comm, size_t max_floats);
+
+/* Reads and clears the peer all-reduce's device error word: LLME_E_TIMEOUT if a peer did not
+ * arrive within the wait limit (its result is then not valid). */
+int llme_comm_status(void);
+
 /* In-place sum all-reduce of `count` fp32 values on `stream` (capturable in a CUDA graph). */
 int llme_allreduce_sum_f32(float* buf, size_t count, llme_comm_t* comm, void* stream);
 

@@ -15,14 +15,41 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <vector>
 
+#include "common.cuh"
 #include "kernels.h"
 #include "llme_b200.h"
+
+namespace {
+constexpr int kPeerMaxRanks = 16;
+constexpr int kPeerCtas = 32;
+constexpr int kPeerThreads = 256;
+
+// Device-side view of the peer all-reduce: every rank's symmetric buffer mapped into this
+// process (own included), laid out as [2 slots x max_floats floats][flags: kPeerCtas x
+// kPeerMaxRanks u32], plus this rank's per-CTA call counters.
+struct PeerArgs {
+    float* base[kPeerMaxRanks];
+    size_t slot_floats;
+    size_t flags_off;  // bytes from base to the flags
+    unsigned* epoch;   // kPeerCtas counters (local memory)
+    unsigned* err;     // device error word
+    int nranks, rank;
+};
+}  // namespace
 
 struct llme_comm {
     ncclComm_t comm = nullptr;
     int nranks = 0;
     int rank = 0;
+    // NVLink peer all-reduce (llme_comm_enable_peer)
+    bool peer = false;
+    size_t peer_max_floats = 0;
+    void* peer_buf = nullptr;
+    void* peer_epoch = nullptr;
+    void* peer_opened[kPeerMaxRanks] = {};
+    PeerArgs pargs{};
 };
 
 namespace {
@@ -34,6 +61,7 @@ struct NcclApi {
     decltype(&ncclCommAbort) abort = nullptr;
     decltype(&ncclCommGetAsyncError) asyncError = nullptr;
     decltype(&ncclAllReduce) allReduce = nullptr;
+    decltype(&ncclAllGather) allGather = nullptr;
     decltype(&ncclGetErrorString) errorString = nullptr;
     bool ok = false;
     std::string why;
@@ -58,9 +86,10 @@ NcclApi& nccl() {
         api.abort = reinterpret_cast<decltype(api.abort)>(sym("ncclCommAbort"));
         api.asyncError = reinterpret_cast<decltype(api.asyncError)>(sym("ncclCommGetAsyncError"));
         api.allReduce = reinterpret_cast<decltype(api.allReduce)>(sym("ncclAllReduce"));
+        api.allGather = reinterpret_cast<decltype(api.allGather)>(sym("ncclAllGather"));
         api.errorString = reinterpret_cast<decltype(api.errorString)>(sym("ncclGetErrorString"));
         api.ok = api.getUniqueId && api.initRankConfig && api.destroy && api.abort &&
-                 api.asyncError && api.allReduce && api.errorString;
+                 api.asyncError && api.allReduce && api.allGather && api.errorString;
         if (!api.ok) api.why = "libnccl.so.2 lacks a needed symbol";
     });
     return api;
@@ -97,6 +126,68 @@ int wait_ready(llme_comm* c, double timeout_s, const char* what) {
 
 // Enqueue-side waits of a non-blocking communicator (the GPU work itself stays async).
 constexpr double kEnqueueTimeoutS = 60.0;
+
+__device__ unsigned int g_comm_error;
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// One-shot all-reduce over NVLink peer memory, in place on `data` (count floats, identical
+// on every rank). CTA b owns elements [b*chunk, (b+1)*chunk): it copies them into slot
+// (epoch & 1) of this rank's symmetric buffer, raises its flag on every rank, waits (bounded)
+// for the same CTA of every rank to do the same, then sums the slots of ranks 0..n-1 in that
+// order -- so every rank gets the same bits. Two slots and monotonic per-CTA epochs make
+// back-to-back calls (and CUDA-graph replays) safe: a rank can only reuse a slot after every
+// peer has started the following call, i.e. finished reading it.
+__global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(float* __restrict__ data,
+                                                                        size_t count,
+                                                                        const PeerArgs p) {
+    __shared__ unsigned s_epoch;
+    __shared__ int s_ok;
+    const int b = blockIdx.x, tid = threadIdx.x;
+    if (tid == 0) {
+        s_epoch = p.epoch[b] + 1;
+        p.epoch[b] = s_epoch;
+        s_ok = 1;
+    }
+    __syncthreads();
+    const unsigned e = s_epoch;
+    const size_t chunk = ((count + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
+    const size_t lo = min(count, b * chunk), hi = min(count, lo + chunk);
+    const size_t slot = (e & 1u) * p.slot_floats;
+    float* mine = p.base[p.rank] + slot;
+    for (size_t i = lo + tid; i < hi; i += kPeerThreads) mine[i] = data[i];
+    __threadfence_system();
+    __syncthreads();
+    if (tid < p.nranks) {
+        unsigned* flags = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(p.base[tid]) + p.flags_off);
+        st_release_sys(flags + b * kPeerMaxRanks + p.rank, e);
+        const unsigned* my_flags =
+            reinterpret_cast<const unsigned*>(reinterpret_cast<char*>(p.base[p.rank]) + p.flags_off);
+        const unsigned* f = my_flags + b * kPeerMaxRanks + tid;
+        const unsigned long long t0 = llme::global_timer_ns();
+        for (uint32_t i = 0; ld_acquire_sys(f) < e; ++i) {
+            if ((i & 255) == 255 && llme::global_timer_ns() - t0 > llme::kWaitLimitNs) {
+                atomicExch(p.err, static_cast<unsigned>(LLME_E_TIMEOUT));
+                s_ok = 0;
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    for (size_t i = lo + tid; i < hi; i += kPeerThreads) {
+        float v = 0.0f;
+        for (int r = 0; r < p.nranks; ++r) v += __ldcg(p.base[r] + slot + i);
+        data[i] = v;
+    }
+}
 
 }  // namespace
 
@@ -143,8 +234,102 @@ int llme_comm_init(llme_comm_t** out, int nranks, int rank, const void* id, doub
     return LLME_OK;
 }
 
+static void peer_release(llme_comm* c) {
+    for (int r = 0; r < kPeerMaxRanks; ++r)
+        if (c->peer_opened[r]) cudaIpcCloseMemHandle(c->peer_opened[r]);
+    if (c->peer_buf) cudaFree(c->peer_buf);
+    if (c->peer_epoch) cudaFree(c->peer_epoch);
+    c->peer = false;
+}
+
+int llme_comm_enable_peer(llme_comm_t* c, size_t max_floats) {
+    if (!c) return llme::set_error(LLME_E_INVALID, "llme_comm_enable_peer: no communicator");
+    if (c->peer) return LLME_OK;
+    if (c->nranks > kPeerMaxRanks)
+        return llme::set_error(LLME_E_UNSUPPORTED, "llme_comm_enable_peer: more than 16 ranks");
+    const size_t slot = (max_floats + 63) / 64 * 64;
+    const size_t flags_off = 2 * slot * sizeof(float);
+    const size_t bytes = flags_off + kPeerCtas * kPeerMaxRanks * sizeof(unsigned);
+    cudaError_t e = cudaMalloc(&c->peer_buf, bytes);
+    if (e == cudaSuccess) e = cudaMemset(c->peer_buf, 0, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&c->peer_epoch, kPeerCtas * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(c->peer_epoch, 0, kPeerCtas * sizeof(unsigned));
+    cudaIpcMemHandle_t mine;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mine, c->peer_buf);
+    if (e != cudaSuccess) {
+        peer_release(c);
+        return llme::set_cuda_error(e, "peer buffer");
+    }
+    // Exchange the handles over the communicator itself.
+    void* d_handles = nullptr;
+    e = cudaMalloc(&d_handles, sizeof(cudaIpcMemHandle_t) * (c->nranks + 1));
+    if (e != cudaSuccess) {
+        peer_release(c);
+        return llme::set_cuda_error(e, "peer handles");
+    }
+    char* dh = static_cast<char*>(d_handles);
+    cudaMemcpy(dh + sizeof(cudaIpcMemHandle_t) * c->nranks, &mine, sizeof(mine), cudaMemcpyHostToDevice);
+    cudaStream_t st;
+    cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    ncclResult_t r = nccl().allGather(dh + sizeof(cudaIpcMemHandle_t) * c->nranks, dh,
+                                      sizeof(cudaIpcMemHandle_t), ncclUint8, c->comm, st);
+    int status = LLME_OK;
+    if (r == ncclInProgress) status = wait_ready(c, kEnqueueTimeoutS, "exchange peer handles");
+    else if (r != ncclSuccess) status = nccl_fail(r, "exchange peer handles");
+    std::vector<cudaIpcMemHandle_t> all(c->nranks);
+    if (!status) {
+        cudaStreamSynchronize(st);
+        e = cudaMemcpy(all.data(), dh, sizeof(cudaIpcMemHandle_t) * c->nranks, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) status = llme::set_cuda_error(e, "peer handles");
+    }
+    cudaStreamDestroy(st);
+    cudaFree(d_handles);
+    if (status) {
+        peer_release(c);
+        return status;
+    }
+    PeerArgs& pa = c->pargs;
+    for (int q = 0; q < c->nranks; ++q) {
+        if (q == c->rank) {
+            pa.base[q] = static_cast<float*>(c->peer_buf);
+            continue;
+        }
+        void* ptr = nullptr;
+        e = cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            peer_release(c);
+            return llme::set_cuda_error(e, "open peer buffer");
+        }
+        c->peer_opened[q] = ptr;
+        pa.base[q] = static_cast<float*>(ptr);
+    }
+    void* err = nullptr;
+    cudaGetSymbolAddress(&err, g_comm_error);
+    pa.slot_floats = slot;
+    pa.flags_off = flags_off;
+    pa.epoch = static_cast<unsigned*>(c->peer_epoch);
+    pa.err = static_cast<unsigned*>(err);
+    pa.nranks = c->nranks;
+    pa.rank = c->rank;
+    c->peer_max_floats = max_floats;
+    c->peer = true;
+    return LLME_OK;
+}
+
+int llme_comm_status(void) {
+    unsigned v = 0, zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_comm_error, sizeof(v));
+    if (e != cudaSuccess) return llme::set_cuda_error(e, "read comm status");
+    if (v) {
+        cudaMemcpyToSymbol(g_comm_error, &zero, sizeof(zero));
+        return llme::set_error(LLME_E_TIMEOUT, "peer all-reduce: a peer did not arrive in time");
+    }
+    return LLME_OK;
+}
+
 int llme_comm_destroy(llme_comm_t* c) {
     if (!c) return LLME_OK;
+    peer_release(c);
     NcclApi& api = nccl();
     ncclResult_t r = api.destroy(c->comm);
     int st = LLME_OK;
@@ -159,6 +344,7 @@ int llme_comm_destroy(llme_comm_t* c) {
 
 int llme_comm_abort(llme_comm_t* c) {
     if (!c) return LLME_OK;
+    peer_release(c);
     ncclResult_t r = nccl().abort(c->comm);
     delete c;
     return r == ncclSuccess ? LLME_OK : nccl_fail(r, "abort");
@@ -171,6 +357,11 @@ int llme_allreduce_sum_f32(float* buf, size_t count, llme_comm_t* c, void* strea
     if (!c) return llme::set_error(LLME_E_INVALID, "llme_allreduce_sum_f32: no communicator");
     if (c->nranks == 1 || count == 0) return LLME_OK;
     cudaStream_t stream = stream_ptr ? static_cast<cudaStream_t>(stream_ptr) : cudaStreamPerThread;
+    if (c->peer && count <= c->peer_max_floats) {
+        peer_allreduce_kernel<<<kPeerCtas, kPeerThreads, 0, stream>>>(buf, count, c->pargs);
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? LLME_OK : llme::set_cuda_error(e, "launch");
+    }
     ncclResult_t r = nccl().allReduce(buf, buf, count, ncclFloat32, ncclSum, c->comm, stream);
     if (r == ncclInProgress) return wait_ready(c, kEnqueueTimeoutS, "all-reduce");
     return r == ncclSuccess ? LLME_OK : nccl_fail(r, "all-reduce");

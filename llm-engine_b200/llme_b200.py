@@ -103,7 +103,10 @@ def load() -> ctypes.CDLL:
     lib.llme_allreduce_sum_f32.argtypes = [vp, sz, vp, vp]
     lib.llme_matmul_q8_rowpar.argtypes = [sz, sz, sz, vp, vp, vp, vp, i, i, u, vp, vp]
     lib.llme_matmul_f32_rowpar.argtypes = [sz, sz, sz, vp, vp, vp, i, i, u, vp, vp]
-    for f in ("llme_comm_unique_id", "llme_comm_init", "llme_comm_destroy", "llme_comm_abort",
+    lib.llme_comm_enable_peer.argtypes = [vp, sz]
+    lib.llme_comm_status.argtypes = []
+    for f in ("llme_comm_enable_peer", "llme_comm_status",
+              "llme_comm_unique_id", "llme_comm_init", "llme_comm_destroy", "llme_comm_abort",
               "llme_comm_size", "llme_comm_rank", "llme_allreduce_sum_f32",
               "llme_matmul_q8_rowpar", "llme_matmul_f32_rowpar"):
         getattr(lib, f).restype = i
@@ -212,6 +215,14 @@ class Comm:
         buf = ctypes.create_string_buffer(COMM_ID_BYTES)
         _check(load().llme_comm_unique_id(buf))
         return buf.raw
+
+    def enable_peer(self, max_floats: int) -> None:
+        """Use the library's NVLink peer all-reduce for up to max_floats values (collective)."""
+        _check(load().llme_comm_enable_peer(self.handle, max_floats))
+
+    @staticmethod
+    def status() -> None:
+        _check(load().llme_comm_status())
 
     def allreduce_sum_f32(self, ptr: int, count: int, stream: int | None = None) -> None:
         _check(load().llme_allreduce_sum_f32(ptr, count, self.handle, stream or None))

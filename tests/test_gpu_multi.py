@@ -2,9 +2,10 @@
 
 * A communicator whose second rank never joins must end in LLME_E_TIMEOUT within its
   deadline, not hang (host-side failure: nothing runs on the GPU; one GPU is enough).
-* On two GPUs (skipped with fewer): column-parallel products on n-shards and row-parallel
-  products on k-shards (llme_matmul_q8_rowpar, all-reduce inside, residual added once), both
-  through the C ABI, against the oracle on the unsharded weights.
+* On two GPUs (skipped with fewer): the library's NVLink peer all-reduce, six calls back to
+  back with exactly known sums; column-parallel products on n-shards and row-parallel products
+  on k-shards (llme_matmul_q8_rowpar, all-reduce inside, residual added once), through the C
+  ABI, against the oracle on the unsharded weights.
 Child processes keep NVLS off (NCCL_NVLS_ENABLE=0), as failure tests on this pool require.
 """
 from __future__ import annotations
@@ -60,6 +61,20 @@ dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank
 uid = [L.Comm.unique_id() if rank == 0 else None]
 dist.broadcast_object_list(uid, src=0)
 comm = L.Comm(world, rank, uid[0], timeout_s=60.0)
+comm.enable_peer(1 << 20)   # the library's NVLink peer all-reduce for up to 1 Mi floats
+# Back-to-back peer all-reduces with no host sync in between (both slots reused several times):
+# rank r contributes (r + 1) * (i + 1) + j, so every sum is known exactly.
+bufs = []
+for i in range(6):
+    x = (torch.arange(300003, dtype=torch.float32, device="cuda") % 7) + (rank + 1) * (i + 1)
+    comm.allreduce_sum_f32(x.data_ptr(), x.numel(), stream=L.torch_stream_handle())
+    bufs.append(x)
+torch.cuda.synchronize()
+L.Comm.status()
+for i, x in enumerate(bufs):
+    want = world * (torch.arange(300003, dtype=torch.float32, device="cuda") % 7) + \
+        sum((r + 1) * (i + 1) for r in range(world))
+    assert torch.equal(x, want), ("peer all-reduce", i)
 rng = np.random.default_rng(31)
 for (m, k, n) in [(1, 4096, 4096), (4, 11008, 4096), (8, 1024, 2048), (130, 512, 1024)]:
     A = rng.uniform(-1, 1, (m, k)).astype(np.float32)
@@ -80,6 +95,7 @@ for (m, k, n) in [(1, 4096, 4096), (4, 11008, 4096), (8, 1024, 2048), (130, 512,
     np.save(f"{out}/col_{m}_{rank}.npy", Cc.cpu().numpy())
     np.save(f"{out}/row_{m}_{rank}.npy", Cr.cpu().numpy())
 L.synchronize()
+L.Comm.status()
 comm.destroy()
 dist.destroy_process_group()
 print("OK", rank)
