@@ -23,7 +23,7 @@
 
 namespace {
 constexpr int kPeerMaxRanks = 16;
-constexpr int kPeerCtas = 32;
+constexpr int kPeerCtas = 64;
 constexpr int kPeerThreads = 256;
 
 // Device-side view of the peer all-reduce: every rank's symmetric buffer mapped into this
@@ -162,7 +162,13 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(float* __r
     const size_t lo = min(count, b * chunk), hi = min(count, lo + chunk);
     const size_t slot = (e & 1u) * p.slot_floats;
     float* mine = p.base[p.rank] + slot;
-    for (size_t i = lo + tid; i < hi; i += kPeerThreads) mine[i] = data[i];
+    // lo is a multiple of 4 and slots are 64-float aligned; data is 16-byte aligned when
+    // vec (checked by the host), so float4 moves cover [lo, lo + 4 * n4).
+    const bool vec = (reinterpret_cast<uintptr_t>(data) & 15) == 0;
+    const size_t n4 = vec ? (hi - lo) / 4 : 0;
+    for (size_t i = tid; i < n4; i += kPeerThreads)
+        reinterpret_cast<float4*>(mine + lo)[i] = reinterpret_cast<const float4*>(data + lo)[i];
+    for (size_t i = lo + 4 * n4 + tid; i < hi; i += kPeerThreads) mine[i] = data[i];
     __threadfence_system();
     __syncthreads();
     if (tid < p.nranks) {
@@ -182,7 +188,51 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(float* __r
     }
     __syncthreads();
     if (!s_ok) return;
-    for (size_t i = lo + tid; i < hi; i += kPeerThreads) {
+    // Every rank's value of a float4 is requested before the first add (8 ranks at most in
+    // flight per vector, two vectors per step), then summed in rank order.
+    constexpr int kMaxR = 8;
+    if (p.nranks <= kMaxR) {
+        for (size_t i = tid; i < n4; i += 2 * kPeerThreads) {
+            const size_t i2 = i + kPeerThreads;
+            float4 t[2][kMaxR];
+#pragma unroll
+            for (int r = 0; r < kMaxR; ++r) {
+                if (r < p.nranks) {
+                    const float4* src = reinterpret_cast<const float4*>(p.base[r] + slot + lo);
+                    t[0][r] = __ldcg(src + i);
+                    if (i2 < n4) t[1][r] = __ldcg(src + i2);
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (h == 1 && i2 >= n4) break;
+                float4 v = t[h][0];
+#pragma unroll
+                for (int r = 1; r < kMaxR; ++r) {
+                    if (r < p.nranks) {
+                        v.x += t[h][r].x;
+                        v.y += t[h][r].y;
+                        v.z += t[h][r].z;
+                        v.w += t[h][r].w;
+                    }
+                }
+                reinterpret_cast<float4*>(data + lo)[h ? i2 : i] = v;
+            }
+        }
+    } else {
+        for (size_t i = tid; i < n4; i += kPeerThreads) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = 0; r < p.nranks; ++r) {
+                const float4 t = __ldcg(reinterpret_cast<const float4*>(p.base[r] + slot + lo) + i);
+                v.x += t.x;
+                v.y += t.y;
+                v.z += t.z;
+                v.w += t.w;
+            }
+            reinterpret_cast<float4*>(data + lo)[i] = v;
+        }
+    }
+    for (size_t i = lo + 4 * n4 + tid; i < hi; i += kPeerThreads) {
         float v = 0.0f;
         for (int r = 0; r < p.nranks; ++r) v += __ldcg(p.base[r] + slot + i);
         data[i] = v;
