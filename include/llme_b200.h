@@ -227,7 +227,9 @@ enum {
     LLME_PATH_GEMV_TMA = 3,    /* weight-streaming GEMV, TMA ring (aligned B, m <= 8) */
     LLME_PATH_GEMV_LDG = 4,    /* weight-streaming GEMV, plain loads (ragged B) */
     LLME_PATH_TILED_SIMT = 5,  /* fp32 SIMT tiles, k split across CTAs */
-    LLME_PATH_TCGEN05 = 6      /* tcgen05/TMEM tensor-core GEMM */
+    LLME_PATH_TCGEN05 = 6,     /* tcgen05/TMEM tensor-core GEMM, TF32 (fp32 weights) */
+    LLME_PATH_TCGEN05_Q8 = 7   /* tcgen05/TMEM tensor-core GEMM, int8 weights (kind::i8 on a
+                                  two-term int8 split of the activation rows) */
 };
 
 typedef struct {
@@ -242,7 +244,8 @@ typedef struct {
     size_t split_bytes;   /* split-K scratch: partial sums (0 when slices == 1) */
     size_t counter_slots; /* split-K tickets needed (one per output tile) */
     size_t norm_bytes;    /* scratch for the normalised copy of A (rms_prepass) */
-    size_t operand_bytes; /* scratch for a re-laid-out copy of B (the tensor-core GEMM's B^T) */
+    size_t operand_bytes; /* scratch for re-laid-out operands: B^T (TF32 tensor-core GEMM) or
+                             the int8 hi / lo activation rows and row scales (int8 one) */
 } llme_plan_t;
 
 /* The plan llme_matmul_f32 (is_q8 == 0) or llme_matmul_q8 (is_q8 == 1) would follow on a

@@ -74,6 +74,22 @@ struct PlanIn {
     int math;
 };
 
+// int8 tcgen05 GEMM scratch: hi rows, lo rows (pitch round_up(k, 16), each region 256-byte
+// aligned), then the m row scales.
+size_t q8tc_pitch(size_t k) { return round_up(k, 16); }
+size_t q8tc_rows_bytes(size_t m, size_t k) { return round_up(m * q8tc_pitch(k), 256); }
+size_t q8tc_operand_bytes(size_t m, size_t k) { return 2 * q8tc_rows_bytes(m, k) + m * sizeof(float); }
+
+// Column tile of the int8 tcgen05 GEMM: the one whose persistent schedule ends first,
+// counting a 128-wide tile as half of a 256-wide one (ties go to 256, which reads each
+// activation tile from shared memory half as often).
+int q8tc_tile_n(size_t m, size_t n, int sms) {
+    const size_t tm = ceil_div(m, static_cast<size_t>(q8tc_tile_m()));
+    const size_t w256 = ceil_div(tm * ceil_div(n, size_t{256}), static_cast<size_t>(sms)) * 2;
+    const size_t w128 = ceil_div(tm * ceil_div(n, size_t{128}), static_cast<size_t>(sms));
+    return w128 < w256 ? 128 : 256;
+}
+
 int make_plan(const PlanIn& in, llme_plan_t* p) {
     std::memset(p, 0, sizeof(*p));
     const size_t m = in.m, n = in.n, k = in.k;
@@ -165,6 +181,24 @@ int make_plan(const PlanIn& in, llme_plan_t* p) {
         p->grid_y = 1;
         p->slices = 1;
         p->span = static_cast<int>(k);
+        return LLME_OK;
+    }
+    // The int8 tcgen05 GEMM: also LLME_MATH_TENSOR only (the activations are split into two
+    // int8 terms); W rows must be TMA-addressable and k small enough for exact s32 sums.
+    // The RMSNorm of A is applied by the split pass, not by a separate one.
+    if (kernel == LLME_KERNEL_TILED && in.math == LLME_MATH_TENSOR && in.q8 && m >= 128 &&
+        n % 16 == 0 && in.b_addr % 16 == 0 && k <= static_cast<size_t>(kQ8TcMaxK)) {
+        p->path = LLME_PATH_TCGEN05_Q8;
+        p->rms_prepass = 0;
+        p->norm_bytes = 0;
+        p->tile_m = q8tc_tile_m();
+        p->tile_n = q8tc_tile_n(m, n, sms);
+        const size_t tiles = ceil_div(m, p->tile_m) * ceil_div(n, p->tile_n);
+        p->grid_x = static_cast<int>(std::min<size_t>(tiles, static_cast<size_t>(sms)));
+        p->grid_y = 1;
+        p->slices = 1;
+        p->span = static_cast<int>(k);
+        p->operand_bytes = q8tc_operand_bytes(m, k);
         return LLME_OK;
     }
     p->path = LLME_PATH_TILED_SIMT;
@@ -296,9 +330,10 @@ struct MapKey {
     int dtype, rank;
     uint64_t d0, d1;
     uint32_t b0, b1;
+    uint64_t pitch;
     bool operator==(const MapKey& o) const {
         return ptr == o.ptr && dtype == o.dtype && rank == o.rank && d0 == o.d0 && d1 == o.d1 &&
-               b0 == o.b0 && b1 == o.b1;
+               b0 == o.b0 && b1 == o.b1 && pitch == o.pitch;
     }
 };
 struct MapKeyHash {
@@ -309,22 +344,24 @@ struct MapKeyHash {
         mix(k.d0);
         mix(k.d1);
         mix(static_cast<uint64_t>(k.b0) << 32 | k.b1);
+        mix(k.pitch);
         return h;
     }
 };
 std::mutex g_map_mu;
 std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 
-// Encodes without the cache (rank 2, or rank 1 when rows == 0).
+// Encodes without the cache (rank 2, or rank 1 when rows == 0). pitch_bytes 0: rows are
+// packed (cols * esz apart).
 int encode_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t rows, uint64_t cols,
                uint32_t box_cols, uint32_t box_rows, CUtensorMap* out,
-               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE, uint64_t pitch_bytes = 0);
 
 // Row-major matrix of `rows` x `cols` elements (rank 2), or a vector (rows == 0, rank 1),
 // tiled into boxes of box_cols x box_rows.
 int tensor_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t rows, uint64_t cols,
                uint32_t box_cols, uint32_t box_rows, CUtensorMap* out,
-               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE, uint64_t pitch_bytes = 0) {
     std::call_once(g_encode_once, [] {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -336,7 +373,7 @@ int tensor_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t 
     if (!g_encode) return fail(LLME_E_UNSUPPORTED, "cuda: cuTensorMapEncodeTiled is unavailable");
     const int rank = rows ? 2 : 1;
     const MapKey key{reinterpret_cast<uintptr_t>(ptr), static_cast<int>(dtype) | (static_cast<int>(swizzle) << 8),
-                     rank, cols, rows, box_cols, box_rows};
+                     rank, cols, rows, box_cols, box_rows, pitch_bytes};
     {
         std::lock_guard<std::mutex> lk(g_map_mu);
         auto it = g_maps.find(key);
@@ -345,7 +382,8 @@ int tensor_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t 
             return LLME_OK;
         }
     }
-    const int st = encode_map(ptr, dtype, esz, rows, cols, box_cols, box_rows, out, swizzle);
+    const int st = encode_map(ptr, dtype, esz, rows, cols, box_cols, box_rows, out, swizzle,
+                              pitch_bytes);
     if (st) return st;
     std::lock_guard<std::mutex> lk(g_map_mu);
     if (g_maps.size() > 8192) g_maps.clear();
@@ -354,7 +392,8 @@ int tensor_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t 
 }
 
 int encode_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t rows, uint64_t cols,
-               uint32_t box_cols, uint32_t box_rows, CUtensorMap* out, CUtensorMapSwizzle swizzle) {
+               uint32_t box_cols, uint32_t box_rows, CUtensorMap* out, CUtensorMapSwizzle swizzle,
+               uint64_t pitch_bytes) {
     std::call_once(g_encode_once, [] {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -366,7 +405,7 @@ int encode_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t 
     if (!g_encode) return fail(LLME_E_UNSUPPORTED, "cuda: cuTensorMapEncodeTiled is unavailable");
     const int rank = rows ? 2 : 1;
     cuuint64_t dims[2] = {cols, rows};
-    cuuint64_t strides[1] = {cols * esz};
+    cuuint64_t strides[1] = {pitch_bytes ? pitch_bytes : cols * esz};
     cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = g_encode(out, dtype, rank, const_cast<void*>(ptr), dims, strides, box, estr,
@@ -495,6 +534,39 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
         t.stream = stream;
         t.pdl = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
         e = launch_gemm_tf32(t, tmA, tmB);
+    } else if (p.path == LLME_PATH_TCGEN05_Q8) {
+        float* ops = nullptr;
+        st = ensure_buffer(g_dev[dev].operand, p.operand_bytes, &ops);
+        if (st) return st;
+        int8_t* hi = reinterpret_cast<int8_t*>(ops);
+        int8_t* lo = hi + q8tc_rows_bytes(m, k);
+        float* rs = reinterpret_cast<float*>(lo + q8tc_rows_bytes(m, k));
+        const size_t kp = q8tc_pitch(k);
+        e = launch_split_rows(static_cast<int>(m), static_cast<int>(k), static_cast<int>(kp), A,
+                              rms, hi, lo, rs, stream, true);
+        if (e != cudaSuccess) return cuda_fail(e, "launch");
+        CUtensorMap tmHi, tmLo, tmB;
+        st = tensor_map(hi, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, m, k, 128, 128, &tmHi,
+                        CU_TENSOR_MAP_SWIZZLE_128B, kp);
+        if (st) return st;
+        st = tensor_map(lo, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, m, k, 128, 128, &tmLo,
+                        CU_TENSOR_MAP_SWIZZLE_128B, kp);
+        if (st) return st;
+        st = tensor_map(B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, 128, 128, &tmB,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+        if (st) return st;
+        Q8TcArgs t;
+        t.m = static_cast<int>(m);
+        t.n = static_cast<int>(n);
+        t.k = static_cast<int>(k);
+        t.scale = scale;
+        t.row_scale = rs;
+        t.C = C;
+        t.accumulate = accumulate;
+        t.tile_n = p.tile_n;
+        t.grid = p.grid_x;
+        t.stream = stream;
+        e = launch_gemm_q8_tc(t, tmHi, tmLo, tmB);
     } else {
         TiledArgs t;
         t.m = static_cast<int>(m);
@@ -791,7 +863,8 @@ int llme_synchronize(void) {
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return cuda_fail(e, "synchronize");
     const unsigned dev_err =
-        read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error();
+        read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error() |
+        read_and_clear_q8tc_error();
     if (dev_err) return fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up");
     return LLME_OK;
 }
@@ -814,7 +887,8 @@ int llme_device_status(void) {
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return cuda_fail(e, "synchronize");
     const unsigned dev_err =
-        read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error();
+        read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error() |
+        read_and_clear_q8tc_error();
     return dev_err ? fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up") : LLME_OK;
 }
 

@@ -142,6 +142,27 @@ def test_tcgen05_path_choice():
     assert L.plan(128, 1028, 512, q8=False, a_addr=260, rms_addr=256)["path_name"] == "tcgen05"
 
 
+def test_tcgen05_q8_path_choice():
+    # int8 weights, m >= 128, tensor math: kind::i8 tensor cores on the split activations.
+    p = L.plan(512, 4096, 4096, q8=True)
+    assert p["path_name"] == "tcgen05_q8" and p["kernel"] == 2      # automatic -> tiled
+    assert p["tile_m"] == 128 and p["tile_n"] == 128 and p["grid_x"] == 128
+    kp = 4096
+    assert p["operand_bytes"] == 2 * ((512 * kp + 255) // 256 * 256) + 512 * 4
+    p = L.plan(130, 1040, 72, q8=True, rms_addr=256)
+    assert p["path_name"] == "tcgen05_q8" and p["rms_prepass"] == 0 and p["norm_bytes"] == 0
+    assert p["operand_bytes"] == 2 * ((130 * 80 + 255) // 256 * 256) + 130 * 4   # pitch 80
+    # 256-wide column tiles when their schedule is no longer: 4 x 37 tiles fill 148 SMs once
+    assert L.plan(512, 256 * 37, 4096, q8=True, sm_count=148)["tile_n"] == 256
+    assert L.plan(512, 4096, 4096, q8=True, math=L.MATH_FP32)["path_name"] == "tiled_simt"
+    assert L.plan(127, 4096, 4096, q8=True)["path_name"] == "tiled_simt"
+    assert L.plan(512, 4104, 4096, q8=True)["path_name"] == "tiled_simt"     # n % 16
+    assert L.plan(512, 4096, 4096, q8=True, b_addr=8)["path_name"] == "tiled_simt"
+    assert L.plan(512, 4096, 131072, q8=True)["path_name"] == "tcgen05_q8"
+    assert L.plan(512, 4096, 131073, q8=True)["path_name"] == "tiled_simt"   # s32 sums exact
+    assert L.plan(512, 4096, 4096, q8=True, kernel="tiled_split")["path_name"] == "tiled_simt"
+
+
 def test_rms_prepass_only_outside_the_gemv():
     assert L.plan(4, 300, 288, q8=False, rms_addr=256)["rms_prepass"] == 0
     p = L.plan(70, 130, 40, q8=False, rms_addr=256)
