@@ -401,6 +401,189 @@ def run_sgemm(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+# ---- the 7B-shaped prefill (m = 512) ----------------------------------
+
+PREFILL_ROWS = 512
+PREFILL_METRIC = "prefill GEMM TFLOP/s (7B-shaped int8 weights, m=512)"
+
+
+class Prefill:
+    """Every product of the 7B-shaped layer stack at m = 512 rows (the classifier on the last
+    row only), int8 weights drawn N(0, 0.02^2) with seed 4 and quantised per column, a fresh
+    U(-1, 1) activation matrix per product. On N GPUs: column-parallel weights split along n,
+    row-parallel (wo, w2) along k with a sum all-reduce of the m x 4096 partial outputs."""
+
+    def __init__(self, world, rank, seed=4):
+        import torch
+        import shard
+        self.world, self.rank = world, rank
+        self.shapes = chain_shapes()
+        g = torch.Generator(device="cuda")
+        ga = torch.Generator(device="cuda")
+        ga.manual_seed(seed * 7)
+        self.items = []  # (q, s, m, k_loc, n_loc, rowp, A_dev, C_dev)
+        for idx, (name, k, n, rowp) in enumerate(self.shapes):
+            g.manual_seed(seed * 100003 + idx)
+            W = torch.randn(k, n, generator=g, device="cuda") * 0.02
+            q, s = quantize_on_device(W)
+            del W
+            m = 1 if name == "cls" else PREFILL_ROWS
+            A = torch.rand(m, k, generator=ga, device="cuda") * 2 - 1  # same on every rank
+            if world > 1:
+                if rowp:
+                    q = shard.row_shard(q, world, rank).contiguous()
+                    s0, kl = shard.shard_range(k, world, rank)
+                    A = A[:, s0:s0 + kl].contiguous()
+                else:
+                    q, s = shard.column_shard(q, s, world, rank)
+                    q, s = q.contiguous(), s.contiguous()
+            kl, nl = q.shape
+            C = torch.empty(m, nl, device="cuda")
+            self.items.append((q, s, m, kl, nl, rowp, A, C))
+        torch.cuda.synchronize()
+        self.flops_total = sum(2.0 * (1 if nm == "cls" else PREFILL_ROWS) * k * n
+                               for (nm, k, n, _) in self.shapes)
+        self.flops_rank = sum(2.0 * m * kl * nl for (_, _, m, kl, nl, _, _, _) in self.items)
+        self.a_host = [it[6].cpu().pin_memory() for it in self.items]
+        self.c_host = [torch.empty(it[7].shape).pin_memory() for it in self.items]
+
+    def launch_all(self, stream_handle, comm=None, join=None):
+        import llme_b200 as L
+        for (q, s, m, kl, nl, rowp, A, C) in self.items:
+            L.matmul_cuda_q8(m, nl, kl, A.data_ptr(), q.data_ptr(), s.data_ptr(), C.data_ptr(),
+                             "automatic", False, 0, L.FLAG_WEIGHTS_STATIC, stream_handle)
+            if rowp and comm is not None:
+                comm(C.data_ptr(), m * nl)
+        if join is not None:
+            join()
+
+    def launches(self):
+        import llme_b200 as L
+        n = 0
+        for (q, s, m, kl, nl, rowp, A, C) in self.items:
+            p = L.plan(m, nl, kl, q8=True, a_addr=A.data_ptr(), b_addr=q.data_ptr())
+            n += 2 if p["path_name"] == "tcgen05_q8" else 1
+        return n
+
+    def h2d(self):
+        for it, h in zip(self.items, self.a_host):
+            it[6].copy_(h, non_blocking=True)
+
+    def d2h(self):
+        for it, h in zip(self.items, self.c_host):
+            h.copy_(it[7], non_blocking=True)
+
+
+def cpu_prefill_sample(pf, budget_s=10.0):
+    """The reference's matmul_parallel (its packed GEMM for m > 4, matmul.cpp:240-306) on
+    layer 0's wq product at m = 512 (the same int8 weights), on all host cores."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle  # the CPU baseline leg only
+    kind = "reference" if oracle.Reference.available(fast=True) else "port"
+    q, s, m, kl, nl = (pf.items[0][0].cpu().numpy(), pf.items[0][1].cpu().numpy(),
+                       pf.items[0][2], pf.items[0][3], pf.items[0][4])
+    A = pf.items[0][6].cpu().numpy()
+    flops = 2.0 * m * kl * nl
+    if kind == "reference":
+        ref = oracle.Reference(fast=True)
+        hq = ref.qtensor(q, s)
+        cores = ref.threads()
+        one = lambda: ref.matmul_parallel_q8(A, hq)  # noqa: E731
+    else:
+        cores = oracle.default_threads()
+        one = lambda: oracle.matmul_parallel(A, q=q, scale=s)  # noqa: E731
+    one()
+    times, t_end = [], time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": round(flops / med / 1e12, 4), "unit": "TFLOP/s", "cores": cores,
+            "kind": kind, "sample": f"layer 0 wq ({m} x {kl} x {nl}, int8 weights), median of "
+                                    f"{len(times)} calls"}
+
+
+def run_prefill(args, world, rank, local):
+    import torch
+    import llme_b200 as L
+    L.set_math(L.MATH_TENSOR)
+    pf = Prefill(world, rank)
+    stream = torch.cuda.Stream()
+    h = stream.cuda_stream
+    tp = comm = join = None
+    if world > 1:
+        import torch.distributed as dist
+        uid = [L.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        tp = L.Comm(world, rank, uid[0], timeout_s=60.0)
+        comm_stream = torch.cuda.Stream()
+
+        def comm(c_ptr, n):
+            comm_stream.wait_stream(torch.cuda.current_stream())
+            tp.allreduce_sum_f32(c_ptr, n, comm_stream.cuda_stream)
+
+        def join():
+            torch.cuda.current_stream().wait_stream(comm_stream)
+    step_fn = lambda: pf.launch_all(h, comm, join)  # noqa: E731
+    graph = capture(step_fn, stream)
+    sampler = ClockSampler(local)
+    secs = max_over_ranks(time_graph(graph, args.steps, args.warmup, stream, world, sampler), world)
+    tflops = pf.flops_total * args.steps / secs / 1e12
+
+    def e2e_fn():
+        pf.h2d()
+        step_fn()
+        pf.d2h()
+    e2e_graph = capture(e2e_fn, stream)
+    e2e_secs = max_over_ranks(time_graph(e2e_graph, args.steps, args.warmup, stream, world), world)
+    e2e = {"value": round(pf.flops_total * args.steps / e2e_secs / 1e12, 1), "unit": "TFLOP/s",
+           "h2d_bytes_per_step": int(sum(t.numel() * 4 for t in pf.a_host)),
+           "d2h_bytes_per_step": int(sum(t.numel() * 4 for t in pf.c_host)),
+           "ms_per_step": round(e2e_secs / args.steps * 1e3, 4)}
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops_sustained"])
+        peak_kind = "measured bf16 sustained"
+    except Exception:
+        peak, peak_kind = 1400.0, "fallback bf16 sustained"
+    achieved = pf.flops_rank * args.steps / secs / 1e12
+    launches = pf.launches()
+    line = {
+        "metric": PREFILL_METRIC, "value": round(tflops, 1), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8 x (int8 hi + int8 lo) -> s32",
+        "data": "synthetic: N(0,0.02^2) weights (seed 4) quantised per column to int8, "
+                "U(-1,1) activations",
+        "config": {"workload": "7B-shaped batched prefill, m=512, int8 weights (BASELINE "
+                               "configs[4]); classifier on the last row",
+                   "rows": PREFILL_ROWS, "products_per_step": len(pf.items),
+                   "launches_per_step": launches, "flops_per_step": pf.flops_total,
+                   "parallelism": f"tp{world}" if world > 1 else "single",
+                   "launch": "one C-ABI call per product (split pass + tcgen05 GEMM), one CUDA "
+                             "graph per step",
+                   "l2": "no flush: 6.6 GB of weights and 2.3 GB of activations per step"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                     "peak_kind": peak_kind + " (each product is two int8 MMAs, together the "
+                                              "bf16 rate)",
+                     "kernel": "gemm_q8_tc_kernel (+ split_rows_kernel)", "traffic": None},
+        "e2e": e2e, "gpu_launches": launches * args.steps, "clocks": sampler.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_extras:
+        line["cpu_baseline"] = cpu_prefill_sample(pf)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph, e2e_graph
+    torch.cuda.synchronize()
+    if tp is not None:
+        tp.destroy()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def peaks():
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
@@ -457,6 +640,8 @@ def run_ours(args):
         raise SystemExit("this benchmark needs an sm_100 (B200) GPU")
     if args.workload == "sgemm":
         return run_sgemm(args, world, rank, local)
+    if args.workload == "prefill":
+        return run_prefill(args, world, rank, local)
     if args.workload == "chain":
         chain = Chain(world, rank, chain_shapes(), seed=3)
     else:
@@ -626,9 +811,10 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["chain", "gemv", "sgemm"], default="chain",
+    ap.add_argument("--workload", choices=["chain", "gemv", "sgemm", "prefill"], default="chain",
                     help="chain: BASELINE configs[3] (default); gemv: configs[0] alone; "
-                         "sgemm: configs[2] (square TF32 GEMM, --size)")
+                         "sgemm: configs[2] (square TF32 GEMM, --size); prefill: configs[4] "
+                         "(m = 512 through the 7B-shaped int8 weights)")
     ap.add_argument("--size", type=int, default=8192, help="N for --workload sgemm")
     ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
                     help="N>1: the library's NVLink peer all-reduce (default) or NCCL")

@@ -80,16 +80,6 @@ size_t q8tc_pitch(size_t k) { return round_up(k, 16); }
 size_t q8tc_rows_bytes(size_t m, size_t k) { return round_up(m * q8tc_pitch(k), 256); }
 size_t q8tc_operand_bytes(size_t m, size_t k) { return 2 * q8tc_rows_bytes(m, k) + m * sizeof(float); }
 
-// Column tile of the int8 tcgen05 GEMM: the one whose persistent schedule ends first,
-// counting a 128-wide tile as half of a 256-wide one (ties go to 256, which reads each
-// activation tile from shared memory half as often).
-int q8tc_tile_n(size_t m, size_t n, int sms) {
-    const size_t tm = ceil_div(m, static_cast<size_t>(q8tc_tile_m()));
-    const size_t w256 = ceil_div(tm * ceil_div(n, size_t{256}), static_cast<size_t>(sms)) * 2;
-    const size_t w128 = ceil_div(tm * ceil_div(n, size_t{128}), static_cast<size_t>(sms));
-    return w128 < w256 ? 128 : 256;
-}
-
 int make_plan(const PlanIn& in, llme_plan_t* p) {
     std::memset(p, 0, sizeof(*p));
     const size_t m = in.m, n = in.n, k = in.k;
@@ -192,7 +182,7 @@ int make_plan(const PlanIn& in, llme_plan_t* p) {
         p->rms_prepass = 0;
         p->norm_bytes = 0;
         p->tile_m = q8tc_tile_m();
-        p->tile_n = q8tc_tile_n(m, n, sms);
+        p->tile_n = q8tc_tile_n();
         const size_t tiles = ceil_div(m, p->tile_m) * ceil_div(n, p->tile_n);
         p->grid_x = static_cast<int>(std::min<size_t>(tiles, static_cast<size_t>(sms)));
         p->grid_y = 1;
@@ -563,7 +553,6 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
         t.row_scale = rs;
         t.C = C;
         t.accumulate = accumulate;
-        t.tile_n = p.tile_n;
         t.grid = p.grid_x;
         t.stream = stream;
         e = launch_gemm_q8_tc(t, tmHi, tmLo, tmB);

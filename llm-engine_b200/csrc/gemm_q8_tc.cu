@@ -24,22 +24,27 @@
 // row's magnitude, inside the 5e-3 tensor-core tolerance, and is bit-for-bit
 // repeatable (every CTA computes its own tile with a fixed instruction order).
 //
-// Layout in shared memory, per pipeline stage (128 k per stage):
-//   hi tile: 128 rows x 128 bytes, K-major, 128-byte swizzle (TMA box 128 x 128)
-//   lo tile: the same for the lo rows
-//   B tile:  TBN/128 boxes of 128 k-rows x 128 columns, MN-major (W as stored,
-//            k x n with n contiguous), 128-byte swizzle; the MMA descriptor
-//            steps 1 KB per 8 k-rows (SBO) and one box (16 KB) per 128 columns
-//            (LBO).
+// Orientation: the MMA computes C^T tiles. Its M operand is a 128-column panel of
+// W (W as stored, k x n with n contiguous, read MN-major), its N operand is 128
+// token rows of hi followed by the same 128 rows of lo (K-major), so one
+// M=128, N=256, K=32 MMA produces both integer sums for 128 columns x 128 rows:
+// TMEM lane = output column, TMEM columns [0,128) = Hi per row, [128,256) = Lo.
+// A tile's accumulator takes 256 of the 512 TMEM columns, so there are two and
+// the epilogue of one tile overlaps the MMAs of the next.
+//
+// Shared memory, per pipeline stage (128 k per stage, 48 KB, 4 stages):
+//   W panel: 128 k-rows x 128 columns, 128-byte swizzle (TMA box 128 x 128); the
+//            MN-major descriptor steps 1 KB per 8 k-rows (SBO);
+//   hi rows: 128 rows x 128 bytes of k, K-major, 128-byte swizzle;
+//   lo rows: the same, directly after, so hi and lo form one 256-row operand.
 // Warp roles (192 threads, one CTA per SM, persistent over output tiles):
-//   warp 0     TMA producer (one thread) over a ring of kStages stages;
-//   warp 1     TMEM allocation (all 512 columns) and MMA issue (one thread):
-//              per stage and 32-deep K step, one MMA into the Hi accumulator
-//              and one into the Lo accumulator; tcgen05.commit frees the stage;
-//   warps 2-5  epilogue: tcgen05.ld of Hi and Lo (each warp its TMEM lane
-//              quadrant), scale, optional residual add, fp32 stores.
-// With TBN = 128 the CTA holds two accumulator pairs, so the epilogue of one
-// tile overlaps the MMAs of the next; with TBN = 256 one pair fills TMEM.
+//   warp 0     TMA producer (one thread);
+//   warp 1     TMEM allocation (512 columns) and MMA issue (one thread), one
+//              commit per stage to free it and one per tile to hand the
+//              accumulator to the epilogue;
+//   warps 2-5  epilogue: each warp owns a TMEM lane quadrant = 32 output
+//              columns; per 32 rows it loads Hi and Lo with tcgen05.ld and
+//              writes each row's 32 columns as one coalesced 128-byte store.
 // Every mbarrier wait is bounded (common.cuh): a wait that runs out sets the
 // file's error word and the kernel winds down instead of hanging.
 #include "kernels.h"
@@ -50,22 +55,18 @@ namespace {
 
 __device__ unsigned int g_q8tc_error;
 
-constexpr int TBM = 128;       // rows of C per tile (TMEM lanes)
-constexpr int TBK = 128;       // k per stage: 128 int8 = one 128-byte swizzle row
+constexpr int TBW = 128;   // output columns per tile (MMA M, TMEM lanes)
+constexpr int TBT = 128;   // output rows per tile (MMA N = 2 * TBT: hi and lo)
+constexpr int TBK = 128;   // k per stage: 128 int8 = one 128-byte swizzle row
 constexpr int kThreads = 192;
-constexpr int kRingBudget = 196608;  // bytes of shared memory for the stage ring
-constexpr int kGroupM = 8;           // row tiles that share each column panel (L2 reuse)
-
-template <int TBN>
-struct Cfg {
-    static constexpr int kABytes = TBM * TBK;           // one of hi / lo: 16 KB
-    static constexpr int kBBytes = TBK * TBN;           // 16 or 32 KB
-    static constexpr int kStageBytes = 2 * kABytes + kBBytes;
-    static constexpr int kStages = kRingBudget / kStageBytes;  // 4 or 3
-    static constexpr int kAccCols = 2 * TBN;            // Hi + Lo
-    static constexpr int kAccBufs = 512 / kAccCols;     // 2 or 1
-    static constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
-};
+constexpr int kWBytes = TBK * TBW;      // 16 KB
+constexpr int kRowBytes = TBT * TBK;    // 16 KB each for hi and lo
+constexpr int kStageBytes = kWBytes + 2 * kRowBytes;
+constexpr int kStages = 4;
+constexpr int kAccCols = 2 * TBT;       // 256
+constexpr int kAccBufs = 2;
+constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
+constexpr int kGroupT = 8;              // row tiles that share each W panel (L2 reuse)
 
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                        uint32_t idesc, uint32_t accumulate) {
@@ -77,9 +78,9 @@ __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t
 }
 
 // Instruction descriptor: s32 accumulator (D format 2), signed int8 A and B (format 1),
-// A K-major, B MN-major.
+// A (the W panel) MN-major, B (the hi / lo rows) K-major.
 constexpr uint32_t idesc_i8(int M, int N) {
-    return (2u << 4) | (1u << 7) | (1u << 10) | (1u << 16) |
+    return (2u << 4) | (1u << 7) | (1u << 10) | (1u << 15) |
            (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
@@ -92,42 +93,40 @@ __device__ __forceinline__ float finish(uint32_t hi, uint32_t lo, float rs, floa
     return __fmul_rn(t, __fmul_rn(rs, sc));
 }
 
-// Tile t -> (row tile, column tile), kGroupM row tiles per column panel.
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int* tm, int* tn) {
-    const int group = kGroupM * tiles_n;
-    const int first_m = (t / group) * kGroupM;
-    const int gm = min(tiles_m - first_m, kGroupM);
-    *tm = first_m + (t % group) % gm;
-    *tn = (t % group) / gm;
+// Tile t -> (row tile, column tile): kGroupT row tiles run next to each other on one W panel.
+__device__ __forceinline__ void tile_coords(int t, int tiles_t, int tiles_w, int* tt, int* tw) {
+    const int group = kGroupT * tiles_w;
+    const int first = (t / group) * kGroupT;
+    const int g = min(tiles_t - first, kGroupT);
+    *tt = first + (t % group) % g;
+    *tw = (t % group) / g;
 }
 
-template <int TBN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_q8_tc_kernel(const __grid_constant__ CUtensorMap tmHi,
                       const __grid_constant__ CUtensorMap tmLo,
                       const __grid_constant__ CUtensorMap tmB, const Q8TcArgs a) {
-    using C = Cfg<TBN>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
-    uint64_t* empty = full + C::kStages;
-    uint64_t* acc_full = empty + C::kStages;
-    uint64_t* acc_empty = acc_full + C::kAccBufs;
-    uint64_t* drain = acc_empty + C::kAccBufs;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* acc_full = empty + kStages;
+    uint64_t* acc_empty = acc_full + kAccBufs;
+    uint64_t* drain = acc_empty + kAccBufs;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tiles_m = (a.m + TBM - 1) / TBM;
-    const int tiles_n = (a.n + TBN - 1) / TBN;
-    const int tiles = tiles_m * tiles_n;
+    const int tiles_t = (a.m + TBT - 1) / TBT;
+    const int tiles_w = (a.n + TBW - 1) / TBW;
+    const int tiles = tiles_t * tiles_w;
     const int nk = (a.k + TBK - 1) / TBK;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::kStages; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < C::kAccBufs; ++b) {
+        for (int b = 0; b < kAccBufs; ++b) {
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
         }
@@ -149,60 +148,55 @@ __global__ void __launch_bounds__(kThreads, 1)
             int it = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                int tm, tn;
-                tile_coords(t, tiles_m, tiles_n, &tm, &tn);
+                int tt, tw;
+                tile_coords(t, tiles_t, tiles_w, &tt, &tw);
                 for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int s = it % C::kStages;
-                    if (it >= C::kStages &&
-                        !mbar_wait(&empty[s], ((it / C::kStages) - 1) & 1, &g_q8tc_error)) {
+                    const int s = it % kStages;
+                    if (it >= kStages &&
+                        !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, &g_q8tc_error)) {
                         ok = false;
                         break;
                     }
-                    uint8_t* st = smem + s * C::kStageBytes;
-                    mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-                    tma_load_2d_nohint(st, &tmHi, kb * TBK, tm * TBM, &full[s]);
-                    tma_load_2d_nohint(st + C::kABytes, &tmLo, kb * TBK, tm * TBM, &full[s]);
-#pragma unroll
-                    for (int j = 0; j < TBN / 128; ++j)
-                        tma_load_2d_nohint(st + 2 * C::kABytes + j * TBK * 128, &tmB,
-                                           tn * TBN + j * 128, kb * TBK, &full[s]);
+                    uint8_t* st = smem + s * kStageBytes;
+                    mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    tma_load_2d_nohint(st, &tmB, tw * TBW, kb * TBK, &full[s]);
+                    tma_load_2d_nohint(st + kWBytes, &tmHi, kb * TBK, tt * TBT, &full[s]);
+                    tma_load_2d_nohint(st + kWBytes + kRowBytes, &tmLo, kb * TBK, tt * TBT,
+                                       &full[s]);
                 }
             }
             // Before the CTA may exit, every copy issued into its shared memory has landed
             // (already true unless a wait above gave up).
-            for (int j = it - 1; j >= 0 && j >= it - C::kStages; --j)
-                mbar_wait(&full[j % C::kStages], (j / C::kStages) & 1, &g_q8tc_error);
+            for (int j = it - 1; j >= 0 && j >= it - kStages; --j)
+                mbar_wait(&full[j % kStages], (j / kStages) & 1, &g_q8tc_error);
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_i8(TBM, TBN);
+            constexpr uint32_t idesc = idesc_i8(TBW, 2 * TBT);
             int it = 0, use = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++use) {
-                const int buf = use % C::kAccBufs;
-                const int round = use / C::kAccBufs;
+                const int buf = use % kAccBufs;
+                const int round = use / kAccBufs;
                 if (round > 0 && !mbar_wait(&acc_empty[buf], (round - 1) & 1, &g_q8tc_error)) break;
                 tc::fence_after_sync();
-                const uint32_t d_hi = tmem + buf * C::kAccCols;
-                const uint32_t d_lo = d_hi + TBN;
+                const uint32_t d = tmem + buf * kAccCols;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int s = it % C::kStages;
-                    if (!mbar_wait(&full[s], (it / C::kStages) & 1, &g_q8tc_error)) {
+                    const int s = it % kStages;
+                    if (!mbar_wait(&full[s], (it / kStages) & 1, &g_q8tc_error)) {
                         ok = false;
                         break;
                     }
                     tc::fence_after_sync();
-                    const uint32_t hi = smem_u32(smem + s * C::kStageBytes);
-                    const uint32_t lo = hi + C::kABytes;
-                    const uint32_t bb = lo + C::kABytes;
+                    const uint32_t wp = smem_u32(smem + s * kStageBytes);
+                    const uint32_t rows = wp + kWBytes;
 #pragma unroll
                     for (int kk = 0; kk < TBK / 32; ++kk) {
-                        // A: K-major 128-byte rows, the 32-deep K step is 32 bytes into the row.
-                        // B: MN-major, 32 k-rows of 128 bytes per K step; LBO = one box.
-                        const uint64_t bd = tc::smem_desc_sw128(bb + kk * 32 * 128, TBK * 128, 1024);
-                        const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
-                        mma_i8(d_hi, tc::smem_desc_sw128(hi + kk * 32, 16, 1024), bd, idesc, acc);
-                        mma_i8(d_lo, tc::smem_desc_sw128(lo + kk * 32, 16, 1024), bd, idesc, acc);
+                        // W: MN-major, 32 k-rows of 128 bytes per K step. Rows: K-major,
+                        // the 32-deep K step is 32 bytes into each 128-byte row.
+                        mma_i8(d, tc::smem_desc_sw128(wp + kk * 32 * 128, kWBytes, 1024),
+                               tc::smem_desc_sw128(rows + kk * 32, 16, 1024), idesc,
+                               (kb | kk) != 0 ? 1u : 0u);
                     }
                     tc::commit(&empty[s]);
                 }
@@ -217,51 +211,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         pdl_wait();              // C may be read by the kernel before this one
         int use = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++use) {
-            int tm, tn;
-            tile_coords(t, tiles_m, tiles_n, &tm, &tn);
-            const int buf = use % C::kAccBufs;
-            const int round = use / C::kAccBufs;
+            int tt, tw;
+            tile_coords(t, tiles_t, tiles_w, &tt, &tw);
+            const int buf = use % kAccBufs;
+            const int round = use / kAccBufs;
             if (!mbar_wait(&acc_full[buf], round & 1, &g_q8tc_error)) break;
             tc::fence_after_sync();
-            const int row = tm * TBM + q * 32 + lane;
-            const bool row_ok = row < a.m;
-            const float rs = row_ok ? a.row_scale[row] : 0.0f;
-            float* out = a.C + static_cast<size_t>(row_ok ? row : 0) * a.n;
-            const uint32_t base = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * C::kAccCols;
-            const bool vec = ((reinterpret_cast<uintptr_t>(a.scale) |
-                               reinterpret_cast<uintptr_t>(a.C)) & 15) == 0;
+            const int col = tw * TBW + q * 32 + lane;
+            const bool col_ok = col < a.n;
+            const float sc = col_ok ? a.scale[col] : 0.0f;
+            const uint32_t base = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * kAccCols;
 #pragma unroll 1
-            for (int c = 0; c < TBN / 32; ++c) {
+            for (int c = 0; c < TBT / 32; ++c) {
                 __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
                 uint32_t h[32], l[32];
                 tc::tmem_ld_32x32b_x32(base + c * 32, h);
-                tc::tmem_ld_32x32b_x32(base + TBN + c * 32, l);
-                const int col0 = tn * TBN + c * 32;
-                if (!row_ok || col0 >= a.n) continue;
-                if (vec && col0 + 32 <= a.n) {
+                tc::tmem_ld_32x32b_x32(base + TBT + c * 32, l);
+                const int row0 = tt * TBT + c * 32;
+                if (row0 >= a.m) continue;
+                // Row scales of these 32 rows, one per lane, passed around by shuffles.
+                const float rs_lane = row0 + lane < a.m ? a.row_scale[row0 + lane] : 0.0f;
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4) {
-                        const float4 sc = *reinterpret_cast<const float4*>(a.scale + col0 + j);
-                        float4* o = reinterpret_cast<float4*>(out + col0 + j);
-                        float4 v = make_float4(finish(h[j], l[j], rs, sc.x), finish(h[j + 1], l[j + 1], rs, sc.y),
-                                               finish(h[j + 2], l[j + 2], rs, sc.z), finish(h[j + 3], l[j + 3], rs, sc.w));
-                        if (a.accumulate) {
-                            const float4 p = *o;
-                            v = make_float4(__fadd_rn(p.x, v.x), __fadd_rn(p.y, v.y),
-                                            __fadd_rn(p.z, v.z), __fadd_rn(p.w, v.w));
-                        }
-                        *o = v;
-                    }
-                } else {
-                    // n % 16 == 0: the last chunk of a row has 16 or 32 columns.
-#pragma unroll
-                    for (int j = 0; j < 32; j += 16) {
-                        if (col0 + j >= a.n) continue;
-#pragma unroll
-                        for (int u = 0; u < 16; ++u) {
-                            const float v = finish(h[j + u], l[j + u], rs, a.scale[col0 + j + u]);
-                            out[col0 + j + u] = a.accumulate ? __fadd_rn(out[col0 + j + u], v) : v;
-                        }
+                for (int j = 0; j < 32; ++j) {
+                    const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
+                    if (row0 + j < a.m && col_ok) {
+                        float* o = a.C + static_cast<size_t>(row0 + j) * a.n + col;
+                        const float v = finish(h[j], l[j], rs, sc);
+                        *o = a.accumulate ? __fadd_rn(*o, v) : v;
                     }
                 }
             }
@@ -389,36 +365,10 @@ __global__ void __launch_bounds__(kSplitThreads)
     }
 }
 
-template <int TBN>
-cudaError_t launch_tbn(const Q8TcArgs& a, const CUtensorMap& tmHi, const CUtensorMap& tmLo,
-                       const CUtensorMap& tmB) {
-    static unsigned configured = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 32 && !(configured & (1u << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q8_tc_kernel<TBN>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             Cfg<TBN>::kSmemBytes);
-        if (e != cudaSuccess) return e;
-        configured |= 1u << dev;
-    }
-    const int tiles = ((a.m + TBM - 1) / TBM) * ((a.n + TBN - 1) / TBN);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(std::max(1, std::min(tiles, a.grid)));
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = Cfg<TBN>::kSmemBytes;
-    cfg.stream = a.stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_q8_tc_kernel<TBN>, tmHi, tmLo, tmB, a);
-}
-
 }  // namespace
 
-int q8tc_tile_m() { return TBM; }
+int q8tc_tile_m() { return TBT; }
+int q8tc_tile_n() { return TBW; }
 
 cudaError_t launch_split_rows(int m, int k, int kp, const float* A, const float* w, int8_t* hi,
                               int8_t* lo, float* row_scale, cudaStream_t stream, bool pdl) {
@@ -438,9 +388,27 @@ cudaError_t launch_split_rows(int m, int k, int kp, const float* A, const float*
 
 cudaError_t launch_gemm_q8_tc(const Q8TcArgs& a, const CUtensorMap& tmHi, const CUtensorMap& tmLo,
                               const CUtensorMap& tmB) {
-    if (a.tile_n == 256) return launch_tbn<256>(a, tmHi, tmLo, tmB);
-    if (a.tile_n == 128) return launch_tbn<128>(a, tmHi, tmLo, tmB);
-    return cudaErrorInvalidValue;
+    static unsigned configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 32 && !(configured & (1u << dev))) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_q8_tc_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (e != cudaSuccess) return e;
+        configured |= 1u << dev;
+    }
+    const int tiles = ((a.m + TBT - 1) / TBT) * ((a.n + TBW - 1) / TBW);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::max(1, std::min(tiles, a.grid)));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = a.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_q8_tc_kernel, tmHi, tmLo, tmB, a);
 }
 
 unsigned read_and_clear_q8tc_error() {

@@ -128,19 +128,20 @@ unsigned read_and_clear_tc_error();
 // int8-weight tcgen05 GEMM (gemm_q8_tc.cu). split_rows writes each fp32 activation row
 // (RMS-normalised when w is set) as int8 hi / lo rows of pitch kp plus a row scale; the GEMM
 // multiplies both by the int8 weights (kind::i8, s32 in TMEM) in persistent CTAs over
-// 128 x tile_n output tiles. Requirements: n % 16 == 0, B 16-byte aligned, k <= 131072.
+// output tiles of q8tc_tile_m() rows x q8tc_tile_n() columns. Requirements: n % 16 == 0,
+// B 16-byte aligned, k <= kQ8TcMaxK.
 struct Q8TcArgs {
     int m = 0, n = 0, k = 0;
     const float* scale = nullptr;      // n column scales
     const float* row_scale = nullptr;  // m row scales from split_rows
     float* C = nullptr;
     bool accumulate = false;
-    int tile_n = 256;                  // 128 or 256
     int grid = 0;                      // persistent CTAs (at most the tile count)
     cudaStream_t stream = nullptr;
 };
 constexpr int kQ8TcMaxK = 131072;  // 127 * 127 * k < 2^31
 int q8tc_tile_m();
+int q8tc_tile_n();
 cudaError_t launch_split_rows(int m, int k, int kp, const float* A, const float* w, int8_t* hi,
                               int8_t* lo, float* row_scale, cudaStream_t stream, bool pdl);
 cudaError_t launch_gemm_q8_tc(const Q8TcArgs& a, const CUtensorMap& tmHi, const CUtensorMap& tmLo,

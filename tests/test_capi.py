@@ -152,8 +152,7 @@ def test_tcgen05_q8_path_choice():
     p = L.plan(130, 1040, 72, q8=True, rms_addr=256)
     assert p["path_name"] == "tcgen05_q8" and p["rms_prepass"] == 0 and p["norm_bytes"] == 0
     assert p["operand_bytes"] == 2 * ((130 * 80 + 255) // 256 * 256) + 130 * 4   # pitch 80
-    # 256-wide column tiles when their schedule is no longer: 4 x 37 tiles fill 148 SMs once
-    assert L.plan(512, 256 * 37, 4096, q8=True, sm_count=148)["tile_n"] == 256
+    assert L.plan(2048, 8192, 4096, q8=True, sm_count=148)["grid_x"] == 148   # persistent
     assert L.plan(512, 4096, 4096, q8=True, math=L.MATH_FP32)["path_name"] == "tiled_simt"
     assert L.plan(127, 4096, 4096, q8=True)["path_name"] == "tiled_simt"
     assert L.plan(512, 4104, 4096, q8=True)["path_name"] == "tiled_simt"     # n % 16
