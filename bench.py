@@ -457,6 +457,40 @@ class Prefill:
         if join is not None:
             join()
 
+    def make_batch(self):
+        """The m = 512 products as grouped launches (they are independent): one batch on one
+        GPU; on several, the row-parallel products first (their partial outputs are summed
+        while the column-parallel batch runs) and the column-parallel ones second. The
+        classifier (last row only, m = 1) stays a single GEMV call."""
+        import llme_b200 as L
+        prods = {False: [], True: []}
+        for (q, s, m, kl, nl, rowp, A, C) in self.items:
+            if m == PREFILL_ROWS:
+                prods[rowp and self.world > 1].append(
+                    (nl, kl, A.data_ptr(), q.data_ptr(), s.data_ptr(), C.data_ptr(), 0))
+        self.batches = [L.Batch(PREFILL_ROWS, prods[True])] if prods[True] else []
+        self.batches.append(L.Batch(PREFILL_ROWS, prods[False]))
+
+    def launch_grouped(self, stream_handle, comm=None, join=None):
+        import llme_b200 as L
+        for b in self.batches:
+            b.run(0, stream_handle)
+            if comm is not None and b is self.batches[0] and len(self.batches) > 1:
+                for (q, s, m, kl, nl, rowp, A, C) in self.items:
+                    if rowp:
+                        comm(C.data_ptr(), m * nl)
+        for (q, s, m, kl, nl, rowp, A, C) in self.items:
+            if m != PREFILL_ROWS:
+                L.matmul_cuda_q8(m, nl, kl, A.data_ptr(), q.data_ptr(), s.data_ptr(),
+                                 C.data_ptr(), "automatic", False, 0, L.FLAG_WEIGHTS_STATIC,
+                                 stream_handle)
+        if join is not None:
+            join()
+
+    def destroy_batches(self):
+        for b in getattr(self, "batches", []):
+            b.destroy()
+
     def launches(self):
         import llme_b200 as L
         n = 0
@@ -525,11 +559,24 @@ def run_prefill(args, world, rank, local):
 
         def join():
             torch.cuda.current_stream().wait_stream(comm_stream)
-    step_fn = lambda: pf.launch_all(h, comm, join)  # noqa: E731
+    grouped = args.launch == "grouped"
+    if grouped:
+        pf.make_batch()
+        step_fn = lambda: pf.launch_grouped(h, comm, join)  # noqa: E731
+    else:
+        step_fn = lambda: pf.launch_all(h, comm, join)  # noqa: E731
     graph = capture(step_fn, stream)
     sampler = ClockSampler(local)
     secs = max_over_ranks(time_graph(graph, args.steps, args.warmup, stream, world, sampler), world)
     tflops = pf.flops_total * args.steps / secs / 1e12
+    per_call = None
+    if grouped:
+        pc_graph = capture(lambda: pf.launch_all(h, comm, join), stream)
+        pc_secs = max_over_ranks(time_graph(pc_graph, args.steps, args.warmup, stream, world), world)
+        per_call = {"value": round(pf.flops_total * args.steps / pc_secs / 1e12, 1),
+                    "unit": "TFLOP/s", "ms_per_step": round(pc_secs / args.steps * 1e3, 4),
+                    "launches_per_step": pf.launches()}
+        del pc_graph
 
     def e2e_fn():
         pf.h2d()
@@ -548,7 +595,7 @@ def run_prefill(args, world, rank, local):
     except Exception:
         peak, peak_kind = 1400.0, "fallback bf16 sustained"
     achieved = pf.flops_rank * args.steps / secs / 1e12
-    launches = pf.launches()
+    launches = 2 * len(pf.batches) + 1 if grouped else pf.launches()
     line = {
         "metric": PREFILL_METRIC, "value": round(tflops, 1), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
@@ -561,7 +608,11 @@ def run_prefill(args, world, rank, local):
                    "rows": PREFILL_ROWS, "products_per_step": len(pf.items),
                    "launches_per_step": launches, "flops_per_step": pf.flops_total,
                    "parallelism": f"tp{world}" if world > 1 else "single",
-                   "launch": "one C-ABI call per product (split pass + tcgen05 GEMM), one CUDA "
+                   "launch": ("grouped: one split launch + one persistent tcgen05 launch over "
+                              "every m=512 product (llme_batch_run; the products are "
+                              "independent) + the classifier GEMV, one CUDA graph per step")
+                             if grouped else
+                             "one C-ABI call per product (split pass + tcgen05 GEMM), one CUDA "
                              "graph per step",
                    "l2": "no flush: 6.6 GB of weights and 2.3 GB of activations per step"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
@@ -569,7 +620,8 @@ def run_prefill(args, world, rank, local):
                      "peak_kind": peak_kind + " (each product is two int8 MMAs, together the "
                                               "bf16 rate)",
                      "kernel": "gemm_q8_tc_kernel (+ split_rows_kernel)", "traffic": None},
-        "e2e": e2e, "gpu_launches": launches * args.steps, "clocks": sampler.summary(),
+        "e2e": e2e, "gpu_launches": launches * args.steps, "per_call": per_call,
+        "clocks": sampler.summary(),
     }
     if rank == 0 and world == 1 and not args.no_extras:
         line["cpu_baseline"] = cpu_prefill_sample(pf)
@@ -577,6 +629,8 @@ def run_prefill(args, world, rank, local):
         print(json.dumps(line), flush=True)
     del graph, e2e_graph
     torch.cuda.synchronize()
+    if grouped:
+        pf.destroy_batches()
     if tp is not None:
         tp.destroy()
     if world > 1:

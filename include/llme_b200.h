@@ -142,13 +142,19 @@ int llme_copy_to_device(void* dst, const void* src, size_t bytes);   /* waits */
 int llme_copy_to_host(void* dst, const void* src, size_t bytes);     /* waits */
 
 /* ---- grouped products ------------------------------------------------------------------------ *
- * Many independent int8 products of the same m (1..8) in ONE persistent launch. The reference
- * issues one matmul_cuda per projection; products that do not read each other's outputs (a
- * decode layer's q/k/v, w1/w3, or the benchmark's chain of fresh activations) can instead be
- * grouped: every CTA walks a list of (product, 128-column strip) units over the product's whole
- * k, streaming weights by TMA without a pause between products, and writes C directly (no
- * cross-CTA reduction). Requirements per product: n % 16 == 0, k % 4 == 0, A and B 16-byte
- * aligned, no product's C overlapping another product's A. */
+ * Many independent int8 products of the same m in ONE persistent launch. The reference issues
+ * one matmul_cuda per projection; products that do not read each other's outputs (a layer's
+ * q/k/v, w1/w3, or the benchmark's chains of fresh activations) can instead be grouped.
+ *   m = 1..8 (decode): every CTA walks a list of (product, 128-column strip) units over the
+ *     product's whole k, streaming weights by TMA without a pause between products, and
+ *     writes C directly (no cross-CTA reduction). Per product: n % 16 == 0, k % 4 == 0,
+ *     A and B 16-byte aligned.
+ *   m >= 128 (prefill; LLME_MATH_TENSOR): one launch splits every product's activation rows
+ *     into int8 hi / lo terms (scratch owned by the batch), then one persistent tcgen05 launch
+ *     runs every product's 128 x 128 output tiles, each CTA its own list balanced by work.
+ *     Per product: n % 16 == 0, B 16-byte aligned, k <= 131072. Results are those of
+ *     llme_matmul_q8 on the same product, bit for bit.
+ * No product's C may overlap another product's A. */
 typedef struct {
     size_t n, k;          /* B is k x n int8, C is m x n */
     const float* A;       /* m x k */

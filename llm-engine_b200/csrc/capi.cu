@@ -667,18 +667,181 @@ struct llme_batch {
     int dev = 0;
     void* dmem = nullptr;
     llme::BatchArgs args;
+    // Tensor-core batches (m >= 128): the grouped tcgen05 launch and its split-row scratch.
+    bool tc = false;
+    llme::Q8TcBatchArgs targs;
+    void* scratch = nullptr;
 };
 
 namespace {
 
+// Longest-processing-time-first: units by decreasing work, each to the CTA with the least work
+// so far (ties to the lower index). Deterministic, and within a few percent of the best
+// possible makespan; each CTA then runs its units in their original order. Returns the units
+// of CTA c as per_cta[c].
+std::vector<std::vector<size_t>> lpt_assign(const std::vector<size_t>& work, int grid) {
+    std::vector<size_t> order(work.size());
+    for (size_t u = 0; u < order.size(); ++u) order[u] = u;
+    std::stable_sort(order.begin(), order.end(),
+                     [&](size_t x, size_t y) { return work[x] > work[y]; });
+    std::vector<std::vector<size_t>> per_cta(grid);
+    using Load = std::pair<size_t, int>;  // (work, cta)
+    std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+    for (int c = 0; c < grid; ++c) heap.push({0, c});
+    for (size_t u : order) {
+        Load l = heap.top();
+        heap.pop();
+        per_cta[l.second].push_back(u);
+        heap.push({l.first + work[u], l.second});
+    }
+    for (auto& v : per_cta) std::sort(v.begin(), v.end());
+    return per_cta;
+}
+
+// Grouped int8 products with m >= 128 on the tensor cores (gemm_q8_tc.cu).
+int batch_create_tc(llme_batch_t** out, size_t m, size_t count, const llme_q8_product* p) {
+    if (math_mode() != LLME_MATH_TENSOR)
+        return fail(LLME_E_UNSUPPORTED,
+                    "llme_batch_q8_create: m >= 128 runs on the tensor cores (LLME_MATH_TENSOR)");
+    if (m * count > (size_t{1} << 30))
+        return fail(LLME_E_INVALID, "llme_batch_q8_create: more than 2^30 rows in all");
+    const size_t tm = ceil_div(m, static_cast<size_t>(q8tc_tile_m()));
+    std::vector<Q8TcItem> items(count);
+    std::vector<size_t> scratch_off(count);
+    size_t scratch_bytes = 0;
+    std::vector<int> row_begin(count + 1, 0);
+    std::vector<uint2> units;
+    std::vector<size_t> work;
+    for (size_t i = 0; i < count; ++i) {
+        const llme_q8_product& q = p[i];
+        const std::string where = "llme_batch_q8_create: product " + std::to_string(i) + " " +
+                                  shapes(m, q.n, q.k);
+        if (q.n == 0 || q.k == 0 || q.n % 16)
+            return fail(LLME_E_INVALID, where + ": needs n % 16 == 0 and nonzero n, k");
+        if (q.k > static_cast<size_t>(kQ8TcMaxK))
+            return fail(LLME_E_INVALID, where + ": k above " + std::to_string(kQ8TcMaxK));
+        if (m * q.k >= kMaxElems || q.k * q.n >= kMaxElems || m * q.n >= kMaxElems)
+            return fail(LLME_E_INVALID, where + ": more than 2^31 elements");
+        if (reinterpret_cast<uintptr_t>(q.B) % 16)
+            return fail(LLME_E_INVALID, where + ": B must be 16-byte aligned");
+        scratch_off[i] = scratch_bytes;
+        scratch_bytes += q8tc_operand_bytes(m, q.k);
+        scratch_bytes = round_up(scratch_bytes, 256);
+        row_begin[i + 1] = row_begin[i] + static_cast<int>(m);
+        const size_t tiles = tm * ceil_div(q.n, static_cast<size_t>(q8tc_tile_n()));
+        for (size_t t = 0; t < tiles; ++t) {
+            units.push_back(make_uint2(static_cast<unsigned>(i), static_cast<unsigned>(t)));
+            // Work of a tile: its k-blocks plus about two for the epilogue.
+            work.push_back(ceil_div(q.k, size_t{128}) + 2);
+        }
+    }
+    int dev = 0, sms = 0;
+    int st = current_device(&dev);
+    if (st) return st;
+    st = device_sms(dev, &sms);
+    if (st) return st;
+    const int grid = static_cast<int>(std::min<size_t>(units.size(), sms));
+    const auto per_cta = lpt_assign(work, grid);
+    std::vector<uint2> table;
+    std::vector<int> cta_begin(grid + 1, 0);
+    for (int c = 0; c < grid; ++c) {
+        cta_begin[c] = static_cast<int>(table.size());
+        for (size_t u : per_cta[c]) table.push_back(units[u]);
+    }
+    cta_begin[grid] = static_cast<int>(table.size());
+
+    auto* b = new llme_batch;
+    b->dev = dev;
+    b->tc = true;
+    cudaError_t e = cudaMalloc(&b->scratch, std::max<size_t>(scratch_bytes, 256));
+    if (e != cudaSuccess) {
+        delete b;
+        return cuda_fail(e, "alloc batch scratch");
+    }
+    std::vector<CUtensorMap> mw(count), mh(count), ml(count);
+    for (size_t i = 0; i < count; ++i) {
+        const llme_q8_product& q = p[i];
+        const size_t kp = q8tc_pitch(q.k);
+        int8_t* hi = static_cast<int8_t*>(b->scratch) + scratch_off[i];
+        int8_t* lo = hi + q8tc_rows_bytes(m, q.k);
+        float* rs = reinterpret_cast<float*>(lo + q8tc_rows_bytes(m, q.k));
+        items[i] = Q8TcItem{q.A, q.C, q.scale, hi, lo, rs, static_cast<int>(m),
+                            static_cast<int>(q.n), static_cast<int>(q.k), static_cast<int>(kp),
+                            q.accumulate ? 1 : 0, 0};
+        st = encode_map(q.B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q.k, q.n, 128, 128, &mw[i],
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!st)
+            st = encode_map(hi, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, m, q.k, 128, 128, &mh[i],
+                            CU_TENSOR_MAP_SWIZZLE_128B, kp);
+        if (!st)
+            st = encode_map(lo, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, m, q.k, 128, 128, &ml[i],
+                            CU_TENSOR_MAP_SWIZZLE_128B, kp);
+        if (st) {
+            cudaFree(b->scratch);
+            delete b;
+            return st;
+        }
+    }
+    // [maps W][maps hi][maps lo][items][row_begin][unit table][cta_begin], 128-byte aligned parts.
+    const size_t maps_bytes = count * sizeof(CUtensorMap);
+    const size_t items_off = 3 * maps_bytes;
+    const size_t rows_off = round_up(items_off + count * sizeof(Q8TcItem), 128);
+    const size_t table_off = round_up(rows_off + row_begin.size() * sizeof(int), 128);
+    const size_t begin_off = round_up(table_off + table.size() * sizeof(uint2), 128);
+    const size_t bytes = begin_off + cta_begin.size() * sizeof(int);
+    e = cudaMalloc(&b->dmem, bytes);
+    if (e != cudaSuccess) {
+        cudaFree(b->scratch);
+        delete b;
+        return cuda_fail(e, "alloc batch");
+    }
+    char* base = static_cast<char*>(b->dmem);
+    e = cudaMemcpy(base, mw.data(), maps_bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(base + maps_bytes, mh.data(), maps_bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(base + 2 * maps_bytes, ml.data(), maps_bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(base + items_off, items.data(), count * sizeof(Q8TcItem), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(base + rows_off, row_begin.data(), row_begin.size() * sizeof(int),
+                       cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(base + table_off, table.data(), table.size() * sizeof(uint2),
+                       cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(base + begin_off, cta_begin.data(), cta_begin.size() * sizeof(int),
+                       cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(b->dmem);
+        cudaFree(b->scratch);
+        delete b;
+        return cuda_fail(e, "upload batch");
+    }
+    Q8TcBatchArgs& a = b->targs;
+    a.count = static_cast<int>(count);
+    a.rows = row_begin[count];
+    a.items = reinterpret_cast<const Q8TcItem*>(base + items_off);
+    a.row_begin = reinterpret_cast<const int*>(base + rows_off);
+    a.tmW = reinterpret_cast<const CUtensorMap*>(base);
+    a.tmHi = reinterpret_cast<const CUtensorMap*>(base + maps_bytes);
+    a.tmLo = reinterpret_cast<const CUtensorMap*>(base + 2 * maps_bytes);
+    a.unit_table = reinterpret_cast<const uint2*>(base + table_off);
+    a.cta_begin = reinterpret_cast<const int*>(base + begin_off);
+    a.grid = grid;
+    *out = b;
+    return LLME_OK;
+}
+
 int batch_create(llme_batch_t** out, size_t m, size_t count, const llme_q8_product* p) {
     g_error.clear();
     *out = nullptr;
-    if (m < 1 || m > 8)
-        return fail(LLME_E_INVALID, "llme_batch_q8_create: m must be 1..8, got " + std::to_string(m));
     if (count < 1 || count > 65535)
         return fail(LLME_E_INVALID, "llme_batch_q8_create: 1..65535 products, got " +
                                         std::to_string(count));
+    if (m >= 128) return batch_create_tc(out, m, count, p);
+    if (m < 1 || m > 8)
+        return fail(LLME_E_INVALID,
+                    "llme_batch_q8_create: m must be 1..8 or at least 128, got " + std::to_string(m));
     std::vector<BatchItem> items(count);
     std::vector<CUtensorMap> mb(count), ma(count);
     std::vector<unsigned> units;
@@ -718,26 +881,10 @@ int batch_create(llme_batch_t** out, size_t m, size_t count, const llme_q8_produ
     // work so far (ties to the lower index). Deterministic, and within a few percent of the
     // best possible makespan; each CTA then runs its units in their original order.
     const int grid = static_cast<int>(std::min<size_t>(units.size(), gemv_batch_ctas_per_sm() * sms));
-    std::vector<size_t> order(units.size());
-    for (size_t u = 0; u < order.size(); ++u) order[u] = u;
-    std::stable_sort(order.begin(), order.end(),
-                     [&](size_t x, size_t y) { return unit_bytes[x] > unit_bytes[y]; });
-    std::vector<std::vector<size_t>> per_cta(grid);
-    {
-        using Load = std::pair<size_t, int>;  // (work, cta)
-        std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
-        for (int c = 0; c < grid; ++c) heap.push({0, c});
-        for (size_t u : order) {
-            Load l = heap.top();
-            heap.pop();
-            per_cta[l.second].push_back(u);
-            heap.push({l.first + unit_bytes[u], l.second});
-        }
-    }
+    const auto per_cta = lpt_assign(unit_bytes, grid);
     std::vector<unsigned> table;
     std::vector<int> cta_begin(grid + 1, 0);
     for (int c = 0; c < grid; ++c) {
-        std::sort(per_cta[c].begin(), per_cta[c].end());
         cta_begin[c] = static_cast<int>(table.size());
         for (size_t u : per_cta[c]) table.push_back(units[u]);
     }
@@ -815,6 +962,12 @@ int llme_batch_run(llme_batch_t* b, unsigned flags, void* stream) {
     int st = current_device(&dev);
     if (st) return st;
     if (dev != b->dev) return fail(LLME_E_INVALID, "llme_batch_run: batch belongs to another device");
+    if (b->tc) {
+        Q8TcBatchArgs t = b->targs;
+        t.stream = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
+        cudaError_t e = launch_q8tc_batch(t);
+        return e == cudaSuccess ? LLME_OK : cuda_fail(e, "launch");
+    }
     BatchArgs a = b->args;
     a.stream = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
     a.pdl = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
@@ -825,6 +978,10 @@ int llme_batch_run(llme_batch_t* b, unsigned flags, void* stream) {
 int llme_batch_destroy(llme_batch_t* b) {
     if (!b) return LLME_OK;
     cudaError_t e = cudaFree(b->dmem);
+    if (b->scratch) {
+        cudaError_t e2 = cudaFree(b->scratch);
+        if (e == cudaSuccess) e = e2;
+    }
     delete b;
     return e == cudaSuccess ? LLME_OK : cuda_fail(e, "free batch");
 }

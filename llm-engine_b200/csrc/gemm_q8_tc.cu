@@ -47,6 +47,9 @@
 //              writes each row's 32 columns as one coalesced 128-byte store.
 // Every mbarrier wait is bounded (common.cuh): a wait that runs out sets the
 // file's error word and the kernel winds down instead of hanging.
+#include <atomic>
+#include <cstring>
+
 #include "kernels.h"
 #include "tc_common.cuh"
 
@@ -102,10 +105,66 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_t, int tiles_w, int
     *tw = (t % group) / g;
 }
 
+// One output tile of one product, as every role of the GEMM sees it.
+struct Unit {
+    const CUtensorMap *w, *hi, *lo;
+    const float* scale;
+    const float* row_scale;
+    float* C;
+    int m, n, nk, tt, tw;
+    bool accumulate;
+};
+
+// The i-th unit of this CTA. Single product: tiles blockIdx.x + i * gridDim.x. Grouped: the
+// CTA's own list from the batch's unit table.
+template <bool G>
+__device__ __forceinline__ bool fetch_unit(int i, const CUtensorMap* tmHi, const CUtensorMap* tmLo,
+                                           const CUtensorMap* tmB, const Q8TcArgs& a,
+                                           const Q8TcBatchArgs& b, Unit& u) {
+    int t, m, n, k;
+    if constexpr (G) {
+        const int idx = b.cta_begin[blockIdx.x] + i;
+        if (idx >= b.cta_begin[blockIdx.x + 1]) return false;
+        const uint2 e = b.unit_table[idx];
+        const Q8TcItem& it = b.items[e.x];
+        t = static_cast<int>(e.y);
+        m = it.m;
+        n = it.n;
+        k = it.k;
+        u.w = b.tmW + e.x;
+        u.hi = b.tmHi + e.x;
+        u.lo = b.tmLo + e.x;
+        u.scale = it.scale;
+        u.row_scale = it.row_scale;
+        u.C = it.C;
+        u.accumulate = it.accumulate != 0;
+    } else {
+        m = a.m;
+        n = a.n;
+        k = a.k;
+        t = blockIdx.x + i * gridDim.x;
+        if (t >= ((m + TBT - 1) / TBT) * ((n + TBW - 1) / TBW)) return false;
+        u.w = tmB;
+        u.hi = tmHi;
+        u.lo = tmLo;
+        u.scale = a.scale;
+        u.row_scale = a.row_scale;
+        u.C = a.C;
+        u.accumulate = a.accumulate;
+    }
+    u.m = m;
+    u.n = n;
+    u.nk = (k + TBK - 1) / TBK;
+    tile_coords(t, (m + TBT - 1) / TBT, (n + TBW - 1) / TBW, &u.tt, &u.tw);
+    return true;
+}
+
+template <bool G>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_q8_tc_kernel(const __grid_constant__ CUtensorMap tmHi,
                       const __grid_constant__ CUtensorMap tmLo,
-                      const __grid_constant__ CUtensorMap tmB, const Q8TcArgs a) {
+                      const __grid_constant__ CUtensorMap tmB, const Q8TcArgs a,
+                      const Q8TcBatchArgs b) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
@@ -116,10 +175,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tiles_t = (a.m + TBT - 1) / TBT;
-    const int tiles_w = (a.n + TBW - 1) / TBW;
-    const int tiles = tiles_t * tiles_w;
-    const int nk = (a.k + TBK - 1) / TBK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -132,9 +187,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(drain, 1);
         fence_mbar_init();
-        prefetch_tensormap(&tmHi);
-        prefetch_tensormap(&tmLo);
-        prefetch_tensormap(&tmB);
+        if (!G) {
+            prefetch_tensormap(&tmHi);
+            prefetch_tensormap(&tmLo);
+            prefetch_tensormap(&tmB);
+        }
     }
     if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
     tc::fence_before_sync();
@@ -147,10 +204,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             pdl_wait();  // the split rows come from the kernel before this one
             int it = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                int tt, tw;
-                tile_coords(t, tiles_t, tiles_w, &tt, &tw);
-                for (int kb = 0; kb < nk; ++kb, ++it) {
+            Unit u;
+            for (int i = 0; ok && fetch_unit<G>(i, &tmHi, &tmLo, &tmB, a, b, u); ++i) {
+                for (int kb = 0; kb < u.nk; ++kb, ++it) {
                     const int s = it % kStages;
                     if (it >= kStages &&
                         !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, &g_q8tc_error)) {
@@ -159,9 +215,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     uint8_t* st = smem + s * kStageBytes;
                     mbar_arrive_expect_tx(&full[s], kStageBytes);
-                    tma_load_2d_nohint(st, &tmB, tw * TBW, kb * TBK, &full[s]);
-                    tma_load_2d_nohint(st + kWBytes, &tmHi, kb * TBK, tt * TBT, &full[s]);
-                    tma_load_2d_nohint(st + kWBytes + kRowBytes, &tmLo, kb * TBK, tt * TBT,
+                    tma_load_2d_nohint(st, u.w, u.tw * TBW, kb * TBK, &full[s]);
+                    tma_load_2d_nohint(st + kWBytes, u.hi, kb * TBK, u.tt * TBT, &full[s]);
+                    tma_load_2d_nohint(st + kWBytes + kRowBytes, u.lo, kb * TBK, u.tt * TBT,
                                        &full[s]);
                 }
             }
@@ -175,13 +231,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t idesc = idesc_i8(TBW, 2 * TBT);
             int it = 0, use = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++use) {
+            Unit u;
+            for (; ok && fetch_unit<G>(use, &tmHi, &tmLo, &tmB, a, b, u); ++use) {
                 const int buf = use % kAccBufs;
                 const int round = use / kAccBufs;
                 if (round > 0 && !mbar_wait(&acc_empty[buf], (round - 1) & 1, &g_q8tc_error)) break;
                 tc::fence_after_sync();
                 const uint32_t d = tmem + buf * kAccCols;
-                for (int kb = 0; kb < nk; ++kb, ++it) {
+                for (int kb = 0; kb < u.nk; ++kb, ++it) {
                     const int s = it % kStages;
                     if (!mbar_wait(&full[s], (it / kStages) & 1, &g_q8tc_error)) {
                         ok = false;
@@ -209,17 +266,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         pdl_wait();              // C may be read by the kernel before this one
-        int use = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++use) {
-            int tt, tw;
-            tile_coords(t, tiles_t, tiles_w, &tt, &tw);
+        Unit u;
+        for (int use = 0; fetch_unit<G>(use, &tmHi, &tmLo, &tmB, a, b, u); ++use) {
             const int buf = use % kAccBufs;
             const int round = use / kAccBufs;
             if (!mbar_wait(&acc_full[buf], round & 1, &g_q8tc_error)) break;
             tc::fence_after_sync();
-            const int col = tw * TBW + q * 32 + lane;
-            const bool col_ok = col < a.n;
-            const float sc = col_ok ? a.scale[col] : 0.0f;
+            const int col = u.tw * TBW + q * 32 + lane;
+            const bool col_ok = col < u.n;
+            const float sc = col_ok ? u.scale[col] : 0.0f;
             const uint32_t base = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * kAccCols;
 #pragma unroll 1
             for (int c = 0; c < TBT / 32; ++c) {
@@ -227,17 +282,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t h[32], l[32];
                 tc::tmem_ld_32x32b_x32(base + c * 32, h);
                 tc::tmem_ld_32x32b_x32(base + TBT + c * 32, l);
-                const int row0 = tt * TBT + c * 32;
-                if (row0 >= a.m) continue;
+                const int row0 = u.tt * TBT + c * 32;
+                if (row0 >= u.m) continue;
                 // Row scales of these 32 rows, one per lane, passed around by shuffles.
-                const float rs_lane = row0 + lane < a.m ? a.row_scale[row0 + lane] : 0.0f;
+                const float rs_lane = row0 + lane < u.m ? u.row_scale[row0 + lane] : 0.0f;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
-                    if (row0 + j < a.m && col_ok) {
-                        float* o = a.C + static_cast<size_t>(row0 + j) * a.n + col;
+                    if (row0 + j < u.m && col_ok) {
+                        float* o = u.C + static_cast<size_t>(row0 + j) * u.n + col;
                         const float v = finish(h[j], l[j], rs, sc);
-                        *o = a.accumulate ? __fadd_rn(*o, v) : v;
+                        *o = u.accumulate ? __fadd_rn(*o, v) : v;
                     }
                 }
             }
@@ -260,45 +315,86 @@ __global__ void __launch_bounds__(kThreads, 1)
 // into hi / lo int8 rows of pitch kp and a row scale (see the file comment). Rows whose
 // largest magnitude is not finite get a NaN row scale, so their outputs are NaN, as an fp32
 // product with that row would be.
+// Aligned rows (k % 4 == 0, 16-byte aligned A and w) are read once: the first
+// kSplitRegs * 4 * kSplitThreads elements stay in registers between the two passes (all
+// loads issued before the reduction), only a longer row's remainder is read again.
 constexpr int kSplitThreads = 256;
+constexpr int kSplitRegs = 12;  // float4 per thread: rows up to 12288 elements in registers
 
-__global__ void __launch_bounds__(kSplitThreads)
-    split_rows_kernel(int k, int kp, const float* __restrict__ A, const float* __restrict__ w,
-                      int8_t* __restrict__ hi, int8_t* __restrict__ lo,
-                      float* __restrict__ row_scale) {
+struct SplitRow {
+    float inv_rms, q, pre;
+    bool norm;
+    // hi / lo of one element (the kernel's whole arithmetic for an element).
+    __device__ __forceinline__ void split(float a, float g, int8_t* h8, int8_t* l8) const {
+        const float x = norm ? a * inv_rms * g : a;
+        float y = pre == 1.0f ? x * q : (x * pre) * q;
+        if (!(fabsf(y) <= 128.0f)) y = 0.0f;  // non-finite rows: the row scale is NaN
+        const float h = fminf(fmaxf(rintf(y), -127.0f), 127.0f);
+        const float l = fminf(fmaxf(rintf((y - h) * 256.0f), -127.0f), 127.0f);
+        *h8 = static_cast<int8_t>(static_cast<int>(h));
+        *l8 = static_cast<int8_t>(static_cast<int>(l));
+    }
+    __device__ __forceinline__ void split4(float4 v, float4 g, int8_t* oh, int8_t* ol) const {
+        char4 h4, l4;
+        split(v.x, g.x, &h4.x, &l4.x);
+        split(v.y, g.y, &h4.y, &l4.y);
+        split(v.z, g.z, &h4.z, &l4.z);
+        split(v.w, g.w, &h4.w, &l4.w);
+        *reinterpret_cast<char4*>(oh) = h4;
+        *reinterpret_cast<char4*>(ol) = l4;
+    }
+};
+
+__device__ __forceinline__ void split_accumulate(float4 v, float4 g, bool norm, float* ss, float* mx) {
+    float4 u = v;
+    if (norm) {
+        *ss = fmaf(v.x, v.x, *ss);
+        *ss = fmaf(v.y, v.y, *ss);
+        *ss = fmaf(v.z, v.z, *ss);
+        *ss = fmaf(v.w, v.w, *ss);
+        u = make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w);
+    }
+    *mx = fmaxf(*mx, fmaxf(fmaxf(fabsf(u.x), fabsf(u.y)), fmaxf(fabsf(u.z), fabsf(u.w))));
+    // fmaxf drops NaN; keep it visible.
+    if (u.x != u.x || u.y != u.y || u.z != u.z || u.w != u.w) *mx = __int_as_float(0x7f800000);
+}
+
+// Splits one row `in` (k floats) into oh / ol and writes its scale to *rs_out. Whole CTA.
+__device__ __forceinline__ void split_row(int k, const float* __restrict__ in,
+                                          const float* __restrict__ w, int8_t* __restrict__ oh,
+                                          int8_t* __restrict__ ol, float* __restrict__ rs_out) {
     __shared__ float red_ss[kSplitThreads / 32], red_mx[kSplitThreads / 32];
-    pdl_launch_dependents();
-    pdl_wait();
-    const float* in = A + static_cast<size_t>(blockIdx.x) * k;
-    int8_t* oh = hi + static_cast<size_t>(blockIdx.x) * kp;
-    int8_t* ol = lo + static_cast<size_t>(blockIdx.x) * kp;
+    const bool norm = w != nullptr;
     const bool vec = (k & 3) == 0 && (reinterpret_cast<uintptr_t>(in) & 15) == 0 &&
-                     (w == nullptr || (reinterpret_cast<uintptr_t>(w) & 15) == 0);
+                     (!norm || (reinterpret_cast<uintptr_t>(w) & 15) == 0);
+    constexpr int kStride = kSplitThreads * 4;
+    const float4 one = make_float4(1.f, 1.f, 1.f, 1.f);
+    // The norm weights are shared by every row (cached), so they are loaded where used rather
+    // than held in registers.
+    auto wload = [&](int j) { return norm ? *reinterpret_cast<const float4*>(w + j) : one; };
+    float4 v[kSplitRegs];
     // Pass 1: sum of squares (for the norm) and the largest |a * w| (or |a|).
     float ss = 0.0f, mx = 0.0f;
     if (vec) {
-        for (int j = threadIdx.x * 4; j < k; j += kSplitThreads * 4) {
-            const float4 v = *reinterpret_cast<const float4*>(in + j);
-            float4 u = v;
-            if (w) {
-                const float4 g = *reinterpret_cast<const float4*>(w + j);
-                ss = fmaf(v.x, v.x, ss);
-                ss = fmaf(v.y, v.y, ss);
-                ss = fmaf(v.z, v.z, ss);
-                ss = fmaf(v.w, v.w, ss);
-                u = make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w);
-            }
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(u.x), fabsf(u.y)), fmaxf(fabsf(u.z), fabsf(u.w))));
-            // fmaxf drops NaN; keep it visible.
-            if (u.x != u.x || u.y != u.y || u.z != u.z || u.w != u.w) mx = __int_as_float(0x7f800000);
+#pragma unroll
+        for (int r = 0; r < kSplitRegs; ++r) {
+            const int j = r * kStride + threadIdx.x * 4;
+            v[r] = j < k ? *reinterpret_cast<const float4*>(in + j) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+#pragma unroll
+        for (int r = 0; r < kSplitRegs; ++r) {
+            const int j = r * kStride + threadIdx.x * 4;
+            if (j < k) split_accumulate(v[r], wload(j), norm, &ss, &mx);
+        }
+        for (int j = kSplitRegs * kStride + threadIdx.x * 4; j < k; j += kStride)
+            split_accumulate(*reinterpret_cast<const float4*>(in + j), wload(j), norm, &ss, &mx);
     } else {
         for (int j = threadIdx.x; j < k; j += kSplitThreads) {
-            const float v = in[j];
-            float u = v;
-            if (w) {
-                ss = fmaf(v, v, ss);
-                u = v * w[j];
+            const float a = in[j];
+            float u = a;
+            if (norm) {
+                ss = fmaf(a, a, ss);
+                u = a * w[j];
             }
             mx = fmaxf(mx, fabsf(u));
             if (u != u) mx = __int_as_float(0x7f800000);
@@ -320,51 +416,83 @@ __global__ void __launch_bounds__(kSplitThreads)
         total += red_ss[i];
         amax = fmaxf(amax, red_mx[i]);
     }
-    const float inv_rms = w ? 1.0f / sqrtf(total / static_cast<float>(k) + kRmsEps) : 1.0f;
-    amax *= inv_rms;
+    SplitRow sr;
+    sr.norm = norm;
+    sr.inv_rms = norm ? 1.0f / sqrtf(total / static_cast<float>(k) + kRmsEps) : 1.0f;
+    amax *= sr.inv_rms;
     // Multiplier to the hi grid (127 at the row's largest magnitude). Rows so small that
-    // 127 / amax overflows are first brought up by 2^64 (exact).
-    float pre = 1.0f;
-    if (amax > 0.0f && amax < 1e-30f) pre = 18446744073709551616.0f;  // 2^64
-    const float q = amax > 0.0f ? 127.0f / (amax * pre) : 0.0f;
+    // 127 / amax would overflow are first brought up by 2^64 (exact).
+    sr.pre = amax > 0.0f && amax < 1e-30f ? 18446744073709551616.0f : 1.0f;  // 2^64
+    sr.q = amax > 0.0f ? 127.0f / (amax * sr.pre) : 0.0f;
     if (threadIdx.x == 0) {
         float s = amax / 127.0f;
         if (!(amax <= 3.402823466e38f)) s = __int_as_float(0x7fc00000);  // inf / NaN rows
-        row_scale[blockIdx.x] = s;
+        *rs_out = s;
     }
-    auto split1 = [&](float a, float g, int8_t* h8, int8_t* l8) {
-        float x = w ? a * inv_rms * g : a;
-        float y = pre == 1.0f ? x * q : (x * pre) * q;
-        if (!(fabsf(y) <= 128.0f)) y = 0.0f;  // non-finite rows: row scale is NaN
-        float h = fminf(fmaxf(rintf(y), -127.0f), 127.0f);
-        float r = (y - h) * 256.0f;
-        float l = fminf(fmaxf(rintf(r), -127.0f), 127.0f);
-        *h8 = static_cast<int8_t>(static_cast<int>(h));
-        *l8 = static_cast<int8_t>(static_cast<int>(l));
-    };
+    // Pass 2: hi / lo.
     if (vec) {
-        for (int j = threadIdx.x * 4; j < k; j += kSplitThreads * 4) {
-            const float4 v = *reinterpret_cast<const float4*>(in + j);
-            float4 g = make_float4(1.f, 1.f, 1.f, 1.f);
-            if (w) g = *reinterpret_cast<const float4*>(w + j);
-            char4 h4, l4;
-            split1(v.x, g.x, &h4.x, &l4.x);
-            split1(v.y, g.y, &h4.y, &l4.y);
-            split1(v.z, g.z, &h4.z, &l4.z);
-            split1(v.w, g.w, &h4.w, &l4.w);
-            *reinterpret_cast<char4*>(oh + j) = h4;
-            *reinterpret_cast<char4*>(ol + j) = l4;
+#pragma unroll
+        for (int r = 0; r < kSplitRegs; ++r) {
+            const int j = r * kStride + threadIdx.x * 4;
+            if (j < k) sr.split4(v[r], wload(j), oh + j, ol + j);
         }
+        for (int j = kSplitRegs * kStride + threadIdx.x * 4; j < k; j += kStride)
+            sr.split4(*reinterpret_cast<const float4*>(in + j), wload(j), oh + j, ol + j);
     } else {
         for (int j = threadIdx.x; j < k; j += kSplitThreads) {
             int8_t h8, l8;
-            split1(in[j], w ? w[j] : 1.0f, &h8, &l8);
+            sr.split(in[j], norm ? w[j] : 1.0f, &h8, &l8);
             oh[j] = h8;
             ol[j] = l8;
         }
     }
 }
 
+__global__ void __launch_bounds__(kSplitThreads)
+    split_rows_kernel(int k, int kp, const float* __restrict__ A, const float* __restrict__ w,
+                      int8_t* __restrict__ hi, int8_t* __restrict__ lo,
+                      float* __restrict__ row_scale) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const size_t r = blockIdx.x;
+    split_row(k, A + r * k, w, hi + r * kp, lo + r * kp, row_scale + r);
+}
+
+// Grouped: CTA r splits global row r, row r - row_begin[p] of product p.
+__global__ void __launch_bounds__(kSplitThreads) split_rows_batch_kernel(const Q8TcBatchArgs b) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int r = blockIdx.x;
+    int lo_p = 0, hi_p = b.count - 1;  // the last p with row_begin[p] <= r
+    while (lo_p < hi_p) {
+        const int mid = (lo_p + hi_p + 1) >> 1;
+        if (b.row_begin[mid] <= r) lo_p = mid;
+        else hi_p = mid - 1;
+    }
+    const Q8TcItem& it = b.items[lo_p];
+    const size_t row = static_cast<size_t>(r - b.row_begin[lo_p]);
+    split_row(it.k, it.A + row * it.k, nullptr, it.hi + row * it.kp, it.lo + row * it.kp,
+              it.row_scale + row);
+}
+
+}  // namespace
+
+namespace {
+// Both GEMM instantiations may use kSmemBytes of dynamic shared memory (once per device).
+cudaError_t configure_smem() {
+    static std::atomic<unsigned long long> configured{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 64 && (configured.load() >> dev & 1ull)) return cudaSuccess;
+    e = cudaFuncSetAttribute(gemm_q8_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_q8_tc_kernel<true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e == cudaSuccess && dev < 64) configured.fetch_or(1ull << dev);
+    return e;
+}
 }  // namespace
 
 int q8tc_tile_m() { return TBT; }
@@ -388,15 +516,8 @@ cudaError_t launch_split_rows(int m, int k, int kp, const float* A, const float*
 
 cudaError_t launch_gemm_q8_tc(const Q8TcArgs& a, const CUtensorMap& tmHi, const CUtensorMap& tmLo,
                               const CUtensorMap& tmB) {
-    static unsigned configured = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 32 && !(configured & (1u << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q8_tc_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-        if (e != cudaSuccess) return e;
-        configured |= 1u << dev;
-    }
+    cudaError_t e = configure_smem();
+    if (e != cudaSuccess) return e;
     const int tiles = ((a.m + TBT - 1) / TBT) * ((a.n + TBW - 1) / TBW);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(std::max(1, std::min(tiles, a.grid)));
@@ -408,7 +529,30 @@ cudaError_t launch_gemm_q8_tc(const Q8TcArgs& a, const CUtensorMap& tmHi, const 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_q8_tc_kernel, tmHi, tmLo, tmB, a);
+    return cudaLaunchKernelEx(&cfg, gemm_q8_tc_kernel<false>, tmHi, tmLo, tmB, a, Q8TcBatchArgs{});
+}
+
+cudaError_t launch_q8tc_batch(const Q8TcBatchArgs& b) {
+    cudaError_t e = configure_smem();
+    if (e != cudaSuccess) return e;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(b.rows);
+    cfg.blockDim = dim3(kSplitThreads);
+    cfg.stream = b.stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, split_rows_batch_kernel, b);
+    if (e != cudaSuccess) return e;
+    cfg.gridDim = dim3(b.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    // The tensor maps are read from the batch's device memory; these are placeholders.
+    CUtensorMap none;
+    memset(&none, 0, sizeof(none));
+    return cudaLaunchKernelEx(&cfg, gemm_q8_tc_kernel<true>, none, none, none, Q8TcArgs{}, b);
 }
 
 unsigned read_and_clear_q8tc_error() {

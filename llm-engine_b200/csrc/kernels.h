@@ -140,6 +140,36 @@ struct Q8TcArgs {
     cudaStream_t stream = nullptr;
 };
 constexpr int kQ8TcMaxK = 131072;  // 127 * 127 * k < 2^31
+
+// Grouped int8 tcgen05 products (llme_batch_* with m >= 128): one split launch over every
+// product's rows, then one persistent GEMM launch whose CTAs walk their own lists of
+// (product, output tile) units, balanced by work when the batch is created. Everything the
+// kernels read lives in device memory, written once at creation.
+struct Q8TcItem {
+    const float* A;          // m x k fp32
+    float* C;                // m x n fp32
+    const float* scale;      // n
+    int8_t* hi;              // m x kp split rows (batch scratch)
+    int8_t* lo;
+    float* row_scale;        // m
+    int m, n, k, kp;
+    int accumulate;
+    int pad;
+};
+struct Q8TcBatchArgs {
+    int count = 0;
+    int rows = 0;                          // sum of m over the products (split grid)
+    const Q8TcItem* items = nullptr;
+    const int* row_begin = nullptr;        // count + 1 prefix sums of m
+    const CUtensorMap* tmW = nullptr;      // per product: W, box 128 x 128, 128B swizzle
+    const CUtensorMap* tmHi = nullptr;     // per product: hi rows, box 128 x 128, 128B swizzle
+    const CUtensorMap* tmLo = nullptr;
+    const uint2* unit_table = nullptr;     // (product, tile) grouped by CTA
+    const int* cta_begin = nullptr;        // CTA c runs unit_table[cta_begin[c], cta_begin[c+1])
+    int grid = 0;
+    cudaStream_t stream = nullptr;
+};
+cudaError_t launch_q8tc_batch(const Q8TcBatchArgs& b);
 int q8tc_tile_m();
 int q8tc_tile_n();
 cudaError_t launch_split_rows(int m, int k, int kp, const float* A, const float* w, int8_t* hi,
