@@ -820,6 +820,12 @@ int batch_create_tc(llme_batch_t** out, size_t m, size_t count, const llme_q8_pr
     Q8TcBatchArgs& a = b->targs;
     a.count = static_cast<int>(count);
     a.rows = row_begin[count];
+    a.bulk = true;
+    for (size_t i = 0; i < count; ++i) {
+        a.max_k = std::max(a.max_k, static_cast<int>(p[i].k));
+        a.bulk = a.bulk && p[i].k % 4 == 0 && reinterpret_cast<uintptr_t>(p[i].A) % 16 == 0;
+    }
+    a.bulk = a.bulk && static_cast<size_t>(a.max_k) * 4 <= static_cast<size_t>(kQ8TcSplitSmemMax);
     a.items = reinterpret_cast<const Q8TcItem*>(base + items_off);
     a.row_begin = reinterpret_cast<const int*>(base + rows_off);
     a.tmW = reinterpret_cast<const CUtensorMap*>(base);

@@ -120,6 +120,17 @@ __device__ __forceinline__ void tma_load_1d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// Untiled bulk copy global -> shared (both 16-byte aligned, bytes a multiple of 16),
+// completing `bar`'s transaction count.
+__device__ __forceinline__ void bulk_load_g2s(void* dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // Programmatic dependent launch. wait: block until the grids this one depends
 // on have finished and their writes are visible (a no-op when launched
 // without the attribute). launch_dependents: allow the next grid on the

@@ -315,11 +315,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 // into hi / lo int8 rows of pitch kp and a row scale (see the file comment). Rows whose
 // largest magnitude is not finite get a NaN row scale, so their outputs are NaN, as an fp32
 // product with that row would be.
-// Aligned rows (k % 4 == 0, 16-byte aligned A and w) are read once: the first
-// kSplitRegs * 4 * kSplitThreads elements stay in registers between the two passes (all
-// loads issued before the reduction), only a longer row's remainder is read again.
+// Aligned rows (k % 4 == 0, 16-byte aligned A and w) that fit the launch's dynamic shared
+// memory arrive with one bulk copy (cp.async.bulk) and both passes read shared memory: one
+// instruction per row keeps the whole row in flight. Other aligned rows keep the first
+// kSplitRegs * 4 * kSplitThreads elements in registers between the passes (a longer row's
+// remainder is read twice); unaligned rows take plain scalar loads.
 constexpr int kSplitThreads = 256;
-constexpr int kSplitRegs = 12;  // float4 per thread: rows up to 12288 elements in registers
+constexpr int kSplitRegs = 12;      // float4 per thread in the register path
+constexpr int kSplitSmemMax = kQ8TcSplitSmemMax;  // rows up to 49152 elements by bulk copy
+__device__ unsigned int g_split_error;
 
 struct SplitRow {
     float inv_rms, q, pre;
@@ -360,29 +364,50 @@ __device__ __forceinline__ void split_accumulate(float4 v, float4 g, bool norm, 
 }
 
 // Splits one row `in` (k floats) into oh / ol and writes its scale to *rs_out. Whole CTA.
+// Bulk: the launch guarantees every row is aligned and fits `srow` (the dynamic shared
+// memory); the generic form takes any row. Two instantiations, so the bulk kernel does not
+// carry the register path's registers.
+template <bool Bulk>
 __device__ __forceinline__ void split_row(int k, const float* __restrict__ in,
                                           const float* __restrict__ w, int8_t* __restrict__ oh,
-                                          int8_t* __restrict__ ol, float* __restrict__ rs_out) {
+                                          int8_t* __restrict__ ol, float* __restrict__ rs_out,
+                                          float* srow) {
     __shared__ float red_ss[kSplitThreads / 32], red_mx[kSplitThreads / 32];
+    __shared__ uint64_t row_bar;
     const bool norm = w != nullptr;
-    const bool vec = (k & 3) == 0 && (reinterpret_cast<uintptr_t>(in) & 15) == 0 &&
-                     (!norm || (reinterpret_cast<uintptr_t>(w) & 15) == 0);
+    const bool vec = Bulk || ((k & 3) == 0 && (reinterpret_cast<uintptr_t>(in) & 15) == 0 &&
+                              (!norm || (reinterpret_cast<uintptr_t>(w) & 15) == 0));
+    constexpr bool bulk = Bulk;
     constexpr int kStride = kSplitThreads * 4;
     const float4 one = make_float4(1.f, 1.f, 1.f, 1.f);
     // The norm weights are shared by every row (cached), so they are loaded where used rather
     // than held in registers.
     auto wload = [&](int j) { return norm ? *reinterpret_cast<const float4*>(w + j) : one; };
-    float4 v[kSplitRegs];
+    float4 v[Bulk ? 1 : kSplitRegs];
     // Pass 1: sum of squares (for the norm) and the largest |a * w| (or |a|).
     float ss = 0.0f, mx = 0.0f;
-    if (vec) {
+    bool landed = true;
+    if constexpr (bulk) {
+        if (threadIdx.x == 0) {
+            mbar_init(&row_bar, 1);
+            fence_mbar_init();
+            mbar_arrive_expect_tx(&row_bar, static_cast<uint32_t>(k) * 4);
+            bulk_load_g2s(srow, in, static_cast<uint32_t>(k) * 4, &row_bar);
+        }
+        __syncthreads();  // the barrier is initialised before anyone waits on it
+        landed = mbar_wait(&row_bar, 0, &g_split_error);
+        if (landed) {
+            for (int j = threadIdx.x * 4; j < k; j += kStride)
+                split_accumulate(*reinterpret_cast<const float4*>(srow + j), wload(j), norm, &ss, &mx);
+        }
+    } else if (vec) {
 #pragma unroll
-        for (int r = 0; r < kSplitRegs; ++r) {
+        for (int r = 0; r < (Bulk ? 0 : kSplitRegs); ++r) {
             const int j = r * kStride + threadIdx.x * 4;
             v[r] = j < k ? *reinterpret_cast<const float4*>(in + j) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
-        for (int r = 0; r < kSplitRegs; ++r) {
+        for (int r = 0; r < (Bulk ? 0 : kSplitRegs); ++r) {
             const int j = r * kStride + threadIdx.x * 4;
             if (j < k) split_accumulate(v[r], wload(j), norm, &ss, &mx);
         }
@@ -430,9 +455,14 @@ __device__ __forceinline__ void split_row(int k, const float* __restrict__ in,
         *rs_out = s;
     }
     // Pass 2: hi / lo.
-    if (vec) {
+    if constexpr (bulk) {
+        if (landed) {
+            for (int j = threadIdx.x * 4; j < k; j += kStride)
+                sr.split4(*reinterpret_cast<const float4*>(srow + j), wload(j), oh + j, ol + j);
+        }
+    } else if (vec) {
 #pragma unroll
-        for (int r = 0; r < kSplitRegs; ++r) {
+        for (int r = 0; r < (Bulk ? 0 : kSplitRegs); ++r) {
             const int j = r * kStride + threadIdx.x * 4;
             if (j < k) sr.split4(v[r], wload(j), oh + j, ol + j);
         }
@@ -448,19 +478,24 @@ __device__ __forceinline__ void split_row(int k, const float* __restrict__ in,
     }
 }
 
+template <bool Bulk>
 __global__ void __launch_bounds__(kSplitThreads)
     split_rows_kernel(int k, int kp, const float* __restrict__ A, const float* __restrict__ w,
                       int8_t* __restrict__ hi, int8_t* __restrict__ lo,
                       float* __restrict__ row_scale) {
-    pdl_launch_dependents();
+    extern __shared__ __align__(16) float split_smem[];
     pdl_wait();
     const size_t r = blockIdx.x;
-    split_row(k, A + r * k, w, hi + r * kp, lo + r * kp, row_scale + r);
+    split_row<Bulk>(k, A + r * k, w, hi + r * kp, lo + r * kp, row_scale + r, split_smem);
+    // Only now may the GEMM's CTAs (197 KB of shared memory each, waiting for this grid) be
+    // placed: placed earlier they would take SMs that this grid's remaining rows still need.
+    pdl_launch_dependents();
 }
 
 // Grouped: CTA r splits global row r, row r - row_begin[p] of product p.
+template <bool Bulk>
 __global__ void __launch_bounds__(kSplitThreads) split_rows_batch_kernel(const Q8TcBatchArgs b) {
-    pdl_launch_dependents();
+    extern __shared__ __align__(16) float split_smem[];
     pdl_wait();
     const int r = blockIdx.x;
     int lo_p = 0, hi_p = b.count - 1;  // the last p with row_begin[p] <= r
@@ -471,8 +506,9 @@ __global__ void __launch_bounds__(kSplitThreads) split_rows_batch_kernel(const Q
     }
     const Q8TcItem& it = b.items[lo_p];
     const size_t row = static_cast<size_t>(r - b.row_begin[lo_p]);
-    split_row(it.k, it.A + row * it.k, nullptr, it.hi + row * it.kp, it.lo + row * it.kp,
-              it.row_scale + row);
+    split_row<Bulk>(it.k, it.A + row * it.k, nullptr, it.hi + row * it.kp, it.lo + row * it.kp,
+                    it.row_scale + row, split_smem);
+    pdl_launch_dependents();  // as in split_rows_kernel: the GEMM's CTAs only after this row
 }
 
 }  // namespace
@@ -490,6 +526,12 @@ cudaError_t configure_smem() {
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(gemm_q8_tc_kernel<true>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(split_rows_kernel<true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kSplitSmemMax);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(split_rows_batch_kernel<true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kSplitSmemMax);
     if (e == cudaSuccess && dev < 64) configured.fetch_or(1ull << dev);
     return e;
 }
@@ -500,9 +542,16 @@ int q8tc_tile_n() { return TBW; }
 
 cudaError_t launch_split_rows(int m, int k, int kp, const float* A, const float* w, int8_t* hi,
                               int8_t* lo, float* row_scale, cudaStream_t stream, bool pdl) {
+    cudaError_t e = configure_smem();
+    if (e != cudaSuccess) return e;
+    // Bulk copies need 16-byte aligned rows (and norm weights) and a row that fits.
+    const bool bulk = k % 4 == 0 && reinterpret_cast<uintptr_t>(A) % 16 == 0 &&
+                      (w == nullptr || reinterpret_cast<uintptr_t>(w) % 16 == 0) &&
+                      static_cast<size_t>(k) * 4 <= static_cast<size_t>(kSplitSmemMax);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(m);
     cfg.blockDim = dim3(kSplitThreads);
+    cfg.dynamicSmemBytes = bulk ? static_cast<size_t>(k) * 4 : 0;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     if (pdl) {
@@ -511,7 +560,8 @@ cudaError_t launch_split_rows(int m, int k, int kp, const float* A, const float*
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    return cudaLaunchKernelEx(&cfg, split_rows_kernel, k, kp, A, w, hi, lo, row_scale);
+    return bulk ? cudaLaunchKernelEx(&cfg, split_rows_kernel<true>, k, kp, A, w, hi, lo, row_scale)
+                : cudaLaunchKernelEx(&cfg, split_rows_kernel<false>, k, kp, A, w, hi, lo, row_scale);
 }
 
 cudaError_t launch_gemm_q8_tc(const Q8TcArgs& a, const CUtensorMap& tmHi, const CUtensorMap& tmLo,
@@ -541,10 +591,12 @@ cudaError_t launch_q8tc_batch(const Q8TcBatchArgs& b) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(b.rows);
     cfg.blockDim = dim3(kSplitThreads);
+    cfg.dynamicSmemBytes = b.bulk ? static_cast<size_t>(b.max_k) * 4 : 0;
     cfg.stream = b.stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, split_rows_batch_kernel, b);
+    e = b.bulk ? cudaLaunchKernelEx(&cfg, split_rows_batch_kernel<true>, b)
+               : cudaLaunchKernelEx(&cfg, split_rows_batch_kernel<false>, b);
     if (e != cudaSuccess) return e;
     cfg.gridDim = dim3(b.grid);
     cfg.blockDim = dim3(kThreads);
@@ -556,10 +608,12 @@ cudaError_t launch_q8tc_batch(const Q8TcBatchArgs& b) {
 }
 
 unsigned read_and_clear_q8tc_error() {
-    unsigned v = 0, zero = 0;
+    unsigned v = 0, w = 0, zero = 0;
     if (cudaMemcpyFromSymbol(&v, g_q8tc_error, sizeof(v)) != cudaSuccess) return 0;
     if (v) cudaMemcpyToSymbol(g_q8tc_error, &zero, sizeof(zero));
-    return v;
+    if (cudaMemcpyFromSymbol(&w, g_split_error, sizeof(w)) != cudaSuccess) return v;
+    if (w) cudaMemcpyToSymbol(g_split_error, &zero, sizeof(zero));
+    return v | w;
 }
 
 }  // namespace llme

@@ -159,6 +159,8 @@ struct Q8TcItem {
 struct Q8TcBatchArgs {
     int count = 0;
     int rows = 0;                          // sum of m over the products (split grid)
+    int max_k = 0;                         // longest activation row (split shared memory)
+    bool bulk = false;                     // every row aligned and short enough for bulk copies
     const Q8TcItem* items = nullptr;
     const int* row_begin = nullptr;        // count + 1 prefix sums of m
     const CUtensorMap* tmW = nullptr;      // per product: W, box 128 x 128, 128B swizzle
@@ -169,6 +171,7 @@ struct Q8TcBatchArgs {
     int grid = 0;
     cudaStream_t stream = nullptr;
 };
+constexpr int kQ8TcSplitSmemMax = 196608;  // bytes of a row the split pass stages in smem
 cudaError_t launch_q8tc_batch(const Q8TcBatchArgs& b);
 int q8tc_tile_m();
 int q8tc_tile_n();
