@@ -36,7 +36,7 @@ DIM, HIDDEN, VOCAB, LAYERS = 4096, 11008, 32000, 32
 METRIC = "int8 decode-GEMV HBM GB/s (7B-shaped chain, m=1)"
 WORKLOAD_CONFIG = {
     "chain": {"workload": "7B-shaped int8 decode matmul chain, m=1 (BASELINE configs[3])",
-              "dim": DIM, "hidden": HIDDEN, "vocab": VOCAB, "layers": LAYERS,
+              "dim": DIM, "hidden": HIDDEN, "vocab": VOCAB,
               "l2": "no flush: 6.6 GB of weights per step (>> 126 MB L2)"},
     "gemv": {"workload": "decode GEMV m=1, 4096x4096 int8 (BASELINE configs[0]), 16 weight "
                          "copies per step",
@@ -45,10 +45,10 @@ WORKLOAD_CONFIG = {
 UNIT = "GB/s"
 
 
-def chain_shapes():
+def chain_shapes(layers=LAYERS):
     """(name, k, n, row_parallel) for every product of one step, in order."""
     out = []
-    for layer in range(LAYERS):
+    for layer in range(layers):
         for name in ("wq", "wk", "wv"):
             out.append((f"{name}{layer}", DIM, DIM, False))
         out.append((f"wo{layer}", DIM, DIM, True))
@@ -413,11 +413,11 @@ class Prefill:
     U(-1, 1) activation matrix per product. On N GPUs: column-parallel weights split along n,
     row-parallel (wo, w2) along k with a sum all-reduce of the m x 4096 partial outputs."""
 
-    def __init__(self, world, rank, seed=4):
+    def __init__(self, world, rank, seed=4, layers=LAYERS):
         import torch
         import shard
         self.world, self.rank = world, rank
-        self.shapes = chain_shapes()
+        self.shapes = chain_shapes(layers)
         g = torch.Generator(device="cuda")
         ga = torch.Generator(device="cuda")
         ga.manual_seed(seed * 7)
@@ -444,6 +444,11 @@ class Prefill:
         self.flops_total = sum(2.0 * (1 if nm == "cls" else PREFILL_ROWS) * k * n
                                for (nm, k, n, _) in self.shapes)
         self.flops_rank = sum(2.0 * m * kl * nl for (_, _, m, kl, nl, _, _, _) in self.items)
+        # This rank's algorithmic bytes: the GEMMs read W, the hi/lo rows and write C; the
+        # split reads A and writes hi/lo (the classifier GEMV's bytes are in the GEMM share).
+        self.gemm_bytes = sum(kl * nl + 4 * nl + 2 * m * kl + 4 * m * nl
+                              for (_, _, m, kl, nl, _, _, _) in self.items)
+        self.split_bytes = sum(6 * m * kl for (_, _, m, kl, nl, _, _, _) in self.items if m > 1)
         self.a_host = [it[6].cpu().pin_memory() for it in self.items]
         self.c_host = [torch.empty(it[7].shape).pin_memory() for it in self.items]
 
@@ -542,7 +547,7 @@ def run_prefill(args, world, rank, local):
     import torch
     import llme_b200 as L
     L.set_math(L.MATH_TENSOR)
-    pf = Prefill(world, rank)
+    pf = Prefill(world, rank, layers=args.layers)
     stream = torch.cuda.Stream()
     h = stream.cuda_stream
     tp = comm = join = None
@@ -605,7 +610,7 @@ def run_prefill(args, world, rank, local):
                 "U(-1,1) activations",
         "config": {"workload": "7B-shaped batched prefill, m=512, int8 weights (BASELINE "
                                "configs[4]); classifier on the last row",
-                   "rows": PREFILL_ROWS, "products_per_step": len(pf.items),
+                   "layers": args.layers, "rows": PREFILL_ROWS, "products_per_step": len(pf.items),
                    "launches_per_step": launches, "flops_per_step": pf.flops_total,
                    "parallelism": f"tp{world}" if world > 1 else "single",
                    "launch": ("grouped: one split launch + one persistent tcgen05 launch over "
@@ -619,7 +624,14 @@ def run_prefill(args, world, rank, local):
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                      "peak_kind": peak_kind + " (each product is two int8 MMAs, together the "
                                               "bf16 rate)",
-                     "kernel": "gemm_q8_tc_kernel (+ split_rows_kernel)", "traffic": None},
+                     "kernel": "gemm_q8_tc_kernel (+ split_rows_kernel)",
+                     # DRAM read+write bytes of the step's launches: the full ncu capture of the
+                     # same kernels on the 2-layer case measured 1.02 x the GEMM's algorithmic
+                     # bytes (weights read once) and the split's reads exactly; scaled here to
+                     # the step: GEMM (W + hi/lo + C) x 1.02 + split (4mk + 2mk).
+                     "traffic": int(1.02 * pf.gemm_bytes + pf.split_bytes),
+                     "traffic_source": "profiles/gemm_q8_tc_prefill.md (ratio scaled)",
+                     "bytes_per_step": int(pf.gemm_bytes + pf.split_bytes)},
         "e2e": e2e, "gpu_launches": launches * args.steps, "per_call": per_call,
         "clocks": sampler.summary(),
     }
@@ -697,7 +709,7 @@ def run_ours(args):
     if args.workload == "prefill":
         return run_prefill(args, world, rank, local)
     if args.workload == "chain":
-        chain = Chain(world, rank, chain_shapes(), seed=3)
+        chain = Chain(world, rank, chain_shapes(args.layers), seed=3)
     else:
         chain = Chain(world, rank, gemv_shapes(), seed=0)
     comm = tp = None
@@ -777,6 +789,7 @@ def run_ours(args):
                       + " of the wo/w2 partial outputs, on a side stream overlapping the "
                         "column-parallel products") if world > 1 else None),
         "config": WORKLOAD_CONFIG[args.workload] | {
+                   "layers": args.layers if args.workload == "chain" else None,
                    "products_per_step": chain.n_launches(), "launches_per_step": launches,
                    "algorithmic_bytes_per_step": int(chain.total_bytes),
                    "parallelism": f"tp{world}" if world > 1 else "single",
@@ -870,6 +883,9 @@ def main():
                          "sgemm: configs[2] (square TF32 GEMM, --size); prefill: configs[4] "
                          "(m = 512 through the 7B-shaped int8 weights)")
     ap.add_argument("--size", type=int, default=8192, help="N for --workload sgemm")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="layers of the chain / prefill (32 = the BASELINE configs; fewer only "
+                         "for small profiling cases)")
     ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
                     help="N>1: the library's NVLink peer all-reduce (default) or NCCL")
     ap.add_argument("--launch", choices=["grouped", "per_call"], default="grouped",
