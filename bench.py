@@ -69,6 +69,7 @@ def algorithmic_bytes(k, n, m=1):
 class ClockSampler:
     def __init__(self, device_index: int):
         self.samples, self.reasons = [], set()
+        self.raw = 0  # union of the raw NVML clocks-event-reason bits seen
         self.max_mhz = None
         self._stop = threading.Event()
         self._thread = None
@@ -92,6 +93,7 @@ class ClockSampler:
             try:
                 self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
                 r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.raw |= r
                 for k, bit in names.items():
                     if r & bit and k != "gpu_idle":
                         self.reasons.add(k)
@@ -113,7 +115,7 @@ class ClockSampler:
     def summary(self):
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
                 "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
-                "reasons": sorted(self.reasons)}
+                "reasons": sorted(self.reasons), "reason_bits": hex(self.raw & ~0x1)}
 
 
 # ---- distributed plumbing -----------------------------------------------------------------

@@ -74,6 +74,16 @@ struct PlanIn {
     int math;
 };
 
+// The int8 tcgen05 GEMM on CTA pairs (one M=256 MMA over two SMs, 256-column tiles) only when
+// LLME_B200_CTA_PAIRS=1 and the SM count is even. Measured on B200 under the 1 kW power cap:
+// pairs do ~3% more work per clock but draw more power per unit of work, so the sustained
+// clock settles ~15% lower (7B prefill: 910 TFLOP/s at 1.16 GHz with pairs, 1030 at 1.37 GHz
+// without); short bursts below the cap run faster on pairs (4096x8192x8192: 1384 vs 1336).
+bool q8tc_use_pairs(int sms) {
+    const char* v = getenv("LLME_B200_CTA_PAIRS");
+    return v && v[0] == '1' && sms >= 2 && sms % 2 == 0;
+}
+
 // int8 tcgen05 GEMM scratch: hi rows, lo rows (pitch round_up(k, 16), each region 256-byte
 // aligned), then the m row scales.
 size_t q8tc_pitch(size_t k) { return round_up(k, 16); }
@@ -181,10 +191,14 @@ int make_plan(const PlanIn& in, llme_plan_t* p) {
         p->path = LLME_PATH_TCGEN05_Q8;
         p->rms_prepass = 0;
         p->norm_bytes = 0;
+        // CTA pairs (cta_group::2) whenever the SMs pair up; grid_x counts CTAs, cluster 2.
+        const bool pair = q8tc_use_pairs(sms);
         p->tile_m = q8tc_tile_m();
-        p->tile_n = q8tc_tile_n();
+        p->tile_n = q8tc_tile_n(pair);
         const size_t tiles = ceil_div(m, p->tile_m) * ceil_div(n, p->tile_n);
-        p->grid_x = static_cast<int>(std::min<size_t>(tiles, static_cast<size_t>(sms)));
+        const size_t slots = std::min<size_t>(tiles, static_cast<size_t>(pair ? sms / 2 : sms));
+        p->grid_x = static_cast<int>(slots * (pair ? 2 : 1));
+        p->cluster = pair ? 2 : 1;
         p->grid_y = 1;
         p->slices = 1;
         p->span = static_cast<int>(k);
@@ -553,7 +567,8 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
         t.row_scale = rs;
         t.C = C;
         t.accumulate = accumulate;
-        t.grid = p.grid_x;
+        t.pair = p.cluster == 2;
+        t.slots = p.grid_x / p.cluster;
         t.stream = stream;
         e = launch_gemm_q8_tc(t, tmHi, tmLo, tmB);
     } else {
@@ -705,6 +720,12 @@ int batch_create_tc(llme_batch_t** out, size_t m, size_t count, const llme_q8_pr
                     "llme_batch_q8_create: m >= 128 runs on the tensor cores (LLME_MATH_TENSOR)");
     if (m * count > (size_t{1} << 30))
         return fail(LLME_E_INVALID, "llme_batch_q8_create: more than 2^30 rows in all");
+    int dev = 0, sms = 0;
+    int st = current_device(&dev);
+    if (st) return st;
+    st = device_sms(dev, &sms);
+    if (st) return st;
+    const bool pair = q8tc_use_pairs(sms);
     const size_t tm = ceil_div(m, static_cast<size_t>(q8tc_tile_m()));
     std::vector<Q8TcItem> items(count);
     std::vector<size_t> scratch_off(count);
@@ -728,19 +749,14 @@ int batch_create_tc(llme_batch_t** out, size_t m, size_t count, const llme_q8_pr
         scratch_bytes += q8tc_operand_bytes(m, q.k);
         scratch_bytes = round_up(scratch_bytes, 256);
         row_begin[i + 1] = row_begin[i] + static_cast<int>(m);
-        const size_t tiles = tm * ceil_div(q.n, static_cast<size_t>(q8tc_tile_n()));
+        const size_t tiles = tm * ceil_div(q.n, static_cast<size_t>(q8tc_tile_n(pair)));
         for (size_t t = 0; t < tiles; ++t) {
             units.push_back(make_uint2(static_cast<unsigned>(i), static_cast<unsigned>(t)));
             // Work of a tile: its k-blocks plus about two for the epilogue.
             work.push_back(ceil_div(q.k, size_t{128}) + 2);
         }
     }
-    int dev = 0, sms = 0;
-    int st = current_device(&dev);
-    if (st) return st;
-    st = device_sms(dev, &sms);
-    if (st) return st;
-    const int grid = static_cast<int>(std::min<size_t>(units.size(), sms));
+    const int grid = static_cast<int>(std::min<size_t>(units.size(), pair ? sms / 2 : sms));
     const auto per_cta = lpt_assign(work, grid);
     std::vector<uint2> table;
     std::vector<int> cta_begin(grid + 1, 0);
@@ -833,7 +849,8 @@ int batch_create_tc(llme_batch_t** out, size_t m, size_t count, const llme_q8_pr
     a.tmLo = reinterpret_cast<const CUtensorMap*>(base + 2 * maps_bytes);
     a.unit_table = reinterpret_cast<const uint2*>(base + table_off);
     a.cta_begin = reinterpret_cast<const int*>(base + begin_off);
-    a.grid = grid;
+    a.pair = pair;
+    a.slots = grid;
     *out = b;
     return LLME_OK;
 }

@@ -80,6 +80,32 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
     }
 }
 
+// As mbar_wait, with cluster-scope acquire: for barriers that the other CTA of a cluster
+// arrives on.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  unsigned int* err) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const unsigned long long t0 = global_timer_ns();
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((i & 63) == 63 && global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicExch(err, static_cast<unsigned int>(LLME_E_TIMEOUT));
+            return false;
+        }
+    }
+}
+
 // L2 policy for data read exactly once (weights streamed by the GEMV).
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     uint64_t p;

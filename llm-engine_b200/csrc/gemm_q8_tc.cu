@@ -64,12 +64,21 @@ constexpr int TBK = 128;   // k per stage: 128 int8 = one 128-byte swizzle row
 constexpr int kThreads = 192;
 constexpr int kWBytes = TBK * TBW;      // 16 KB
 constexpr int kRowBytes = TBT * TBK;    // 16 KB each for hi and lo
-constexpr int kStageBytes = kWBytes + 2 * kRowBytes;
-constexpr int kStages = 4;
 constexpr int kAccCols = 2 * TBT;       // 256
 constexpr int kAccBufs = 2;
-constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
+constexpr int kRingBudget = 196608;
 constexpr int kGroupT = 8;              // row tiles that share each W panel (L2 reuse)
+
+// One CTA: a stage holds the W panel, the hi rows and the lo rows (48 KB, 4 stages).
+// A CTA pair (Pair): each CTA holds its 128-column half of a 256-column W panel and one of
+// hi (even CTA) / lo (odd CTA) (32 KB, 6 stages); one M=256 N=256 MMA over both.
+template <bool Pair>
+struct Geo {
+    static constexpr int kStageBytes = Pair ? kWBytes + kRowBytes : kWBytes + 2 * kRowBytes;
+    static constexpr int kStages = kRingBudget / kStageBytes;
+    static constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
+    static constexpr int kTileW = Pair ? 2 * TBW : TBW;  // output columns per unit
+};
 
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                        uint32_t idesc, uint32_t accumulate) {
@@ -117,14 +126,18 @@ struct Unit {
 
 // The i-th unit of this CTA. Single product: tiles blockIdx.x + i * gridDim.x. Grouped: the
 // CTA's own list from the batch's unit table.
-template <bool G>
+template <bool G, bool Pair>
 __device__ __forceinline__ bool fetch_unit(int i, const CUtensorMap* tmHi, const CUtensorMap* tmLo,
                                            const CUtensorMap* tmB, const Q8TcArgs& a,
                                            const Q8TcBatchArgs& b, Unit& u) {
+    // Scheduling slot: the CTA, or the CTA pair (both CTAs of a pair walk the same units).
+    const int slot = Pair ? blockIdx.x >> 1 : blockIdx.x;
+    const int slots = Pair ? gridDim.x >> 1 : gridDim.x;
+    constexpr int kTileW = Geo<Pair>::kTileW;
     int t, m, n, k;
     if constexpr (G) {
-        const int idx = b.cta_begin[blockIdx.x] + i;
-        if (idx >= b.cta_begin[blockIdx.x + 1]) return false;
+        const int idx = b.cta_begin[slot] + i;
+        if (idx >= b.cta_begin[slot + 1]) return false;
         const uint2 e = b.unit_table[idx];
         const Q8TcItem& it = b.items[e.x];
         t = static_cast<int>(e.y);
@@ -142,8 +155,8 @@ __device__ __forceinline__ bool fetch_unit(int i, const CUtensorMap* tmHi, const
         m = a.m;
         n = a.n;
         k = a.k;
-        t = blockIdx.x + i * gridDim.x;
-        if (t >= ((m + TBT - 1) / TBT) * ((n + TBW - 1) / TBW)) return false;
+        t = slot + i * slots;
+        if (t >= ((m + TBT - 1) / TBT) * ((n + kTileW - 1) / kTileW)) return false;
         u.w = tmB;
         u.hi = tmHi;
         u.lo = tmLo;
@@ -155,16 +168,28 @@ __device__ __forceinline__ bool fetch_unit(int i, const CUtensorMap* tmHi, const
     u.m = m;
     u.n = n;
     u.nk = (k + TBK - 1) / TBK;
-    tile_coords(t, (m + TBT - 1) / TBT, (n + TBW - 1) / TBW, &u.tt, &u.tw);
+    tile_coords(t, (m + TBT - 1) / TBT, (n + kTileW - 1) / kTileW, &u.tt, &u.tw);
     return true;
 }
 
-template <bool G>
+__device__ __forceinline__ void mma_i8_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+template <bool G, bool Pair>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_q8_tc_kernel(const __grid_constant__ CUtensorMap tmHi,
                       const __grid_constant__ CUtensorMap tmLo,
                       const __grid_constant__ CUtensorMap tmB, const Q8TcArgs a,
                       const Q8TcBatchArgs b) {
+    using Gm = Geo<Pair>;
+    constexpr int kStages = Gm::kStages;
+    constexpr int kStageBytes = Gm::kStageBytes;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
@@ -175,15 +200,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // Pair: rank 0 issues the MMAs and holds the full barriers (its loads and the peer's are
+    // counted there); each CTA's empty / accumulator-full barriers are signalled by rank 0's
+    // commits; rank 0's accumulator-empty barriers count the epilogue warps of both CTAs.
+    const uint32_t rank = Pair ? tc::cluster_rank() : 0;
+    auto in_cta = [](const void* p, uint32_t r) { return tc::map_to_cta(smem_u32(p), r); };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < kAccBufs; ++b) {
-            mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+        for (int bf = 0; bf < kAccBufs; ++bf) {
+            mbar_init(&acc_full[bf], 1);
+            mbar_init(&acc_empty[bf], Pair ? 8 : 4);  // one arrival per epilogue warp
         }
         mbar_init(drain, 1);
         fence_mbar_init();
@@ -193,9 +223,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             prefetch_tensormap(&tmB);
         }
     }
-    if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
+    if (warp == 1) {
+        if constexpr (Pair) tc::tmem_alloc_pair(tmem_slot, 512);
+        else tc::tmem_alloc(tmem_slot, 512);
+    }
     tc::fence_before_sync();
     __syncthreads();
+    if constexpr (Pair) tc::pair_sync();  // both CTAs' barriers and TMEM exist
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
@@ -205,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int it = 0;
             bool ok = true;
             Unit u;
-            for (int i = 0; ok && fetch_unit<G>(i, &tmHi, &tmLo, &tmB, a, b, u); ++i) {
+            for (int i = 0; ok && fetch_unit<G, Pair>(i, &tmHi, &tmLo, &tmB, a, b, u); ++i) {
                 for (int kb = 0; kb < u.nk; ++kb, ++it) {
                     const int s = it % kStages;
                     if (it >= kStages &&
@@ -214,28 +248,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     uint8_t* st = smem + s * kStageBytes;
-                    mbar_arrive_expect_tx(&full[s], kStageBytes);
-                    tma_load_2d_nohint(st, u.w, u.tw * TBW, kb * TBK, &full[s]);
-                    tma_load_2d_nohint(st + kWBytes, u.hi, kb * TBK, u.tt * TBT, &full[s]);
-                    tma_load_2d_nohint(st + kWBytes + kRowBytes, u.lo, kb * TBK, u.tt * TBT,
-                                       &full[s]);
+                    if constexpr (Pair) {
+                        const uint32_t fb = in_cta(&full[s], 0);
+                        if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * kStageBytes);
+                        tc::tma_load_2d_pair(st, u.w, u.tw * Gm::kTileW + rank * TBW, kb * TBK, fb);
+                        tc::tma_load_2d_pair(st + kWBytes, rank == 0 ? u.hi : u.lo, kb * TBK,
+                                             u.tt * TBT, fb);
+                    } else {
+                        mbar_arrive_expect_tx(&full[s], kStageBytes);
+                        tma_load_2d_nohint(st, u.w, u.tw * TBW, kb * TBK, &full[s]);
+                        tma_load_2d_nohint(st + kWBytes, u.hi, kb * TBK, u.tt * TBT, &full[s]);
+                        tma_load_2d_nohint(st + kWBytes + kRowBytes, u.lo, kb * TBK, u.tt * TBT,
+                                           &full[s]);
+                    }
                 }
             }
-            // Before the CTA may exit, every copy issued into its shared memory has landed
-            // (already true unless a wait above gave up).
-            for (int j = it - 1; j >= 0 && j >= it - kStages; --j)
-                mbar_wait(&full[j % kStages], (j / kStages) & 1, &g_q8tc_error);
+            // Before the CTA (pair) may exit, every copy issued into its shared memory has
+            // landed (already true unless a wait above gave up). A pair's copies are all
+            // counted on rank 0's full barriers; the final pair_sync keeps rank 1 until then.
+            if (rank == 0) {
+                for (int j = it - 1; j >= 0 && j >= it - kStages; --j)
+                    mbar_wait(&full[j % kStages], (j / kStages) & 1, &g_q8tc_error);
+            }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_i8(TBW, 2 * TBT);
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_i8(Pair ? 2 * TBW : TBW, 2 * TBT);
             int it = 0, use = 0;
             bool ok = true;
             Unit u;
-            for (; ok && fetch_unit<G>(use, &tmHi, &tmLo, &tmB, a, b, u); ++use) {
+            for (; ok && fetch_unit<G, Pair>(use, &tmHi, &tmLo, &tmB, a, b, u); ++use) {
                 const int buf = use % kAccBufs;
                 const int round = use / kAccBufs;
-                if (round > 0 && !mbar_wait(&acc_empty[buf], (round - 1) & 1, &g_q8tc_error)) break;
+                if (round > 0) {
+                    const bool freed = Pair ? mbar_wait_cluster(&acc_empty[buf], (round - 1) & 1,
+                                                                &g_q8tc_error)
+                                            : mbar_wait(&acc_empty[buf], (round - 1) & 1,
+                                                        &g_q8tc_error);
+                    if (!freed) break;
+                }
                 tc::fence_after_sync();
                 const uint32_t d = tmem + buf * kAccCols;
                 for (int kb = 0; kb < u.nk; ++kb, ++it) {
@@ -250,29 +301,46 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < TBK / 32; ++kk) {
                         // W: MN-major, 32 k-rows of 128 bytes per K step. Rows: K-major,
-                        // the 32-deep K step is 32 bytes into each 128-byte row.
-                        mma_i8(d, tc::smem_desc_sw128(wp + kk * 32 * 128, kWBytes, 1024),
-                               tc::smem_desc_sw128(rows + kk * 32, 16, 1024), idesc,
-                               (kb | kk) != 0 ? 1u : 0u);
+                        // the 32-deep K step is 32 bytes into each 128-byte row. A pair's
+                        // descriptors name this CTA's halves; the peer's sit at the same
+                        // offsets in its own shared memory.
+                        const uint64_t ad = tc::smem_desc_sw128(wp + kk * 32 * 128, kWBytes, 1024);
+                        const uint64_t bd = tc::smem_desc_sw128(rows + kk * 32, 16, 1024);
+                        const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
+                        if constexpr (Pair) mma_i8_pair(d, ad, bd, idesc, acc);
+                        else mma_i8(d, ad, bd, idesc, acc);
                     }
-                    tc::commit(&empty[s]);
+                    if constexpr (Pair) {
+                        tc::commit_pair(in_cta(&empty[s], 0));
+                        tc::commit_pair(in_cta(&empty[s], 1));
+                    } else {
+                        tc::commit(&empty[s]);
+                    }
                 }
-                tc::commit(&acc_full[buf]);
+                if constexpr (Pair) {
+                    tc::commit_pair(in_cta(&acc_full[buf], 0));
+                    tc::commit_pair(in_cta(&acc_full[buf], 1));
+                } else {
+                    tc::commit(&acc_full[buf]);
+                }
             }
             // No MMA may still be writing TMEM when it is released.
-            tc::commit(drain);
+            if constexpr (Pair) tc::commit_pair(in_cta(drain, 0));
+            else tc::commit(drain);
             mbar_wait(drain, 0, &g_q8tc_error);
         }
     } else {
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         pdl_wait();              // C may be read by the kernel before this one
         Unit u;
-        for (int use = 0; fetch_unit<G>(use, &tmHi, &tmLo, &tmB, a, b, u); ++use) {
+        for (int use = 0; fetch_unit<G, Pair>(use, &tmHi, &tmLo, &tmB, a, b, u); ++use) {
             const int buf = use % kAccBufs;
             const int round = use / kAccBufs;
-            if (!mbar_wait(&acc_full[buf], round & 1, &g_q8tc_error)) break;
+            const bool ready = Pair ? mbar_wait_cluster(&acc_full[buf], round & 1, &g_q8tc_error)
+                                    : mbar_wait(&acc_full[buf], round & 1, &g_q8tc_error);
+            if (!ready) break;
             tc::fence_after_sync();
-            const int col = u.tw * TBW + q * 32 + lane;
+            const int col = u.tw * Gm::kTileW + static_cast<int>(rank) * TBW + q * 32 + lane;
             const bool col_ok = col < u.n;
             const float sc = col_ok ? u.scale[col] : 0.0f;
             const uint32_t base = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * kAccCols;
@@ -299,15 +367,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             // This warp's reads of the buffer are complete (tcgen05.ld waits inside the helper).
             tc::fence_before_sync();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+            if (lane == 0) {
+                if constexpr (Pair) tc::mbar_arrive_cluster(in_cta(&acc_empty[buf], 0));
+                else mbar_arrive(&acc_empty[buf]);
+            }
         }
     }
     tc::fence_before_sync();
     __syncthreads();
+    if constexpr (Pair) tc::pair_sync();  // rank 0's MMAs drained, both epilogues done
     if (warp == 1) {
         __syncwarp();
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, 512);
+        if constexpr (Pair) tc::tmem_dealloc_pair(tmem, 512);
+        else tc::tmem_dealloc(tmem, 512);
     }
 }
 
@@ -521,11 +594,17 @@ cudaError_t configure_smem() {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 64 && (configured.load() >> dev & 1ull)) return cudaSuccess;
-    e = cudaFuncSetAttribute(gemm_q8_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemBytes);
+    e = cudaFuncSetAttribute(gemm_q8_tc_kernel<false, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<false>::kSmemBytes);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemm_q8_tc_kernel<true>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        e = cudaFuncSetAttribute(gemm_q8_tc_kernel<true, false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<false>::kSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_q8_tc_kernel<false, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<true>::kSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_q8_tc_kernel<true, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<true>::kSmemBytes);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(split_rows_kernel<true>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kSplitSmemMax);
@@ -538,7 +617,33 @@ cudaError_t configure_smem() {
 }  // namespace
 
 int q8tc_tile_m() { return TBT; }
-int q8tc_tile_n() { return TBW; }
+int q8tc_tile_n(bool pair) { return pair ? 2 * TBW : TBW; }
+
+namespace {
+// The GEMM launch (G: grouped): `slots` scheduling slots, each one CTA or (pair) a cluster of
+// two CTAs; PDL after the split launch.
+template <bool G>
+cudaError_t launch_gemm(int slots, bool pair, cudaStream_t stream, const CUtensorMap& tmHi,
+                        const CUtensorMap& tmLo, const CUtensorMap& tmB, const Q8TcArgs& a,
+                        const Q8TcBatchArgs& b) {
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = pair ? 2 : 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(slots * (pair ? 2 : 1));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = pair ? Geo<true>::kSmemBytes : Geo<false>::kSmemBytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = pair ? 2 : 1;
+    return pair ? cudaLaunchKernelEx(&cfg, gemm_q8_tc_kernel<G, true>, tmHi, tmLo, tmB, a, b)
+                : cudaLaunchKernelEx(&cfg, gemm_q8_tc_kernel<G, false>, tmHi, tmLo, tmB, a, b);
+}
+}  // namespace
 
 cudaError_t launch_split_rows(int m, int k, int kp, const float* A, const float* w, int8_t* hi,
                               int8_t* lo, float* row_scale, cudaStream_t stream, bool pdl) {
@@ -568,18 +673,10 @@ cudaError_t launch_gemm_q8_tc(const Q8TcArgs& a, const CUtensorMap& tmHi, const 
                               const CUtensorMap& tmB) {
     cudaError_t e = configure_smem();
     if (e != cudaSuccess) return e;
-    const int tiles = ((a.m + TBT - 1) / TBT) * ((a.n + TBW - 1) / TBW);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(std::max(1, std::min(tiles, a.grid)));
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemBytes;
-    cfg.stream = a.stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_q8_tc_kernel<false>, tmHi, tmLo, tmB, a, Q8TcBatchArgs{});
+    const int tile_w = q8tc_tile_n(a.pair);
+    const int tiles = ((a.m + TBT - 1) / TBT) * ((a.n + tile_w - 1) / tile_w);
+    return launch_gemm<false>(std::max(1, std::min(tiles, a.slots)), a.pair, a.stream, tmHi, tmLo,
+                              tmB, a, Q8TcBatchArgs{});
 }
 
 cudaError_t launch_q8tc_batch(const Q8TcBatchArgs& b) {
@@ -598,13 +695,10 @@ cudaError_t launch_q8tc_batch(const Q8TcBatchArgs& b) {
     e = b.bulk ? cudaLaunchKernelEx(&cfg, split_rows_batch_kernel<true>, b)
                : cudaLaunchKernelEx(&cfg, split_rows_batch_kernel<false>, b);
     if (e != cudaSuccess) return e;
-    cfg.gridDim = dim3(b.grid);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemBytes;
     // The tensor maps are read from the batch's device memory; these are placeholders.
     CUtensorMap none;
     memset(&none, 0, sizeof(none));
-    return cudaLaunchKernelEx(&cfg, gemm_q8_tc_kernel<true>, none, none, none, Q8TcArgs{}, b);
+    return launch_gemm<true>(b.slots, b.pair, b.stream, none, none, none, Q8TcArgs{}, b);
 }
 
 unsigned read_and_clear_q8tc_error() {

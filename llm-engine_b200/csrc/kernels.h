@@ -136,7 +136,8 @@ struct Q8TcArgs {
     const float* row_scale = nullptr;  // m row scales from split_rows
     float* C = nullptr;
     bool accumulate = false;
-    int grid = 0;                      // persistent CTAs (at most the tile count)
+    bool pair = false;                 // CTA pairs (cta_group::2 MMAs, 256-column tiles)
+    int slots = 0;                     // persistent CTAs or pairs (at most the tile count)
     cudaStream_t stream = nullptr;
 };
 constexpr int kQ8TcMaxK = 131072;  // 127 * 127 * k < 2^31
@@ -167,14 +168,15 @@ struct Q8TcBatchArgs {
     const CUtensorMap* tmHi = nullptr;     // per product: hi rows, box 128 x 128, 128B swizzle
     const CUtensorMap* tmLo = nullptr;
     const uint2* unit_table = nullptr;     // (product, tile) grouped by CTA
-    const int* cta_begin = nullptr;        // CTA c runs unit_table[cta_begin[c], cta_begin[c+1])
-    int grid = 0;
+    const int* cta_begin = nullptr;        // slot c runs unit_table[cta_begin[c], cta_begin[c+1])
+    bool pair = false;                     // slots are CTA pairs (cta_group::2)
+    int slots = 0;                         // CTAs, or CTA pairs
     cudaStream_t stream = nullptr;
 };
 constexpr int kQ8TcSplitSmemMax = 196608;  // bytes of a row the split pass stages in smem
 cudaError_t launch_q8tc_batch(const Q8TcBatchArgs& b);
 int q8tc_tile_m();
-int q8tc_tile_n();
+int q8tc_tile_n(bool pair);          // output columns per tile: 128, or 256 for CTA pairs
 cudaError_t launch_split_rows(int m, int k, int kp, const float* A, const float* w, int8_t* hi,
                               int8_t* lo, float* row_scale, cudaStream_t stream, bool pdl);
 cudaError_t launch_gemm_q8_tc(const Q8TcArgs& a, const CUtensorMap& tmHi, const CUtensorMap& tmLo,

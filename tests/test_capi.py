@@ -146,7 +146,19 @@ def test_tcgen05_q8_path_choice():
     # int8 weights, m >= 128, tensor math: kind::i8 tensor cores on the split activations.
     p = L.plan(512, 4096, 4096, q8=True)
     assert p["path_name"] == "tcgen05_q8" and p["kernel"] == 2      # automatic -> tiled
-    assert p["tile_m"] == 128 and p["tile_n"] == 128 and p["grid_x"] == 128
+    assert p["tile_m"] == 128 and p["tile_n"] == 128 and p["cluster"] == 1
+    assert p["grid_x"] == 128
+
+
+def test_tcgen05_q8_cta_pairs_plan(monkeypatch):
+    # LLME_B200_CTA_PAIRS=1: cta_group::2, 128 x 256 tiles, 4 x 16 of them on 64 pairs.
+    monkeypatch.setenv("LLME_B200_CTA_PAIRS", "1")
+    p = L.plan(512, 4096, 4096, q8=True)
+    assert p["tile_n"] == 256 and p["cluster"] == 2 and p["grid_x"] == 128
+    assert L.plan(2048, 8192, 4096, q8=True)["grid_x"] == 148
+    # an odd SM count keeps single CTAs with 128 x 128 tiles
+    p1 = L.plan(512, 4096, 4096, q8=True, sm_count=147)
+    assert p1["tile_n"] == 128 and p1["cluster"] == 1 and p1["grid_x"] == 128
     kp = 4096
     assert p["operand_bytes"] == 2 * ((512 * kp + 255) // 256 * 256) + 512 * 4
     p = L.plan(130, 1040, 72, q8=True, rms_addr=256)

@@ -72,8 +72,11 @@ def test_batch_rejects_ragged_rows():
 TC_SHAPES = [(512, 512), (1000, 272), (2048, 1040), (4100, 48), (300, 4096), (4096, 4096)]
 
 
+@pytest.mark.parametrize("pairs", ["0", "1"])
 @pytest.mark.parametrize("m", [128, 200, 512])
-def test_tc_batch_matches_single_calls_bit_for_bit(m):
+def test_tc_batch_matches_single_calls_bit_for_bit(m, pairs, monkeypatch):
+    # pairs = "1": the batch and the single calls run on CTA pairs (cta_group::2).
+    monkeypatch.setenv("LLME_B200_CTA_PAIRS", pairs)
     rng = np.random.default_rng(200 + m)
     prev = L.set_math(L.MATH_TENSOR)
     try:

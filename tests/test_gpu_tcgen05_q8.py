@@ -9,8 +9,12 @@ Three checks per shape:
 * bit for bit against a numpy restatement of the kernel's own arithmetic (the split of each
   row, exact integer sums, the rounded epilogue), for rows without RMSNorm;
 * repeats bit-identical.
+Each test runs with single CTAs (the default) and with CTA pairs (cta_group::2), which must
+give the same bits.
 """
 from __future__ import annotations
+
+import os
 
 import numpy as np
 import pytest
@@ -77,11 +81,18 @@ def run(A, q8, scale, C0=None, accumulate=False, rms=None, kernel="tiled"):
     return dC.cpu().numpy()
 
 
-@pytest.fixture(scope="module", autouse=True)
-def _tensor_math():
+@pytest.fixture(scope="module", autouse=True, params=["single", "pairs"])
+def _tensor_math(request):
+    """Every test twice: single CTAs (default) and CTA pairs (LLME_B200_CTA_PAIRS=1)."""
     L.load()
     prev = L.set_math(L.MATH_TENSOR)
+    old = os.environ.get("LLME_B200_CTA_PAIRS")
+    os.environ["LLME_B200_CTA_PAIRS"] = "1" if request.param == "pairs" else "0"
     yield
+    if old is None:
+        del os.environ["LLME_B200_CTA_PAIRS"]
+    else:
+        os.environ["LLME_B200_CTA_PAIRS"] = old
     L.set_math(prev)
     L.device_status()
 
