@@ -155,14 +155,10 @@ def max_over_ranks(x: float, world: int) -> float:
 # ---- the chain on the GPU -----------------------------------------------------------------
 
 def quantize_on_device(W):
-    """Synthetic-weight preparation (not timed): per-column symmetric int8 with the rule of the
-    reference's quant.cpp:6-28 (scale = max|col| / 127, round half away from zero, clamp)."""
-    import torch
-    scale = W.abs().amax(dim=0) / 127.0
-    inv = torch.where(scale > 0, 1.0 / scale, torch.zeros_like(scale))
-    x = W * inv
-    q = torch.sign(x) * torch.floor(x.abs() + 0.5)
-    return q.clamp_(-127, 127).to(torch.int8), scale.float()
+    """Synthetic-weight preparation (not timed): the library's GPU quantiser, bit for bit the
+    reference's quantize_q8 (quant.cpp:6-28)."""
+    import llme_b200 as L
+    return L.quantize_q8(W.contiguous())
 
 
 def gemv_shapes(copies=16):

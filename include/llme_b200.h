@@ -141,6 +141,14 @@ int llme_free(void* ptr);                      /* cudaFree; NULL is fine */
 int llme_copy_to_device(void* dst, const void* src, size_t bytes);   /* waits */
 int llme_copy_to_host(void* dst, const void* src, size_t bytes);     /* waits */
 
+/* ---- int8 weight quantisation on the GPU --------------------------------------------------- *
+ * Replaces the reference's CPU quantize_q8 (src/quant.h:6, src/quant.cpp:6-28) for weights
+ * already in device memory, with the same result bit for bit: W is k x n fp32 row-major;
+ * scale[c] = max_r |W[r][c]| / 127 (n floats), q[r][c] = clamp(lround(W[r][c] * (1 / scale[c])),
+ * -127, 127) (k x n int8; columns of zeros give scale 0 and q 0). Asynchronous on `stream`
+ * (NULL: the per-thread default stream); allocates nothing; k == 0 or n == 0 is a no-op. */
+int llme_quantize_q8(size_t k, size_t n, const float* W, int8_t* q, float* scale, void* stream);
+
 /* ---- grouped products ------------------------------------------------------------------------ *
  * Many independent int8 products of the same m in ONE persistent launch. The reference issues
  * one matmul_cuda per projection; products that do not read each other's outputs (a layer's

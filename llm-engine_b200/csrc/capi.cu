@@ -973,6 +973,18 @@ int llme_matmul_q8_noalloc(size_t m, size_t n, size_t k, const float* A, const i
     return run_noalloc(m, n, k, A, B, scale, C, accumulate != 0, stream);
 }
 
+int llme_quantize_q8(size_t k, size_t n, const float* W, int8_t* q, float* scale, void* stream) {
+    g_error.clear();
+    if (k == 0 || n == 0) return LLME_OK;
+    if (!W || !q || !scale) return fail(LLME_E_INVALID, "llme_quantize_q8: null pointer");
+    if (k * n >= kMaxElems)
+        return fail(LLME_E_INVALID, "llme_quantize_q8: more than 2^31 elements (" +
+                                        std::to_string(k) + "x" + std::to_string(n) + ")");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
+    cudaError_t e = launch_quantize_q8(static_cast<int>(k), static_cast<int>(n), W, q, scale, s);
+    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "quantize");
+}
+
 int llme_batch_q8_create(llme_batch_t** batch, size_t m, size_t count,
                          const llme_q8_product* products) {
     return batch_create(batch, m, count, products);

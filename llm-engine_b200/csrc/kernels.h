@@ -183,6 +183,11 @@ cudaError_t launch_gemm_q8_tc(const Q8TcArgs& a, const CUtensorMap& tmHi, const 
                               const CUtensorMap& tmB);
 unsigned read_and_clear_q8tc_error();
 
+// The reference's quantize_q8 (src/quant.cpp:6-28) on device memory, bit for bit (quant.cu):
+// per-column scale = max|B[:,c]| / 127 and q = clamp(lround(B * (1 / scale)), -127, 127).
+cudaError_t launch_quantize_q8(int k, int n, const float* B, int8_t* q, float* scale,
+                               cudaStream_t stream);
+
 // out = rmsnorm(A) * w per row (eps 1e-5), m rows of k.
 cudaError_t launch_rmsnorm_rows(int m, int k, const float* A, const float* w, float* out,
                                 cudaStream_t stream);

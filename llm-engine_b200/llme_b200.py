@@ -91,6 +91,7 @@ def load() -> ctypes.CDLL:
     lib.llme_matmul_f32.restype = lib.llme_matmul_q8.restype = i
     lib.llme_matmul_q8_noalloc.argtypes = [sz, sz, sz, vp, vp, vp, vp, i, vp]
     lib.llme_matmul_q8_noalloc.restype = i
+    lib.llme_quantize_q8.argtypes = [sz, sz, vp, vp, vp, vp]
     lib.llme_batch_q8_create.argtypes = [ctypes.POINTER(vp), sz, sz, ctypes.POINTER(Q8Product)]
     lib.llme_batch_run.argtypes = [vp, u, vp]
     lib.llme_batch_destroy.argtypes = [vp]
@@ -166,6 +167,24 @@ def matmul_cuda_q8(m: int, n: int, k: int, A: int, B: int, scale: int, C: int,
     """C (+)= [rmsnorm(A)] x (B * scale) with int8 B on device pointers (cuda_matmul.h:105-107)."""
     _check(load().llme_matmul_q8(m, n, k, A, B, scale, C, _kernel_id(kernel),
                                  int(bool(accumulate)), rms_weight or None, flags, stream or None))
+
+
+def quantize_q8_cuda(k: int, n: int, W: int, q: int, scale: int, stream: int | None = None) -> None:
+    """The reference's quantize_q8 (quant.cpp:6-28) on device pointers: W (k x n fp32) ->
+    q (k x n int8) and scale (n fp32), bit for bit."""
+    _check(load().llme_quantize_q8(k, n, W, q, scale, stream or None))
+
+
+def quantize_q8(W):
+    """quantize_q8 over a torch CUDA tensor W (k x n fp32): returns (q int8, scale fp32)."""
+    import torch
+    if W.dtype != torch.float32 or W.dim() != 2 or not W.is_contiguous():
+        raise InvalidArgument("quantize_q8: W must be a contiguous 2-D float32 tensor")
+    k, n = W.shape
+    q = torch.empty((k, n), dtype=torch.int8, device=W.device)
+    scale = torch.empty(n, dtype=torch.float32, device=W.device)
+    quantize_q8_cuda(k, n, W.data_ptr(), q.data_ptr(), scale.data_ptr(), torch_stream_handle())
+    return q, scale
 
 
 def matmul_cuda_q8_noalloc(m: int, n: int, k: int, A: int, B: int, scale: int, C: int,
