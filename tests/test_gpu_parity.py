@@ -308,3 +308,23 @@ def test_reference_test_cuda_passes_unmodified():
                        text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-4000:]
     assert "all tests passed" in r.stdout
+
+
+MODEL_DROPIN = os.path.join(os.path.dirname(oracle.HERE), "oracle", "_ref",
+                            "test_cuda_model_dropin")
+
+
+@pytest.mark.skipif(not os.path.exists(MODEL_DROPIN),
+                    reason="oracle/_ref/test_cuda_model_dropin not built")
+@pytest.mark.parametrize("math", ["tensor", "fp32"])
+def test_reference_cuda_model_runs_on_the_library(math):
+    """The real caller: the reference's CudaTransformer (src/cuda_model.cu, built from its
+    sources) with every projection and the classifier going through this library's
+    matmul_cuda, checked by the reference's own tests/test_cuda_model.cpp against its CPU
+    Transformer (decode, chunked prefill, rewinds, bad inputs; tolerance 1e-4), f32 and int8
+    weights, in both arithmetic modes."""
+    env = dict(os.environ, LLME_B200_MATH=math)
+    r = subprocess.run([MODEL_DROPIN], env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+                       text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-4000:]
+    assert "all tests passed" in r.stdout
