@@ -242,8 +242,11 @@ enum {
     LLME_PATH_GEMV_LDG = 4,    /* weight-streaming GEMV, plain loads (ragged B) */
     LLME_PATH_TILED_SIMT = 5,  /* fp32 SIMT tiles, k split across CTAs */
     LLME_PATH_TCGEN05 = 6,     /* tcgen05/TMEM tensor-core GEMM, TF32 (fp32 weights) */
-    LLME_PATH_TCGEN05_Q8 = 7   /* tcgen05/TMEM tensor-core GEMM, int8 weights (kind::i8 on a
+    LLME_PATH_TCGEN05_Q8 = 7,  /* tcgen05/TMEM tensor-core GEMM, int8 weights (kind::i8 on a
                                   two-term int8 split of the activation rows) */
+    LLME_PATH_TCGEN05_SKINNY = 8  /* decode-shaped int8 products on tcgen05: three-term split
+                                     (fp32-decode accuracy), k split across CTAs, exact int64
+                                     sums */
 };
 
 typedef struct {

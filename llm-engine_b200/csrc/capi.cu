@@ -89,6 +89,8 @@ bool q8tc_use_pairs(int sms) {
 size_t q8tc_pitch(size_t k) { return round_up(k, 16); }
 size_t q8tc_rows_bytes(size_t m, size_t k) { return round_up(m * q8tc_pitch(k), 256); }
 size_t q8tc_operand_bytes(size_t m, size_t k) { return 2 * q8tc_rows_bytes(m, k) + m * sizeof(float); }
+// The skinny GEMM's three term planes, then the row scales.
+size_t skinny_operand_bytes(size_t m, size_t k) { return 3 * q8tc_rows_bytes(m, k) + m * sizeof(float); }
 
 int make_plan(const PlanIn& in, llme_plan_t* p) {
     std::memset(p, 0, sizeof(*p));
@@ -183,6 +185,36 @@ int make_plan(const PlanIn& in, llme_plan_t* p) {
         p->span = static_cast<int>(k);
         return LLME_OK;
     }
+    // Decode-shaped int8 products on tcgen05 (three-term split: the fp32 decode path's
+    // accuracy): tiled_split, or tiled below 128 rows, in LLME_MATH_TENSOR.
+    const bool skinny_kernel =
+        kernel == LLME_KERNEL_TILED_SPLIT || (kernel == LLME_KERNEL_TILED && m < 128);
+    if (skinny_kernel && in.math == LLME_MATH_TENSOR && in.q8 && n % 16 == 0 &&
+        in.b_addr % 16 == 0 && k <= static_cast<size_t>(kQ8TcMaxK)) {
+        p->path = LLME_PATH_TCGEN05_SKINNY;
+        p->rms_prepass = 0;
+        p->norm_bytes = 0;
+        const int t = skinny_rows_per_tile(static_cast<int>(std::min<size_t>(m, 64)));
+        p->tile_m = t;
+        p->tile_n = 128;
+        p->grid_x = static_cast<int>(ceil_div(n, size_t{128}));
+        p->grid_y = static_cast<int>(ceil_div(m, static_cast<size_t>(t)));
+        const size_t units = static_cast<size_t>(p->grid_x) * p->grid_y;
+        const size_t nkb = ceil_div(k, size_t{128});
+        const size_t target = static_cast<size_t>(skinny_ctas_per_sm(t)) * sms;
+        // k slices: as many as keep every CTA resident in one wave, each at least 4 blocks deep.
+        size_t slices = std::max<size_t>(1, std::min(target / units, ceil_div(nkb, size_t{4})));
+        const size_t span_blocks = ceil_div(nkb, slices);
+        slices = ceil_div(nkb, span_blocks);
+        p->slices = static_cast<int>(slices);
+        p->span = static_cast<int>(span_blocks * 128);
+        p->operand_bytes = skinny_operand_bytes(m, k);
+        if (slices > 1) {
+            p->counter_slots = units;
+            p->split_bytes = m * n * sizeof(long long);
+        }
+        return LLME_OK;
+    }
     // The int8 tcgen05 GEMM: also LLME_MATH_TENSOR only (the activations are split into two
     // int8 terms); W rows must be TMA-addressable and k small enough for exact s32 sums.
     // The RMSNorm of A is applied by the split pass, not by a separate one.
@@ -248,6 +280,11 @@ struct DeviceState {
     size_t partial_cap = 0;
     Scratch norm;
     Scratch operand;  // transposed weights for the tensor-core GEMM
+    // Skinny tcgen05 GEMM: [tickets: skinny_counters x u32][int64 sums], zero between launches
+    // (zeroed when it grows; each launch leaves it zero).
+    Scratch skinny;
+    size_t skinny_counters = 0;
+    size_t skinny_accum_bytes = 0;
 };
 
 std::mutex g_dev_mu;
@@ -323,6 +360,36 @@ int ensure_buffer(Scratch& b, size_t bytes, float** out) {
 }
 
 int ensure_norm(int dev, size_t bytes, float** out) { return ensure_buffer(g_dev[dev].norm, bytes, out); }
+
+// The skinny GEMM's zeroed tickets and int64 accumulators; both regions grow to the largest
+// size seen, the whole buffer is zeroed when it grows, and every launch leaves it zero.
+int ensure_skinny(int dev, size_t counters, size_t accum_bytes, cudaStream_t stream,
+                  unsigned** ctr, long long** acc) {
+    DeviceState& d = g_dev[dev];
+    const size_t want_c = std::max(counters, d.skinny_counters);
+    const size_t want_a = std::max(round_up(accum_bytes, 256), d.skinny_accum_bytes);
+    if (!d.skinny.ptr || want_c > d.skinny_counters || want_a > d.skinny_accum_bytes) {
+        if (d.skinny.ptr) {
+            cudaError_t e = cudaFree(d.skinny.ptr);
+            if (e != cudaSuccess) return cuda_fail(e, "free scratch");
+            d.skinny.ptr = nullptr;
+            d.skinny.cap = d.skinny_counters = d.skinny_accum_bytes = 0;
+        }
+        const size_t bytes = round_up(want_c * sizeof(unsigned), 256) + want_a;
+        cudaError_t e = cudaMalloc(&d.skinny.ptr, bytes);
+        if (e != cudaSuccess) return cuda_fail(e, "alloc scratch");
+        d.skinny.cap = bytes;
+        d.skinny_counters = want_c;
+        d.skinny_accum_bytes = want_a;
+        e = cudaMemsetAsync(d.skinny.ptr, 0, bytes, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "zero scratch");
+        g_generation.fetch_add(1);
+    }
+    *ctr = static_cast<unsigned*>(d.skinny.ptr);
+    *acc = reinterpret_cast<long long*>(static_cast<char*>(d.skinny.ptr) +
+                                        round_up(d.skinny_counters * sizeof(unsigned), 256));
+    return LLME_OK;
+}
 
 // ---- TMA descriptors -------------------------------------------------------------------
 
@@ -453,7 +520,7 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
 
     std::lock_guard<std::mutex> lk(g_dev_mu);  // scratch is shared per device
     SplitScratch split;
-    if (p.split_bytes > 0) {
+    if (p.split_bytes > 0 && p.path != LLME_PATH_TCGEN05_SKINNY) {
         // Partial sums first, then (GEMV with RMSNorm) the per-slice sums of squares.
         const size_t partial_floats =
             p.path == LLME_PATH_TILED_SIMT
@@ -538,6 +605,50 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
         t.stream = stream;
         t.pdl = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
         e = launch_gemm_tf32(t, tmA, tmB);
+    } else if (p.path == LLME_PATH_TCGEN05_SKINNY) {
+        float* ops = nullptr;
+        st = ensure_buffer(g_dev[dev].operand, p.operand_bytes, &ops);
+        if (st) return st;
+        const size_t plane = q8tc_rows_bytes(m, k);
+        int8_t* t0 = reinterpret_cast<int8_t*>(ops);
+        int8_t* t1 = t0 + plane;
+        int8_t* t2 = t1 + plane;
+        float* rs = reinterpret_cast<float*>(t2 + plane);
+        const size_t kp = q8tc_pitch(k);
+        SkinnyArgs t;
+        if (p.slices > 1) {
+            st = ensure_skinny(dev, p.counter_slots, p.split_bytes, stream, &t.counters, &t.accum);
+            if (st) return st;
+        }
+        e = launch_split_rows(static_cast<int>(m), static_cast<int>(k), static_cast<int>(kp), A,
+                              rms, t0, t1, t2, rs, stream, true);
+        if (e != cudaSuccess) return cuda_fail(e, "launch");
+        CUtensorMap tmW, tm0, tm1, tm2;
+        st = tensor_map(B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, 128, 128, &tmW,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!st)
+            st = tensor_map(t0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, m, k, 128, p.tile_m, &tm0,
+                            CU_TENSOR_MAP_SWIZZLE_128B, kp);
+        if (!st)
+            st = tensor_map(t1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, m, k, 128, p.tile_m, &tm1,
+                            CU_TENSOR_MAP_SWIZZLE_128B, kp);
+        if (!st)
+            st = tensor_map(t2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, m, k, 128, p.tile_m, &tm2,
+                            CU_TENSOR_MAP_SWIZZLE_128B, kp);
+        if (st) return st;
+        t.m = static_cast<int>(m);
+        t.n = static_cast<int>(n);
+        t.k = static_cast<int>(k);
+        t.scale = scale;
+        t.row_scale = rs;
+        t.C = C;
+        t.accumulate = accumulate;
+        t.weights_static = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
+        t.rows_per_tile = p.tile_m;
+        t.slices = p.slices;
+        t.span_blocks = p.span / 128;
+        t.stream = stream;
+        e = launch_gemm_q8_skinny(t, tmW, tm0, tm1, tm2);
     } else if (p.path == LLME_PATH_TCGEN05_Q8) {
         float* ops = nullptr;
         st = ensure_buffer(g_dev[dev].operand, p.operand_bytes, &ops);
@@ -547,7 +658,7 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
         float* rs = reinterpret_cast<float*>(lo + q8tc_rows_bytes(m, k));
         const size_t kp = q8tc_pitch(k);
         e = launch_split_rows(static_cast<int>(m), static_cast<int>(k), static_cast<int>(kp), A,
-                              rms, hi, lo, rs, stream, true);
+                              rms, hi, lo, nullptr, rs, stream, true);
         if (e != cudaSuccess) return cuda_fail(e, "launch");
         CUtensorMap tmHi, tmLo, tmB;
         st = tensor_map(hi, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, m, k, 128, 128, &tmHi,
@@ -1045,7 +1156,7 @@ int llme_synchronize(void) {
     if (e != cudaSuccess) return cuda_fail(e, "synchronize");
     const unsigned dev_err =
         read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error() |
-        read_and_clear_q8tc_error();
+        read_and_clear_q8tc_error() | read_and_clear_skinny_error();
     if (dev_err) return fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up");
     return LLME_OK;
 }
@@ -1069,7 +1180,7 @@ int llme_device_status(void) {
     if (e != cudaSuccess) return cuda_fail(e, "synchronize");
     const unsigned dev_err =
         read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error() |
-        read_and_clear_q8tc_error();
+        read_and_clear_q8tc_error() | read_and_clear_skinny_error();
     return dev_err ? fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up") : LLME_OK;
 }
 

@@ -354,13 +354,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (row0 >= u.m) continue;
                 // Row scales of these 32 rows, one per lane, passed around by shuffles.
                 const float rs_lane = row0 + lane < u.m ? u.row_scale[row0 + lane] : 0.0f;
+                if (u.accumulate) {
+                    // 16 old values in flight before the first of their stores (they may alias).
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
-                    if (row0 + j < u.m && col_ok) {
-                        float* o = u.C + static_cast<size_t>(row0 + j) * u.n + col;
-                        const float v = finish(h[j], l[j], rs, sc);
-                        *o = u.accumulate ? __fadd_rn(*o, v) : v;
+                    for (int j0 = 0; j0 < 32; j0 += 16) {
+                        float old[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            old[j] = row0 + j0 + j < u.m && col_ok
+                                         ? u.C[static_cast<size_t>(row0 + j0 + j) * u.n + col]
+                                         : 0.0f;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const float rs = __shfl_sync(0xffffffffu, rs_lane, j0 + j);
+                            if (row0 + j0 + j < u.m && col_ok)
+                                u.C[static_cast<size_t>(row0 + j0 + j) * u.n + col] =
+                                    __fadd_rn(old[j], finish(h[j0 + j], l[j0 + j], rs, sc));
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float rs = __shfl_sync(0xffffffffu, rs_lane, j);
+                        if (row0 + j < u.m && col_ok)
+                            u.C[static_cast<size_t>(row0 + j) * u.n + col] =
+                                finish(h[j], l[j], rs, sc);
                     }
                 }
             }
@@ -398,27 +416,39 @@ constexpr int kSplitRegs = 12;      // float4 per thread in the register path
 constexpr int kSplitSmemMax = kQ8TcSplitSmemMax;  // rows up to 49152 elements by bulk copy
 __device__ unsigned int g_split_error;
 
+// The split of one row. Two terms: x = s * (t0 + t1 / 256). Three terms (the skinny GEMM,
+// held to the decode path's 1e-5 bound): x = s * (t0 + t1 / 256 + t2 / 65536), each residual
+// scaled by 256 exactly (y - rint(y) and its multiples by 256 are exact in fp32).
 struct SplitRow {
     float inv_rms, q, pre;
     bool norm;
-    // hi / lo of one element (the kernel's whole arithmetic for an element).
-    __device__ __forceinline__ void split(float a, float g, int8_t* h8, int8_t* l8) const {
+    bool three;
+    // The terms of one element (the kernel's whole arithmetic for an element).
+    __device__ __forceinline__ void split(float a, float g, int8_t* o0, int8_t* o1,
+                                          int8_t* o2) const {
         const float x = norm ? a * inv_rms * g : a;
         float y = pre == 1.0f ? x * q : (x * pre) * q;
         if (!(fabsf(y) <= 128.0f)) y = 0.0f;  // non-finite rows: the row scale is NaN
-        const float h = fminf(fmaxf(rintf(y), -127.0f), 127.0f);
-        const float l = fminf(fmaxf(rintf((y - h) * 256.0f), -127.0f), 127.0f);
-        *h8 = static_cast<int8_t>(static_cast<int>(h));
-        *l8 = static_cast<int8_t>(static_cast<int>(l));
+        const float t0 = fminf(fmaxf(rintf(y), -127.0f), 127.0f);
+        const float r1 = (y - t0) * 256.0f;
+        const float t1 = fminf(fmaxf(rintf(r1), -127.0f), 127.0f);
+        *o0 = static_cast<int8_t>(static_cast<int>(t0));
+        *o1 = static_cast<int8_t>(static_cast<int>(t1));
+        if (three) {
+            const float t2 = fminf(fmaxf(rintf((r1 - t1) * 256.0f), -127.0f), 127.0f);
+            *o2 = static_cast<int8_t>(static_cast<int>(t2));
+        }
     }
-    __device__ __forceinline__ void split4(float4 v, float4 g, int8_t* oh, int8_t* ol) const {
-        char4 h4, l4;
-        split(v.x, g.x, &h4.x, &l4.x);
-        split(v.y, g.y, &h4.y, &l4.y);
-        split(v.z, g.z, &h4.z, &l4.z);
-        split(v.w, g.w, &h4.w, &l4.w);
-        *reinterpret_cast<char4*>(oh) = h4;
-        *reinterpret_cast<char4*>(ol) = l4;
+    __device__ __forceinline__ void split4(float4 v, float4 g, int8_t* p0, int8_t* p1,
+                                           int8_t* p2) const {
+        char4 a, b, c;
+        split(v.x, g.x, &a.x, &b.x, &c.x);
+        split(v.y, g.y, &a.y, &b.y, &c.y);
+        split(v.z, g.z, &a.z, &b.z, &c.z);
+        split(v.w, g.w, &a.w, &b.w, &c.w);
+        *reinterpret_cast<char4*>(p0) = a;
+        *reinterpret_cast<char4*>(p1) = b;
+        if (three) *reinterpret_cast<char4*>(p2) = c;
     }
 };
 
@@ -436,15 +466,16 @@ __device__ __forceinline__ void split_accumulate(float4 v, float4 g, bool norm, 
     if (u.x != u.x || u.y != u.y || u.z != u.z || u.w != u.w) *mx = __int_as_float(0x7f800000);
 }
 
-// Splits one row `in` (k floats) into oh / ol and writes its scale to *rs_out. Whole CTA.
+// Splits one row `in` (k floats) into the term rows o0, o1 (and o2 when not null: three
+// terms) and writes its scale to *rs_out. Whole CTA.
 // Bulk: the launch guarantees every row is aligned and fits `srow` (the dynamic shared
 // memory); the generic form takes any row. Two instantiations, so the bulk kernel does not
 // carry the register path's registers.
 template <bool Bulk>
 __device__ __forceinline__ void split_row(int k, const float* __restrict__ in,
                                           const float* __restrict__ w, int8_t* __restrict__ oh,
-                                          int8_t* __restrict__ ol, float* __restrict__ rs_out,
-                                          float* srow) {
+                                          int8_t* __restrict__ ol, int8_t* __restrict__ o2,
+                                          float* __restrict__ rs_out, float* srow) {
     __shared__ float red_ss[kSplitThreads / 32], red_mx[kSplitThreads / 32];
     __shared__ uint64_t row_bar;
     const bool norm = w != nullptr;
@@ -516,6 +547,7 @@ __device__ __forceinline__ void split_row(int k, const float* __restrict__ in,
     }
     SplitRow sr;
     sr.norm = norm;
+    sr.three = o2 != nullptr;
     sr.inv_rms = norm ? 1.0f / sqrtf(total / static_cast<float>(k) + kRmsEps) : 1.0f;
     amax *= sr.inv_rms;
     // Multiplier to the hi grid (127 at the row's largest magnitude). Rows so small that
@@ -531,22 +563,24 @@ __device__ __forceinline__ void split_row(int k, const float* __restrict__ in,
     if constexpr (bulk) {
         if (landed) {
             for (int j = threadIdx.x * 4; j < k; j += kStride)
-                sr.split4(*reinterpret_cast<const float4*>(srow + j), wload(j), oh + j, ol + j);
+                sr.split4(*reinterpret_cast<const float4*>(srow + j), wload(j), oh + j, ol + j,
+                          o2 + j);
         }
     } else if (vec) {
 #pragma unroll
         for (int r = 0; r < (Bulk ? 0 : kSplitRegs); ++r) {
             const int j = r * kStride + threadIdx.x * 4;
-            if (j < k) sr.split4(v[r], wload(j), oh + j, ol + j);
+            if (j < k) sr.split4(v[r], wload(j), oh + j, ol + j, o2 + j);
         }
         for (int j = kSplitRegs * kStride + threadIdx.x * 4; j < k; j += kStride)
-            sr.split4(*reinterpret_cast<const float4*>(in + j), wload(j), oh + j, ol + j);
+            sr.split4(*reinterpret_cast<const float4*>(in + j), wload(j), oh + j, ol + j, o2 + j);
     } else {
         for (int j = threadIdx.x; j < k; j += kSplitThreads) {
-            int8_t h8, l8;
-            sr.split(in[j], norm ? w[j] : 1.0f, &h8, &l8);
-            oh[j] = h8;
-            ol[j] = l8;
+            int8_t a8, b8, c8;
+            sr.split(in[j], norm ? w[j] : 1.0f, &a8, &b8, &c8);
+            oh[j] = a8;
+            ol[j] = b8;
+            if (o2) o2[j] = c8;
         }
     }
 }
@@ -554,12 +588,16 @@ __device__ __forceinline__ void split_row(int k, const float* __restrict__ in,
 template <bool Bulk>
 __global__ void __launch_bounds__(kSplitThreads)
     split_rows_kernel(int k, int kp, const float* __restrict__ A, const float* __restrict__ w,
-                      int8_t* __restrict__ hi, int8_t* __restrict__ lo,
+                      int8_t* __restrict__ hi, int8_t* __restrict__ lo, int8_t* __restrict__ t2,
                       float* __restrict__ row_scale) {
     extern __shared__ __align__(16) float split_smem[];
+    // A grid of one wave (decode-sized m) lets the next launch be placed at once: all its own
+    // CTAs are already resident, so the early arrivals cannot crowd them out.
+    if (gridDim.x <= 256) pdl_launch_dependents();
     pdl_wait();
     const size_t r = blockIdx.x;
-    split_row<Bulk>(k, A + r * k, w, hi + r * kp, lo + r * kp, row_scale + r, split_smem);
+    split_row<Bulk>(k, A + r * k, w, hi + r * kp, lo + r * kp, t2 ? t2 + r * kp : nullptr,
+                    row_scale + r, split_smem);
     // Only now may the GEMM's CTAs (197 KB of shared memory each, waiting for this grid) be
     // placed: placed earlier they would take SMs that this grid's remaining rows still need.
     pdl_launch_dependents();
@@ -580,7 +618,7 @@ __global__ void __launch_bounds__(kSplitThreads) split_rows_batch_kernel(const Q
     const Q8TcItem& it = b.items[lo_p];
     const size_t row = static_cast<size_t>(r - b.row_begin[lo_p]);
     split_row<Bulk>(it.k, it.A + row * it.k, nullptr, it.hi + row * it.kp, it.lo + row * it.kp,
-                    it.row_scale + row, split_smem);
+                    nullptr, it.row_scale + row, split_smem);
     pdl_launch_dependents();  // as in split_rows_kernel: the GEMM's CTAs only after this row
 }
 
@@ -646,7 +684,8 @@ cudaError_t launch_gemm(int slots, bool pair, cudaStream_t stream, const CUtenso
 }  // namespace
 
 cudaError_t launch_split_rows(int m, int k, int kp, const float* A, const float* w, int8_t* hi,
-                              int8_t* lo, float* row_scale, cudaStream_t stream, bool pdl) {
+                              int8_t* lo, int8_t* t2, float* row_scale, cudaStream_t stream,
+                              bool pdl) {
     cudaError_t e = configure_smem();
     if (e != cudaSuccess) return e;
     // Bulk copies need 16-byte aligned rows (and norm weights) and a row that fits.
@@ -665,8 +704,10 @@ cudaError_t launch_split_rows(int m, int k, int kp, const float* A, const float*
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    return bulk ? cudaLaunchKernelEx(&cfg, split_rows_kernel<true>, k, kp, A, w, hi, lo, row_scale)
-                : cudaLaunchKernelEx(&cfg, split_rows_kernel<false>, k, kp, A, w, hi, lo, row_scale);
+    return bulk ? cudaLaunchKernelEx(&cfg, split_rows_kernel<true>, k, kp, A, w, hi, lo, t2,
+                                     row_scale)
+                : cudaLaunchKernelEx(&cfg, split_rows_kernel<false>, k, kp, A, w, hi, lo, t2,
+                                     row_scale);
 }
 
 cudaError_t launch_gemm_q8_tc(const Q8TcArgs& a, const CUtensorMap& tmHi, const CUtensorMap& tmLo,

@@ -177,11 +177,39 @@ constexpr int kQ8TcSplitSmemMax = 196608;  // bytes of a row the split pass stag
 cudaError_t launch_q8tc_batch(const Q8TcBatchArgs& b);
 int q8tc_tile_m();
 int q8tc_tile_n(bool pair);          // output columns per tile: 128, or 256 for CTA pairs
+// Rows of A into int8 term rows of pitch kp: (hi, lo) for two terms, (hi, lo = the middle
+// term, t2) for three (t2 null: two terms).
 cudaError_t launch_split_rows(int m, int k, int kp, const float* A, const float* w, int8_t* hi,
-                              int8_t* lo, float* row_scale, cudaStream_t stream, bool pdl);
+                              int8_t* lo, int8_t* t2, float* row_scale, cudaStream_t stream,
+                              bool pdl);
 cudaError_t launch_gemm_q8_tc(const Q8TcArgs& a, const CUtensorMap& tmHi, const CUtensorMap& tmLo,
                               const CUtensorMap& tmB);
 unsigned read_and_clear_q8tc_error();
+
+// Decode-shaped int8 products on tcgen05 (gemm_q8_skinny.cu): three-term split rows, one CTA
+// per (128-column, rows_per_tile-row) tile and k-slice; slices > 1 add exact int64 sums into
+// `accum` (m x n, zero between launches) and the last CTA of a tile (per `counters`, zero
+// between launches) writes C.
+struct SkinnyArgs {
+    int m = 0, n = 0, k = 0;
+    const float* scale = nullptr;
+    const float* row_scale = nullptr;
+    float* C = nullptr;
+    long long* accum = nullptr;
+    unsigned* counters = nullptr;
+    bool accumulate = false;
+    bool weights_static = false;  // weight loads may start before the previous launch ends
+    int rows_per_tile = 16;       // 16, 32 or 64
+    int slices = 1;
+    int span_blocks = 0;          // 128-deep k blocks per slice
+    cudaStream_t stream = nullptr;
+};
+int skinny_rows_per_tile(int m);
+int skinny_ctas_per_sm(int rows_per_tile);
+cudaError_t launch_gemm_q8_skinny(const SkinnyArgs& a, const CUtensorMap& tmW,
+                                  const CUtensorMap& t0, const CUtensorMap& t1,
+                                  const CUtensorMap& t2);
+unsigned read_and_clear_skinny_error();
 
 // The reference's quantize_q8 (src/quant.cpp:6-28) on device memory, bit for bit (quant.cu):
 // per-column scale = max|B[:,c]| / 127 and q = clamp(lround(B * (1 / scale)), -127, 127).

@@ -150,6 +150,28 @@ def test_tcgen05_q8_path_choice():
     assert p["grid_x"] == 128
 
 
+def test_tcgen05_skinny_plan():
+    # Decode-shaped int8 (9..127 rows, or tiled_split / tiled below 128) in tensor math.
+    p = L.plan(16, 4096, 4096, q8=True)
+    assert p["path_name"] == "tcgen05_skinny" and p["kernel"] == 3       # -> tiled_split
+    assert (p["tile_m"], p["tile_n"], p["grid_x"], p["grid_y"]) == (16, 128, 32, 1)
+    assert p["slices"] == 8 and p["span"] == 512                          # 256 CTAs
+    assert p["counter_slots"] == 32 and p["split_bytes"] == 16 * 4096 * 8
+    assert p["operand_bytes"] == 3 * 16 * 4096 + 16 * 4
+    p = L.plan(64, 4096, 4096, q8=True)
+    assert p["tile_m"] == 64 and p["slices"] == 4 and p["grid_x"] * p["slices"] <= 148
+    p = L.plan(100, 11008, 4096, q8=True)
+    assert (p["tile_m"], p["grid_y"], p["slices"]) == (64, 2, 1) and p["split_bytes"] == 0
+    for m, k in [(9, 4096), (33, 11008), (127, 100)]:
+        p = L.plan(m, 4096, k, q8=True)
+        assert (p["slices"] - 1) * p["span"] < k <= p["slices"] * p["span"]
+    assert L.plan(4, 4096, 4096, q8=True)["path_name"] == "gemv_tma"
+    assert L.plan(4, 4096, 4096, q8=True, kernel="tiled_split")["path_name"] == "tcgen05_skinny"
+    assert L.plan(16, 4096, 4096, q8=True, math=L.MATH_FP32)["path_name"] == "tiled_simt"
+    assert L.plan(16, 4104, 4096, q8=True)["path_name"] == "tiled_simt"     # n % 16
+    assert L.plan(16, 4096, 4096, q8=False)["path_name"] == "tiled_simt"    # fp32 weights
+
+
 def test_tcgen05_q8_cta_pairs_plan(monkeypatch):
     # LLME_B200_CTA_PAIRS=1: cta_group::2, 128 x 256 tiles, 4 x 16 of them on 64 pairs.
     monkeypatch.setenv("LLME_B200_CTA_PAIRS", "1")
@@ -166,12 +188,12 @@ def test_tcgen05_q8_cta_pairs_plan(monkeypatch):
     assert p["operand_bytes"] == 2 * ((130 * 80 + 255) // 256 * 256) + 130 * 4   # pitch 80
     assert L.plan(2048, 8192, 4096, q8=True, sm_count=148)["grid_x"] == 148   # persistent
     assert L.plan(512, 4096, 4096, q8=True, math=L.MATH_FP32)["path_name"] == "tiled_simt"
-    assert L.plan(127, 4096, 4096, q8=True)["path_name"] == "tiled_simt"
+    assert L.plan(127, 4096, 4096, q8=True)["path_name"] == "tcgen05_skinny"
     assert L.plan(512, 4104, 4096, q8=True)["path_name"] == "tiled_simt"     # n % 16
     assert L.plan(512, 4096, 4096, q8=True, b_addr=8)["path_name"] == "tiled_simt"
     assert L.plan(512, 4096, 131072, q8=True)["path_name"] == "tcgen05_q8"
     assert L.plan(512, 4096, 131073, q8=True)["path_name"] == "tiled_simt"   # s32 sums exact
-    assert L.plan(512, 4096, 4096, q8=True, kernel="tiled_split")["path_name"] == "tiled_simt"
+    assert L.plan(512, 4096, 4096, q8=True, kernel="tiled_split")["path_name"] == "tcgen05_skinny"
 
 
 def test_rms_prepass_only_outside_the_gemv():
@@ -181,7 +203,7 @@ def test_rms_prepass_only_outside_the_gemv():
 
 
 def test_tiled_split_sizes():
-    p = L.plan(16, 4096, 4096, q8=True, kernel="tiled_split")
+    p = L.plan(16, 4096, 4096, q8=True, kernel="tiled_split", math=L.MATH_FP32)
     assert p["path_name"] == "tiled_simt" and p["slices"] > 1
     assert (p["slices"] - 1) * p["span"] < 4096 <= p["slices"] * p["span"]
     p = L.plan(200, 33, 513, q8=False, kernel="tiled")
