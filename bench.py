@@ -399,6 +399,117 @@ def run_sgemm(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+# ---- the decode-shaped sweep ------------------------------------------
+
+SWEEP_ROWS = (1, 4, 16, 64)
+SWEEP_COPIES = 12  # distinct 4096 x 4096 weights per case (201 MB int8 / 805 MB fp32 > L2)
+
+
+def run_sweep(args, world, rank, local):
+    """m in {1, 4, 16, 64} x 4096 x 4096, fp32 and int8 weights (N(0, 0.02^2), seed 1, the
+    int8 ones quantised as quant.cpp does), U(-1, 1) activations: one C-ABI call per product,
+    12 distinct weights per case captured in one CUDA graph. `value` is the sweep's total
+    algorithmic bytes over its total time; every case is reported in `cases`."""
+    import torch
+    import llme_b200 as L
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1)
+    stream = torch.cuda.Stream()
+    h = stream.cuda_stream
+    sampler = ClockSampler(local)
+    cases, tot_bytes, tot_s = [], 0, 0.0
+    for q8 in (False, True):
+        Ws = [torch.randn(DIM, DIM, generator=g, device="cuda") * 0.02 for _ in range(SWEEP_COPIES)]
+        if q8:
+            Ws = [quantize_on_device(w) for w in Ws]
+        for m in SWEEP_ROWS:
+            A = torch.rand(m, DIM, generator=g, device="cuda") * 2 - 1
+            C = torch.empty(m, DIM, device="cuda")
+
+            def fn():
+                for i in range(SWEEP_COPIES):
+                    if q8:
+                        q, sc = Ws[i]
+                        L.matmul_cuda_q8(m, DIM, DIM, A.data_ptr(), q.data_ptr(), sc.data_ptr(),
+                                         C.data_ptr(), "automatic", False, 0,
+                                         L.FLAG_WEIGHTS_STATIC, h)
+                    else:
+                        L.matmul_cuda_f32(m, DIM, DIM, A.data_ptr(), Ws[i].data_ptr(),
+                                          C.data_ptr(), "automatic", False, 0,
+                                          L.FLAG_WEIGHTS_STATIC, h)
+            graph = capture(fn, stream)
+            secs = max_over_ranks(time_graph(graph, args.steps, args.warmup, stream, world,
+                                             sampler if q8 and m == 64 else None), world)
+            del graph
+            nbytes = (algorithmic_bytes(DIM, DIM, m) if q8 else
+                      4 * DIM * DIM + 4 * m * DIM + 4 * m * DIM)
+            us = secs / (args.steps * SWEEP_COPIES) * 1e6
+            cases.append({"w": "int8" if q8 else "fp32", "m": m, "us": round(us, 2),
+                          "GB_s": round(nbytes / us / 1e3, 1),
+                          "path": L.plan(m, DIM, DIM, q8=q8)["path_name"]})
+            tot_bytes += nbytes * args.steps * SWEEP_COPIES
+            tot_s += secs
+    hbm, hbm_kind = peaks()
+    value = tot_bytes / tot_s / 1e9
+    cpu = cpu_sweep_sample() if rank == 0 and world == 1 and not args.no_extras else None
+    line = {"metric": "decode sweep GB/s (m in {1,4,16,64} x 4096^2, fp32 and int8 W, per call)",
+            "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(tot_s / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: N(0,0.02^2) weights (seed 1), U(-1,1) activations",
+            "config": {"workload": "decode-shaped sweep (BASELINE configs[1]), one C-ABI call "
+                                   "per product, 12 distinct weights per case in a CUDA graph",
+                       "l2": "no flush: 12 distinct weights per case (201 MB int8, 805 MB fp32)"},
+            "cases": cases,
+            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(value / hbm, 4), "peak_kind": hbm_kind,
+                         "kernel": "per case (see cases[].path)", "traffic": None},
+            "gpu_launches": None, "clocks": sampler.summary()}
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def cpu_sweep_sample(budget_s=2.0):
+    """The reference's matmul_parallel on each sweep case (one 4096 x 4096 weight, fp32 and
+    int8), on all host cores: the same total-bytes / total-time figure as the GPU line."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle  # the CPU baseline leg only
+    rng = np.random.default_rng(1)
+    W = (rng.standard_normal((DIM, DIM), dtype=np.float32) * 0.02).astype(np.float32)
+    kind = "reference" if oracle.Reference.available(fast=True) else "port"
+    ref = oracle.Reference(fast=True) if kind == "reference" else None
+    q, sc = ref.quantize_q8(W) if ref else oracle.quantize_q8(W)
+    qh = ref.qtensor(q, sc) if ref else None
+    wh = ref.tensor(W) if ref else None  # weights held on the reference side, not copied per call
+    cases, tb, ts = [], 0, 0.0
+    for q8 in (False, True):
+        for m in SWEEP_ROWS:
+            A = rng.uniform(-1, 1, (m, DIM)).astype(np.float32)
+            if ref:
+                one = (lambda: ref.matmul_parallel_q8(A, qh)) if q8 else \
+                    (lambda: ref.matmul_parallel_h(A, wh))
+            else:
+                one = (lambda: oracle.matmul_parallel(A, q=q, scale=sc)) if q8 else \
+                    (lambda: oracle.matmul_parallel(A, W))
+            one()
+            times, t_end = [], time.perf_counter() + budget_s
+            while time.perf_counter() < t_end or len(times) < 3:
+                t0 = time.perf_counter()
+                one()
+                times.append(time.perf_counter() - t0)
+            med = statistics.median(times)
+            nbytes = algorithmic_bytes(DIM, DIM, m) if q8 else 4 * DIM * DIM + 8 * m * DIM
+            cases.append({"w": "int8" if q8 else "fp32", "m": m, "us": round(med * 1e6, 1)})
+            tb += nbytes
+            ts += med
+    return {"value": round(tb / ts / 1e9, 2), "unit": "GB/s",
+            "cores": ref.threads() if ref else oracle.default_threads(), "kind": kind,
+            "sample": "each sweep case once (median of repeated calls, about 2 s per case)",
+            "cases": cases}
+
+
 # ---- BASELINE configs[4]: the 7B-shaped prefill (m = 512) ----------------------------------
 
 PREFILL_ROWS = 512
@@ -706,6 +817,8 @@ def run_ours(args):
         return run_sgemm(args, world, rank, local)
     if args.workload == "prefill":
         return run_prefill(args, world, rank, local)
+    if args.workload == "sweep":
+        return run_sweep(args, world, rank, local)
     if args.workload == "chain":
         chain = Chain(world, rank, chain_shapes(args.layers), seed=3)
     else:
@@ -876,10 +989,12 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["chain", "gemv", "sgemm", "prefill"], default="chain",
+    ap.add_argument("--workload", choices=["chain", "gemv", "sgemm", "prefill", "sweep"],
+                    default="chain",
                     help="chain: BASELINE configs[3] (default); gemv: configs[0] alone; "
                          "sgemm: configs[2] (square TF32 GEMM, --size); prefill: configs[4] "
-                         "(m = 512 through the 7B-shaped int8 weights)")
+                         "(m = 512 through the 7B-shaped int8 weights); sweep: configs[1] "
+                         "(m in {1,4,16,64} x 4096^2, fp32 and int8 W, per call)")
     ap.add_argument("--size", type=int, default=8192, help="N for --workload sgemm")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers of the chain / prefill (32 = the BASELINE configs; fewer only "

@@ -150,6 +150,11 @@ class Reference:
         lib.ref_qtensor_free.argtypes = [ctypes.c_void_p]
         lib.ref_matmul_parallel_q8.argtypes = [ctypes.c_void_p, _sz, _sz, _f32p, _f32p,
                                                ctypes.c_uint]
+        lib.ref_tensor_new.argtypes = [_sz, _sz, _f32p]
+        lib.ref_tensor_new.restype = ctypes.c_void_p
+        lib.ref_tensor_free.argtypes = [ctypes.c_void_p]
+        lib.ref_matmul_parallel_f32_h.argtypes = [ctypes.c_void_p, _sz, _sz, _f32p, _f32p,
+                                                  ctypes.c_uint]
         self.lib = lib
 
     @staticmethod
@@ -216,12 +221,28 @@ class Reference:
         return C
 
 
+    def tensor(self, B):
+        """An fp32 Tensor kept alive on the reference side; pass to matmul_parallel_h."""
+        B = _c(B, np.float32)
+        return _QHandle(self, self.lib.ref_tensor_new(B.shape[0], B.shape[1], B), B.shape,
+                        self.lib.ref_tensor_free)
+
+    def matmul_parallel_h(self, A, th: "_QHandle", threads: int = 0, out=None):
+        """matmul_parallel(A, B) with B from tensor(): the weight is not copied per call."""
+        A = _c(A, np.float32)
+        m, k = A.shape
+        C = out if out is not None else np.empty((m, th.shape[1]), np.float32)
+        self._check(self.lib.ref_matmul_parallel_f32_h(th.handle, m, k, A, C, threads))
+        return C
+
+
 class _QHandle:
-    def __init__(self, ref: Reference, handle, shape):
+    def __init__(self, ref: Reference, handle, shape, free=None):
         self.ref, self.handle, self.shape = ref, handle, shape
+        self.free = free if free is not None else ref.lib.ref_qtensor_free
 
     def __del__(self):
         try:
-            self.ref.lib.ref_qtensor_free(self.handle)
+            self.free(self.handle)
         except Exception:
             pass

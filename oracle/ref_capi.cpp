@@ -114,6 +114,22 @@ void* ref_qtensor_new(std::size_t rows, std::size_t cols, const std::int8_t* q,
 
 void ref_qtensor_free(void* h) { delete static_cast<QTensor*>(h); }
 
+// The same for fp32 weights: a Tensor kept alive across calls of matmul_parallel.
+void* ref_tensor_new(std::size_t rows, std::size_t cols, const float* B) {
+    return new Tensor(make_tensor(rows, cols, B));
+}
+
+void ref_tensor_free(void* h) { delete static_cast<Tensor*>(h); }
+
+// matmul.h:17-22 (fp32 weights, a handle from ref_tensor_new)
+int ref_matmul_parallel_f32_h(void* h, std::size_t m, std::size_t k, const float* A, float* C,
+                              unsigned threads) {
+    return guarded([&] {
+        const Tensor& B = *static_cast<const Tensor*>(h);
+        copy_out(matmul_parallel(make_tensor(m, k, A), B, threads), C);
+    });
+}
+
 // matmul.cpp:315-318, with B the QTensor made by ref_qtensor_new.
 int ref_matmul_parallel_q8(void* h, std::size_t m, std::size_t k, const float* A, float* C,
                            unsigned threads) {
