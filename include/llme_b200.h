@@ -149,6 +149,32 @@ int llme_copy_to_host(void* dst, const void* src, size_t bytes);     /* waits */
  * (NULL: the per-thread default stream); allocates nothing; k == 0 or n == 0 is a no-op. */
 int llme_quantize_q8(size_t k, size_t n, const float* W, int8_t* q, float* scale, void* stream);
 
+/* ---- causal decode attention over a KV cache -------------------------------------------------- *
+ * The C form of the reference's cuda_attention.h (src/cuda_attention.h:8-45), which
+ * include/cuda_attention.h restates for C++ callers over these three functions. */
+typedef struct {
+    int n_heads, n_kv_heads, head_size, seq_len;
+    size_t q_stride;   /* floats between rows of q; head h starts at h * head_size */
+    size_t kv_stride;  /* floats between positions of the caches */
+    size_t out_stride; /* floats between rows of out */
+} llme_attention_shape;
+
+enum { LLME_ATTN_AUTOMATIC = 0, LLME_ATTN_SINGLE_BLOCK = 1, LLME_ATTN_SPLIT = 2 };
+
+/* LLME_E_INVALID (message in llme_last_error) when `kernel` cannot run shape s: non-positive
+ * sizes, n_heads % n_kv_heads, a cache past 32-bit indexing; split: head_size or a stride not
+ * divisible by 4, head_size > 512; single_block: head_size + seq_len floats over 48 KB. */
+int llme_attention_check(const llme_attention_shape* s, int kernel);
+/* Floats of scratch llme_attention needs for up to `rows` rows (0 for single_block). */
+size_t llme_attention_scratch_floats(const llme_attention_shape* s, size_t rows, int kernel);
+/* out[i][h * head_size + d] = sum over t <= *pos_dev + i of softmax_t(q_i,h . k_t / sqrt(hs))
+ * v_t[d], kv head h / (n_heads / n_kv_heads); the position is read from device memory.
+ * scratch: zero-filled before its first use, left ready by every call. Asynchronous on
+ * `stream` (NULL: per-thread default stream); deterministic bit for bit. */
+int llme_attention(const llme_attention_shape* s, size_t rows, const int* pos_dev,
+                   const float* q, const float* key_cache, const float* value_cache, float* out,
+                   float* scratch, int kernel, void* stream);
+
 /* ---- grouped products ------------------------------------------------------------------------ *
  * Many independent int8 products of the same m in ONE persistent launch. The reference issues
  * one matmul_cuda per projection; products that do not read each other's outputs (a layer's

@@ -1156,7 +1156,7 @@ int llme_synchronize(void) {
     if (e != cudaSuccess) return cuda_fail(e, "synchronize");
     const unsigned dev_err =
         read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error() |
-        read_and_clear_q8tc_error() | read_and_clear_skinny_error();
+        read_and_clear_q8tc_error() | read_and_clear_skinny_error() | read_and_clear_attn_error();
     if (dev_err) return fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up");
     return LLME_OK;
 }
@@ -1180,7 +1180,7 @@ int llme_device_status(void) {
     if (e != cudaSuccess) return cuda_fail(e, "synchronize");
     const unsigned dev_err =
         read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error() |
-        read_and_clear_q8tc_error() | read_and_clear_skinny_error();
+        read_and_clear_q8tc_error() | read_and_clear_skinny_error() | read_and_clear_attn_error();
     return dev_err ? fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up") : LLME_OK;
 }
 

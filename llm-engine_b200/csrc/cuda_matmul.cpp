@@ -154,3 +154,51 @@ Tensor matmul_cuda(const Tensor& A, const QTensor& B, GpuKernel kernel) {
 void cuda_synchronize() { check(llme_synchronize()); }
 
 bool cuda_available() { return llme_device_available() != 0; }
+
+// ---- include/cuda_attention.h over llme_attention* -------------------------------------------
+
+#include "cuda_attention.h"
+
+namespace {
+
+llme_attention_shape c_shape(const AttentionShape& s) {
+    llme_attention_shape c;
+    c.n_heads = s.n_heads;
+    c.n_kv_heads = s.n_kv_heads;
+    c.head_size = s.head_size;
+    c.seq_len = s.seq_len;
+    c.q_stride = s.q_stride;
+    c.kv_stride = s.kv_stride;
+    c.out_stride = s.out_stride;
+    return c;
+}
+
+int attention_kernel_id(AttentionKernel k) {
+    switch (k) {
+        case AttentionKernel::automatic: return LLME_ATTN_AUTOMATIC;
+        case AttentionKernel::single_block: return LLME_ATTN_SINGLE_BLOCK;
+        case AttentionKernel::split: return LLME_ATTN_SPLIT;
+    }
+    return -1;
+}
+
+}  // namespace
+
+std::size_t attention_scratch_floats(const AttentionShape& s, std::size_t rows,
+                                     AttentionKernel kernel) {
+    const llme_attention_shape c = c_shape(s);
+    return llme_attention_scratch_floats(&c, rows, attention_kernel_id(kernel));
+}
+
+void attention_check(const AttentionShape& s, AttentionKernel kernel) {
+    const llme_attention_shape c = c_shape(s);
+    check(llme_attention_check(&c, attention_kernel_id(kernel)));
+}
+
+void attention_cuda(const AttentionShape& s, std::size_t rows, const int* pos_dev, const float* q,
+                    const float* key_cache, const float* value_cache, float* out, float* scratch,
+                    AttentionKernel kernel) {
+    const llme_attention_shape c = c_shape(s);
+    check(llme_attention(&c, rows, pos_dev, q, key_cache, value_cache, out, scratch,
+                         attention_kernel_id(kernel), nullptr));
+}

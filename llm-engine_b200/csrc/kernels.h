@@ -211,6 +211,22 @@ cudaError_t launch_gemm_q8_skinny(const SkinnyArgs& a, const CUtensorMap& tmW,
                                   const CUtensorMap& t2);
 unsigned read_and_clear_skinny_error();
 
+// Causal decode attention (attention.cu). The split kernel's scratch: partial o (rows x
+// heads x splits x head_size), (m, l) pairs, tickets per (row, head group).
+struct AttnArgs {
+    int n_heads = 0, head_size = 0, group = 1, chunk_cap = 0;
+    size_t q_stride = 0, kv_stride = 0, out_stride = 0;
+    const int* pos = nullptr;
+    const float* q = nullptr;
+    const float* k = nullptr;
+    const float* v = nullptr;
+    float* out = nullptr;
+    float* part_o = nullptr;
+    float2* part_ml = nullptr;
+    unsigned* counters = nullptr;
+};
+unsigned read_and_clear_attn_error();
+
 // The reference's quantize_q8 (src/quant.cpp:6-28) on device memory, bit for bit (quant.cu):
 // per-column scale = max|B[:,c]| / 127 and q = clamp(lround(B * (1 / scale)), -127, 127).
 cudaError_t launch_quantize_q8(int k, int n, const float* B, int8_t* q, float* scale,

@@ -92,6 +92,11 @@ def load() -> ctypes.CDLL:
     lib.llme_matmul_q8_noalloc.argtypes = [sz, sz, sz, vp, vp, vp, vp, i, vp]
     lib.llme_matmul_q8_noalloc.restype = i
     lib.llme_quantize_q8.argtypes = [sz, sz, vp, vp, vp, vp]
+    lib.llme_attention_check.argtypes = [ctypes.POINTER(AttentionShape), i]
+    lib.llme_attention_scratch_floats.argtypes = [ctypes.POINTER(AttentionShape), sz, i]
+    lib.llme_attention_scratch_floats.restype = sz
+    lib.llme_attention.argtypes = [ctypes.POINTER(AttentionShape), sz, vp, vp, vp, vp, vp, vp, i,
+                                   vp]
     lib.llme_batch_q8_create.argtypes = [ctypes.POINTER(vp), sz, sz, ctypes.POINTER(Q8Product)]
     lib.llme_batch_run.argtypes = [vp, u, vp]
     lib.llme_batch_destroy.argtypes = [vp]
@@ -167,6 +172,32 @@ def matmul_cuda_q8(m: int, n: int, k: int, A: int, B: int, scale: int, C: int,
     """C (+)= [rmsnorm(A)] x (B * scale) with int8 B on device pointers (cuda_matmul.h:105-107)."""
     _check(load().llme_matmul_q8(m, n, k, A, B, scale, C, _kernel_id(kernel),
                                  int(bool(accumulate)), rms_weight or None, flags, stream or None))
+
+
+class AttentionShape(ctypes.Structure):
+    """llme_attention_shape (the reference's AttentionShape, src/cuda_attention.h:8-14)."""
+    _fields_ = [("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int),
+                ("head_size", ctypes.c_int), ("seq_len", ctypes.c_int),
+                ("q_stride", ctypes.c_size_t), ("kv_stride", ctypes.c_size_t),
+                ("out_stride", ctypes.c_size_t)]
+
+
+ATTN_KERNELS = {"automatic": 0, "single_block": 1, "split": 2}
+
+
+def attention_check(shape: AttentionShape, kernel="automatic") -> None:
+    _check(load().llme_attention_check(ctypes.byref(shape), ATTN_KERNELS[kernel]))
+
+
+def attention_scratch_floats(shape: AttentionShape, rows: int, kernel="automatic") -> int:
+    return load().llme_attention_scratch_floats(ctypes.byref(shape), rows, ATTN_KERNELS[kernel])
+
+
+def attention(shape: AttentionShape, rows: int, pos_dev: int, q: int, k_cache: int, v_cache: int,
+              out: int, scratch: int, kernel="automatic", stream: int | None = None) -> None:
+    """Causal attention over a KV cache on device pointers (cuda_attention.h:38-45)."""
+    _check(load().llme_attention(ctypes.byref(shape), rows, pos_dev, q, k_cache, v_cache, out,
+                                 scratch or None, ATTN_KERNELS[kernel], stream or None))
 
 
 def quantize_q8_cuda(k: int, n: int, W: int, q: int, scale: int, stream: int | None = None) -> None:

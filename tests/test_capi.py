@@ -217,3 +217,26 @@ def test_math_mode_roundtrip():
     L.set_math(prev)
     with pytest.raises(L.InvalidArgument):
         L.set_math(5)
+
+
+def test_attention_check_rules():
+    # The reference's attention_check rules (src/cuda_attention.cu:306-325), host only.
+    S = L.AttentionShape
+    ok = S(8, 2, 64, 1000, 768, 128, 512)
+    for k in ("automatic", "split", "single_block"):
+        L.attention_check(ok, k)
+    with pytest.raises(L.InvalidArgument):        # head_size % 4 for split
+        L.attention_check(S(2, 2, 6, 64, 36, 12, 12), "split")
+    L.attention_check(S(2, 2, 6, 64, 36, 12, 12), "single_block")
+    with pytest.raises(L.InvalidArgument):        # 6 heads over 4 kv heads
+        L.attention_check(S(6, 4, 8, 64, 96, 32, 48), "automatic")
+    with pytest.raises(L.InvalidArgument):        # empty context
+        L.attention_check(S(4, 4, 8, 0, 64, 32, 32), "automatic")
+    long = S(4, 1, 128, 20000, 768, 128, 512)
+    with pytest.raises(L.InvalidArgument):        # single_block's 48 KB of scores
+        L.attention_check(long, "single_block")
+    L.attention_check(long, "split")
+    assert L.attention_scratch_floats(long, 1, "single_block") == 0
+    assert L.attention_scratch_floats(long, 10, "automatic") >= 10 * 4 * 128
+    # automatic splits at most 8 rows when single_block fits
+    assert L.attention_scratch_floats(ok, 100, "automatic") == L.attention_scratch_floats(ok, 8, "split")

@@ -328,3 +328,19 @@ def test_reference_cuda_model_runs_on_the_library(math):
                        text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-4000:]
     assert "all tests passed" in r.stdout
+
+
+ATTN_DROPIN = os.path.join(os.path.dirname(oracle.HERE), "oracle", "_ref",
+                           "test_cuda_attention_dropin")
+
+
+@pytest.mark.skipif(not os.path.exists(ATTN_DROPIN),
+                    reason="oracle/_ref/test_cuda_attention_dropin not built")
+def test_reference_cuda_attention_test_passes_on_the_library():
+    """The reference's tests/test_cuda_attention.cpp, unmodified, against this library's
+    attention (include/cuda_attention.h): every kernel and shape case against its float64
+    reference (5e-5), repeat bits, the long context and the rejections."""
+    r = subprocess.run([ATTN_DROPIN], stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True,
+                       timeout=900)
+    assert r.returncode == 0, r.stdout[-4000:]
+    assert "all tests passed" in r.stdout
