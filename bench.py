@@ -510,6 +510,116 @@ def cpu_sweep_sample(budget_s=2.0):
             "cases": cases}
 
 
+# ---- decode attention over a KV cache (the path after wqkv) ----------------------------------
+
+ATTN_CASES = [  # (name, heads, kv heads, head size, cached positions)
+    ("7B MHA", 32, 32, 128, 4096),
+    ("7B GQA 32/8", 32, 8, 128, 4096),
+    ("MQA long context", 4, 1, 128, 20000),
+]
+ATTN_LAYERS = 8  # distinct caches per step, so the keys and values come from HBM
+
+
+def run_attention(args, world, rank, local):
+    """One decode row (position = the last cached one) through each case, per layer cache,
+    one call each, in a CUDA graph: this library's llme_attention (split kernel) and, on the
+    same inputs, the reference's own GPU kernel (src/cuda_attention.cu built for sm_100a into
+    oracle/_ref/libref_attention.so by `make -C oracle refgpu`), outputs cross-checked.
+    Bytes per call: the keys and values of the context + the query row + the output row."""
+    import ctypes
+    import torch
+    import llme_b200 as L
+    refp = os.path.join(REPO, "oracle", "_ref", "libref_attention.so")
+    ref = ctypes.CDLL(refp) if os.path.exists(refp) else None  # the comparison arm only
+    if ref:
+        sz, vp, ci = ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int
+        ref.ref_attention_scratch_floats.argtypes = [ci, ci, ci, ci, sz, sz, sz, sz, ci]
+        ref.ref_attention_scratch_floats.restype = sz
+        ref.ref_attention.argtypes = [ci, ci, ci, ci, sz, sz, sz, sz, vp, vp, vp, vp, vp, vp, ci]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    stream = torch.cuda.Stream()
+    h = stream.cuda_stream
+    sampler = ClockSampler(local)
+    cases = []
+    tot_bytes = tot_s = 0.0
+    for name, heads, kvh, hs, T in ATTN_CASES:
+        kv, dim = kvh * hs, heads * hs
+        shape = L.AttentionShape(heads, kvh, hs, T, dim + 2 * kv, kv, dim)
+        q = torch.rand(1, dim + 2 * kv, generator=g, device="cuda") * 2 - 1
+        ks = [torch.rand(T, kv, generator=g, device="cuda") * 2 - 1 for _ in range(ATTN_LAYERS)]
+        vs = [torch.rand(T, kv, generator=g, device="cuda") * 2 - 1 for _ in range(ATTN_LAYERS)]
+        pos = torch.full((1,), T - 1, dtype=torch.int32, device="cuda")
+        nbytes = 2 * T * kv * 4 + dim * 4 * 2
+        res = {"case": name, "heads": heads, "kv_heads": kvh, "head_size": hs, "positions": T}
+        arms = [("ours", None)] + ([("reference_gpu", ref)] if ref else [])
+        outs = {}
+        for arm, lib in arms:
+            out = torch.zeros(ATTN_LAYERS, dim, device="cuda")
+            if lib is None:
+                n = L.attention_scratch_floats(shape, 1, "automatic")
+            else:
+                n = lib.ref_attention_scratch_floats(heads, kvh, hs, T, dim + 2 * kv, kv, dim, 1, 0)
+            scratch = torch.zeros(max(1, n), device="cuda")
+
+            def fn():
+                for l in range(ATTN_LAYERS):
+                    if lib is None:
+                        L.attention(shape, 1, pos.data_ptr(), q.data_ptr(), ks[l].data_ptr(),
+                                    vs[l].data_ptr(), out[l].data_ptr(), scratch.data_ptr(),
+                                    "automatic", h)
+                    else:
+                        # the reference runs on the per-thread default stream
+                        assert lib.ref_attention(heads, kvh, hs, T, dim + 2 * kv, kv, dim, 1,
+                                                 pos.data_ptr(), q.data_ptr(), ks[l].data_ptr(),
+                                                 vs[l].data_ptr(), out[l].data_ptr(),
+                                                 scratch.data_ptr(), 0) == 0
+            if lib is None:
+                graph = capture(fn, stream)
+                secs = max_over_ranks(time_graph(graph, args.steps, args.warmup, stream, world,
+                                                 sampler if name == "7B MHA" else None), world)
+                del graph
+            else:
+                for _ in range(args.warmup):
+                    fn()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(torch.cuda.default_stream())
+                for _ in range(args.steps):
+                    fn()
+                torch.cuda.synchronize()
+                e1.record(torch.cuda.default_stream())
+                torch.cuda.synchronize()
+                secs = e0.elapsed_time(e1) / 1e3
+            us = secs / (args.steps * ATTN_LAYERS) * 1e6
+            res[arm] = {"us": round(us, 2), "GB_s": round(nbytes / us / 1e3, 1)}
+            outs[arm] = out.cpu()
+            if arm == "ours":
+                tot_bytes += nbytes * args.steps * ATTN_LAYERS
+                tot_s += secs
+        if "reference_gpu" in outs:
+            res["max_abs_diff_vs_reference"] = float((outs["ours"] - outs["reference_gpu"]).abs().max())
+        cases.append(res)
+    hbm, hbm_kind = peaks()
+    value = tot_bytes / tot_s / 1e9
+    line = {"metric": "decode attention GB/s (KV-cache bytes, 1 row, llme_attention split kernel)",
+            "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(tot_s / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic U(-1,1) queries and caches",
+            "config": {"workload": "decode attention over KV caches (the path after wqkv, "
+                                   "reference cuda_attention.cu), 8 layer caches per case",
+                       "l2": "no flush: 8 distinct caches per case"},
+            "cases": cases,
+            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(value / hbm, 4), "peak_kind": hbm_kind,
+                         "kernel": "attn_split_kernel", "traffic": None},
+            "gpu_launches": len(ATTN_CASES) * ATTN_LAYERS * args.steps,
+            "clocks": sampler.summary()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 # ---- BASELINE configs[4]: the 7B-shaped prefill (m = 512) ----------------------------------
 
 PREFILL_ROWS = 512
@@ -819,6 +929,8 @@ def run_ours(args):
         return run_prefill(args, world, rank, local)
     if args.workload == "sweep":
         return run_sweep(args, world, rank, local)
+    if args.workload == "attention":
+        return run_attention(args, world, rank, local)
     if args.workload == "chain":
         chain = Chain(world, rank, chain_shapes(args.layers), seed=3)
     else:
@@ -989,7 +1101,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["chain", "gemv", "sgemm", "prefill", "sweep"],
+    ap.add_argument("--workload", choices=["chain", "gemv", "sgemm", "prefill", "sweep",
+                                           "attention"],
                     default="chain",
                     help="chain: BASELINE configs[3] (default); gemv: configs[0] alone; "
                          "sgemm: configs[2] (square TF32 GEMM, --size); prefill: configs[4] "

@@ -3,18 +3,21 @@
 //
 // split (flash-decoding; the decode path, few rows): one CTA per (group of G query heads
 // sharing a kv head, row, chunk of positions). Each CTA brings its whole K chunk and V chunk
-// into shared memory at once -- one cp.async.bulk per position row, issued by the 32 lanes of
-// one warp, completing two mbarriers -- so all of the chunk's bytes are in flight from the
-// start; while they land it stages the queries. Scores: a group of lanes per position
-// (head_size / 4 lanes, one float4 each, at most 32), the G queries' float4s held in
-// registers, the dot products finished by shuffles. The chunk's softmax is kept
-// unnormalised (max m, sum l of exp(score - m)) and the exp-weighted sum of values o is
-// formed with one thread per (head, float4 of the head) and position slots. A context that
-// fits one chunk is normalised and written directly; otherwise each CTA writes (o, m, l) to
-// scratch and the CTA that completes the (head group, row)'s ticket merges the chunks in
-// chunk order -- deterministic, no second launch -- and resets the ticket. The grid is sized
-// for seq_len and the context length is read from device memory, so a graph captured once
-// serves every position; chunks past the context exit at once.
+// into shared memory at once -- 2D TMA boxes of 16 positions x head_size floats over the
+// caches (per-position bulk copies for heads wider than 256), completing two mbarriers -- so
+// all of the chunk's bytes are in flight from the start; while they land it stages the
+// queries. Scores: a group of lanes per position (head_size / 4 lanes, one float4 each, at
+// most 32), the G queries' float4s held in registers, the dot products finished by shuffles.
+// The chunk's softmax is kept unnormalised (max m, sum l of exp(score - m)) and the
+// exp-weighted sum of values o is formed with one thread per (head, float4 of the head) and
+// position slots. A context that fits one chunk is normalised and written directly;
+// otherwise each CTA writes (o, m, l) to scratch and the partials are merged in a fixed
+// two-level tree: the CTA completing a group of 64 chunks' ticket merges that group in chunk
+// order, the CTA completing the (head group, row)'s ticket merges the groups in group order --
+// deterministic, no second launch, tickets reset for the next call. Chunks are sized for
+// about two to three CTAs per SM; the grid is sized for seq_len and the context length is
+// read from device memory, so a graph captured once serves every position; chunks past the
+// context exit at once.
 //
 // single_block (many rows): one CTA per (query head, row), the whole context's scores in
 // shared memory: a warp per position for the dot products (coalesced key reads), block
@@ -24,6 +27,7 @@
 // Every mbarrier wait is bounded (common.cuh).
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <string>
 
 #include "common.cuh"
@@ -35,23 +39,108 @@ namespace {
 __device__ unsigned int g_attn_error;
 
 constexpr int kAttnThreads = 256;
-constexpr int kMinChunk = 16;               // positions per split CTA, at least
-constexpr int kMaxSplitsDefault = 256;
-constexpr size_t kSplitSmemBudget = 110 * 1024;  // two CTAs per SM
+constexpr int kMinChunk = 64;               // positions per split CTA, at least
+constexpr int kTargetCtas = 296;            // split CTAs a single row aims for (2 per SM)
+// A split CTA's shared memory, at most: three CTAs per SM, so some load while others compute
+// (measured on B200: 7B MHA decode 41 us against 47 us with two larger CTAs per SM).
+constexpr size_t kSplitSmemBudget = 72 * 1024;
 constexpr size_t kSingleSmemMax = 48 * 1024;     // the interface's documented cap
 constexpr std::size_t kSplitMaxRows = 8;         // automatic: split up to this many rows
 constexpr int kAttnSmemAttr = 200 * 1024;        // dynamic shared memory the kernels may ask for
 
+constexpr int kBoxRows = 16;                // positions per TMA box of keys / values
+
+// Positions per chunk: a multiple of the box height, so only a context's last chunk reads a
+// partial box.
 __host__ __device__ inline int chunk_size(int n_ctx, int splits) {
-    const int c = (n_ctx + splits - 1) / splits;
-    return c > kMinChunk ? c : kMinChunk;
+    int c = (n_ctx + splits - 1) / splits;
+    c = c > kMinChunk ? c : kMinChunk;
+    return (c + kBoxRows - 1) / kBoxRows * kBoxRows;
+}
+
+constexpr int kMergeGroup = 64;             // chunks merged by one CTA at the first level
+
+// Combines partials c0 .. c0 + cnt - 1 (of `stride` per head) of the G heads starting at
+// head_row, in that order: per head (a warp each) M = max m_c, w_c = exp(m_c - M) and
+// L = sum w_c l_c into res[g] = (M, L); then O = sum w_c o_c, `slots` threads per (head,
+// float4) with eight independent loads in flight, added in slot order into red[0 .. pairs).
+// Other CTAs' partials are read through L2 (__ldcg): this SM's L1 may hold stale lines.
+template <int G>
+__device__ void merge_partials(const float2* ml_src, const float4* o_src, size_t head_row,
+                               int stride, int c0, int cnt, int hs4, int pairs, int slots,
+                               float* wts, float2* res, float4* red) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int g = warp; g < G; g += kAttnThreads / 32) {
+        const size_t b = (head_row + g) * stride + c0;
+        float m = -INFINITY;
+        for (int c = lane; c < cnt; c += 32) m = fmaxf(m, __ldcg(&ml_src[b + c]).x);
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.0f;
+        for (int c = lane; c < cnt; c += 32) {
+            const float2 p = __ldcg(&ml_src[b + c]);
+            const float w = expf(p.x - m);
+            wts[g * cnt + c] = w;
+            l += w * p.y;
+        }
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) res[g] = make_float2(m, l);
+    }
+    __syncthreads();
+    for (int base = 0; base < pairs; base += kAttnThreads) {
+        const int j = base + tid % (slots > 1 ? pairs : kAttnThreads);
+        const int r = slots > 1 ? tid / pairs : 0;
+        if (j < pairs && r < slots) {
+            const int g = j / hs4, d4 = j % hs4;
+            const float4* po = o_src + ((head_row + g) * stride + c0) * hs4 + d4;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            int c = r;
+            for (; c + 7 * slots < cnt; c += 8 * slots) {
+                float4 o[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) o[u] = __ldcg(po + static_cast<size_t>(c + u * slots) * hs4);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const float w = wts[g * cnt + c + u * slots];
+                    acc.x += w * o[u].x;
+                    acc.y += w * o[u].y;
+                    acc.z += w * o[u].z;
+                    acc.w += w * o[u].w;
+                }
+            }
+            for (; c < cnt; c += slots) {
+                const float4 o = __ldcg(po + static_cast<size_t>(c) * hs4);
+                const float w = wts[g * cnt + c];
+                acc.x += w * o.x;
+                acc.y += w * o.y;
+                acc.z += w * o.z;
+                acc.w += w * o.w;
+            }
+            red[r * pairs + j] = acc;
+        }
+    }
+    __syncthreads();
+    for (int j = tid; j < pairs; j += kAttnThreads) {
+        float4 acc = red[j];
+        for (int r = 1; r < slots; ++r) {
+            const float4 x = red[r * pairs + j];
+            acc.x += x.x;
+            acc.y += x.y;
+            acc.z += x.z;
+            acc.w += x.w;
+        }
+        red[j] = acc;
+    }
+    __syncthreads();
 }
 
 // The G queries of one lane: float4 number sub + j * lpp of each head, j < QV.
 template <int G, int QV>
 __global__ void __launch_bounds__(kAttnThreads)
-    attn_split_kernel(AttnArgs a) {
-    extern __shared__ __align__(16) float smem[];
+    attn_split_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                      AttnArgs a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    // TMA destinations start on 128-byte boundaries (the launch adds 128 bytes of slack).
+    float* smem = reinterpret_cast<float*>(smem_raw + ((128 - (smem_u32(smem_raw) & 127)) & 127));
     const int hs = a.head_size, hs4 = hs / 4;
     const int cap = a.chunk_cap;
     float* sK = smem;                              // cap x hs
@@ -81,7 +170,22 @@ __global__ void __launch_bounds__(kAttnThreads)
         fence_mbar_init();
     }
     __syncthreads();
-    if (warp == 0) {
+    if (a.boxes) {
+        // Boxes of kBoxRows positions x head_size floats; the last box of a context's final
+        // chunk may cover positions past it (zero fill past the cache) that are never used.
+        if (tid == 0) {
+            const int nbox = (len + kBoxRows - 1) / kBoxRows;
+            const uint32_t box = static_cast<uint32_t>(kBoxRows * hs) * 4;
+            mbar_arrive_expect_tx(&bar[0], box * nbox);
+            mbar_arrive_expect_tx(&bar[1], box * nbox);
+            for (int b = 0; b < nbox; ++b)
+                tma_load_2d_nohint(sK + static_cast<size_t>(b) * kBoxRows * hs, &tmK, kv_off,
+                                   t0 + b * kBoxRows, &bar[0]);
+            for (int b = 0; b < nbox; ++b)
+                tma_load_2d_nohint(sV + static_cast<size_t>(b) * kBoxRows * hs, &tmV, kv_off,
+                                   t0 + b * kBoxRows, &bar[1]);
+        }
+    } else if (warp == 0) {
         const uint32_t bytes = static_cast<uint32_t>(hs) * 4;
         if (lane == 0) {
             mbar_arrive_expect_tx(&bar[0], bytes * len);
@@ -211,39 +315,54 @@ __global__ void __launch_bounds__(kAttnThreads)
     if (n == 1) return;
     if (tid < G) a.part_ml[(head_row + tid) * splits + s] = ml[tid];
 
-    // Publish, then let the CTA that completes the ticket merge.
+    // Merge, two levels deep, fixed order (deterministic): chunks in groups of kMergeGroup, the
+    // CTA that completes a group's ticket merges it into a group partial; the CTA that
+    // completes the (head group, row)'s ticket merges the group partials into the output.
+    const int ngroups = (n + kMergeGroup - 1) / kMergeGroup;
+    const int max_groups = (splits + kMergeGroup - 1) / kMergeGroup;
+    const int grp = s / kMergeGroup, c0 = grp * kMergeGroup;
+    const int cnt = min(kMergeGroup, n - c0);
+    unsigned* tickets = a.counters + (static_cast<size_t>(i) * gridDim.x + hg) * (max_groups + 1);
+    float* wts = reinterpret_cast<float*>(red + slots * pairs);  // G x max(kMergeGroup, groups)
+    // G x (M, L), 16-byte aligned after the weights
+    float2* res = reinterpret_cast<float2*>(wts + (G * max(kMergeGroup, max_groups) + 3) / 4 * 4);
     __threadfence();
     __syncthreads();
     if (tid == 0) {
-        unsigned* c = a.counters + static_cast<size_t>(i) * gridDim.x + hg;
-        last = atomicAdd(c, 1u) == static_cast<unsigned>(n - 1);
-        if (last) *c = 0;  // ready for the next call
+        last = atomicAdd(&tickets[1 + grp], 1u) == static_cast<unsigned>(cnt - 1);
+        if (last) tickets[1 + grp] = 0;  // ready for the next call
     }
     __syncthreads();
     if (!last) return;
     __threadfence();
-    // Other CTAs' partials through L2 (__ldcg): this SM's L1 may hold stale lines.
+    merge_partials<G>(a.part_ml, reinterpret_cast<const float4*>(a.part_o), head_row, splits, c0,
+                      cnt, hs4, pairs, slots, wts, res, red);
+    if (ngroups > 1) {
+        // Publish the group partial, then the last group's CTA merges the groups.
+        for (int j = tid; j < pairs; j += kAttnThreads) {
+            const int g = j / hs4, d4 = j % hs4;
+            reinterpret_cast<float4*>(a.part2_o)[((head_row + g) * max_groups + grp) * hs4 + d4] = red[j];
+        }
+        if (tid < G) a.part2_ml[(head_row + tid) * max_groups + grp] = res[tid];
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            last = atomicAdd(&tickets[0], 1u) == static_cast<unsigned>(ngroups - 1);
+            if (last) tickets[0] = 0;
+        }
+        __syncthreads();
+        if (!last) return;
+        __threadfence();
+        merge_partials<G>(a.part2_ml, reinterpret_cast<const float4*>(a.part2_o), head_row,
+                          max_groups, 0, ngroups, hs4, pairs, slots, wts, res, red);
+    }
     for (int j = tid; j < pairs; j += kAttnThreads) {
         const int g = j / hs4, d4 = j % hs4;
-        const size_t b = (head_row + g) * splits;
-        float m = -INFINITY;
-        for (int c = 0; c < n; ++c) m = fmaxf(m, __ldcg(&a.part_ml[b + c]).x);
-        float l = 0.0f;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int c = 0; c < n; ++c) {
-            const float2 p = __ldcg(&a.part_ml[b + c]);
-            const float w = expf(p.x - m);
-            const float4 o = __ldcg(reinterpret_cast<const float4*>(a.part_o) + (b + c) * hs4 + d4);
-            l += w * p.y;
-            acc.x += w * o.x;
-            acc.y += w * o.y;
-            acc.z += w * o.z;
-            acc.w += w * o.w;
-        }
-        const float inv = 1.0f / l;
+        const float4 o = red[j];
+        const float inv = 1.0f / res[g].y;
         reinterpret_cast<float4*>(a.out + static_cast<size_t>(i) * a.out_stride +
                                   static_cast<size_t>(h0 + g) * hs)[d4] =
-            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
     }
 }
 
@@ -348,25 +467,31 @@ struct SplitGeo {
     size_t smem;
 };
 
-size_t split_smem_bytes(const llme_attention_shape& s, int cap) {
+// K and V chunks, the queries, the scores, the slot sums and the merge's chunk weights.
+size_t split_smem_bytes(const llme_attention_shape& s, int cap, int splits) {
     const size_t G = heads_per_block(s), hs = s.head_size, hs4 = hs / 4;
     const size_t cap4 = (static_cast<size_t>(cap) + 3) / 4 * 4;
     const size_t pairs = G * hs4;
     const size_t slots = std::max<size_t>(1, kAttnThreads / pairs);
+    const size_t groups = (static_cast<size_t>(splits) + kMergeGroup - 1) / kMergeGroup;
+    const size_t wts = (G * std::max<size_t>(kMergeGroup, groups) + 3) / 4 * 4;
     return (2 * static_cast<size_t>(cap) * hs + G * hs + G * cap4) * sizeof(float) +
-           slots * pairs * 16;
+           slots * pairs * 16 + (wts + 2 * G) * sizeof(float) + 128;  // + alignment slack
 }
 
+// Splits: enough for one row to give about kTargetCtas CTAs, no chunk below kMinChunk
+// positions, and more whenever a chunk's keys and values would not fit the shared-memory
+// budget. Independent of the number of rows, so the scratch grows in proportion to rows.
 SplitGeo split_geo(const llme_attention_shape& s) {
-    int splits = std::min(kMaxSplitsDefault, (s.seq_len + kMinChunk - 1) / kMinChunk);
-    splits = std::max(splits, 1);
+    const int groups = s.n_heads / heads_per_block(s);
+    const int most = std::max(1, (s.seq_len + kMinChunk - 1) / kMinChunk);
+    int splits = std::min(most, std::max(1, (kTargetCtas + groups - 1) / groups));
     int cap = chunk_size(s.seq_len, splits);
-    while (split_smem_bytes(s, cap) > kSplitSmemBudget && cap > 1) {
-        splits *= 2;
+    while (split_smem_bytes(s, cap, splits) > kSplitSmemBudget && cap > kMinChunk) {
+        ++splits;
         cap = chunk_size(s.seq_len, splits);
-        if (cap <= kMinChunk) break;
     }
-    return {splits, cap, split_smem_bytes(s, cap)};
+    return {splits, cap, split_smem_bytes(s, cap, splits)};
 }
 
 size_t single_smem_bytes(const llme_attention_shape& s) {
@@ -389,20 +514,27 @@ int resolve(const llme_attention_shape& s, int kernel, size_t rows) {
 
 // Scratch for `rows` rows (floats): partial o, then (m, l) pairs, then a ticket per
 // (row, head group), each part 16-byte aligned.
+// Scratch for `rows` rows (floats): chunk partials o and (m, l), group partials o and
+// (m, l), then per (row, head group) one second-level ticket and a ticket per chunk group;
+// every part 16-byte aligned.
 struct ScratchLayout {
-    size_t o, ml, counters, total;
+    size_t o, ml, o2, ml2, counters, total;
 };
 
 ScratchLayout scratch_layout(const llme_attention_shape& s, size_t rows) {
     const SplitGeo g = split_geo(s);
     const size_t heads = rows * static_cast<size_t>(s.n_heads);
     const size_t chunks = heads * static_cast<size_t>(g.splits);
+    const size_t groups = (static_cast<size_t>(g.splits) + kMergeGroup - 1) / kMergeGroup;
     auto up4 = [](size_t x) { return (x + 3) / 4 * 4; };
     ScratchLayout l{};
     l.o = 0;
     l.ml = up4(chunks * static_cast<size_t>(s.head_size));
-    l.counters = l.ml + up4(2 * chunks);
-    l.total = l.counters + up4(rows * static_cast<size_t>(s.n_heads / heads_per_block(s)));
+    l.o2 = l.ml + up4(2 * chunks);
+    l.ml2 = l.o2 + up4(heads * groups * static_cast<size_t>(s.head_size));
+    l.counters = l.ml2 + up4(2 * heads * groups);
+    l.total = l.counters +
+              up4(rows * static_cast<size_t>(s.n_heads / heads_per_block(s)) * (groups + 1));
     return l;
 }
 
@@ -429,7 +561,8 @@ int check(const llme_attention_shape& s, int kernel) {
 }
 
 template <int G, int QV>
-cudaError_t launch_split(const AttnArgs& a, dim3 grid, size_t smem, cudaStream_t stream) {
+cudaError_t launch_split(const CUtensorMap& tmK, const CUtensorMap& tmV, const AttnArgs& a,
+                         dim3 grid, size_t smem, cudaStream_t stream) {
     static unsigned configured = 0;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -450,18 +583,19 @@ cudaError_t launch_split(const AttnArgs& a, dim3 grid, size_t smem, cudaStream_t
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attn_split_kernel<G, QV>, a);
+    return cudaLaunchKernelEx(&cfg, attn_split_kernel<G, QV>, tmK, tmV, a);
 }
 
 template <int G>
-cudaError_t launch_split_g(const AttnArgs& a, dim3 grid, size_t smem, cudaStream_t stream) {
+cudaError_t launch_split_g(const CUtensorMap& tmK, const CUtensorMap& tmV, const AttnArgs& a,
+                           dim3 grid, size_t smem, cudaStream_t stream) {
     const int hs4 = a.head_size / 4;
     int lpp = 1;
     while (lpp < hs4 && lpp < 32) lpp *= 2;
     const int qv = (hs4 + lpp - 1) / lpp;
-    if (qv <= 1) return launch_split<G, 1>(a, grid, smem, stream);
-    if (qv <= 2) return launch_split<G, 2>(a, grid, smem, stream);
-    return launch_split<G, 4>(a, grid, smem, stream);  // head_size <= 512
+    if (qv <= 1) return launch_split<G, 1>(tmK, tmV, a, grid, smem, stream);
+    if (qv <= 2) return launch_split<G, 2>(tmK, tmV, a, grid, smem, stream);
+    return launch_split<G, 4>(tmK, tmV, a, grid, smem, stream);  // head_size <= 512
 }
 
 }  // namespace
@@ -547,15 +681,31 @@ int llme_attention(const llme_attention_shape* s, size_t rows, const int* pos_de
         a.chunk_cap = g.cap;
         a.part_o = scratch + l.o;
         a.part_ml = reinterpret_cast<float2*>(scratch + l.ml);
+        a.part2_o = scratch + l.o2;
+        a.part2_ml = reinterpret_cast<float2*>(scratch + l.ml2);
         a.counters = reinterpret_cast<unsigned*>(scratch + l.counters);
         const int G = heads_per_block(*s);
         const dim3 grid(static_cast<unsigned>(s->n_heads / G), static_cast<unsigned>(rows),
                         static_cast<unsigned>(g.splits));
+        // Keys and values by TMA boxes over the whole cache (kv_stride floats a row); a head
+        // wider than one box (256 elements) takes the per-position copies.
+        CUtensorMap tmK, tmV;
+        std::memset(&tmK, 0, sizeof(tmK));
+        std::memset(&tmV, 0, sizeof(tmV));
+        a.boxes = s->head_size <= 256;
+        if (a.boxes) {
+            st = tensor_map_2d(key_cache, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, s->seq_len,
+                               s->kv_stride, s->kv_stride * 4, s->head_size, kBoxRows, &tmK);
+            if (!st)
+                st = tensor_map_2d(value_cache, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, s->seq_len,
+                                   s->kv_stride, s->kv_stride * 4, s->head_size, kBoxRows, &tmV);
+            if (st) return st;
+        }
         switch (G) {
-            case 8: e = launch_split_g<8>(a, grid, g.smem, stream); break;
-            case 4: e = launch_split_g<4>(a, grid, g.smem, stream); break;
-            case 2: e = launch_split_g<2>(a, grid, g.smem, stream); break;
-            default: e = launch_split_g<1>(a, grid, g.smem, stream); break;
+            case 8: e = launch_split_g<8>(tmK, tmV, a, grid, g.smem, stream); break;
+            case 4: e = launch_split_g<4>(tmK, tmV, a, grid, g.smem, stream); break;
+            case 2: e = launch_split_g<2>(tmK, tmV, a, grid, g.smem, stream); break;
+            default: e = launch_split_g<1>(tmK, tmV, a, grid, g.smem, stream); break;
         }
     }
     return e == cudaSuccess ? LLME_OK : set_cuda_error(e, "attention");

@@ -1068,6 +1068,12 @@ int batch_create(llme_batch_t** out, size_t m, size_t count, const llme_q8_produ
 }  // namespace
 
 namespace llme {
+int tensor_map_2d(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t rows,
+                  uint64_t cols, uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows,
+                  CUtensorMap* out) {
+    return tensor_map(ptr, dtype, esz, rows, cols, box_cols, box_rows, out,
+                      CU_TENSOR_MAP_SWIZZLE_NONE, pitch_bytes);
+}
 int set_error(int code, const std::string& msg) { return fail(code, msg); }
 int set_cuda_error(cudaError_t e, const char* what) { return cuda_fail(e, what); }
 int run_product(size_t m, size_t n, size_t k, const float* A, const void* B, const float* scale,

@@ -13,6 +13,11 @@ namespace llme {
 // The calling thread's llme_last_error message (defined in capi.cu); return `code`.
 int set_error(int code, const std::string& msg);
 int set_cuda_error(cudaError_t e, const char* what);
+// A cached 2D tensor map (no swizzle) over `rows` x `cols` elements of esz bytes, rows
+// pitch_bytes apart (capi.cu).
+int tensor_map_2d(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t rows,
+                  uint64_t cols, uint64_t pitch_bytes, uint32_t box_cols, uint32_t box_rows,
+                  CUtensorMap* out);
 // The C ABI's products without the public wrapper (capi.cu), for the sharded entry points.
 int run_product(size_t m, size_t n, size_t k, const float* A, const void* B, const float* scale,
                 float* C, bool q8, int kernel, bool accumulate, const float* rms, unsigned flags,
@@ -215,6 +220,7 @@ unsigned read_and_clear_skinny_error();
 // heads x splits x head_size), (m, l) pairs, tickets per (row, head group).
 struct AttnArgs {
     int n_heads = 0, head_size = 0, group = 1, chunk_cap = 0;
+    bool boxes = false;  // keys and values by 2D TMA boxes (head_size <= 256), else row copies
     size_t q_stride = 0, kv_stride = 0, out_stride = 0;
     const int* pos = nullptr;
     const float* q = nullptr;
@@ -223,6 +229,8 @@ struct AttnArgs {
     float* out = nullptr;
     float* part_o = nullptr;
     float2* part_ml = nullptr;
+    float* part2_o = nullptr;     // group partials (the merge's second level)
+    float2* part2_ml = nullptr;
     unsigned* counters = nullptr;
 };
 unsigned read_and_clear_attn_error();
