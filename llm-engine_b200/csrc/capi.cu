@@ -215,6 +215,30 @@ int make_plan(const PlanIn& in, llme_plan_t* p) {
         }
         return LLME_OK;
     }
+    // Decode-shaped fp32 products on tcgen05 in three TF32 terms (the fp32 decode path's
+    // accuracy); A rows come from the RMSNorm pass when there is one.
+    if (skinny_kernel && in.math == LLME_MATH_TENSOR && !in.q8 && n % 4 == 0 && k % 4 == 0 &&
+        in.b_addr % 16 == 0 && (has_rms || in.a_addr % 16 == 0)) {
+        p->path = LLME_PATH_TCGEN05_F32_SKINNY;
+        const int t = skinny_rows_per_tile(static_cast<int>(std::min<size_t>(m, 64)));
+        p->tile_m = t;
+        p->tile_n = 128;
+        p->grid_x = static_cast<int>(ceil_div(n, size_t{128}));
+        p->grid_y = static_cast<int>(ceil_div(m, static_cast<size_t>(t)));
+        const size_t units = static_cast<size_t>(p->grid_x) * p->grid_y;
+        const size_t fk = static_cast<size_t>(f32_skinny_stage_k());
+        const size_t nkb = ceil_div(k, fk);
+        const size_t target = static_cast<size_t>(t <= 16 ? 2 : 1) * sms;
+        // k slices (one cluster, at most 8): fill the GPU once, each at least 8 blocks deep.
+        size_t slices = std::max<size_t>(1, std::min({target / units, ceil_div(nkb, size_t{8}),
+                                                      size_t{8}}));
+        const size_t span_blocks = ceil_div(nkb, slices);
+        slices = ceil_div(nkb, span_blocks);
+        p->slices = static_cast<int>(slices);
+        p->cluster = static_cast<int>(slices);
+        p->span = static_cast<int>(span_blocks * fk);
+        return LLME_OK;
+    }
     // The int8 tcgen05 GEMM: also LLME_MATH_TENSOR only (the activations are split into two
     // int8 terms); W rows must be TMA-addressable and k small enough for exact s32 sums.
     // The RMSNorm of A is applied by the split pass, not by a separate one.
@@ -605,6 +629,26 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
         t.stream = stream;
         t.pdl = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
         e = launch_gemm_tf32(t, tmA, tmB);
+    } else if (p.path == LLME_PATH_TCGEN05_F32_SKINNY) {
+        CUtensorMap tmW, tmA;
+        st = tensor_map(B, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k, n, 32, 32, &tmW,
+                        CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+        if (!st)
+            st = tensor_map(a_in, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, k, 32, p.tile_m, &tmA,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+        if (st) return st;
+        F32SkinnyArgs t;
+        t.m = static_cast<int>(m);
+        t.n = static_cast<int>(n);
+        t.k = static_cast<int>(k);
+        t.C = C;
+        t.accumulate = accumulate;
+        t.weights_static = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
+        t.rows_per_tile = p.tile_m;
+        t.slices = p.slices;
+        t.span_blocks = p.span / f32_skinny_stage_k();
+        t.stream = stream;
+        e = launch_gemm_f32_skinny(t, tmW, tmA);
     } else if (p.path == LLME_PATH_TCGEN05_SKINNY) {
         float* ops = nullptr;
         st = ensure_buffer(g_dev[dev].operand, p.operand_bytes, &ops);
@@ -1162,7 +1206,8 @@ int llme_synchronize(void) {
     if (e != cudaSuccess) return cuda_fail(e, "synchronize");
     const unsigned dev_err =
         read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error() |
-        read_and_clear_q8tc_error() | read_and_clear_skinny_error() | read_and_clear_attn_error();
+        read_and_clear_q8tc_error() | read_and_clear_skinny_error() | read_and_clear_attn_error() |
+        read_and_clear_f32sk_error();
     if (dev_err) return fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up");
     return LLME_OK;
 }
@@ -1186,7 +1231,8 @@ int llme_device_status(void) {
     if (e != cudaSuccess) return cuda_fail(e, "synchronize");
     const unsigned dev_err =
         read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error() |
-        read_and_clear_q8tc_error() | read_and_clear_skinny_error() | read_and_clear_attn_error();
+        read_and_clear_q8tc_error() | read_and_clear_skinny_error() | read_and_clear_attn_error() |
+        read_and_clear_f32sk_error();
     return dev_err ? fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up") : LLME_OK;
 }
 

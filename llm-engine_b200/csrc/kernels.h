@@ -235,6 +235,25 @@ struct AttnArgs {
 };
 unsigned read_and_clear_attn_error();
 
+// Decode-shaped fp32-weight products on tcgen05 in three TF32 terms (gemm_f32_skinny.cu):
+// one CTA per (128 columns, rows_per_tile rows, k slice); the k slices of a tile form one
+// thread-block cluster (at most 8) and add their partials through DSMEM in rank order.
+// Requirements: A and B rows 16-byte aligned (k % 4 == 0, n % 4 == 0).
+struct F32SkinnyArgs {
+    int m = 0, n = 0, k = 0;
+    float* C = nullptr;
+    bool accumulate = false;
+    bool weights_static = false;
+    int rows_per_tile = 16;   // 16, 32 or 64
+    int slices = 1;           // grid z = cluster size, at most 8
+    int span_blocks = 0;      // 32-deep k blocks per slice
+    cudaStream_t stream = nullptr;
+};
+int f32_skinny_stage_k();
+cudaError_t launch_gemm_f32_skinny(const F32SkinnyArgs& a, const CUtensorMap& tmW,
+                                   const CUtensorMap& tmA);
+unsigned read_and_clear_f32sk_error();
+
 // The reference's quantize_q8 (src/quant.cpp:6-28) on device memory, bit for bit (quant.cu):
 // per-column scale = max|B[:,c]| / 127 and q = clamp(lround(B * (1 / scale)), -127, 127).
 cudaError_t launch_quantize_q8(int k, int n, const float* B, int8_t* q, float* scale,

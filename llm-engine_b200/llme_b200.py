@@ -22,7 +22,8 @@ LIB_PATH = os.path.join(PKG, "lib", "libllme_b200.so")
 
 KERNELS = {"automatic": 0, "naive": 1, "tiled": 2, "tiled_split": 3, "skinny": 4}
 PATHS = {0: "none", 1: "zero", 2: "naive", 3: "gemv_tma", 4: "gemv_ldg", 5: "tiled_simt",
-         6: "tcgen05", 7: "tcgen05_q8", 8: "tcgen05_skinny"}
+         6: "tcgen05", 7: "tcgen05_q8", 8: "tcgen05_skinny",
+         9: "tcgen05_f32_skinny"}
 MATH_TENSOR, MATH_FP32 = 0, 1
 FLAG_WEIGHTS_STATIC = 1
 

@@ -134,7 +134,8 @@ def test_tcgen05_path_choice():
     # TF32 tensor cores for m >= 128 with TMA-addressable fp32 operands, in tensor math only.
     assert L.plan(128, 4096, 4096, q8=False)["path_name"] == "tcgen05"
     assert L.plan(8192, 8192, 8192, q8=False)["grid_x"] == 64 * 32
-    assert L.plan(127, 4096, 4096, q8=False)["path_name"] == "tiled_simt"
+    assert L.plan(127, 4096, 4096, q8=False)["path_name"] == "tcgen05_f32_skinny"
+    assert L.plan(127, 4096, 4096, q8=False, math=L.MATH_FP32)["path_name"] == "tiled_simt"
     assert L.plan(128, 4096, 4096, q8=False, math=L.MATH_FP32)["path_name"] == "tiled_simt"
     assert L.plan(128, 1030, 4096, q8=False)["path_name"] == "tiled_simt"   # n % 4
     assert L.plan(128, 1028, 513, q8=False)["path_name"] == "tiled_simt"    # k % 4
@@ -169,7 +170,34 @@ def test_tcgen05_skinny_plan():
     assert L.plan(4, 4096, 4096, q8=True, kernel="tiled_split")["path_name"] == "tcgen05_skinny"
     assert L.plan(16, 4096, 4096, q8=True, math=L.MATH_FP32)["path_name"] == "tiled_simt"
     assert L.plan(16, 4104, 4096, q8=True)["path_name"] == "tiled_simt"     # n % 16
-    assert L.plan(16, 4096, 4096, q8=False)["path_name"] == "tiled_simt"    # fp32 weights
+    assert L.plan(16, 4096, 4096, q8=False)["path_name"] == "tcgen05_f32_skinny"  # fp32 W
+
+
+def test_tcgen05_f32_skinny_plan():
+    # Decode-shaped fp32 weights (tiled_split, or tiled below 128 rows) in tensor math: three
+    # TF32 terms, k slices as one thread-block cluster of at most 8.
+    p = L.plan(16, 4096, 4096, q8=False)
+    assert p["path_name"] == "tcgen05_f32_skinny" and p["kernel"] == 3
+    assert (p["tile_m"], p["tile_n"], p["grid_x"], p["grid_y"]) == (16, 128, 32, 1)
+    assert p["slices"] == 8 and p["cluster"] == 8 and p["span"] == 512   # 256 CTAs, 2 per SM
+    assert p["split_bytes"] == 0 and p["counter_slots"] == 0 and p["operand_bytes"] == 0
+    p = L.plan(64, 4096, 4096, q8=False)
+    assert (p["tile_m"], p["slices"], p["span"]) == (64, 4, 1024)        # 128 CTAs, 1 per SM
+    p = L.plan(100, 11008, 4096, q8=False)
+    assert (p["tile_m"], p["grid_x"], p["grid_y"], p["slices"]) == (64, 86, 2, 1)
+    for m, k in [(9, 4096), (33, 11008), (127, 100), (20, 4)]:
+        p = L.plan(m, 4096, k, q8=False)
+        assert p["slices"] <= 8 and p["span"] % 32 == 0
+        assert (p["slices"] - 1) * p["span"] < k <= p["slices"] * p["span"]
+    assert L.plan(4, 4096, 4096, q8=False, kernel="tiled_split")["path_name"] == \
+        "tcgen05_f32_skinny"
+    assert L.plan(4, 4096, 4096, q8=False)["path_name"] == "gemv_tma"
+    p = L.plan(24, 1028, 512, q8=False, a_addr=260, rms_addr=256)
+    assert p["path_name"] == "tcgen05_f32_skinny" and p["rms_prepass"] == 1
+    assert L.plan(24, 1028, 512, q8=False, a_addr=260)["path_name"] == "tiled_simt"
+    assert L.plan(24, 1030, 512, q8=False)["path_name"] == "tiled_simt"   # n % 4
+    assert L.plan(24, 1028, 514, q8=False)["path_name"] == "tiled_simt"   # k % 4
+    assert L.plan(24, 1028, 512, q8=False, b_addr=8)["path_name"] == "tiled_simt"
 
 
 def test_tcgen05_q8_cta_pairs_plan(monkeypatch):
