@@ -228,7 +228,7 @@ int make_plan(const PlanIn& in, llme_plan_t* p) {
         const size_t units = static_cast<size_t>(p->grid_x) * p->grid_y;
         const size_t fk = static_cast<size_t>(f32_skinny_stage_k());
         const size_t nkb = ceil_div(k, fk);
-        const size_t target = static_cast<size_t>(t <= 16 ? 2 : 1) * sms;
+        const size_t target = static_cast<size_t>(sms);  // one CTA per SM
         // k slices (one cluster, at most 8): fill the GPU once, each at least 8 blocks deep.
         size_t slices = std::max<size_t>(1, std::min({target / units, ceil_div(nkb, size_t{8}),
                                                       size_t{8}}));
@@ -631,8 +631,7 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
         e = launch_gemm_tf32(t, tmA, tmB);
     } else if (p.path == LLME_PATH_TCGEN05_F32_SKINNY) {
         CUtensorMap tmW, tmA;
-        st = tensor_map(B, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k, n, 32, 32, &tmW,
-                        CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+        st = tensor_map(B, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k, n, 128, 32, &tmW);
         if (!st)
             st = tensor_map(a_in, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, k, 32, p.tile_m, &tmA,
                             CU_TENSOR_MAP_SWIZZLE_128B);
@@ -791,11 +790,15 @@ int run_noalloc(size_t m, size_t n, size_t k, const float* A, const int8_t* B, c
     if (st) return st;
     st = device_sms(dev, &sms);
     if (st) return st;
+    // The plan of the kernel this entry point launches (the SIMT tiles with split k), whatever
+    // the process-wide arithmetic would pick for tiled_split.
     PlanIn in{m, n, k, true, LLME_KERNEL_TILED_SPLIT, accumulate, reinterpret_cast<uintptr_t>(A),
-              reinterpret_cast<uintptr_t>(B), 0, sms, math_mode()};
+              reinterpret_cast<uintptr_t>(B), 0, sms, LLME_MATH_FP32};
     llme_plan_t p;
     st = make_plan(in, &p);
     if (st) return st;
+    if (p.path != LLME_PATH_TILED_SIMT && p.path != LLME_PATH_NONE && p.path != LLME_PATH_ZERO)
+        return fail(LLME_E_UNSUPPORTED, "llme_matmul_q8_noalloc: no split-K tile plan " + shapes(m, n, k));
     if (p.path == LLME_PATH_NONE) return LLME_OK;
     if (p.path == LLME_PATH_ZERO) {
         cudaError_t e = cudaMemsetAsync(C, 0, m * n * sizeof(float), stream);

@@ -179,7 +179,7 @@ def test_tcgen05_f32_skinny_plan():
     p = L.plan(16, 4096, 4096, q8=False)
     assert p["path_name"] == "tcgen05_f32_skinny" and p["kernel"] == 3
     assert (p["tile_m"], p["tile_n"], p["grid_x"], p["grid_y"]) == (16, 128, 32, 1)
-    assert p["slices"] == 8 and p["cluster"] == 8 and p["span"] == 512   # 256 CTAs, 2 per SM
+    assert p["slices"] == 4 and p["cluster"] == 4 and p["span"] == 1024  # 128 CTAs, 1 per SM
     assert p["split_bytes"] == 0 and p["counter_slots"] == 0 and p["operand_bytes"] == 0
     p = L.plan(64, 4096, 4096, q8=False)
     assert (p["tile_m"], p["slices"], p["span"]) == (64, 4, 1024)        # 128 CTAs, 1 per SM

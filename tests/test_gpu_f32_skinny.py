@@ -105,8 +105,8 @@ def test_f32_skinny_fusion():
 def test_f32_skinny_accumulate_through_a_cluster():
     # k split over 8 CTAs: C += A W read and written once, by the CTA that owns the row.
     rng = np.random.default_rng(14)
-    A, W, C0 = uni(rng, 16, 4096), weights(rng, 4096, 4096), uni(rng, 16, 4096)
-    assert L.plan(16, 4096, 4096, q8=False)["slices"] == 8
+    A, W, C0 = uni(rng, 16, 4096), weights(rng, 4096, 1024), uni(rng, 16, 1024)
+    assert L.plan(16, 1024, 4096, q8=False)["slices"] == 8
     got = run(A, W, C0=C0, accumulate=True)
     assert row_rel_err(got, C0 + oracle.matmul_naive(A, W)) <= 1e-5
 
