@@ -356,7 +356,7 @@ def gemv_4096_probe(steps=200):
 
 def run_sgemm(args, world, rank, local):
     """C = A x B, fp32 N x N, A and B ~ U(-1, 1) (seed 2), through the
-    C ABI on the tcgen05 TF32 path (including its B^T re-layout pass). Inputs 768 MB > L2."""
+    C ABI on the tcgen05 TF32 path (B read as stored, MN-major). Inputs 768 MB > L2."""
     import torch
     import llme_b200 as L
     n = args.size
@@ -392,7 +392,7 @@ def run_sgemm(args, world, rank, local):
                        "l2": "no flush: 768 MB of operands (> 126 MB L2)"},
             "roofline": {"bound": "tensor", "achieved": round(tflops / world, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(tflops / world / peak, 4),
-                         "peak_kind": kind, "kernel": "gemm_tf32_kernel (+ transpose)",
+                         "peak_kind": kind, "kernel": "gemm_tf32_kernel",
                          "traffic": None},
             "gpu_launches": 2 * args.steps, "clocks": sampler.summary()}
     if rank == 0:

@@ -53,12 +53,15 @@ enum {
 
 /* ---- arithmetic of the tensor-core path ------------------------------------------------ */
 enum {
-    /* The tensor-core GEMM multiplies in TF32 (fp32 B) or bf16 (int8 B, exact; A rounded
-       to bf16), accumulating in fp32. Error bound: 5e-3 of the row's L2 norm. Default. */
+    /* Tensor cores (tcgen05) where they pay. m >= 128: fp32 B multiplies in TF32, int8 B
+       in kind::i8 against the activations split into two int8 terms (16 bits), both
+       accumulating in fp32 / s32; error bound 5e-3 of the row's L2 norm. 9 <= m <= 127
+       (and tiled_split): three TF32 terms (fp32 B) or three int8 activation terms (int8 B),
+       the fp32 decode path's bound of 1e-5. m <= 8: the fp32-FMA GEMV. Default. */
     LLME_MATH_TENSOR = 0,
-    /* fp32-faithful: every kernel keeps fp32 products (the tensor-core GEMM splits each
-       operand into high and low parts and runs three products), as the reference's SIMT
-       kernels do. Selected at load time by LLME_B200_MATH=fp32 in the environment. */
+    /* fp32-faithful: every product with m >= 9 runs on the SIMT tiles with fp32 FMA, as the
+       reference's kernels do (the GEMV is fp32 FMA in both modes). Selected at load time by
+       LLME_B200_MATH=fp32 in the environment. */
     LLME_MATH_FP32 = 1
 };
 
@@ -290,8 +293,9 @@ typedef struct {
     size_t split_bytes;   /* split-K scratch: partial sums (0 when slices == 1) */
     size_t counter_slots; /* split-K tickets needed (one per output tile) */
     size_t norm_bytes;    /* scratch for the normalised copy of A (rms_prepass) */
-    size_t operand_bytes; /* scratch for re-laid-out operands: B^T (TF32 tensor-core GEMM) or
-                             the int8 hi / lo activation rows and row scales (int8 one) */
+    size_t operand_bytes; /* scratch for re-laid-out operands: the int8 hi / lo (/ third)
+                             activation rows and row scales of the int8 tensor-core GEMMs, or
+                             B^T for the TF32 GEMM at m >= 6144 */
 } llme_plan_t;
 
 /* The plan llme_matmul_f32 (is_q8 == 0) or llme_matmul_q8 (is_q8 == 1) would follow on a

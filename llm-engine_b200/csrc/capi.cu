@@ -178,7 +178,8 @@ int make_plan(const PlanIn& in, llme_plan_t* p) {
         p->path = LLME_PATH_TCGEN05;
         p->tile_m = tc_tile_m();
         p->tile_n = tc_tile_n();
-        p->operand_bytes = k * n * sizeof(float);  // B^T for the K-major MMA operand
+        // B^T for the K-major operand only where the pass repays itself.
+        if (m >= kTcTransposeMinRows) p->operand_bytes = k * n * sizeof(float);
         p->grid_x = static_cast<int>(ceil_div(m, p->tile_m) * ceil_div(n, p->tile_n));
         p->grid_y = 1;
         p->slices = 1;
@@ -303,7 +304,7 @@ struct DeviceState {
     size_t counter_cap = 0;
     size_t partial_cap = 0;
     Scratch norm;
-    Scratch operand;  // transposed weights for the tensor-core GEMM
+    Scratch operand;  // split activation rows (int8 tensor-core GEMMs) or B^T (TF32 GEMM)
     // Skinny tcgen05 GEMM: [tickets: skinny_counters x u32][int64 sums], zero between launches
     // (zeroed when it grows; each launch leaves it zero).
     Scratch skinny;
@@ -605,18 +606,24 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
             e = launch_gemv_ldg(g);
         }
     } else if (p.path == LLME_PATH_TCGEN05) {
-        float* bt = nullptr;
-        st = ensure_buffer(g_dev[dev].operand, p.operand_bytes, &bt);
-        if (st) return st;
-        e = launch_transpose(static_cast<const float*>(B), bt, static_cast<int>(k),
-                             static_cast<int>(n), stream);
-        if (e != cudaSuccess) return cuda_fail(e, "launch");
         CUtensorMap tmA, tmB;
         st = tensor_map(a_in, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, k, 32, 128, &tmA,
                         CU_TENSOR_MAP_SWIZZLE_128B);
         if (st) return st;
-        st = tensor_map(bt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, n, k, 32, 256, &tmB,
-                        CU_TENSOR_MAP_SWIZZLE_128B);
+        const bool transposed = p.operand_bytes > 0;
+        if (transposed) {
+            float* bt = nullptr;
+            st = ensure_buffer(g_dev[dev].operand, p.operand_bytes, &bt);
+            if (st) return st;
+            e = launch_transpose(static_cast<const float*>(B), bt, static_cast<int>(k),
+                                 static_cast<int>(n), stream);
+            if (e != cudaSuccess) return cuda_fail(e, "launch");
+            st = tensor_map(bt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, n, k, 32, 256, &tmB,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+        } else {
+            st = tensor_map(B, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k, n, 32, 32, &tmB,
+                            CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+        }
         if (st) return st;
         TcArgs t;
         t.m = static_cast<int>(m);
@@ -624,6 +631,7 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
         t.k = static_cast<int>(k);
         t.C = C;
         t.accumulate = accumulate;
+        t.b_transposed = transposed;
         t.tiles_m = static_cast<int>(ceil_div(m, p.tile_m));
         t.tiles_n = static_cast<int>(ceil_div(n, p.tile_n));
         t.stream = stream;

@@ -4,11 +4,14 @@
 //
 // The reference runs these shapes on its SIMT sgemm_tiled<128,8>
 // (src/cuda_matmul.cu:71-125). Here one CTA per SM computes a 128 x 256 tile:
-//   warp 0      one thread issues TMA loads of A and B, both K-major and
-//               128-byte swizzled, into a 4-stage ring guarded by mbarriers
-//               (B is stored k x n, n contiguous; a transpose pass first
-//               writes B^T, n x k, into scratch -- the TF32 MMA is run with
-//               both operands K-major);
+//   warp 0      one thread issues TMA loads into a 4-stage ring guarded by
+//               mbarriers: A K-major (128-byte swizzle); B either straight
+//               from the caller's k x n weights as the MN-major operand --
+//               eight 32-column boxes per stage in the 128-byte swizzle with
+//               32-byte atoms, the layout tcgen05 takes for 32-bit MN-major
+//               operands -- or, for m large enough to repay a transpose pass
+//               (the MN-major MMAs run ~9% slower), from B^T written by that
+//               pass, K-major like A;
 //   warp 1      allocates 256 TMEM columns; one thread issues
 //               tcgen05.mma.kind::tf32 (M=128, N=256, K=8) four times per
 //               32-deep stage and releases each stage with tcgen05.commit;
@@ -29,12 +32,14 @@ constexpr int TBM = 128, TBN = 256, TBK = 32;  // 32 fp32 = 128 bytes along K
 constexpr int kStages = 4;
 constexpr int kThreads = 192;
 constexpr int kABytes = TBM * TBK * 4;        // 16 KB
-constexpr int kBBytes = TBK * TBN * 4;        // 32 KB: B^T box of 256 rows (n) x 32 (k)
+constexpr int kBBytes = TBK * TBN * 4;        // 32 KB: B^T box of 256 rows (n) x 32 (k), or
+constexpr int kBBoxBytes = TBK * 32 * 4;      // 8 MN-major boxes of 32 rows (k) x 32 columns
 constexpr int kRingBytes = kStages * (kABytes + kBBytes);
 constexpr int kSmemBytes = kRingBytes + 256 + 1024;  // barriers + alignment slack
 constexpr int kGroupM = 8;
 constexpr uint32_t kTmemCols = 256;
 
+template <bool BMn>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const TcArgs a) {
@@ -85,12 +90,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
                 tma_load_2d_nohint(sA + s * kABytes, &tmA, kb * TBK, m0, &full[s]);
-                tma_load_2d_nohint(sB + s * kBBytes, &tmB, kb * TBK, n0, &full[s]);
+                if (BMn) {
+#pragma unroll
+                    for (int j = 0; j < TBN / 32; ++j)
+                        tma_load_2d_nohint(sB + s * kBBytes + j * kBBoxBytes, &tmB, n0 + j * 32,
+                                           kb * TBK, &full[s]);
+                } else {
+                    tma_load_2d_nohint(sB + s * kBBytes, &tmB, kb * TBK, n0, &full[s]);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::instr_desc(tc::kFmtTF32, tc::kFmtTF32, false, false, TBM, TBN);
+            constexpr uint32_t idesc = tc::instr_desc(tc::kFmtTF32, tc::kFmtTF32, false, BMn, TBM, TBN);
             for (int kb = 0; kb < nk; ++kb) {
                 const int s = kb % kStages;
                 if (!mbar_wait(&full[s], (kb / kStages) & 1, &g_tc_error)) break;
@@ -99,10 +111,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t bbase = smem_u32(sB + s * kBBytes);
 #pragma unroll
                 for (int kk = 0; kk < TBK / 8; ++kk) {
-                    // K-major rows of 128 B (8-row groups 1 KB apart); the 8-deep K step is
-                    // 32 B into each row.
+                    // K-major rows of 128 B (8-row groups 1 KB apart), the 8-deep K step
+                    // 32 B into each row; MN-major B: the K step is 8 rows = 1 KB.
                     const uint64_t ad = tc::smem_desc_sw128(abase + kk * 32, 16, 1024);
-                    const uint64_t bd = tc::smem_desc_sw128(bbase + kk * 32, 16, 1024);
+                    const uint64_t bd = BMn ? tc::smem_desc_sw128_32b(bbase + kk * 1024, kBBoxBytes)
+                                            : tc::smem_desc_sw128(bbase + kk * 32, 16, 1024);
                     tc::mma_tf32(tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
                 }
                 tc::commit(&empty[s]);
@@ -178,23 +191,13 @@ __global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict_
     }
 }
 
-}  // namespace
-
-cudaError_t launch_transpose(const float* B, float* out, int k, int n, cudaStream_t stream) {
-    const dim3 grid((n + 31) / 32, (k + 31) / 32);
-    transpose_kernel<<<grid, 256, 0, stream>>>(B, out, k, n);
-    return cudaGetLastError();
-}
-
-int tc_tile_m() { return TBM; }
-int tc_tile_n() { return TBN; }
-
-cudaError_t launch_gemm_tf32(const TcArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB) {
+template <bool BMn>
+cudaError_t launch_t(const TcArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB) {
     static unsigned configured = 0;
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 32 && !(configured & (1u << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_tf32_kernel,
+        cudaError_t e = cudaFuncSetAttribute(gemm_tf32_kernel<BMn>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
         if (e != cudaSuccess) return e;
         configured |= 1u << dev;
@@ -211,7 +214,22 @@ cudaError_t launch_gemm_tf32(const TcArgs& a, const CUtensorMap& tmA, const CUte
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    return cudaLaunchKernelEx(&cfg, gemm_tf32_kernel, tmA, tmB, a);
+    return cudaLaunchKernelEx(&cfg, gemm_tf32_kernel<BMn>, tmA, tmB, a);
+}
+
+}  // namespace
+
+cudaError_t launch_transpose(const float* B, float* out, int k, int n, cudaStream_t stream) {
+    const dim3 grid((n + 31) / 32, (k + 31) / 32);
+    transpose_kernel<<<grid, 256, 0, stream>>>(B, out, k, n);
+    return cudaGetLastError();
+}
+
+int tc_tile_m() { return TBM; }
+int tc_tile_n() { return TBN; }
+
+cudaError_t launch_gemm_tf32(const TcArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB) {
+    return a.b_transposed ? launch_t<false>(a, tmA, tmB) : launch_t<true>(a, tmA, tmB);
 }
 
 unsigned read_and_clear_tc_error() {

@@ -114,18 +114,23 @@ cudaError_t launch_tiled_simt(const TiledArgs& a);
 cudaError_t launch_naive(const TiledArgs& a);
 
 // tcgen05 tensor-core GEMM (gemm_tc.cu): 128 x 256 output tiles, TF32 operands read by
-// TMA with 128-byte swizzle, both K-major (A: box 32 x 128 of A; B: box 32 x 256 of B^T).
+// TMA: A K-major (box 32 x 128, 128-byte swizzle); B as stored, MN-major (8 boxes of 32 x 32,
+// 128-byte swizzle with 32-byte atoms), or with b_transposed from B^T written by
+// launch_transpose, K-major (box 32 x 256, 128-byte swizzle).
 struct TcArgs {
     int m = 0, n = 0, k = 0;
     float* C = nullptr;
     bool accumulate = false;
+    bool b_transposed = false;
     int tiles_m = 0, tiles_n = 0;
     cudaStream_t stream = nullptr;
     bool pdl = false;
 };
 int tc_tile_m();
 int tc_tile_n();
-cudaError_t launch_gemm_tf32(const TcArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmBt);
+// Rows of A from which a B^T pass pays for itself (the MN-major MMAs run ~9% slower).
+constexpr size_t kTcTransposeMinRows = 6144;
+cudaError_t launch_gemm_tf32(const TcArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB);
 // out (n x k) = B^T for fp32 B (k x n).
 cudaError_t launch_transpose(const float* B, float* out, int k, int n, cudaStream_t stream);
 unsigned read_and_clear_tc_error();

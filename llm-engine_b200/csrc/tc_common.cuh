@@ -30,6 +30,13 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
     return d;
 }
 
+// 32-bit MN-major operands (kind::tf32, k x n as stored) take the 128-byte swizzle with
+// 32-byte atoms (TMA CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, layout type 1): 128-byte runs along
+// M/N, 4-row atoms of 512 bytes along K (SBO = 512), LBO = distance between 32-column runs.
+__device__ __forceinline__ uint64_t smem_desc_sw128_32b(uint32_t saddr, uint32_t lbo) {
+    return (smem_desc_sw128(saddr, lbo, 512) & ~(7ull << 61)) | (1ull << 61);
+}
+
 // Instruction descriptor (32 bit) for dense MMA with an fp32 accumulator:
 //   [4,6) D format (1 = f32)  [7,10) A format  [10,13) B format
 //   [15] A major (0 = K, 1 = MN)  [16] B major  [17,23) N >> 3  [24,29) M >> 4

@@ -134,6 +134,9 @@ def test_tcgen05_path_choice():
     # TF32 tensor cores for m >= 128 with TMA-addressable fp32 operands, in tensor math only.
     assert L.plan(128, 4096, 4096, q8=False)["path_name"] == "tcgen05"
     assert L.plan(8192, 8192, 8192, q8=False)["grid_x"] == 64 * 32
+    # B read as stored (MN-major operand) below 6144 rows; a B^T pass from there on.
+    assert L.plan(6143, 4096, 1024, q8=False)["operand_bytes"] == 0
+    assert L.plan(6144, 4096, 1024, q8=False)["operand_bytes"] == 4096 * 1024 * 4
     assert L.plan(127, 4096, 4096, q8=False)["path_name"] == "tcgen05_f32_skinny"
     assert L.plan(127, 4096, 4096, q8=False, math=L.MATH_FP32)["path_name"] == "tiled_simt"
     assert L.plan(128, 4096, 4096, q8=False, math=L.MATH_FP32)["path_name"] == "tiled_simt"

@@ -54,9 +54,12 @@ def _tensor_math():
     L.device_status()
 
 
+# B read as stored (MN-major) below 6144 rows; from 6144 rows through a B^T pass (K-major).
 @pytest.mark.parametrize("m,k,n", [(128, 32, 256), (128, 256, 256), (256, 512, 512),
-                                   (130, 72, 1028), (300, 1000, 260), (128, 4096, 4096)])
+                                   (130, 72, 1028), (300, 1000, 260), (128, 4096, 4096),
+                                   (6200, 264, 516), (6144, 96, 260), (4096, 96, 260)])
 def test_tf32_gemm_matches_oracle(m, k, n):
+    assert (L.plan(m, n, k, q8=False)["operand_bytes"] > 0) == (m >= 6144)
     rng = np.random.default_rng(m + 3 * k + 7 * n)
     A, B = uni(rng, m, k), uni(rng, k, n)
     got = run(A, B)
