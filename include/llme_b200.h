@@ -178,6 +178,30 @@ int llme_attention(const llme_attention_shape* s, size_t rows, const int* pos_de
                    const float* q, const float* key_cache, const float* value_cache, float* out,
                    float* scratch, int kernel, void* stream);
 
+/* ---- decode-step helpers (the transformer's elementwise steps, one rank's heads) ------------ *
+ * The steps of a decoder layer around the matmuls and the attention (the reference's
+ * src/cuda_model.cu:22-75 kernels and src/model.cpp:171-184 RoPE tables), for the
+ * tensor-parallel transformer: a rank holds nq query heads and nkv kv heads, and a qkv row is
+ * [q: nq * head_size | k: nkv * head_size | v: nkv * head_size]. Positions and token ids are
+ * read from device memory, feed[0] = the first position, feed[1 .. n] = the tokens, so one
+ * captured graph serves every position. All asynchronous on `stream` (NULL: per-thread
+ * default stream). */
+/* x[i] = table[feed[1 + i]] (rows of dim floats), i < n; token ids must lie in the table. */
+int llme_embed_rows(size_t n, size_t dim, const int* feed, const float* table, float* x,
+                    void* stream);
+/* For row i at position feed[0] + i: rotates each (even, odd) pair of q and k by the angle of
+ * the pair's index within its head (cos / sin: seq_len x head_size / 2, llme_rope_tables), and
+ * writes the rotated k and the v row into the caches (rows of nkv * head_size floats) at that
+ * position. head_size even. */
+int llme_rope_cache(size_t n, int nq, int nkv, int head_size, const int* feed, const float* cos,
+                    const float* sin, float* qkv, float* key_cache, float* value_cache,
+                    void* stream);
+/* hb[r][c] = silu(gu[r][c]) * gu[r][hidden + c] for r < n, c < hidden (SwiGLU, gate | up). */
+int llme_swiglu(size_t n, size_t hidden, const float* gu, float* hb, void* stream);
+/* Host: the RoPE angle tables (seq_len x head_size / 2 each) with the reference's float
+ * expressions, cos[p][j] = cos(p / 10000^(2j / head_size)). */
+int llme_rope_tables(size_t seq_len, size_t head_size, float* cos, float* sin);
+
 /* ---- grouped products ------------------------------------------------------------------------ *
  * Many independent int8 products of the same m in ONE persistent launch. The reference issues
  * one matmul_cuda per projection; products that do not read each other's outputs (a layer's

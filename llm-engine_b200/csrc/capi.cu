@@ -1157,6 +1157,55 @@ int llme_quantize_q8(size_t k, size_t n, const float* W, int8_t* q, float* scale
     return e == cudaSuccess ? LLME_OK : cuda_fail(e, "quantize");
 }
 
+int llme_embed_rows(size_t n, size_t dim, const int* feed, const float* table, float* x,
+                    void* stream) {
+    g_error.clear();
+    if (n == 0 || dim == 0) return LLME_OK;
+    if (!feed || !table || !x) return fail(LLME_E_INVALID, "llme_embed_rows: null pointer");
+    if (n >= 65536 || n * dim >= kMaxElems)
+        return fail(LLME_E_INVALID, "llme_embed_rows: too many rows or elements");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
+    cudaError_t e = launch_embed_rows(static_cast<int>(n), static_cast<int>(dim), feed, table, x, s);
+    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "embed");
+}
+
+int llme_rope_cache(size_t n, int nq, int nkv, int head_size, const int* feed, const float* cos,
+                    const float* sin, float* qkv, float* key_cache, float* value_cache,
+                    void* stream) {
+    g_error.clear();
+    if (n == 0) return LLME_OK;
+    if (!feed || !cos || !sin || !qkv || !key_cache || !value_cache)
+        return fail(LLME_E_INVALID, "llme_rope_cache: null pointer");
+    if (nq < 0 || nkv <= 0 || head_size <= 0 || head_size % 2 != 0 || n >= 65536 ||
+        static_cast<size_t>(nq + 2 * nkv) * head_size * n >= kMaxElems)
+        return fail(LLME_E_INVALID, "llme_rope_cache: head_size must be even and positive, nkv "
+                                    "positive, n below 65536");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
+    cudaError_t e = launch_rope_cache(static_cast<int>(n), nq, nkv, head_size, feed, cos, sin, qkv,
+                                      key_cache, value_cache, s);
+    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "rope");
+}
+
+int llme_swiglu(size_t n, size_t hidden, const float* gu, float* hb, void* stream) {
+    g_error.clear();
+    if (n == 0 || hidden == 0) return LLME_OK;
+    if (!gu || !hb) return fail(LLME_E_INVALID, "llme_swiglu: null pointer");
+    if (2 * n * hidden >= kMaxElems) return fail(LLME_E_INVALID, "llme_swiglu: too many elements");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
+    cudaError_t e = launch_swiglu(static_cast<int>(n), static_cast<int>(hidden), gu, hb, s);
+    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "swiglu");
+}
+
+int llme_rope_tables(size_t seq_len, size_t head_size, float* cos, float* sin) {
+    g_error.clear();
+    if (seq_len == 0) return LLME_OK;
+    if (!cos || !sin) return fail(LLME_E_INVALID, "llme_rope_tables: null pointer");
+    if (head_size == 0 || head_size % 2 != 0)
+        return fail(LLME_E_INVALID, "llme_rope_tables: head_size must be even and positive");
+    rope_tables(seq_len, head_size, cos, sin);
+    return LLME_OK;
+}
+
 int llme_batch_q8_create(llme_batch_t** batch, size_t m, size_t count,
                          const llme_q8_product* products) {
     return batch_create(batch, m, count, products);

@@ -264,6 +264,16 @@ unsigned read_and_clear_f32sk_error();
 cudaError_t launch_quantize_q8(int k, int n, const float* B, int8_t* q, float* scale,
                                cudaStream_t stream);
 
+// Decode-step helpers (decode_ops.cu): the transformer's elementwise steps for one rank's
+// heads; feed[0] = first position, feed[1..n] = token ids, in device memory.
+cudaError_t launch_embed_rows(int n, int dim, const int* feed, const float* table, float* x,
+                              cudaStream_t stream);
+cudaError_t launch_rope_cache(int n, int nq, int nkv, int head_size, const int* feed,
+                              const float* cos_t, const float* sin_t, float* qkv, float* key_cache,
+                              float* value_cache, cudaStream_t stream);
+cudaError_t launch_swiglu(int n, int hidden, const float* gu, float* hb, cudaStream_t stream);
+void rope_tables(size_t seq_len, size_t head_size, float* cos_out, float* sin_out);
+
 // out = rmsnorm(A) * w per row (eps 1e-5), m rows of k.
 cudaError_t launch_rmsnorm_rows(int m, int k, const float* A, const float* w, float* out,
                                 cudaStream_t stream);

@@ -98,6 +98,12 @@ def load() -> ctypes.CDLL:
     lib.llme_attention_scratch_floats.restype = sz
     lib.llme_attention.argtypes = [ctypes.POINTER(AttentionShape), sz, vp, vp, vp, vp, vp, vp, i,
                                    vp]
+    lib.llme_embed_rows.argtypes = [sz, sz, vp, vp, vp, vp]
+    lib.llme_rope_cache.argtypes = [sz, i, i, i, vp, vp, vp, vp, vp, vp, vp]
+    lib.llme_swiglu.argtypes = [sz, sz, vp, vp, vp]
+    lib.llme_rope_tables.argtypes = [sz, sz, vp, vp]
+    for f in ("llme_embed_rows", "llme_rope_cache", "llme_swiglu", "llme_rope_tables"):
+        getattr(lib, f).restype = i
     lib.llme_batch_q8_create.argtypes = [ctypes.POINTER(vp), sz, sz, ctypes.POINTER(Q8Product)]
     lib.llme_batch_run.argtypes = [vp, u, vp]
     lib.llme_batch_destroy.argtypes = [vp]
@@ -199,6 +205,35 @@ def attention(shape: AttentionShape, rows: int, pos_dev: int, q: int, k_cache: i
     """Causal attention over a KV cache on device pointers (cuda_attention.h:38-45)."""
     _check(load().llme_attention(ctypes.byref(shape), rows, pos_dev, q, k_cache, v_cache, out,
                                  scratch or None, ATTN_KERNELS[kernel], stream or None))
+
+
+def embed_rows(n: int, dim: int, feed: int, table: int, x: int, stream: int | None = None) -> None:
+    """x[i] = table[feed[1 + i]] on device pointers (the reference's embed, cuda_model.cu:27-31)."""
+    _check(load().llme_embed_rows(n, dim, feed, table, x, stream or None))
+
+
+def rope_cache(n: int, nq: int, nkv: int, head_size: int, feed: int, cos: int, sin: int, qkv: int,
+               key_cache: int, value_cache: int, stream: int | None = None) -> None:
+    """RoPE on a rank's q / k heads at positions feed[0] + i and the KV-cache write
+    (the reference's rope_and_cache, cuda_model.cu:33-66), on device pointers."""
+    _check(load().llme_rope_cache(n, nq, nkv, head_size, feed, cos, sin, qkv, key_cache,
+                                  value_cache, stream or None))
+
+
+def swiglu(n: int, hidden: int, gu: int, hb: int, stream: int | None = None) -> None:
+    """hb = silu(gate) * up for n rows of [gate | up] (cuda_model.cu:68-75), device pointers."""
+    _check(load().llme_swiglu(n, hidden, gu, hb, stream or None))
+
+
+def rope_tables(seq_len: int, head_size: int):
+    """The RoPE cos / sin tables (seq_len x head_size / 2, numpy float32), computed by the
+    library's host code with the reference's float expressions (model.cpp:171-184)."""
+    import numpy as np
+    half = head_size // 2
+    cos = np.zeros((seq_len, half), np.float32)
+    sin = np.zeros((seq_len, half), np.float32)
+    _check(load().llme_rope_tables(seq_len, head_size, cos.ctypes.data, sin.ctypes.data))
+    return cos, sin
 
 
 def quantize_q8_cuda(k: int, n: int, W: int, q: int, scale: int, stream: int | None = None) -> None:

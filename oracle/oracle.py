@@ -246,3 +246,70 @@ class _QHandle:
             self.free(self.handle)
         except Exception:
             pass
+
+
+# ---- the reference's CPU Transformer (oracle/_ref/libref_model.so) ---------------------------
+
+REF_MODEL_SO = os.path.join(HERE, "_ref", "libref_model.so")
+_ref_model_lib = None
+
+
+def _model_lib() -> ctypes.CDLL:
+    global _ref_model_lib
+    if _ref_model_lib is None:
+        if not os.path.exists(REF_MODEL_SO):
+            raise FileNotFoundError(REF_MODEL_SO)
+        lib = ctypes.CDLL(REF_MODEL_SO)
+        vp = ctypes.c_void_p
+        lib.ref_model_error.restype = ctypes.c_char_p
+        lib.ref_model_load.argtypes = [ctypes.c_char_p, ctypes.c_int]
+        lib.ref_model_load.restype = vp
+        lib.ref_model_free.argtypes = [vp]
+        lib.ref_model_vocab.argtypes = [vp]
+        lib.ref_model_vocab.restype = _sz
+        lib.ref_model_run.argtypes = [vp, np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS"),
+                                      _sz, _sz, _f32p]
+        lib.ref_rope_tables.argtypes = [_sz, _sz, _sz, _f32p, _f32p]
+        _ref_model_lib = lib
+    return _ref_model_lib
+
+
+class RefModel:
+    """The reference's CPU Transformer (model.cpp) over a llama2.c checkpoint file: the oracle
+    of the tensor-parallel transformer. run(tokens, pos) feeds tokens at [pos, pos + n) and
+    returns the last row's logits."""
+
+    @staticmethod
+    def available() -> bool:
+        return os.path.exists(REF_MODEL_SO)
+
+    def __init__(self, path: str, q8: bool):
+        lib = _model_lib()
+        self.handle = lib.ref_model_load(path.encode(), int(q8))
+        if not self.handle:
+            raise RuntimeError(lib.ref_model_error().decode())
+        self.vocab = int(lib.ref_model_vocab(self.handle))
+
+    def run(self, tokens, pos: int) -> np.ndarray:
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.zeros(self.vocab, np.float32)
+        if _model_lib().ref_model_run(self.handle, t, t.size, pos, out):
+            raise RuntimeError(_model_lib().ref_model_error().decode())
+        return out
+
+    def close(self) -> None:
+        if self.handle:
+            _model_lib().ref_model_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+
+def ref_rope_tables(seq_len: int, dim: int, n_heads: int):
+    """The reference's rope_tables (model.cpp:171-184) for head_size = dim / n_heads."""
+    half = dim // n_heads // 2
+    cos = np.zeros(seq_len * half, np.float32)
+    sin = np.zeros(seq_len * half, np.float32)
+    _model_lib().ref_rope_tables(seq_len, dim, n_heads, cos, sin)
+    return cos.reshape(seq_len, half), sin.reshape(seq_len, half)
