@@ -520,6 +520,97 @@ ATTN_CASES = [  # (name, heads, kv heads, head size, cached positions)
 ATTN_LAYERS = 8  # distinct caches per step, so the keys and values come from HBM
 
 
+def run_tp_decode(args, world, rank, local):
+    """Decode tokens/s of a 7B-shaped int8 transformer (32 layers, dim 4096, 32 heads, hidden
+    11008, vocab 32000; the reference's CudaTransformer architecture, src/cuda_model.cu) split
+    over N GPUs by llm-engine_b200/tp_decode.py: heads by kv head, column-parallel wqkv / w13 /
+    classifier, row-parallel wo / w2 with the NVLink peer all-reduce fused into the residual
+    add. One step = one token at context length --context (a synthetic history in the caches),
+    captured once as a CUDA graph of C-ABI calls. Synthetic weights drawn on the device."""
+    import torch
+    import llme_b200 as L
+    from checkpoint import Config
+    from tp_decode import TPTransformer
+    ctx = args.context
+    cfg = Config(DIM, HIDDEN, args.layers, 32, 32, VOCAB, ctx + 16)
+    comm = None
+    if world > 1:
+        import torch.distributed as dist
+        uid = [L.Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = L.Comm(world, rank, uid[0], timeout_s=60.0)
+        comm.enable_peer(VOCAB)  # the largest all-reduce: the logits
+    tp = TPTransformer.synthetic(cfg, world, rank, q8=True, comm=comm, seed=5)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11 + rank)
+    for lw in tp.layers:  # the keys and values of ctx earlier positions
+        lw["kc"][:ctx].uniform_(-1, 1, generator=g)
+        lw["vc"][:ctx].uniform_(-1, 1, generator=g)
+    tp.filled = ctx
+    tp.run([1], ctx)  # eager step: grows every buffer the step uses
+    graph = tp.capture_decode()
+    tp.feed_host[0], tp.feed_host[1] = ctx, 1
+    stream = torch.cuda.Stream()
+    sampler = ClockSampler(local)
+    secs = max_over_ranks(time_graph(graph, args.steps, args.warmup, stream, world, sampler),
+                          world)
+    tokens_s = args.steps / secs
+
+    # Bytes one rank streams per token: its int8 shards + scales, its heads' KV history.
+    hs, L_ = cfg.head_size, cfg.n_layers
+    w_bytes = sum(t[0].numel() + 4 * t[1].numel() for lw in tp.layers
+                  for t in (lw["wqkv"], lw["wo"], lw["w13"], lw["w2"]))
+    w_bytes += tp.wcls[0].numel() + 4 * tp.wcls[1].numel()
+    kv_bytes = 2 * (ctx + 1) * tp.nkv * hs * 4 * L_
+    per_gpu = w_bytes + kv_bytes
+    hbm, hbm_kind = peaks()
+    achieved = per_gpu / (secs / args.steps) / 1e9
+
+    # e2e: decode() per token through the same graph -- feed copied in, logits copied out and
+    # the host waiting for them, as a caller of forward() does.
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            tp.forward(1, ctx)
+        barrier(world)
+        torch.cuda.synchronize()
+        import time
+        t0 = time.perf_counter()
+        e2e_steps = min(args.steps, 100)
+        for _ in range(e2e_steps):
+            tp.forward(1, ctx)
+        e2e_secs = max_over_ranks(time.perf_counter() - t0, world)
+    del graph
+    tp.graph = None
+    line = {"metric": f"decode tokens/s (7B-shaped int8 transformer, tensor-parallel over N GPUs, "
+                      f"context {ctx})",
+            "value": round(tokens_s, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 W, f32",
+            "data": "synthetic: N(0,0.02^2) weights drawn on the device, quantised per column; "
+                    "U(-1,1) embedding and KV history",
+            "config": {"workload": "tensor-parallel decode (SURVEY (f)2), one token per step",
+                       "layers": L_, "dim": DIM, "hidden": HIDDEN, "heads": 32, "vocab": VOCAB,
+                       "context": ctx, "parallelism": f"tp{world}",
+                       "launch": "one CUDA graph per token: embed, per layer rmsnorm+wqkv, "
+                                 "rope+cache, attention, wo+all-reduce+residual, rmsnorm+w13, "
+                                 "swiglu, w2+all-reduce+residual; classifier + all-reduce",
+                       "l2": f"no flush: {per_gpu / 1e9:.2f} GB per token per GPU (> L2)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_kind": hbm_kind,
+                         "kernel": "whole decode step (per GPU)", "bytes_per_token_per_gpu": per_gpu,
+                         "traffic": None},
+            "e2e": {"value": round(e2e_steps / e2e_secs, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4 * VOCAB},
+            "gpu_launches": None, "cpu_baseline": None,
+            "cpu_baseline_note": "the reference's CPU Transformer needs a 27 GB fp32 checkpoint at "
+                                 "this size; its parity is tested on small checkpoints",
+            "clocks": sampler.summary()}
+    if comm is not None:
+        comm.destroy()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_attention(args, world, rank, local):
     """One decode row (position = the last cached one) through each case, per layer cache,
     one call each, in a CUDA graph: this library's llme_attention (split kernel) and, on the
@@ -931,6 +1022,8 @@ def run_ours(args):
         return run_sweep(args, world, rank, local)
     if args.workload == "attention":
         return run_attention(args, world, rank, local)
+    if args.workload == "tp_decode":
+        return run_tp_decode(args, world, rank, local)
     if args.workload == "chain":
         chain = Chain(world, rank, chain_shapes(args.layers), seed=3)
     else:
@@ -1102,13 +1195,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["chain", "gemv", "sgemm", "prefill", "sweep",
-                                           "attention"],
+                                           "attention", "tp_decode"],
                     default="chain",
                     help="chain: BASELINE configs[3] (default); gemv: configs[0] alone; "
                          "sgemm: configs[2] (square TF32 GEMM, --size); prefill: configs[4] "
                          "(m = 512 through the 7B-shaped int8 weights); sweep: configs[1] "
-                         "(m in {1,4,16,64} x 4096^2, fp32 and int8 W, per call)")
+                         "(m in {1,4,16,64} x 4096^2, fp32 and int8 W, per call); attention: "
+                         "decode attention over KV caches; tp_decode: tokens/s of the "
+                         "7B-shaped int8 transformer, tensor-parallel over --gpus")
     ap.add_argument("--size", type=int, default=8192, help="N for --workload sgemm")
+    ap.add_argument("--context", type=int, default=1024,
+                    help="cached positions before the decoded token (--workload tp_decode)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers of the chain / prefill (32 = the BASELINE configs; fewer only "
                          "for small profiling cases)")

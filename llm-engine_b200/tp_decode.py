@@ -70,21 +70,8 @@ class TPTransformer:
 
     def __init__(self, ckpt: Checkpoint, world: int = 1, rank: int = 0, q8: bool = False,
                  comm=None):
-        import torch
-        self.torch = torch
-        cfg = self.cfg = ckpt.config
-        self.world, self.rank, self.q8, self.comm = world, rank, q8, comm
-        dev = torch.device("cuda", torch.cuda.current_device())
-        self.dev = dev
-        hs = cfg.head_size
-        self.q0, self.nq, self.kv0, self.nkv = head_partition(cfg.n_heads, cfg.n_kv_heads,
-                                                              world, rank)
-        self.h0, self.hc = shard_range(cfg.hidden_dim, world, rank)
-        self.v0, self.vc = shard_range(cfg.vocab_size, world, rank)
-        self.qkv_cols = (self.nq + 2 * self.nkv) * hs
-        self.shape = L.AttentionShape(self.nq, self.nkv, hs, cfg.seq_len, self.qkv_cols,
-                                      self.nkv * hs, self.nq * hs)
-        L.attention_check(self.shape)
+        self._setup(ckpt.config, world, rank, q8, comm)
+        torch, dev, cfg = self.torch, self.dev, self.cfg
 
         def dev_f32(a):
             return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev)
@@ -104,20 +91,73 @@ class TPTransformer:
         self.emb = dev_f32(ckpt.token_embedding)
         self.rms_final = dev_f32(ckpt.rms_final)
         self.wcls = proj(ckpt.wcls, cols=(self.v0, self.vc))
-        self.layers = []
         for lw in ckpt.layers:
             sh = shard_layer(lw, cfg, world, rank)
-            self.layers.append({
-                "rms_att": dev_f32(lw.rms_att), "rms_ffn": dev_f32(lw.rms_ffn),
-                "wqkv": proj(sh["wqkv"]), "wo": proj(lw.wo, rows=sh["wo_rows"]),
-                "w13": proj(sh["w13"]), "w2": proj(lw.w2, rows=sh["w2_rows"]),
-                "kc": torch.zeros(cfg.seq_len, self.nkv * hs, device=dev),
-                "vc": torch.zeros(cfg.seq_len, self.nkv * hs, device=dev)})
-        cos, sin = L.rope_tables(cfg.seq_len, hs)
-        self.cos, self.sin = dev_f32(cos), dev_f32(sin)
-        self.feed_host = torch.zeros(cfg.seq_len + 1, dtype=torch.int32).pin_memory()
-        self.feed = torch.zeros(cfg.seq_len + 1, dtype=torch.int32, device=dev)
-        self.logits = torch.zeros(cfg.vocab_size, device=dev)
+            self._add_layer(dev_f32(lw.rms_att), dev_f32(lw.rms_ffn), proj(sh["wqkv"]),
+                            proj(lw.wo, rows=sh["wo_rows"]), proj(sh["w13"]),
+                            proj(lw.w2, rows=sh["w2_rows"]))
+        self._finish()
+
+    @classmethod
+    def synthetic(cls, cfg, world: int = 1, rank: int = 0, q8: bool = True, comm=None,
+                  seed: int = 0):
+        """A model of cfg's shape with random weights drawn on the device (projections
+        N(0, 0.02^2), embedding U(-1, 1), unit RMSNorm weights), each rank drawing only its
+        own shards -- for benchmarks at full size, where a host checkpoint would not fit."""
+        self = cls.__new__(cls)
+        self._setup(cfg, world, rank, q8, comm)
+        torch, dev = self.torch, self.dev
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed * 1009 + rank)
+
+        def proj(rows, cols):
+            w = torch.randn(rows, cols, generator=g, device=dev) * 0.02
+            return L.quantize_q8(w) if q8 else (w, None)
+
+        D, hs = cfg.dim, cfg.head_size
+        self.emb = torch.rand(cfg.vocab_size, D, generator=g, device=dev) * 2 - 1
+        self.rms_final = torch.ones(D, device=dev)
+        self.wcls = proj(D, self.vc)
+        for _ in range(cfg.n_layers):
+            self._add_layer(torch.ones(D, device=dev), torch.ones(D, device=dev),
+                            proj(D, self.qkv_cols), proj(self.nq * hs, D),
+                            proj(D, 2 * self.hc), proj(self.hc, D))
+        self._finish()
+        return self
+
+    def _setup(self, cfg, world, rank, q8, comm):
+        import torch
+        self.torch = torch
+        self.cfg = cfg
+        self.world, self.rank, self.q8, self.comm = world, rank, q8, comm
+        self.dev = torch.device("cuda", torch.cuda.current_device())
+        hs = cfg.head_size
+        self.q0, self.nq, self.kv0, self.nkv = head_partition(cfg.n_heads, cfg.n_kv_heads,
+                                                              world, rank)
+        self.h0, self.hc = shard_range(cfg.hidden_dim, world, rank)
+        self.v0, self.vc = shard_range(cfg.vocab_size, world, rank)
+        self.qkv_cols = (self.nq + 2 * self.nkv) * hs
+        self.shape = L.AttentionShape(self.nq, self.nkv, hs, cfg.seq_len, self.qkv_cols,
+                                      self.nkv * hs, self.nq * hs)
+        L.attention_check(self.shape)
+        self.layers = []
+        self.graph = None
+
+    def _add_layer(self, rms_att, rms_ffn, wqkv, wo, w13, w2):
+        t, cfg = self.torch, self.cfg
+        kv = self.nkv * cfg.head_size
+        self.layers.append({"rms_att": rms_att, "rms_ffn": rms_ffn, "wqkv": wqkv, "wo": wo,
+                            "w13": w13, "w2": w2,
+                            "kc": t.zeros(cfg.seq_len, kv, device=self.dev),
+                            "vc": t.zeros(cfg.seq_len, kv, device=self.dev)})
+
+    def _finish(self):
+        t, cfg = self.torch, self.cfg
+        cos, sin = L.rope_tables(cfg.seq_len, cfg.head_size)
+        self.cos, self.sin = t.from_numpy(cos).to(self.dev), t.from_numpy(sin).to(self.dev)
+        self.feed_host = t.zeros(cfg.seq_len + 1, dtype=t.int32).pin_memory()
+        self.feed = t.zeros(cfg.seq_len + 1, dtype=t.int32, device=self.dev)
+        self.logits = t.zeros(cfg.vocab_size, device=self.dev)
         self.rows = 0
         self.filled = 0
         self._reserve(1)
@@ -222,7 +262,47 @@ class TPTransformer:
         return self.logits.cpu().numpy()
 
     def forward(self, token: int, pos: int) -> np.ndarray:
+        if self.graph is not None:
+            return self.decode(token, pos).cpu().numpy()
         return self.run([token], pos)
+
+    def capture_decode(self):
+        """Captures the one-token step as a CUDA graph, as the reference's CudaTransformer
+        does (src/cuda_model.cu:190-220): token and position are read from device memory, so
+        one graph serves every position. Call after an eager one-token run(), which has grown
+        every buffer the step uses, so capturing allocates nothing; nothing runs while
+        capturing. Returns the graph; decode() replays it."""
+        t = self.torch
+        if self.filled == 0:
+            raise L.InvalidArgument("capture_decode: run one token eagerly first")
+        saved = self.filled
+        s = t.cuda.Stream()
+        s.wait_stream(t.cuda.current_stream())
+        g = t.cuda.CUDAGraph()
+        with t.cuda.stream(s):
+            with t.cuda.graph(g, stream=s):
+                for _ in self.steps([0], saved - 1):
+                    raise L.InvalidArgument("tensor parallel: graphs need a communicator")
+        t.cuda.current_stream().wait_stream(s)
+        self.filled = saved
+        self.graph = g
+        return g
+
+    def decode(self, token: int, pos: int):
+        """One token through the captured graph on the current stream; returns the logits
+        (device tensor, valid once the stream reaches this point)."""
+        cfg = self.cfg
+        if not 0 <= int(token) < cfg.vocab_size:
+            raise IndexError(f"forward: token {int(token)} outside vocab")
+        if pos + 1 > cfg.seq_len or pos > self.filled:
+            raise IndexError(f"forward: positions {pos}..{pos} with {self.filled} cached of "
+                             f"{cfg.seq_len}")
+        self.torch.cuda.current_stream().synchronize()  # the previous replay read the feed
+        self.feed_host[0] = pos
+        self.feed_host[1] = int(token)
+        self.graph.replay()
+        self.filled = max(self.filled, pos + 1)
+        return self.logits
 
     def prefill(self, tokens, pos: int) -> np.ndarray:
         return self.run(list(tokens), pos)

@@ -98,6 +98,21 @@ def test_emulated_ranks_match_the_reference_model(tmp_path, world, q8):
         assert close(got, want), (world, tokens, pos, float(np.abs(got - want).max()))
 
 
+@pytest.mark.parametrize("q8", [False, True])
+def test_graph_decode_matches_the_reference_model(tmp_path, q8):
+    # The one-token step captured once (after an eager step) and replayed at later positions,
+    # including a rewind that overwrites a cached position, as the reference's graph serves
+    # every position (src/cuda_model.cu:190-220).
+    p = checkpoint(tmp_path, "gqa", seed=10)
+    ref = oracle.RefModel(p, q8)
+    tp = TPTransformer(load_checkpoint(p), q8=q8)
+    assert close(tp.run([3], 0), ref.run([3], 0))
+    tp.capture_decode()
+    for token, pos in [(8, 1), (21, 2), (4, 3), (40, 2), (6, 3), (11, 4)]:
+        got, want = tp.forward(token, pos), ref.run([token], pos)
+        assert close(got, want), (token, pos, float(np.abs(got - want).max()))
+
+
 def test_positions_are_checked(tmp_path):
     tp = TPTransformer(load_checkpoint(checkpoint(tmp_path, "gqa")))
     with pytest.raises(IndexError):
