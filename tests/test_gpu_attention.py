@@ -93,3 +93,13 @@ def test_attention_long_context():
         L.attention_check(shape, "single_block")
     run_case(4, 1, 128, 20000, "split", [0, 5000, 19999], 1, rng)
     run_case(4, 1, 128, 20000, "automatic", [12345, 19990], 10, rng)
+
+
+@pytest.mark.parametrize("case", [(4, 4, 256, 900), (2, 1, 320, 700), (16, 4, 128, 1100)])
+def test_attention_wide_heads_and_long_chunks(case):
+    # The widest head TMA boxes take (256), a head past them (320: per-position bulk copies),
+    # and a grouped case with chunks of many boxes; rows 1 and 5.
+    rng = np.random.default_rng(sum(case))
+    heads, kv_heads, hs, seq_len = case
+    for rows in (1, 5):
+        run_case(heads, kv_heads, hs, seq_len, "split", [0, 17, 16 * 37, seq_len - rows], rows, rng)
