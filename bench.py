@@ -417,7 +417,7 @@ def run_sweep(args, world, rank, local):
     stream = torch.cuda.Stream()
     h = stream.cuda_stream
     sampler = ClockSampler(local)
-    cases, tot_bytes, tot_s = [], 0, 0.0
+    cases, tot_bytes, tot_s, launches = [], 0, 0.0, 0
     for q8 in (False, True):
         Ws = [torch.randn(DIM, DIM, generator=g, device="cuda") * 0.02 for _ in range(SWEEP_COPIES)]
         if q8:
@@ -444,9 +444,13 @@ def run_sweep(args, world, rank, local):
             nbytes = (algorithmic_bytes(DIM, DIM, m) if q8 else
                       4 * DIM * DIM + 4 * m * DIM + 4 * m * DIM)
             us = secs / (args.steps * SWEEP_COPIES) * 1e6
+            path = L.plan(m, DIM, DIM, q8=q8)["path_name"]
+            # launches per call: the split pass before the three-term int8 kernel, else one
+            per_call = 2 if path == "tcgen05_skinny" else 1
+            launches += per_call * SWEEP_COPIES * args.steps
             cases.append({"w": "int8" if q8 else "fp32", "m": m, "us": round(us, 2),
-                          "GB_s": round(nbytes / us / 1e3, 1),
-                          "path": L.plan(m, DIM, DIM, q8=q8)["path_name"]})
+                          "GB_s": round(nbytes / us / 1e3, 1), "path": path,
+                          "launches_per_call": per_call})
             tot_bytes += nbytes * args.steps * SWEEP_COPIES
             tot_s += secs
     hbm, hbm_kind = peaks()
@@ -464,7 +468,7 @@ def run_sweep(args, world, rank, local):
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(value / hbm, 4), "peak_kind": hbm_kind,
                          "kernel": "per case (see cases[].path)", "traffic": None},
-            "gpu_launches": None, "clocks": sampler.summary()}
+            "gpu_launches": launches, "clocks": sampler.summary()}
     if cpu is not None:
         line["cpu_baseline"] = cpu
     if rank == 0:
@@ -555,6 +559,10 @@ def run_tp_decode(args, world, rank, local):
     secs = max_over_ranks(time_graph(graph, args.steps, args.warmup, stream, world, sampler),
                           world)
     tokens_s = args.steps / secs
+    # Kernels of one token: embed; per layer wqkv, RoPE + cache, attention, wo, w13, SwiGLU,
+    # w2 (each product one launch at m = 1), with N > 1 an all-reduce after wo and w2; the
+    # classifier (+ its all-reduce).
+    launches_per_token = 1 + cfg.n_layers * (7 + (2 if world > 1 else 0)) + 1 + (1 if world > 1 else 0)
 
     # Bytes one rank streams per token: its int8 shards + scales, its heads' KV history.
     hs, L_ = cfg.head_size, cfg.n_layers
@@ -601,7 +609,7 @@ def run_tp_decode(args, world, rank, local):
                          "traffic": None},
             "e2e": {"value": round(e2e_steps / e2e_secs, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4 * VOCAB},
-            "gpu_launches": None, "cpu_baseline": None,
+            "gpu_launches": launches_per_token * args.steps, "cpu_baseline": None,
             "cpu_baseline_note": "the reference's CPU Transformer needs a 27 GB fp32 checkpoint at "
                                  "this size; its parity is tested on small checkpoints",
             "clocks": sampler.summary()}
