@@ -1040,6 +1040,8 @@ def cpu_baseline_sample(chain, budget_s=8.0):
 def run_ours(args):
     import torch
     import llme_b200 as L
+    if not torch.cuda.is_available():
+        raise SystemExit("this benchmark needs an sm_100 (B200) GPU; none is visible")
     world, rank, local = dist_setup(args.gpus)
     L.load()
     if not L.device_supported():
