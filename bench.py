@@ -979,7 +979,7 @@ def run_prefill(args, world, rank, local):
         line["cpu_baseline"] = cpu_prefill_sample(pf)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graph, e2e_graphs
+    del graph, e2e_graph
     torch.cuda.synchronize()
     if grouped:
         pf.destroy_batches()
