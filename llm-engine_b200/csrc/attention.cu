@@ -292,7 +292,15 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
     __syncthreads();
 
-    const size_t head_row = static_cast<size_t>(i) * a.n_heads + h0;  // (row, first head)
+    // This row's block of the scratch: [tickets | chunk partials | group partials], at a
+    // stride that depends on the shape only, so calls of any row count leave every row's
+    // tickets where the next call looks for them.
+    const size_t rb = static_cast<size_t>(i) * a.scratch_row;
+    float* part_o = a.part_o + rb;
+    float2* part_ml = a.part_ml + rb / 2;
+    float* part2_o = a.part2_o + rb;
+    float2* part2_ml = a.part2_ml + rb / 2;
+    const size_t head_row = h0;  // first head of the group within the row's block
     for (int j = tid; j < pairs; j += kAttnThreads) {
         const int g = j / hs4, d4 = j % hs4;
         float4 o = red[j];
@@ -309,11 +317,11 @@ __global__ void __launch_bounds__(kAttnThreads)
                                       static_cast<size_t>(h0 + g) * hs)[d4] =
                 make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
         } else {
-            reinterpret_cast<float4*>(a.part_o)[((head_row + g) * splits + s) * hs4 + d4] = o;
+            reinterpret_cast<float4*>(part_o)[((head_row + g) * splits + s) * hs4 + d4] = o;
         }
     }
     if (n == 1) return;
-    if (tid < G) a.part_ml[(head_row + tid) * splits + s] = ml[tid];
+    if (tid < G) part_ml[(head_row + tid) * splits + s] = ml[tid];
 
     // Merge, two levels deep, fixed order (deterministic): chunks in groups of kMergeGroup, the
     // CTA that completes a group's ticket merges it into a group partial; the CTA that
@@ -322,7 +330,7 @@ __global__ void __launch_bounds__(kAttnThreads)
     const int max_groups = (splits + kMergeGroup - 1) / kMergeGroup;
     const int grp = s / kMergeGroup, c0 = grp * kMergeGroup;
     const int cnt = min(kMergeGroup, n - c0);
-    unsigned* tickets = a.counters + (static_cast<size_t>(i) * gridDim.x + hg) * (max_groups + 1);
+    unsigned* tickets = a.counters + rb + static_cast<size_t>(hg) * (max_groups + 1);
     float* wts = reinterpret_cast<float*>(red + slots * pairs);  // G x max(kMergeGroup, groups)
     // G x (M, L), 16-byte aligned after the weights
     float2* res = reinterpret_cast<float2*>(wts + (G * max(kMergeGroup, max_groups) + 3) / 4 * 4);
@@ -335,15 +343,15 @@ __global__ void __launch_bounds__(kAttnThreads)
     __syncthreads();
     if (!last) return;
     __threadfence();
-    merge_partials<G>(a.part_ml, reinterpret_cast<const float4*>(a.part_o), head_row, splits, c0,
+    merge_partials<G>(part_ml, reinterpret_cast<const float4*>(part_o), head_row, splits, c0,
                       cnt, hs4, pairs, slots, wts, res, red);
     if (ngroups > 1) {
         // Publish the group partial, then the last group's CTA merges the groups.
         for (int j = tid; j < pairs; j += kAttnThreads) {
             const int g = j / hs4, d4 = j % hs4;
-            reinterpret_cast<float4*>(a.part2_o)[((head_row + g) * max_groups + grp) * hs4 + d4] = red[j];
+            reinterpret_cast<float4*>(part2_o)[((head_row + g) * max_groups + grp) * hs4 + d4] = red[j];
         }
-        if (tid < G) a.part2_ml[(head_row + tid) * max_groups + grp] = res[tid];
+        if (tid < G) part2_ml[(head_row + tid) * max_groups + grp] = res[tid];
         __threadfence();
         __syncthreads();
         if (tid == 0) {
@@ -353,7 +361,7 @@ __global__ void __launch_bounds__(kAttnThreads)
         __syncthreads();
         if (!last) return;
         __threadfence();
-        merge_partials<G>(a.part2_ml, reinterpret_cast<const float4*>(a.part2_o), head_row,
+        merge_partials<G>(part2_ml, reinterpret_cast<const float4*>(part2_o), head_row,
                           max_groups, 0, ngroups, hs4, pairs, slots, wts, res, red);
     }
     for (int j = tid; j < pairs; j += kAttnThreads) {
@@ -512,29 +520,28 @@ int resolve(const llme_attention_shape& s, int kernel, size_t rows) {
     return rows <= kSplitMaxRows || !single_fits(s) ? LLME_ATTN_SPLIT : LLME_ATTN_SINGLE_BLOCK;
 }
 
-// Scratch for `rows` rows (floats): partial o, then (m, l) pairs, then a ticket per
-// (row, head group), each part 16-byte aligned.
-// Scratch for `rows` rows (floats): chunk partials o and (m, l), group partials o and
-// (m, l), then per (row, head group) one second-level ticket and a ticket per chunk group;
-// every part 16-byte aligned.
+// Scratch (floats): one block per row, at a stride that depends on the shape only --
+// [tickets: per head group one second-level ticket and one per chunk group | chunk partials o
+// | chunk (m, l) | group partials o | group (m, l)], each part 16-byte aligned. Offsets are
+// within a row's block; a call with fewer rows uses a prefix of the blocks, so every row's
+// tickets sit in the same place whatever the row count (each call leaves them at zero).
 struct ScratchLayout {
-    size_t o, ml, o2, ml2, counters, total;
+    size_t counters, o, ml, o2, ml2, row;
 };
 
-ScratchLayout scratch_layout(const llme_attention_shape& s, size_t rows) {
+ScratchLayout scratch_layout(const llme_attention_shape& s) {
     const SplitGeo g = split_geo(s);
-    const size_t heads = rows * static_cast<size_t>(s.n_heads);
+    const size_t heads = static_cast<size_t>(s.n_heads);
     const size_t chunks = heads * static_cast<size_t>(g.splits);
     const size_t groups = (static_cast<size_t>(g.splits) + kMergeGroup - 1) / kMergeGroup;
     auto up4 = [](size_t x) { return (x + 3) / 4 * 4; };
     ScratchLayout l{};
-    l.o = 0;
-    l.ml = up4(chunks * static_cast<size_t>(s.head_size));
+    l.counters = 0;
+    l.o = up4(static_cast<size_t>(s.n_heads / heads_per_block(s)) * (groups + 1));
+    l.ml = l.o + up4(chunks * static_cast<size_t>(s.head_size));
     l.o2 = l.ml + up4(2 * chunks);
     l.ml2 = l.o2 + up4(heads * groups * static_cast<size_t>(s.head_size));
-    l.counters = l.ml2 + up4(2 * heads * groups);
-    l.total = l.counters +
-              up4(rows * static_cast<size_t>(s.n_heads / heads_per_block(s)) * (groups + 1));
+    l.row = l.ml2 + up4(2 * heads * groups);
     return l;
 }
 
@@ -625,7 +632,7 @@ size_t llme_attention_scratch_floats(const llme_attention_shape* s, size_t rows,
         return 0;
     // The most rows a call of up to `rows` rows splits.
     if (kernel == LLME_ATTN_AUTOMATIC && single_fits(*s)) rows = std::min(rows, kSplitMaxRows);
-    return scratch_layout(*s, rows).total;
+    return scratch_layout(*s).row * rows;
 }
 
 int llme_attention(const llme_attention_shape* s, size_t rows, const int* pos_dev, const float* q,
@@ -677,13 +684,14 @@ int llme_attention(const llme_attention_shape* s, size_t rows, const int* pos_de
             return set_error(LLME_E_INVALID, "attention: split needs 16-byte aligned q, caches and out");
         if (!scratch) return set_error(LLME_E_INVALID, "attention: split needs scratch");
         const SplitGeo g = split_geo(*s);
-        const ScratchLayout l = scratch_layout(*s, rows);
+        const ScratchLayout l = scratch_layout(*s);
         a.chunk_cap = g.cap;
         a.part_o = scratch + l.o;
         a.part_ml = reinterpret_cast<float2*>(scratch + l.ml);
         a.part2_o = scratch + l.o2;
         a.part2_ml = reinterpret_cast<float2*>(scratch + l.ml2);
         a.counters = reinterpret_cast<unsigned*>(scratch + l.counters);
+        a.scratch_row = l.row;
         const int G = heads_per_block(*s);
         const dim3 grid(static_cast<unsigned>(s->n_heads / G), static_cast<unsigned>(rows),
                         static_cast<unsigned>(g.splits));

@@ -237,6 +237,7 @@ struct AttnArgs {
     float* part2_o = nullptr;     // group partials (the merge's second level)
     float2* part2_ml = nullptr;
     unsigned* counters = nullptr;
+    size_t scratch_row = 0;       // floats between rows' scratch blocks (the pointers: row 0)
 };
 unsigned read_and_clear_attn_error();
 

@@ -103,3 +103,30 @@ def test_attention_wide_heads_and_long_chunks(case):
     heads, kv_heads, hs, seq_len = case
     for rows in (1, 5):
         run_case(heads, kv_heads, hs, seq_len, "split", [0, 17, 16 * 37, seq_len - rows], rows, rng)
+
+
+def test_attention_scratch_reused_across_row_counts():
+    # One scratch, zero-filled once, sized for the most rows; calls of 3, 1, 8, 1 and 5 rows in
+    # turn on a context long enough to split into chunks (tickets in use), as a model's prefill
+    # and decode share it: each call must leave the scratch ready for the next whatever its
+    # row count (tests/test_cuda_attention.cpp's contract).
+    rng = np.random.default_rng(21)
+    heads, kv_heads, hs, seq_len = 8, 2, 64, 1200
+    kv, dim = kv_heads * hs, heads * hs
+    shape = L.AttentionShape(heads, kv_heads, hs, seq_len, dim + 2 * kv, kv, dim)
+    kc = rng.uniform(-1, 1, (seq_len, kv)).astype(np.float32)
+    vc = rng.uniform(-1, 1, (seq_len, kv)).astype(np.float32)
+    dk, dv = torch.from_numpy(kc).cuda(), torch.from_numpy(vc).cuda()
+    scratch = torch.zeros(max(1, L.attention_scratch_floats(shape, 8, "split")), device="cuda")
+    pos_dev = torch.zeros(1, dtype=torch.int32, device="cuda")
+    pos = 700
+    for rows in (3, 1, 8, 1, 5):
+        q = rng.uniform(-1, 1, (rows, shape.q_stride)).astype(np.float32)
+        out = torch.zeros(rows, dim, device="cuda")
+        pos_dev.fill_(pos)
+        L.attention(shape, rows, pos_dev.data_ptr(), torch.from_numpy(q).cuda().data_ptr(),
+                    dk.data_ptr(), dv.data_ptr(), out.data_ptr(), scratch.data_ptr(), "split",
+                    L.torch_stream_handle())
+        diff = np.abs(out.cpu().numpy() - reference(shape, rows, pos, q, kc, vc)).max()
+        assert diff <= TOL, (rows, pos, diff)
+        pos += rows
