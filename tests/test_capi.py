@@ -271,3 +271,10 @@ def test_attention_check_rules():
     assert L.attention_scratch_floats(long, 10, "automatic") >= 10 * 4 * 128
     # automatic splits at most 8 rows when single_block fits
     assert L.attention_scratch_floats(ok, 100, "automatic") == L.attention_scratch_floats(ok, 8, "split")
+    # one block per row at a stride set by the shape alone (16-byte multiples): a call with
+    # fewer rows uses a prefix of a larger call's blocks, tickets included
+    for shape in (ok, long, S(32, 32, 128, 4112, 12288, 4096, 4096)):
+        one = L.attention_scratch_floats(shape, 1, "split")
+        assert one % 4 == 0
+        for rows in (2, 3, 8, 13):
+            assert L.attention_scratch_floats(shape, rows, "split") == rows * one
