@@ -1,4 +1,4 @@
-"""Benchmark: the 7B-shaped int8 decode matmul chain.
+"""Benchmark: the 7B-shaped int8 decode matmul chain (default) and the other workloads.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -377,7 +377,7 @@ def gemv_4096_probe(steps=200):
 
 
 def run_sgemm(args, world, rank, local):
-    """C = A x B, fp32 N x N, A and B ~ U(-1, 1) (seed 2), through the
+    """The square SGEMM: C = A x B, fp32 N x N, A and B ~ U(-1, 1) (seed 2), through the
     C ABI on the tcgen05 TF32 path (B read as stored, MN-major). Inputs 768 MB > L2."""
     import torch
     import llme_b200 as L
@@ -421,7 +421,7 @@ def run_sgemm(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
-# ---- the decode-shaped sweep ------------------------------------------
+# ---- the decode-shaped sweep ------------------------------------------------------------
 
 SWEEP_ROWS = (1, 4, 16, 64)
 SWEEP_COPIES = 12  # distinct 4096 x 4096 weights per case (201 MB int8 / 805 MB fp32 > L2)
@@ -618,7 +618,7 @@ def run_tp_decode(args, world, rank, local):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 W, f32",
             "data": "synthetic: N(0,0.02^2) weights drawn on the device, quantised per column; "
                     "U(-1,1) embedding and KV history",
-            "config": {"workload": "tensor-parallel decode (SURVEY (f)2), one token per step",
+            "config": {"workload": "tensor-parallel transformer decode, one token per step",
                        "layers": L_, "dim": DIM, "hidden": HIDDEN, "heads": 32, "vocab": VOCAB,
                        "context": ctx, "parallelism": f"tp{world}",
                        "launch": "one CUDA graph per token: embed, per layer rmsnorm+wqkv, "
@@ -741,7 +741,7 @@ def run_attention(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
-# ---- the 7B-shaped prefill (m = 512) ----------------------------------
+# ---- the 7B-shaped prefill (m = 512) ---------------------------------------------------
 
 PREFILL_ROWS = 512
 PREFILL_METRIC = "prefill GEMM TFLOP/s (7B-shaped int8 weights, m=512)"
@@ -1282,17 +1282,17 @@ def main():
     ap.add_argument("--workload", choices=["chain", "gemv", "sgemm", "prefill", "sweep",
                                            "attention", "tp_decode"],
                     default="chain",
-                    help="chain: BASELINE configs[3] (default); gemv: configs[0] alone; "
-                         "sgemm: configs[2] (square TF32 GEMM, --size); prefill: configs[4] "
-                         "(m = 512 through the 7B-shaped int8 weights); sweep: configs[1] "
-                         "(m in {1,4,16,64} x 4096^2, fp32 and int8 W, per call); attention: "
+                    help="chain: m = 1 through the 32 layers of 7B-shaped int8 weights (default); "
+                         "gemv: one int8 4096 x 4096 weight at m = 1; sgemm: square TF32 "
+                         "GEMM (--size); prefill: m = 512 through the 7B-shaped int8 weights; "
+                         "sweep: m in {1,4,16,64} x 4096^2, fp32 and int8 W, per call; attention: "
                          "decode attention over KV caches; tp_decode: tokens/s of the "
                          "7B-shaped int8 transformer, tensor-parallel over --gpus")
     ap.add_argument("--size", type=int, default=8192, help="N for --workload sgemm")
     ap.add_argument("--context", type=int, default=1024,
                     help="cached positions before the decoded token (--workload tp_decode)")
     ap.add_argument("--layers", type=int, default=LAYERS,
-                    help="layers of the chain / prefill (32 = the BASELINE configs; fewer only "
+                    help="layers of the chain / prefill (32 = a 7B model; fewer only "
                          "for small profiling cases)")
     ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
                     help="N>1: the library's NVLink peer all-reduce (default) or NCCL")

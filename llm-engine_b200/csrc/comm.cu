@@ -1,6 +1,6 @@
 // Tensor-parallel products over NCCL (include/llme_b200.h, "multi-GPU").
 //
-// The reference has no collective; the north star adds exactly one: a sum all-reduce of the
+// The reference has no collective; tensor parallelism adds exactly one: a sum all-reduce of the
 // row-parallel (k-split) partial outputs of wo and w2. NCCL (libnccl.so.2) is opened with
 // dlopen on first use, so single-GPU users of the library need no NCCL at all, and a process
 // that already loaded NCCL (PyTorch does) shares that copy.

@@ -1,6 +1,6 @@
 """Tensor-parallel sharding of the matmul path (host side).
 
-The reference runs on one GPU (one CudaTransformer, src/cuda_model.h); the north star
+The reference runs on one GPU (one CudaTransformer, src/cuda_model.h); this module
 splits the 7B-shaped chain across the GPUs of one box:
 
 * column-parallel weights (wq, wk, wv, w1, w3, classifier): B (k x n) is split along n;

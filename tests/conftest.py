@@ -62,7 +62,7 @@ def close_to(got: np.ndarray, want: np.ndarray, k: int, factor: float = 1.0) -> 
 
 
 def row_rel_err(got: np.ndarray, want: np.ndarray) -> float:
-    """max over rows of ||C - C_ref||_inf / ||C_ref row||_2, the north-star error metric."""
+    """max over rows of ||C - C_ref||_inf / ||C_ref row||_2, the path's error metric."""
     g = got.astype(np.float64)
     w = want.astype(np.float64)
     num = np.abs(g - w).max(axis=1)

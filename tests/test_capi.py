@@ -124,7 +124,7 @@ def test_split_k_plan_covers_k_exactly_once(n, k, q8, sms):
 
 
 def test_decode_shapes_fill_the_gpu():
-    # The BASELINE decode shapes launch close to two CTAs per SM on 148 SMs.
+    # The 7B decode shapes launch close to two CTAs per SM on 148 SMs.
     for n, k in [(4096, 4096), (11008, 4096), (4096, 11008)]:
         p = L.plan(1, n, k, q8=True)
         assert 0.8 * 296 <= p["grid_x"] * p["grid_y"] <= 296, (n, k, p)

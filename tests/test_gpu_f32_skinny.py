@@ -2,11 +2,11 @@
 TF32 terms (W_hi A_hi + W_hi A_lo + W_lo A_hi), k slices of a column tile added through
 distributed shared memory of one thread-block cluster.
 
-Held to the decode path's bound from the north star: max over rows of
+Held to the decode path's accuracy bound: max over rows of
 ||C - C_ref||_inf / ||C_ref row||_2 <= 1e-5 against the oracle (matmul_naive, the reference's
 src/matmul.cpp restated and pinned); repeats bit-identical (the cluster adds its partials in
-rank order); MatmulFusion's accumulate and RMSNorm (tests/test_cuda.cpp:190-212); and BASELINE
-configs[1]'s fp32 shapes (m = 16, 64 x 4096^2) at full size.
+rank order); MatmulFusion's accumulate and RMSNorm (tests/test_cuda.cpp:190-212); and the
+decode sweep's fp32 shapes (m = 16, 64 x 4096^2) at full size.
 """
 from __future__ import annotations
 
@@ -122,7 +122,7 @@ def test_f32_skinny_repeats_bit_identical():
 
 
 def test_config1_fp32_decode_sweep_full_size():
-    # BASELINE configs[1], fp32 half: m in {16, 64} (the rows this path takes), 4096 x 4096.
+    # The decode sweep, fp32 half: m in {16, 64} (the rows this path takes), 4096 x 4096.
     rng = np.random.default_rng(1)
     W = weights(rng, 4096, 4096)
     for m in (16, 64):

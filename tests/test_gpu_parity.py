@@ -5,8 +5,8 @@ Mirrors the reference's tests/test_cuda.cpp: the shape list on and around tile e
 int8 weights plain and fused (:170-213), back-to-back split-K launches that must repeat
 bit for bit (:221-275) and the argument errors (:277-287). Tolerance as the reference:
 |got - want| <= 1e-5 * k (2e-5 * k fused) against matmul_naive on identical inputs (the
-dequantised weights for int8). BASELINE's decode configs run at full size against the
-north-star bound, max over rows of ||C - C_ref||_inf / ||C_ref row||_2 <= 1e-5.
+dequantised weights for int8). The benchmark's decode shapes run at full size against the
+decode path's accuracy bound, max over rows of ||C - C_ref||_inf / ||C_ref row||_2 <= 1e-5.
 """
 from __future__ import annotations
 
@@ -47,8 +47,8 @@ def path_of(m, n, k, q8, kernel, accumulate=False, rms=False):
 
 
 def check(got, want, k, factor, path):
-    """The reference's absolute 1e-5 * k bound for fp32-product paths
-    (5e-3 of the row's L2 norm) for the tensor-core paths."""
+    """The reference's absolute 1e-5 * k bound for fp32-product paths; the tensor-core
+    bound (5e-3 of the row's L2 norm) for the tensor-core paths."""
     if path in ("tcgen05", "tcgen05_q8"):
         return row_rel_err(got, want) <= 5e-3
     return close_to(got, want, k, factor)
@@ -247,7 +247,7 @@ def test_bad_shapes_raise_invalid_argument():
     assert "2x3" in str(e.value) and "4x2" in str(e.value)
 
 
-# ---- BASELINE.json configs at full size --------------------------------------------------
+# ---- the benchmark's decode shapes at full size -----------------------------------------
 
 def baseline_weights(seed, k, n):
     rng = np.random.default_rng(seed)

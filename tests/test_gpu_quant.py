@@ -1,6 +1,6 @@
 """The GPU quantiser (llme_quantize_q8) against the reference's quantize_q8 (src/quant.cpp:6-28),
 bit for bit: the oracle's restatement, itself pinned bit for bit to the reference's compiled
-code (tests/test_oracle.py), on the same fp32 weights. Shapes: BASELINE's weights
+code (tests/test_oracle.py), on the same fp32 weights. Shapes: the benchmark's weights
 (N(0, 0.02^2)), ragged column counts, a single row, columns of zeros, exact halfway products
 (round half away from zero) and values that hit the +-127 clamp."""
 from __future__ import annotations

@@ -1,11 +1,11 @@
 """Decode-shaped int8 products on the tensor cores (LLME_PATH_TCGEN05_SKINNY): activation rows
 split into three int8 terms, kind::i8 MMAs, k split across CTAs with exact int64 sums.
 
-Held to the decode path's bound from the north star: max over rows of
+Held to the decode path's accuracy bound: max over rows of
 ||C - C_ref||_inf / ||C_ref row||_2 <= 1e-5 against the oracle (matmul_naive on the dequantised
 weights, tests/test_quant.cpp:57-79); bit for bit against a numpy restatement of the kernel's
 own arithmetic for rows without RMSNorm; repeats bit-identical whatever order the k slices'
-atomic adds arrive in; and BASELINE configs[1]'s int8 shapes (m = 16, 64 x 4096^2) at full size.
+atomic adds arrive in; and the decode sweep's int8 shapes (m = 16, 64 x 4096^2) at full size.
 """
 from __future__ import annotations
 
@@ -132,7 +132,7 @@ def test_skinny_repeats_bit_identical_and_scratch_settles():
 
 
 def test_config1_int8_decode_sweep_full_size():
-    # BASELINE configs[1], int8 half: m in {16, 64} (the rows this path takes), 4096 x 4096.
+    # The decode sweep, int8 half: m in {16, 64} (the rows this path takes), 4096 x 4096.
     rng = np.random.default_rng(1)
     q, s = weights(rng, 4096, 4096)
     for m in (16, 64):

@@ -1,6 +1,6 @@
 """The tcgen05/TMEM tensor-core GEMM (m >= 128, fp32 weights, TF32 multiplies).
 
-Parity bound from the north star: max over rows of ||C - C_ref||_inf / ||C_ref row||_2 <=
+Parity bound of the tensor-core path: max over rows of ||C - C_ref||_inf / ||C_ref row||_2 <=
 5e-3 against matmul_naive on identical inputs. Tighter checks pin the arithmetic: the result
 must sit within the fp32-accumulation noise of a float64 product of TF32-converted operands,
 and repeats must be bit-identical.
@@ -91,7 +91,7 @@ def test_tf32_gemm_repeats_bit_identical():
 
 
 def test_config2_square_1024():
-    # BASELINE configs[2] at N = 1024 (A, B ~ U(-1, 1)), checked against the oracle.
+    # The square SGEMM at N = 1024 (A, B ~ U(-1, 1)), checked against the oracle.
     rng = np.random.default_rng(2)
     A, B = uni(rng, 1024, 1024), uni(rng, 1024, 1024)
     assert row_rel_err(run(A, B), oracle.matmul_naive(A, B)) <= 5e-3

@@ -3,7 +3,7 @@ int8 terms, kind::i8 MMAs with exact s32 sums in TMEM, fp32 epilogue.
 
 Three checks per shape:
 * against the oracle (matmul_naive on the dequantised weights, the reference's int8 parity
-  reference, tests/test_quant.cpp:57-79) with the north-star tensor-core bound: max over rows
+  reference, tests/test_quant.cpp:57-79) with the tensor-core path's bound: max over rows
   of ||C - C_ref||_inf / ||C_ref row||_2 <= 5e-3 -- and, since the split keeps 16 bits of each
   activation, a much tighter 1e-4 that pins the arithmetic as well;
 * bit for bit against a numpy restatement of the kernel's own arithmetic (the split of each
@@ -98,7 +98,7 @@ def _tensor_math(request):
 
 
 # (m, k, n): tile edges, ragged m, k not a multiple of 16 or 128, n a multiple of 16 but not
-# of 128, both column tiles (128 and 256 wide), and BASELINE configs[4]'s prefill shapes
+# of 128, both column tiles (128 and 256 wide), and the 7B prefill shapes
 # (m = 512 through the 4096 x 4096, 4096 x 11008 and 11008 x 4096 weights).
 SHAPES = [(128, 128, 256), (128, 32, 128), (256, 512, 512), (130, 72, 1040), (300, 1000, 272),
           (129, 4100, 48), (512, 4096, 4096), (512, 4096, 11008), (512, 11008, 4096),

@@ -40,7 +40,7 @@ def test_shard_range_covers_everything_once(total, world):
     assert max(counts) - min(counts) <= 1
 
 
-def test_parallelism_table_matches_the_north_star():
+def test_only_wo_and_w2_are_row_parallel():
     assert [k for k, v in shard.PARALLELISM.items() if v == "row"] == ["wo", "w2"]
 
 
