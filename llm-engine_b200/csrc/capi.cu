@@ -63,6 +63,7 @@ int math_mode() {
 constexpr size_t kMaxElems = size_t{1} << 31;  // kernels index with int
 constexpr int kSkinnyMaxRows = 8;
 constexpr int kSplitMaxRows = 127;             // automatic: tiled_split below 128 rows
+constexpr size_t kMaxGridY = 65535;            // CUDA's limit on gridDim.y
 
 struct PlanIn {
     size_t m, n, k;
@@ -92,7 +93,7 @@ size_t q8tc_operand_bytes(size_t m, size_t k) { return 2 * q8tc_rows_bytes(m, k)
 // The skinny GEMM's three term planes, then the row scales.
 size_t skinny_operand_bytes(size_t m, size_t k) { return 3 * q8tc_rows_bytes(m, k) + m * sizeof(float); }
 
-int make_plan(const PlanIn& in, llme_plan_t* p) {
+int plan_path(const PlanIn& in, llme_plan_t* p) {
     std::memset(p, 0, sizeof(*p));
     const size_t m = in.m, n = in.n, k = in.k;
     int kernel = in.kernel;
@@ -281,6 +282,22 @@ int make_plan(const PlanIn& in, llme_plan_t* p) {
     if (slices > 1) {
         p->counter_slots = tiles;
         p->split_bytes = tiles * slices * kTiledBM * kTiledBN * sizeof(float);
+    }
+    return LLME_OK;
+}
+
+// The SIMT and decode-shaped tensor-core paths put row tiles on grid y, whose limit is 65535
+// (the prefill GEMMs put every tile on x): the planner refuses more row tiles than that
+// rather than let the launch fail.
+int make_plan(const PlanIn& in, llme_plan_t* p) {
+    const int st = plan_path(in, p);
+    if (st != LLME_OK) return st;
+    if (static_cast<size_t>(p->grid_y) > kMaxGridY) {
+        const llme_plan_t planned = *p;
+        std::memset(p, 0, sizeof(*p));
+        return fail(LLME_E_INVALID, "matmul_cuda: " + std::to_string(planned.grid_y) +
+                                        " row tiles of " + std::to_string(planned.tile_m) +
+                                        " exceed the grid's 65535 " + shapes(in.m, in.n, in.k));
     }
     return LLME_OK;
 }

@@ -278,3 +278,19 @@ def test_attention_check_rules():
         assert one % 4 == 0
         for rows in (2, 3, 8, 13):
             assert L.attention_scratch_floats(shape, rows, "split") == rows * one
+
+
+@pytest.mark.parametrize("q8,kernel,math,tile", [(False, "naive", L.MATH_TENSOR, 16),
+                                                 (False, "tiled", L.MATH_FP32, 64),
+                                                 (True, "tiled_split", L.MATH_TENSOR, 64),
+                                                 (False, "tiled_split", L.MATH_TENSOR, 64)])
+def test_row_tiles_beyond_the_grid_are_invalid(q8, kernel, math, tile):
+    # Paths with row tiles on grid y take at most 65535 of them; the prefill GEMMs (all tiles
+    # on x) take the same rows.
+    rows = 65535 * tile
+    assert L.plan(rows, 16, 16, q8=q8, kernel=kernel, math=math)["grid_y"] == 65535
+    with pytest.raises(L.InvalidArgument) as e:
+        L.plan(rows + 1, 16, 16, q8=q8, kernel=kernel, math=math)
+    assert "exceed the grid's 65535" in str(e.value)
+    big = L.plan(rows + 1, 16, 16, q8=q8, kernel="tiled", math=L.MATH_TENSOR)
+    assert big["path_name"] in ("tcgen05", "tcgen05_q8") and big["grid_y"] == 1
