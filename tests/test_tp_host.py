@@ -127,3 +127,25 @@ def test_reference_model_oracle(q8, tmp_path):
     np.testing.assert_allclose(pre, last, rtol=1e-4, atol=1e-4)
     with pytest.raises(RuntimeError, match="positions"):
         a.run([1], 7 + 2)
+
+
+def test_decode_step_arguments_are_checked_before_any_launch():
+    # Every refusal here happens on the host; nothing is launched and the fake addresses are
+    # never read. Empty work is a no-op that touches no GPU either.
+    P = 256
+    L.embed_rows(0, 64, P, P, P)
+    L.rope_cache(0, 4, 2, 8, P, P, P, P, P, P)
+    L.swiglu(0, 96, P, P)
+    bad = [lambda: L.embed_rows(1, 64, 0, P, P),
+           lambda: L.embed_rows(65536, 64, P, P, P),
+           lambda: L.embed_rows(1 << 15, 1 << 16, P, P, P),           # 2^31 elements
+           lambda: L.rope_cache(1, 4, 2, 7, P, P, P, P, P, P),        # odd head_size
+           lambda: L.rope_cache(1, 4, 0, 8, P, P, P, P, P, P),        # no kv heads
+           lambda: L.rope_cache(65536, 4, 2, 8, P, P, P, P, P, P),
+           lambda: L.rope_cache(1, 4, 2, 8, P, P, P, 0, P, P),
+           lambda: L.swiglu(1, 1 << 30, P, P),
+           lambda: L.swiglu(1, 96, P, 0),
+           lambda: L.rope_tables(4, 7)]
+    for call in bad:
+        with pytest.raises(L.InvalidArgument):
+            call()
