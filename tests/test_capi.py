@@ -8,6 +8,7 @@ errors and their messages (:411-417, test_cuda.cpp:277-287), empty and k == 0 ha
 """
 from __future__ import annotations
 
+import ctypes
 import os
 import re
 import subprocess
@@ -53,6 +54,49 @@ def test_cxx_shim_exports_reference_api():
                 "DeviceTensor::upload(Tensor const&)", "DeviceTensor::download() const",
                 "DeviceQTensor::DeviceQTensor(QTensor const&)"]:
         assert sig in syms, sig
+
+
+C_CLIENT = r"""
+#include <stdio.h>
+#include <string.h>
+#include "llme_b200.h"
+
+int main(void) {
+    llme_plan_t p;
+    if (llme_plan(1, 4096, 4096, 1, LLME_KERNEL_AUTOMATIC, 0, 256, 256, 0, 148, LLME_MATH_TENSOR,
+                  &p) != LLME_OK || p.path != LLME_PATH_GEMV_TMA)
+        return 1;
+    if (llme_plan(9, 2, 2, 0, LLME_KERNEL_SKINNY, 0, 256, 256, 0, 148, LLME_MATH_TENSOR, &p) !=
+            LLME_E_INVALID || strstr(llme_last_error(), "at most 8 rows") == NULL)
+        return 2;
+    printf("%d %d %d\n", p.path, LLME_PATH_TCGEN05_F32_SKINNY, (int)sizeof(llme_plan_t));
+    return 0;
+}
+"""
+
+
+@pytest.mark.skipif(subprocess.run(["which", "gcc"], stdout=subprocess.DEVNULL).returncode != 0,
+                    reason="no C compiler")
+def test_header_is_plain_c_and_links_from_c(tmp_path):
+    # The boundary a cgo / FFI binding sees: strict C99, no C++ or CUDA types, and a program
+    # linked to the library plans a call and reads an error message without touching a GPU.
+    src, exe = tmp_path / "client.c", tmp_path / "client"
+    src.write_text(C_CLIENT)
+    libdir = os.path.dirname(L.library_path())
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror",
+                    "-I", os.path.join(REPO, "include"), str(src), "-o", str(exe), "-L", libdir,
+                    "-lllme_b200", f"-Wl,-rpath,{libdir}"], check=True)
+    out = subprocess.run([str(exe)], stdout=subprocess.PIPE, text=True)
+    assert out.returncode == 0, out.returncode
+    assert int(out.stdout.split()[2]) == ctypes.sizeof(L.Plan)
+
+
+def test_cxx_headers_compile_against_the_bundled_tensor_layout():
+    src = '#include "llme_b200.h"\n#include "cuda_matmul.h"\n#include "cuda_attention.h"\n'
+    inc = os.path.join(REPO, "include")
+    subprocess.run(["g++", "-std=c++17", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", inc,
+                    "-I", os.path.join(inc, "tensor"), "-x", "c++", "-fsyntax-only", "-"],
+                   input=src, text=True, check=True)
 
 
 @pytest.mark.parametrize("m,kernel", [(1, "skinny"), (8, "skinny"), (9, "tiled_split"),
