@@ -14,7 +14,17 @@
  * Streams: `stream` is a cudaStream_t. NULL means the calling thread's
  * per-thread default stream, which is where the reference launches (it is
  * built with --default-stream=per-thread, cuda_matmul.h:7-12). Calls are
- * asynchronous: they return before the GPU finishes.
+ * asynchronous: they return before the GPU finishes. The matmul calls share
+ * one scratch per device (split-K partial sums and tickets, the RMSNorm'd copy
+ * of A, the split int8 activation rows, B^T); paths that use it are those
+ * whose plan has split_bytes, norm_bytes or operand_bytes nonzero. Two such
+ * calls whose kernels may overlap on the GPU (different streams with no
+ * event between them, concurrent graphs) race on it, as the reference's
+ * calls from several host threads do: order them on one stream. Plans with
+ * all three zero (the TMA weight-streaming GEMV; the fp32 decode-shaped
+ * kernel without RMSNorm) reduce in distributed shared memory and touch no
+ * scratch; the grouped batch and the attention take their buffers from the
+ * caller.
  *
  * Errors: a nonzero status; llme_last_error() then holds a message for the
  * calling thread (the text the reference puts in its exceptions).

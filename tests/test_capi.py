@@ -338,3 +338,20 @@ def test_row_tiles_beyond_the_grid_are_invalid(q8, kernel, math, tile):
     assert "exceed the grid's 65535" in str(e.value)
     big = L.plan(rows + 1, 16, 16, q8=q8, kernel="tiled", math=L.MATH_TENSOR)
     assert big["path_name"] in ("tcgen05", "tcgen05_q8") and big["grid_y"] == 1
+
+
+def test_scratch_free_plans_are_the_ones_the_header_names():
+    # Plans with split_bytes, norm_bytes and operand_bytes all zero touch no shared scratch.
+    def scratch(p):
+        return p["split_bytes"] + p["norm_bytes"] + p["operand_bytes"]
+    for q8 in (False, True):
+        for n, k in [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]:
+            for rms in (0, 256):
+                p = L.plan(1, n, k, q8=q8, rms_addr=rms)
+                assert p["path_name"] == "gemv_tma" and scratch(p) == 0
+    p = L.plan(16, 4096, 4096, q8=False, math=L.MATH_TENSOR)
+    assert p["path_name"] == "tcgen05_f32_skinny" and scratch(p) == 0
+    p = L.plan(16, 4096, 4096, q8=False, rms_addr=256, math=L.MATH_TENSOR)
+    assert p["path_name"] == "tcgen05_f32_skinny" and p["norm_bytes"] == 16 * 4096 * 4
+    assert scratch(L.plan(16, 4096, 4096, q8=True, math=L.MATH_TENSOR)) > 0
+    assert scratch(L.plan(512, 4096, 4096, q8=True, math=L.MATH_TENSOR)) > 0
