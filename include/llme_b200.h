@@ -27,7 +27,10 @@
  * caller.
  *
  * Errors: a nonzero status; llme_last_error() then holds a message for the
- * calling thread (the text the reference puts in its exceptions).
+ * calling thread (the text the reference puts in its exceptions). A NULL
+ * pointer that a call would read or write is LLME_E_INVALID, decided before
+ * any device work; pointers a call does not touch (all of them for an empty
+ * product, A and B when k == 0) may be NULL.
  */
 #ifndef LLME_B200_H
 #define LLME_B200_H

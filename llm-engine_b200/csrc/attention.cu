@@ -642,6 +642,8 @@ int llme_attention(const llme_attention_shape* s, size_t rows, const int* pos_de
     int st = check(*s, kernel);
     if (st) return st;
     if (rows == 0) return LLME_OK;
+    if (!pos_dev || !q || !key_cache || !value_cache || !out)
+        return set_error(LLME_E_INVALID, "attention: null pointer");
     kernel = resolve(*s, kernel, rows);
     st = check(*s, kernel);
     if (st) return st;

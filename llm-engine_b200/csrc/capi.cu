@@ -531,9 +531,20 @@ int encode_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t 
 
 // ---- the call --------------------------------------------------------------------------
 
+// The pointers a product reads or writes must be set: none for an empty product, only C when
+// k == 0 zeroes it, all of A, B, C (and the int8 scales) otherwise.
+bool missing_pointer(size_t m, size_t n, size_t k, const float* A, const void* B,
+                     const float* scale, const float* C, bool q8, bool accumulate) {
+    if (m == 0 || n == 0) return false;
+    if (k == 0) return !accumulate && !C;
+    return !A || !B || !C || (q8 && !scale);
+}
+
 int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float* scale, float* C,
         bool q8, int kernel, bool accumulate, const float* rms, unsigned flags, void* stream_ptr) {
     g_error.clear();
+    if (missing_pointer(m, n, k, A, B, scale, C, q8, accumulate))
+        return fail(LLME_E_INVALID, "matmul_cuda: null pointer " + shapes(m, n, k));
     cudaStream_t stream = stream_ptr ? static_cast<cudaStream_t>(stream_ptr) : cudaStreamPerThread;
     int dev = 0, sms = 0;
     int st = current_device(&dev);
@@ -809,6 +820,8 @@ int noalloc_setup(int dev, cudaStream_t stream, unsigned char** base) {
 int run_noalloc(size_t m, size_t n, size_t k, const float* A, const int8_t* B, const float* scale,
                 float* C, bool accumulate, void* stream_ptr) {
     g_error.clear();
+    if (missing_pointer(m, n, k, A, B, scale, C, true, accumulate))
+        return fail(LLME_E_INVALID, "llme_matmul_q8_noalloc: null pointer " + shapes(m, n, k));
     cudaStream_t stream = stream_ptr ? static_cast<cudaStream_t>(stream_ptr) : cudaStreamPerThread;
     int dev = 0, sms = 0;
     int st = current_device(&dev);
@@ -1040,10 +1053,16 @@ int batch_create_tc(llme_batch_t** out, size_t m, size_t count, const llme_q8_pr
 
 int batch_create(llme_batch_t** out, size_t m, size_t count, const llme_q8_product* p) {
     g_error.clear();
+    if (!out) return fail(LLME_E_INVALID, "llme_batch_q8_create: null result pointer");
     *out = nullptr;
     if (count < 1 || count > 65535)
         return fail(LLME_E_INVALID, "llme_batch_q8_create: 1..65535 products, got " +
                                         std::to_string(count));
+    if (!p) return fail(LLME_E_INVALID, "llme_batch_q8_create: null products");
+    for (size_t i = 0; i < count; ++i)
+        if (!p[i].A || !p[i].B || !p[i].scale || !p[i].C)
+            return fail(LLME_E_INVALID, "llme_batch_q8_create: product " + std::to_string(i) +
+                                            ": null pointer");
     if (m >= 128) return batch_create_tc(out, m, count, p);
     if (m < 1 || m > 8)
         return fail(LLME_E_INVALID,
@@ -1356,6 +1375,7 @@ int llme_plan(size_t m, size_t n, size_t k, int is_q8, int kernel, int accumulat
               uintptr_t a_addr, uintptr_t b_addr, uintptr_t rms_addr, int sm_count, int math,
               llme_plan_t* out) {
     g_error.clear();
+    if (!out) return fail(LLME_E_INVALID, "llme_plan: null result pointer");
     PlanIn in{m, n, k, is_q8 != 0, kernel, accumulate != 0, a_addr, b_addr, rms_addr, sm_count, math};
     return make_plan(in, out);
 }

@@ -244,6 +244,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(float* __r
 extern "C" {
 
 int llme_comm_unique_id(void* id) {
+    if (!id) return llme::set_error(LLME_E_INVALID, "llme_comm_unique_id: null id");
     int st = need_nccl();
     if (st) return st;
     static_assert(sizeof(ncclUniqueId) == LLME_COMM_ID_BYTES, "NCCL unique id size");
@@ -255,6 +256,7 @@ int llme_comm_unique_id(void* id) {
 }
 
 int llme_comm_init(llme_comm_t** out, int nranks, int rank, const void* id, double timeout_s) {
+    if (!out || !id) return llme::set_error(LLME_E_INVALID, "llme_comm_init: null pointer");
     *out = nullptr;
     int st = need_nccl();
     if (st) return st;
@@ -406,6 +408,7 @@ int llme_comm_rank(const llme_comm_t* c) { return c ? c->rank : -1; }
 int llme_allreduce_sum_f32(float* buf, size_t count, llme_comm_t* c, void* stream_ptr) {
     if (!c) return llme::set_error(LLME_E_INVALID, "llme_allreduce_sum_f32: no communicator");
     if (c->nranks == 1 || count == 0) return LLME_OK;
+    if (!buf) return llme::set_error(LLME_E_INVALID, "llme_allreduce_sum_f32: null buffer");
     cudaStream_t stream = stream_ptr ? static_cast<cudaStream_t>(stream_ptr) : cudaStreamPerThread;
     if (c->peer && count <= c->peer_max_floats) {
         peer_allreduce_kernel<<<kPeerCtas, kPeerThreads, 0, stream>>>(buf, count, c->pargs);

@@ -355,3 +355,41 @@ def test_scratch_free_plans_are_the_ones_the_header_names():
     assert p["path_name"] == "tcgen05_f32_skinny" and p["norm_bytes"] == 16 * 4096 * 4
     assert scratch(L.plan(16, 4096, 4096, q8=True, math=L.MATH_TENSOR)) > 0
     assert scratch(L.plan(512, 4096, 4096, q8=True, math=L.MATH_TENSOR)) > 0
+
+
+def test_null_pointers_are_refused_before_any_device_work():
+    # A pointer the call would read or write that is NULL is LLME_E_INVALID, decided on the host
+    # before the device is queried; pointers a call never touches may be NULL.
+    lib, P, INVALID = L.load(), 256, 1
+
+    def refused(rc, text="null"):
+        return rc == INVALID and text in L.last_error()
+
+    assert refused(lib.llme_matmul_f32(2, 3, 4, None, P, P, 0, 0, None, 0, None))
+    assert refused(lib.llme_matmul_f32(2, 3, 4, P, None, P, 0, 0, None, 0, None))
+    assert refused(lib.llme_matmul_f32(2, 3, 4, P, P, None, 0, 0, None, 0, None))
+    assert refused(lib.llme_matmul_q8(2, 3, 4, P, P, None, P, 0, 0, None, 0, None))
+    assert refused(lib.llme_matmul_f32(2, 3, 0, None, None, None, 0, 0, None, 0, None))  # zeroes C
+    assert refused(lib.llme_matmul_q8_noalloc(2, 3, 4, P, P, None, P, 0, None))
+    # empty products and k == 0 with accumulate touch nothing: not refused (without a GPU they
+    # go on to fail at the device query instead)
+    assert lib.llme_matmul_f32(0, 3, 4, None, None, None, 0, 0, None, 0, None) != INVALID
+    assert lib.llme_matmul_q8(2, 0, 4, None, None, None, None, 0, 0, None, 0, None) != INVALID
+    assert lib.llme_matmul_f32(2, 3, 0, None, None, None, 0, 1, None, 0, None) != INVALID
+    # plans, batches, communicators and attention
+    assert refused(lib.llme_plan(1, 1, 1, 0, 0, 0, P, P, 0, 148, 0, None))
+    assert refused(lib.llme_batch_q8_create(None, 1, 1, None))
+    handle = ctypes.c_void_p()
+    assert refused(lib.llme_batch_q8_create(ctypes.byref(handle), 1, 1, None))
+    prods = (L.Q8Product * 2)(L.Q8Product(16, 16, P, P, P, P, 0), L.Q8Product(16, 16, P, P, None, P, 0))
+    assert refused(lib.llme_batch_q8_create(ctypes.byref(handle), 1, 2, prods), "product 1")
+    assert refused(lib.llme_batch_q8_create(ctypes.byref(handle), 128, 2, prods), "product 1")
+    assert handle.value is None
+    assert refused(lib.llme_comm_unique_id(None))
+    assert refused(lib.llme_comm_init(None, 2, 0, b"x" * 128, 1.0))
+    assert refused(lib.llme_comm_init(ctypes.byref(handle), 2, 0, None, 1.0))
+    assert refused(lib.llme_allreduce_sum_f32(P, 4, None, None), "no communicator")
+    shape = L.AttentionShape(8, 8, 64, 128, 512, 512, 512)
+    assert refused(lib.llme_attention(ctypes.byref(shape), 1, None, P, P, P, P, P, 0, None))
+    assert refused(lib.llme_attention(ctypes.byref(shape), 1, P, P, P, P, None, P, 0, None))
+    assert lib.llme_attention(ctypes.byref(shape), 0, None, None, None, None, None, None, 0, None) == 0
