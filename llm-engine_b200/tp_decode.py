@@ -142,6 +142,10 @@ class TPTransformer:
         L.attention_check(self.shape)
         self.layers = []
         self.graph = None
+        # Reallocations of this model's activation buffers; with the library's scratch
+        # generation it tells whether a captured graph still points at live buffers.
+        self.own_generation = 0
+        self.graph_generation = -1
 
     def _add_layer(self, rms_att, rms_ffn, wqkv, wo, w13, w2):
         t, cfg = self.torch, self.cfg
@@ -173,6 +177,12 @@ class TPTransformer:
         self.hb = t.zeros(n, self.hc, device=dev)
         self.scratch = t.zeros(max(1, L.attention_scratch_floats(self.shape, n)), device=dev)
         self.rows = n
+        self.own_generation += 1
+
+    def buffers_generation(self) -> int:
+        """Changes whenever a buffer a captured step points at is replaced: this model's
+        activation rows or the library's scratch (src/cuda_model.cu:175-177)."""
+        return self.own_generation + L.scratch_generation()
 
     # ---- the products --------------------------------------------------------------------
     def _matmul(self, m, n, k, A, w, C, accumulate=False, rms=0):
@@ -286,6 +296,7 @@ class TPTransformer:
         t.cuda.current_stream().wait_stream(s)
         self.filled = saved
         self.graph = g
+        self.graph_generation = self.buffers_generation()
         return g
 
     def decode(self, token: int, pos: int):
@@ -298,6 +309,10 @@ class TPTransformer:
             raise IndexError(f"forward: positions {pos}..{pos} with {self.filled} cached of "
                              f"{cfg.seq_len}")
         self.torch.cuda.current_stream().synchronize()  # the previous replay read the feed
+        if self.graph_generation != self.buffers_generation():
+            # A longer prefill replaced the buffers the graph was captured on (the reference
+            # re-captures in the same case, src/cuda_model.cu:196-227).
+            self.capture_decode()
         self.feed_host[0] = pos
         self.feed_host[1] = int(token)
         self.graph.replay()

@@ -113,6 +113,27 @@ def test_graph_decode_matches_the_reference_model(tmp_path, q8):
         assert close(got, want), (token, pos, float(np.abs(got - want).max()))
 
 
+@pytest.mark.parametrize("q8", [False, True])
+def test_graph_recaptured_after_a_longer_prefill(tmp_path, q8):
+    # A prefill longer than any run before replaces the activation buffers the graph points
+    # at; the next decode() sees the generation move and captures again, as the reference's
+    # CudaTransformer does (src/cuda_model.cu:175-177, 196-227).
+    p = checkpoint(tmp_path, "mha", seed=12)
+    ref = oracle.RefModel(p, q8)
+    tp = TPTransformer(load_checkpoint(p), q8=q8)
+    assert close(tp.run([3], 0), ref.run([3], 0))
+    tp.capture_decode()
+    captured = tp.graph_generation
+    assert close(tp.forward(8, 1), ref.run([8], 1))
+    assert tp.graph_generation == captured
+    assert close(tp.prefill([4, 9, 1, 30], 2), ref.run([4, 9, 1, 30], 2))
+    assert tp.buffers_generation() != captured
+    for token, pos in [(5, 6), (12, 7), (2, 8)]:
+        got, want = tp.forward(token, pos), ref.run([token], pos)
+        assert close(got, want), (token, pos, float(np.abs(got - want).max()))
+    assert tp.graph_generation == tp.buffers_generation() != captured
+
+
 def test_positions_are_checked(tmp_path):
     tp = TPTransformer(load_checkpoint(checkpoint(tmp_path, "gqa")))
     with pytest.raises(IndexError):
