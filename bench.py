@@ -425,6 +425,51 @@ def run_sgemm(args, world, rank, local):
 
 SWEEP_ROWS = (1, 4, 16, 64)
 SWEEP_COPIES = 12  # distinct 4096 x 4096 weights per case (201 MB int8 / 805 MB fp32 > L2)
+SWEEP_METRIC = "decode sweep GB/s (m in {1,4,16,64} x 4096^2, fp32 and int8 W, per call)"
+
+
+def ref_matmul_gpu():
+    """The reference's own GPU matmul (src/cuda_matmul.cu for sm_100a, built into
+    oracle/_ref/libref_matmul_gpu.so by `make -C oracle refmatmul`), or None: timed only by
+    the reference arm (`--impl reference --workload sweep`)."""
+    import ctypes
+    path = os.path.join(REPO, "oracle", "_ref", "libref_matmul_gpu.so")
+    if not os.path.exists(path):
+        return None
+    lib = ctypes.CDLL(path)
+    sz, vp, ci = ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int
+    lib.ref_gpu_matmul_f32.argtypes = [sz, sz, sz, vp, vp, vp, ci, ci, vp]
+    lib.ref_gpu_matmul_q8.argtypes = [sz, sz, sz, vp, vp, vp, vp, ci, ci, vp]
+    lib.ref_gpu_error.restype = ctypes.c_char_p
+    lib.ref_gpu_capture_end.argtypes = [ctypes.POINTER(vp)]
+    lib.ref_gpu_time_graph.argtypes = [vp, ci, ci, ctypes.POINTER(ctypes.c_float)]
+    lib.ref_gpu_graph_destroy.argtypes = [vp]
+    return lib
+
+
+def time_ref_matmul_gpu(ref, calls, steps, warmup):
+    """Seconds for `steps` replays of the reference's calls captured as one CUDA graph on the
+    stream they launch on (its per-thread default stream), after one eager pass that grows its
+    scratch -- the way its CudaTransformer captures its decode step."""
+    import ctypes
+    import torch
+
+    def ok(rc):
+        if rc:
+            raise RuntimeError("reference GPU matmul: " + ref.ref_gpu_error().decode())
+    torch.cuda.synchronize()  # inputs written on torch's streams are in place
+    calls(ok)
+    ok(ref.ref_gpu_synchronize())
+    ok(ref.ref_gpu_capture_begin())
+    calls(ok)
+    graph = ctypes.c_void_p()
+    ok(ref.ref_gpu_capture_end(ctypes.byref(graph)))
+    ms = ctypes.c_float()
+    try:
+        ok(ref.ref_gpu_time_graph(graph, steps, warmup, ctypes.byref(ms)))
+    finally:
+        ref.ref_gpu_graph_destroy(graph)
+    return ms.value / 1e3
 
 
 def run_sweep(args, world, rank, local):
@@ -478,7 +523,7 @@ def run_sweep(args, world, rank, local):
     hbm, hbm_kind = peaks()
     value = tot_bytes / tot_s / 1e9
     cpu = cpu_sweep_sample() if rank == 0 and world == 1 and not args.no_extras else None
-    line = {"metric": "decode sweep GB/s (m in {1,4,16,64} x 4096^2, fp32 and int8 W, per call)",
+    line = {"metric": SWEEP_METRIC,
             "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(tot_s / args.steps * 1e3, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
@@ -544,6 +589,7 @@ ATTN_CASES = [  # (name, heads, kv heads, head size, cached positions)
     ("MQA long context", 4, 1, 128, 20000),
 ]
 ATTN_LAYERS = 8  # distinct caches per step, so the keys and values come from HBM
+ATTN_METRIC = "decode attention GB/s (KV-cache bytes, 1 row)"
 
 
 def run_tp_decode(args, world, rank, local):
@@ -641,22 +687,31 @@ def run_tp_decode(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def attention_case_inputs(torch, g, heads, kvh, hs, T):
+    """One attention case's inputs drawn from `g` in a fixed order, so both arms of the
+    attention benchmark see the same bytes: the query row, ATTN_LAYERS key and value caches of
+    T positions, and the position (the last cached one) in device memory."""
+    kv, dim = kvh * hs, heads * hs
+    q = torch.rand(1, dim + 2 * kv, generator=g, device="cuda") * 2 - 1
+    ks = [torch.rand(T, kv, generator=g, device="cuda") * 2 - 1 for _ in range(ATTN_LAYERS)]
+    vs = [torch.rand(T, kv, generator=g, device="cuda") * 2 - 1 for _ in range(ATTN_LAYERS)]
+    pos = torch.full((1,), T - 1, dtype=torch.int32, device="cuda")
+    return q, ks, vs, pos
+
+
+def attention_case_bytes(heads, kvh, hs, T):
+    """Algorithmic bytes of one call: the context's keys and values, the query and output rows."""
+    return 2 * T * kvh * hs * 4 + heads * hs * 4 * 2
+
+
 def run_attention(args, world, rank, local):
     """One decode row (position = the last cached one) through each case, per layer cache,
-    one call each, in a CUDA graph: this library's llme_attention (split kernel) and, on the
-    same inputs, the reference's own GPU kernel (src/cuda_attention.cu built for sm_100a into
-    oracle/_ref/libref_attention.so by `make -C oracle refgpu`), outputs cross-checked.
-    Bytes per call: the keys and values of the context + the query row + the output row."""
-    import ctypes
+    one call each, in a CUDA graph through this library's llme_attention (split kernel).
+    `--impl reference --workload attention` times the reference's own GPU kernel on the same
+    inputs. Bytes per call: the keys and values of the context + the query row + the output
+    row."""
     import torch
     import llme_b200 as L
-    refp = os.path.join(REPO, "oracle", "_ref", "libref_attention.so")
-    ref = ctypes.CDLL(refp) if os.path.exists(refp) else None  # the comparison arm only
-    if ref:
-        sz, vp, ci = ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int
-        ref.ref_attention_scratch_floats.argtypes = [ci, ci, ci, ci, sz, sz, sz, sz, ci]
-        ref.ref_attention_scratch_floats.restype = sz
-        ref.ref_attention.argtypes = [ci, ci, ci, ci, sz, sz, sz, sz, vp, vp, vp, vp, vp, vp, ci]
     g = torch.Generator(device="cuda")
     g.manual_seed(5)
     stream = torch.cuda.Stream()
@@ -667,63 +722,30 @@ def run_attention(args, world, rank, local):
     for name, heads, kvh, hs, T in ATTN_CASES:
         kv, dim = kvh * hs, heads * hs
         shape = L.AttentionShape(heads, kvh, hs, T, dim + 2 * kv, kv, dim)
-        q = torch.rand(1, dim + 2 * kv, generator=g, device="cuda") * 2 - 1
-        ks = [torch.rand(T, kv, generator=g, device="cuda") * 2 - 1 for _ in range(ATTN_LAYERS)]
-        vs = [torch.rand(T, kv, generator=g, device="cuda") * 2 - 1 for _ in range(ATTN_LAYERS)]
-        pos = torch.full((1,), T - 1, dtype=torch.int32, device="cuda")
-        nbytes = 2 * T * kv * 4 + dim * 4 * 2
-        res = {"case": name, "heads": heads, "kv_heads": kvh, "head_size": hs, "positions": T}
-        arms = [("ours", None)] + ([("reference_gpu", ref)] if ref else [])
-        outs = {}
-        for arm, lib in arms:
-            out = torch.zeros(ATTN_LAYERS, dim, device="cuda")
-            if lib is None:
-                n = L.attention_scratch_floats(shape, 1, "automatic")
-            else:
-                n = lib.ref_attention_scratch_floats(heads, kvh, hs, T, dim + 2 * kv, kv, dim, 1, 0)
-            scratch = torch.zeros(max(1, n), device="cuda")
+        q, ks, vs, pos = attention_case_inputs(torch, g, heads, kvh, hs, T)
+        nbytes = attention_case_bytes(heads, kvh, hs, T)
+        out = torch.zeros(ATTN_LAYERS, dim, device="cuda")
+        scratch = torch.zeros(max(1, L.attention_scratch_floats(shape, 1, "automatic")),
+                              device="cuda")
 
-            def fn():
-                for l in range(ATTN_LAYERS):
-                    if lib is None:
-                        L.attention(shape, 1, pos.data_ptr(), q.data_ptr(), ks[l].data_ptr(),
-                                    vs[l].data_ptr(), out[l].data_ptr(), scratch.data_ptr(),
-                                    "automatic", h)
-                    else:
-                        # the reference runs on the per-thread default stream
-                        assert lib.ref_attention(heads, kvh, hs, T, dim + 2 * kv, kv, dim, 1,
-                                                 pos.data_ptr(), q.data_ptr(), ks[l].data_ptr(),
-                                                 vs[l].data_ptr(), out[l].data_ptr(),
-                                                 scratch.data_ptr(), 0) == 0
-            if lib is None:
-                graph = capture(fn, stream)
-                secs = max_over_ranks(time_graph(graph, args.steps, args.warmup, stream, world,
-                                                 sampler if name == "7B MHA" else None), world)
-                del graph
-            else:
-                for _ in range(args.warmup):
-                    fn()
-                torch.cuda.synchronize()
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(torch.cuda.default_stream())
-                for _ in range(args.steps):
-                    fn()
-                torch.cuda.synchronize()
-                e1.record(torch.cuda.default_stream())
-                torch.cuda.synchronize()
-                secs = e0.elapsed_time(e1) / 1e3
-            us = secs / (args.steps * ATTN_LAYERS) * 1e6
-            res[arm] = {"us": round(us, 2), "GB_s": round(nbytes / us / 1e3, 1)}
-            outs[arm] = out.cpu()
-            if arm == "ours":
-                tot_bytes += nbytes * args.steps * ATTN_LAYERS
-                tot_s += secs
-        if "reference_gpu" in outs:
-            res["max_abs_diff_vs_reference"] = float((outs["ours"] - outs["reference_gpu"]).abs().max())
-        cases.append(res)
+        def fn():
+            for l in range(ATTN_LAYERS):
+                L.attention(shape, 1, pos.data_ptr(), q.data_ptr(), ks[l].data_ptr(),
+                            vs[l].data_ptr(), out[l].data_ptr(), scratch.data_ptr(),
+                            "automatic", h)
+        graph = capture(fn, stream)
+        secs = max_over_ranks(time_graph(graph, args.steps, args.warmup, stream, world,
+                                         sampler if name == "7B MHA" else None), world)
+        del graph
+        us = secs / (args.steps * ATTN_LAYERS) * 1e6
+        cases.append({"case": name, "heads": heads, "kv_heads": kvh, "head_size": hs,
+                      "positions": T, "ours": {"us": round(us, 2),
+                                               "GB_s": round(nbytes / us / 1e3, 1)}})
+        tot_bytes += nbytes * args.steps * ATTN_LAYERS
+        tot_s += secs
     hbm, hbm_kind = peaks()
     value = tot_bytes / tot_s / 1e9
-    line = {"metric": "decode attention GB/s (KV-cache bytes, 1 row, llme_attention split kernel)",
+    line = {"metric": ATTN_METRIC,
             "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(tot_s / args.steps * 1e3, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
@@ -1210,10 +1232,142 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def ref_gpu_attention(args, path):
+    """The reference's own GPU attention (src/cuda_attention.cu for sm_100a) on the attention
+    workload's cases and inputs, called through its attention_cuda() on its per-thread default
+    stream, not captured, timed with events around synchronised batches of calls."""
+    import ctypes
+    import torch
+    ref = ctypes.CDLL(path)
+    sz, vp, ci = ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int
+    ref.ref_attention_scratch_floats.argtypes = [ci, ci, ci, ci, sz, sz, sz, sz, ci]
+    ref.ref_attention_scratch_floats.restype = sz
+    ref.ref_attention.argtypes = [ci, ci, ci, ci, sz, sz, sz, sz, vp, vp, vp, vp, vp, vp, ci]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)  # the same draws, in the same order, as run_attention
+    cases, tot_bytes, tot_s = [], 0.0, 0.0
+    for name, heads, kvh, hs, T in ATTN_CASES:
+        kv, dim = kvh * hs, heads * hs
+        q, ks, vs, pos = attention_case_inputs(torch, g, heads, kvh, hs, T)
+        nbytes = attention_case_bytes(heads, kvh, hs, T)
+        out = torch.zeros(ATTN_LAYERS, dim, device="cuda")
+        n = ref.ref_attention_scratch_floats(heads, kvh, hs, T, dim + 2 * kv, kv, dim, 1, 0)
+        scratch = torch.zeros(max(1, n), device="cuda")
+
+        def fn():
+            for l in range(ATTN_LAYERS):
+                if ref.ref_attention(heads, kvh, hs, T, dim + 2 * kv, kv, dim, 1, pos.data_ptr(),
+                                     q.data_ptr(), ks[l].data_ptr(), vs[l].data_ptr(),
+                                     out[l].data_ptr(), scratch.data_ptr(), 0):
+                    raise RuntimeError("reference attention failed")
+        torch.cuda.synchronize()
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(torch.cuda.default_stream())  # the legacy stream orders the per-thread one
+        for _ in range(args.steps):
+            fn()
+        torch.cuda.synchronize()
+        e1.record(torch.cuda.default_stream())
+        torch.cuda.synchronize()
+        secs = e0.elapsed_time(e1) / 1e3
+        us = secs / (args.steps * ATTN_LAYERS) * 1e6
+        cases.append({"case": name, "heads": heads, "kv_heads": kvh, "head_size": hs,
+                      "positions": T, "reference_gpu": {"us": round(us, 2),
+                                                        "GB_s": round(nbytes / us / 1e3, 1)}})
+        tot_bytes += nbytes * args.steps * ATTN_LAYERS
+        tot_s += secs
+    value = tot_bytes / tot_s / 1e9
+    return {"metric": ATTN_METRIC, "value": round(value, 1), "unit": "GB/s",
+            "ms_per_step": round(tot_s / args.steps * 1e3, 4),
+            "data": "synthetic U(-1,1) queries and caches, the same bytes as this library's arm",
+            "config": {"workload": "decode attention over KV caches, 8 layer caches per case",
+                       "reference": "src/cuda_attention.cu built for sm_100a, attention_cuda() "
+                                    "uncaptured on its per-thread default stream"},
+            "cases": cases}
+
+
+def ref_gpu_sweep(args):
+    """The reference's own GPU matmul (src/cuda_matmul.cu for sm_100a) on the sweep's cases
+    and inputs, automatic kernel choice, each case's 12 calls captured as one CUDA graph on its
+    per-thread default stream (as its CudaTransformer captures), timed with events there."""
+    import torch
+    ref = ref_matmul_gpu()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1)  # the same draws, in the same order, as run_sweep
+    cases, tot_bytes, tot_s = [], 0, 0.0
+    for q8 in (False, True):
+        Ws = [torch.randn(DIM, DIM, generator=g, device="cuda") * 0.02 for _ in range(SWEEP_COPIES)]
+        if q8:
+            Ws = [quantize_on_device(w) for w in Ws]  # bit-identical to its quantize_q8
+        for m in SWEEP_ROWS:
+            A = torch.rand(m, DIM, generator=g, device="cuda") * 2 - 1
+            C = torch.empty(m, DIM, device="cuda")
+
+            def calls(ok):
+                for i in range(SWEEP_COPIES):
+                    if q8:
+                        q, sc = Ws[i]
+                        ok(ref.ref_gpu_matmul_q8(m, DIM, DIM, A.data_ptr(), q.data_ptr(),
+                                                 sc.data_ptr(), C.data_ptr(), 0, 0, None))
+                    else:
+                        ok(ref.ref_gpu_matmul_f32(m, DIM, DIM, A.data_ptr(), Ws[i].data_ptr(),
+                                                  C.data_ptr(), 0, 0, None))
+            secs = time_ref_matmul_gpu(ref, calls, args.steps, args.warmup)
+            nbytes = (algorithmic_bytes(DIM, DIM, m) if q8 else
+                      4 * DIM * DIM + 4 * m * DIM + 4 * m * DIM)
+            us = secs / (args.steps * SWEEP_COPIES) * 1e6
+            cases.append({"w": "int8" if q8 else "fp32", "m": m, "us": round(us, 2),
+                          "GB_s": round(nbytes / us / 1e3, 1)})
+            tot_bytes += nbytes * args.steps * SWEEP_COPIES
+            tot_s += secs
+    value = tot_bytes / tot_s / 1e9
+    return {"metric": SWEEP_METRIC, "value": round(value, 1), "unit": "GB/s",
+            "ms_per_step": round(tot_s / args.steps * 1e3, 4),
+            "data": "synthetic: N(0,0.02^2) weights (seed 1), U(-1,1) activations, the same "
+                    "bytes as this library's arm",
+            "config": {"workload": "decode-shaped sweep, one call per product, 12 distinct "
+                                   "weights per case in a CUDA graph",
+                       "reference": "src/cuda_matmul.cu built for sm_100a, matmul_cuda() with "
+                                    "GpuKernel::automatic, captured on its per-thread default "
+                                    "stream"},
+            "cases": cases}
+
+
+def run_reference_gpu(args):
+    """`--impl reference` for the attention and sweep workloads: the reference's own GPU code
+    for the path (built from its sources for sm_100a into oracle/_ref by `make -C oracle
+    refgpu` / `make -C oracle refmatmul`), on the same B200 and the same inputs as this
+    library's arm, through its public API."""
+    import torch
+    lib, target = (("libref_attention.so", "refgpu") if args.workload == "attention"
+                   else ("libref_matmul_gpu.so", "refmatmul"))
+    path = os.path.join(REPO, "oracle", "_ref", lib)
+    if not torch.cuda.is_available() or not os.path.exists(path):
+        why = (f"the reference's GPU code for --workload {args.workload} needs a CUDA device"
+               if not torch.cuda.is_available() else
+               f"oracle/_ref/{lib} is not built (make -C oracle {target})")
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+        return
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    with sampler:
+        body = ref_gpu_attention(args, path) if args.workload == "attention" else ref_gpu_sweep(args)
+    line = {"impl": "reference", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            **body,
+            "e2e": {"value": body["value"], "unit": body["unit"], "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "clocks": sampler.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    if args.workload in ("attention", "sweep"):
+        return run_reference_gpu(args)
     if args.workload not in ("chain", "gemv"):
         # The other workloads time the reference's CPU code inside their own line
         # (cpu_baseline) on a bounded sample; tp_decode's reference model would need a 27 GB
