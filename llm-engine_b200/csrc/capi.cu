@@ -438,6 +438,20 @@ int ensure_skinny(int dev, size_t counters, size_t accum_bytes, cudaStream_t str
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 
+// The driver's cuTensorMapEncodeTiled, resolved once through the runtime (no link against
+// libcuda); null where the driver does not offer it.
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                             &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    return g_encode;
+}
+
 struct MapKey {
     uintptr_t ptr;
     int dtype, rank;
@@ -475,15 +489,7 @@ int encode_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t 
 int tensor_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t rows, uint64_t cols,
                uint32_t box_cols, uint32_t box_rows, CUtensorMap* out,
                CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE, uint64_t pitch_bytes = 0) {
-    std::call_once(g_encode_once, [] {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
-                                             &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    });
-    if (!g_encode) return fail(LLME_E_UNSUPPORTED, "cuda: cuTensorMapEncodeTiled is unavailable");
+    if (!encoder()) return fail(LLME_E_UNSUPPORTED, "cuda: cuTensorMapEncodeTiled is unavailable");
     const int rank = rows ? 2 : 1;
     const MapKey key{reinterpret_cast<uintptr_t>(ptr), static_cast<int>(dtype) | (static_cast<int>(swizzle) << 8),
                      rank, cols, rows, box_cols, box_rows, pitch_bytes};
@@ -507,15 +513,7 @@ int tensor_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t 
 int encode_map(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t rows, uint64_t cols,
                uint32_t box_cols, uint32_t box_rows, CUtensorMap* out, CUtensorMapSwizzle swizzle,
                uint64_t pitch_bytes) {
-    std::call_once(g_encode_once, [] {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
-                                             &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    });
-    if (!g_encode) return fail(LLME_E_UNSUPPORTED, "cuda: cuTensorMapEncodeTiled is unavailable");
+    if (!encoder()) return fail(LLME_E_UNSUPPORTED, "cuda: cuTensorMapEncodeTiled is unavailable");
     const int rank = rows ? 2 : 1;
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {pitch_bytes ? pitch_bytes : cols * esz};
