@@ -51,7 +51,9 @@ enum {
     LLME_E_CUDA = 2,        /* CUDA error: std::runtime_error("cuda: <what>: <msg>") */
     LLME_E_TIMEOUT = 3,     /* a bounded device-side wait gave up (see llme_device_status) */
     LLME_E_UNSUPPORTED = 4, /* no usable sm_100 device, or a feature this build lacks */
-    LLME_E_NCCL = 5         /* NCCL error in a sharded call */
+    LLME_E_NCCL = 5,        /* NCCL error in a sharded call */
+    LLME_E_HOST = 6         /* host side: memory exhausted or an internal error; no
+                               exception ever crosses this interface */
 };
 
 /* ---- kernel choice: GpuKernel, cuda_matmul.h:66-72 ---------------------------------- */

@@ -621,8 +621,10 @@ using namespace llme;
 extern "C" {
 
 int llme_attention_check(const llme_attention_shape* s, int kernel) {
-    if (!s) return set_error(LLME_E_INVALID, "attention: null shape");
-    return check(*s, kernel);
+    return llme::guarded([&]() -> int {
+        if (!s) return set_error(LLME_E_INVALID, "attention: null shape");
+        return check(*s, kernel);
+    });
 }
 
 size_t llme_attention_scratch_floats(const llme_attention_shape* s, size_t rows, int kernel) {
@@ -638,87 +640,89 @@ size_t llme_attention_scratch_floats(const llme_attention_shape* s, size_t rows,
 int llme_attention(const llme_attention_shape* s, size_t rows, const int* pos_dev, const float* q,
                    const float* key_cache, const float* value_cache, float* out, float* scratch,
                    int kernel, void* stream_ptr) {
-    if (!s) return set_error(LLME_E_INVALID, "attention: null shape");
-    int st = check(*s, kernel);
-    if (st) return st;
-    if (rows == 0) return LLME_OK;
-    if (!pos_dev || !q || !key_cache || !value_cache || !out)
-        return set_error(LLME_E_INVALID, "attention: null pointer");
-    kernel = resolve(*s, kernel, rows);
-    st = check(*s, kernel);
-    if (st) return st;
-    if (rows > 65535) return set_error(LLME_E_INVALID, "attention: more than 65535 rows");
-    cudaStream_t stream = stream_ptr ? static_cast<cudaStream_t>(stream_ptr) : cudaStreamPerThread;
-    AttnArgs a;
-    a.n_heads = s->n_heads;
-    a.head_size = s->head_size;
-    a.group = s->n_heads / s->n_kv_heads;
-    a.q_stride = s->q_stride;
-    a.kv_stride = s->kv_stride;
-    a.out_stride = s->out_stride;
-    a.pos = pos_dev;
-    a.q = q;
-    a.k = key_cache;
-    a.v = value_cache;
-    a.out = out;
-    cudaError_t e;
-    if (kernel == LLME_ATTN_SINGLE_BLOCK) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(static_cast<unsigned>(s->n_heads), static_cast<unsigned>(rows));
-        cfg.blockDim = dim3(kAttnThreads);
-        cfg.dynamicSmemBytes = single_smem_bytes(*s);
-        cfg.stream = stream;
-        if (cfg.dynamicSmemBytes > 48 * 1024) {
-            e = cudaFuncSetAttribute(attn_single_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kAttnSmemAttr);
-            if (e != cudaSuccess) return set_cuda_error(e, "attention");
+    return llme::guarded([&]() -> int {
+        if (!s) return set_error(LLME_E_INVALID, "attention: null shape");
+        int st = check(*s, kernel);
+        if (st) return st;
+        if (rows == 0) return LLME_OK;
+        if (!pos_dev || !q || !key_cache || !value_cache || !out)
+            return set_error(LLME_E_INVALID, "attention: null pointer");
+        kernel = resolve(*s, kernel, rows);
+        st = check(*s, kernel);
+        if (st) return st;
+        if (rows > 65535) return set_error(LLME_E_INVALID, "attention: more than 65535 rows");
+        cudaStream_t stream = stream_ptr ? static_cast<cudaStream_t>(stream_ptr) : cudaStreamPerThread;
+        AttnArgs a;
+        a.n_heads = s->n_heads;
+        a.head_size = s->head_size;
+        a.group = s->n_heads / s->n_kv_heads;
+        a.q_stride = s->q_stride;
+        a.kv_stride = s->kv_stride;
+        a.out_stride = s->out_stride;
+        a.pos = pos_dev;
+        a.q = q;
+        a.k = key_cache;
+        a.v = value_cache;
+        a.out = out;
+        cudaError_t e;
+        if (kernel == LLME_ATTN_SINGLE_BLOCK) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(static_cast<unsigned>(s->n_heads), static_cast<unsigned>(rows));
+            cfg.blockDim = dim3(kAttnThreads);
+            cfg.dynamicSmemBytes = single_smem_bytes(*s);
+            cfg.stream = stream;
+            if (cfg.dynamicSmemBytes > 48 * 1024) {
+                e = cudaFuncSetAttribute(attn_single_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kAttnSmemAttr);
+                if (e != cudaSuccess) return set_cuda_error(e, "attention");
+            }
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            e = cudaLaunchKernelEx(&cfg, attn_single_kernel, a);
+        } else {
+            // The caches are read by bulk copies: their rows must start on 16-byte boundaries.
+            if ((reinterpret_cast<uintptr_t>(key_cache) | reinterpret_cast<uintptr_t>(value_cache) |
+                 reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) % 16)
+                return set_error(LLME_E_INVALID, "attention: split needs 16-byte aligned q, caches and out");
+            if (!scratch) return set_error(LLME_E_INVALID, "attention: split needs scratch");
+            const SplitGeo g = split_geo(*s);
+            const ScratchLayout l = scratch_layout(*s);
+            a.chunk_cap = g.cap;
+            a.part_o = scratch + l.o;
+            a.part_ml = reinterpret_cast<float2*>(scratch + l.ml);
+            a.part2_o = scratch + l.o2;
+            a.part2_ml = reinterpret_cast<float2*>(scratch + l.ml2);
+            a.counters = reinterpret_cast<unsigned*>(scratch + l.counters);
+            a.scratch_row = l.row;
+            const int G = heads_per_block(*s);
+            const dim3 grid(static_cast<unsigned>(s->n_heads / G), static_cast<unsigned>(rows),
+                            static_cast<unsigned>(g.splits));
+            // Keys and values by TMA boxes over the whole cache (kv_stride floats a row); a head
+            // wider than one box (256 elements) takes the per-position copies.
+            CUtensorMap tmK, tmV;
+            std::memset(&tmK, 0, sizeof(tmK));
+            std::memset(&tmV, 0, sizeof(tmV));
+            a.boxes = s->head_size <= 256;
+            if (a.boxes) {
+                st = tensor_map_2d(key_cache, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, s->seq_len,
+                                   s->kv_stride, s->kv_stride * 4, s->head_size, kBoxRows, &tmK);
+                if (!st)
+                    st = tensor_map_2d(value_cache, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, s->seq_len,
+                                       s->kv_stride, s->kv_stride * 4, s->head_size, kBoxRows, &tmV);
+                if (st) return st;
+            }
+            switch (G) {
+                case 8: e = launch_split_g<8>(tmK, tmV, a, grid, g.smem, stream); break;
+                case 4: e = launch_split_g<4>(tmK, tmV, a, grid, g.smem, stream); break;
+                case 2: e = launch_split_g<2>(tmK, tmV, a, grid, g.smem, stream); break;
+                default: e = launch_split_g<1>(tmK, tmV, a, grid, g.smem, stream); break;
+            }
         }
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, attn_single_kernel, a);
-    } else {
-        // The caches are read by bulk copies: their rows must start on 16-byte boundaries.
-        if ((reinterpret_cast<uintptr_t>(key_cache) | reinterpret_cast<uintptr_t>(value_cache) |
-             reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) % 16)
-            return set_error(LLME_E_INVALID, "attention: split needs 16-byte aligned q, caches and out");
-        if (!scratch) return set_error(LLME_E_INVALID, "attention: split needs scratch");
-        const SplitGeo g = split_geo(*s);
-        const ScratchLayout l = scratch_layout(*s);
-        a.chunk_cap = g.cap;
-        a.part_o = scratch + l.o;
-        a.part_ml = reinterpret_cast<float2*>(scratch + l.ml);
-        a.part2_o = scratch + l.o2;
-        a.part2_ml = reinterpret_cast<float2*>(scratch + l.ml2);
-        a.counters = reinterpret_cast<unsigned*>(scratch + l.counters);
-        a.scratch_row = l.row;
-        const int G = heads_per_block(*s);
-        const dim3 grid(static_cast<unsigned>(s->n_heads / G), static_cast<unsigned>(rows),
-                        static_cast<unsigned>(g.splits));
-        // Keys and values by TMA boxes over the whole cache (kv_stride floats a row); a head
-        // wider than one box (256 elements) takes the per-position copies.
-        CUtensorMap tmK, tmV;
-        std::memset(&tmK, 0, sizeof(tmK));
-        std::memset(&tmV, 0, sizeof(tmV));
-        a.boxes = s->head_size <= 256;
-        if (a.boxes) {
-            st = tensor_map_2d(key_cache, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, s->seq_len,
-                               s->kv_stride, s->kv_stride * 4, s->head_size, kBoxRows, &tmK);
-            if (!st)
-                st = tensor_map_2d(value_cache, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, s->seq_len,
-                                   s->kv_stride, s->kv_stride * 4, s->head_size, kBoxRows, &tmV);
-            if (st) return st;
-        }
-        switch (G) {
-            case 8: e = launch_split_g<8>(tmK, tmV, a, grid, g.smem, stream); break;
-            case 4: e = launch_split_g<4>(tmK, tmV, a, grid, g.smem, stream); break;
-            case 2: e = launch_split_g<2>(tmK, tmV, a, grid, g.smem, stream); break;
-            default: e = launch_split_g<1>(tmK, tmV, a, grid, g.smem, stream); break;
-        }
-    }
-    return e == cudaSuccess ? LLME_OK : set_cuda_error(e, "attention");
+        return e == cudaSuccess ? LLME_OK : set_cuda_error(e, "attention");
+    });
 }
 
 }  // extern "C"

@@ -1164,6 +1164,14 @@ int tensor_map_2d(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64
                       CU_TENSOR_MAP_SWIZZLE_NONE, pitch_bytes);
 }
 int set_error(int code, const std::string& msg) { return fail(code, msg); }
+int host_failure(bool out_of_memory) noexcept {
+    g_error.clear();
+    try {
+        g_error = out_of_memory ? "host: out of memory" : "host: internal error";
+    } catch (...) {
+    }
+    return LLME_E_HOST;
+}
 int set_cuda_error(cudaError_t e, const char* what) { return cuda_fail(e, what); }
 int run_product(size_t m, size_t n, size_t k, const float* A, const void* B, const float* scale,
                 float* C, bool q8, int kernel, bool accumulate, const float* rms, unsigned flags,
@@ -1176,118 +1184,140 @@ extern "C" {
 
 int llme_matmul_q8_noalloc(size_t m, size_t n, size_t k, const float* A, const int8_t* B,
                            const float* scale, float* C, int accumulate, void* stream) {
-    return run_noalloc(m, n, k, A, B, scale, C, accumulate != 0, stream);
+    return llme::guarded([&]() -> int {
+        return run_noalloc(m, n, k, A, B, scale, C, accumulate != 0, stream);
+    });
 }
 
 int llme_quantize_q8(size_t k, size_t n, const float* W, int8_t* q, float* scale, void* stream) {
-    g_error.clear();
-    if (k == 0 || n == 0) return LLME_OK;
-    if (!W || !q || !scale) return fail(LLME_E_INVALID, "llme_quantize_q8: null pointer");
-    if (k * n >= kMaxElems)
-        return fail(LLME_E_INVALID, "llme_quantize_q8: more than 2^31 elements (" +
-                                        std::to_string(k) + "x" + std::to_string(n) + ")");
-    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
-    cudaError_t e = launch_quantize_q8(static_cast<int>(k), static_cast<int>(n), W, q, scale, s);
-    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "quantize");
+    return llme::guarded([&]() -> int {
+        g_error.clear();
+        if (k == 0 || n == 0) return LLME_OK;
+        if (!W || !q || !scale) return fail(LLME_E_INVALID, "llme_quantize_q8: null pointer");
+        if (k * n >= kMaxElems)
+            return fail(LLME_E_INVALID, "llme_quantize_q8: more than 2^31 elements (" +
+                                            std::to_string(k) + "x" + std::to_string(n) + ")");
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
+        cudaError_t e = launch_quantize_q8(static_cast<int>(k), static_cast<int>(n), W, q, scale, s);
+        return e == cudaSuccess ? LLME_OK : cuda_fail(e, "quantize");
+    });
 }
 
 int llme_embed_rows(size_t n, size_t dim, const int* feed, const float* table, float* x,
                     void* stream) {
-    g_error.clear();
-    if (n == 0 || dim == 0) return LLME_OK;
-    if (!feed || !table || !x) return fail(LLME_E_INVALID, "llme_embed_rows: null pointer");
-    if (n >= 65536 || n * dim >= kMaxElems)
-        return fail(LLME_E_INVALID, "llme_embed_rows: too many rows or elements");
-    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
-    cudaError_t e = launch_embed_rows(static_cast<int>(n), static_cast<int>(dim), feed, table, x, s);
-    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "embed");
+    return llme::guarded([&]() -> int {
+        g_error.clear();
+        if (n == 0 || dim == 0) return LLME_OK;
+        if (!feed || !table || !x) return fail(LLME_E_INVALID, "llme_embed_rows: null pointer");
+        if (n >= 65536 || n * dim >= kMaxElems)
+            return fail(LLME_E_INVALID, "llme_embed_rows: too many rows or elements");
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
+        cudaError_t e = launch_embed_rows(static_cast<int>(n), static_cast<int>(dim), feed, table, x, s);
+        return e == cudaSuccess ? LLME_OK : cuda_fail(e, "embed");
+    });
 }
 
 int llme_rope_cache(size_t n, int nq, int nkv, int head_size, const int* feed, const float* cos,
                     const float* sin, float* qkv, float* key_cache, float* value_cache,
                     void* stream) {
-    g_error.clear();
-    if (n == 0) return LLME_OK;
-    if (!feed || !cos || !sin || !qkv || !key_cache || !value_cache)
-        return fail(LLME_E_INVALID, "llme_rope_cache: null pointer");
-    if (nq < 0 || nkv <= 0 || head_size <= 0 || head_size % 2 != 0 || n >= 65536 ||
-        static_cast<size_t>(nq + 2 * nkv) * head_size * n >= kMaxElems)
-        return fail(LLME_E_INVALID, "llme_rope_cache: head_size must be even and positive, nkv "
-                                    "positive, n below 65536");
-    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
-    cudaError_t e = launch_rope_cache(static_cast<int>(n), nq, nkv, head_size, feed, cos, sin, qkv,
-                                      key_cache, value_cache, s);
-    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "rope");
+    return llme::guarded([&]() -> int {
+        g_error.clear();
+        if (n == 0) return LLME_OK;
+        if (!feed || !cos || !sin || !qkv || !key_cache || !value_cache)
+            return fail(LLME_E_INVALID, "llme_rope_cache: null pointer");
+        if (nq < 0 || nkv <= 0 || head_size <= 0 || head_size % 2 != 0 || n >= 65536 ||
+            static_cast<size_t>(nq + 2 * nkv) * head_size * n >= kMaxElems)
+            return fail(LLME_E_INVALID, "llme_rope_cache: head_size must be even and positive, nkv "
+                                        "positive, n below 65536");
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
+        cudaError_t e = launch_rope_cache(static_cast<int>(n), nq, nkv, head_size, feed, cos, sin, qkv,
+                                          key_cache, value_cache, s);
+        return e == cudaSuccess ? LLME_OK : cuda_fail(e, "rope");
+    });
 }
 
 int llme_swiglu(size_t n, size_t hidden, const float* gu, float* hb, void* stream) {
-    g_error.clear();
-    if (n == 0 || hidden == 0) return LLME_OK;
-    if (!gu || !hb) return fail(LLME_E_INVALID, "llme_swiglu: null pointer");
-    if (2 * n * hidden >= kMaxElems) return fail(LLME_E_INVALID, "llme_swiglu: too many elements");
-    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
-    cudaError_t e = launch_swiglu(static_cast<int>(n), static_cast<int>(hidden), gu, hb, s);
-    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "swiglu");
+    return llme::guarded([&]() -> int {
+        g_error.clear();
+        if (n == 0 || hidden == 0) return LLME_OK;
+        if (!gu || !hb) return fail(LLME_E_INVALID, "llme_swiglu: null pointer");
+        if (2 * n * hidden >= kMaxElems) return fail(LLME_E_INVALID, "llme_swiglu: too many elements");
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
+        cudaError_t e = launch_swiglu(static_cast<int>(n), static_cast<int>(hidden), gu, hb, s);
+        return e == cudaSuccess ? LLME_OK : cuda_fail(e, "swiglu");
+    });
 }
 
 int llme_rope_tables(size_t seq_len, size_t head_size, float* cos, float* sin) {
-    g_error.clear();
-    if (seq_len == 0) return LLME_OK;
-    if (!cos || !sin) return fail(LLME_E_INVALID, "llme_rope_tables: null pointer");
-    if (head_size == 0 || head_size % 2 != 0)
-        return fail(LLME_E_INVALID, "llme_rope_tables: head_size must be even and positive");
-    rope_tables(seq_len, head_size, cos, sin);
-    return LLME_OK;
+    return llme::guarded([&]() -> int {
+        g_error.clear();
+        if (seq_len == 0) return LLME_OK;
+        if (!cos || !sin) return fail(LLME_E_INVALID, "llme_rope_tables: null pointer");
+        if (head_size == 0 || head_size % 2 != 0)
+            return fail(LLME_E_INVALID, "llme_rope_tables: head_size must be even and positive");
+        rope_tables(seq_len, head_size, cos, sin);
+        return LLME_OK;
+    });
 }
 
 int llme_batch_q8_create(llme_batch_t** batch, size_t m, size_t count,
                          const llme_q8_product* products) {
-    return batch_create(batch, m, count, products);
+    return llme::guarded([&]() -> int {
+        return batch_create(batch, m, count, products);
+    });
 }
 
 int llme_batch_run(llme_batch_t* b, unsigned flags, void* stream) {
-    g_error.clear();
-    if (!b) return fail(LLME_E_INVALID, "llme_batch_run: null batch");
-    int dev = 0;
-    int st = current_device(&dev);
-    if (st) return st;
-    if (dev != b->dev) return fail(LLME_E_INVALID, "llme_batch_run: batch belongs to another device");
-    if (b->tc) {
-        Q8TcBatchArgs t = b->targs;
-        t.stream = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
-        cudaError_t e = launch_q8tc_batch(t);
+    return llme::guarded([&]() -> int {
+        g_error.clear();
+        if (!b) return fail(LLME_E_INVALID, "llme_batch_run: null batch");
+        int dev = 0;
+        int st = current_device(&dev);
+        if (st) return st;
+        if (dev != b->dev) return fail(LLME_E_INVALID, "llme_batch_run: batch belongs to another device");
+        if (b->tc) {
+            Q8TcBatchArgs t = b->targs;
+            t.stream = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
+            cudaError_t e = launch_q8tc_batch(t);
+            return e == cudaSuccess ? LLME_OK : cuda_fail(e, "launch");
+        }
+        BatchArgs a = b->args;
+        a.stream = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
+        a.pdl = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
+        cudaError_t e = launch_gemv_batch(a);
         return e == cudaSuccess ? LLME_OK : cuda_fail(e, "launch");
-    }
-    BatchArgs a = b->args;
-    a.stream = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
-    a.pdl = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
-    cudaError_t e = launch_gemv_batch(a);
-    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "launch");
+    });
 }
 
 int llme_batch_destroy(llme_batch_t* b) {
-    if (!b) return LLME_OK;
-    cudaError_t e = cudaFree(b->dmem);
-    if (b->scratch) {
-        cudaError_t e2 = cudaFree(b->scratch);
-        if (e == cudaSuccess) e = e2;
-    }
-    delete b;
-    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "free batch");
+    return llme::guarded([&]() -> int {
+        if (!b) return LLME_OK;
+        cudaError_t e = cudaFree(b->dmem);
+        if (b->scratch) {
+            cudaError_t e2 = cudaFree(b->scratch);
+            if (e == cudaSuccess) e = e2;
+        }
+        delete b;
+        return e == cudaSuccess ? LLME_OK : cuda_fail(e, "free batch");
+    });
 }
 
 
 int llme_matmul_f32(size_t m, size_t n, size_t k, const float* A, const float* B, float* C,
                     int kernel, int accumulate, const float* rms_weight, unsigned flags,
                     void* stream) {
-    return run(m, n, k, A, B, nullptr, C, false, kernel, accumulate != 0, rms_weight, flags,
-               stream);
+    return llme::guarded([&]() -> int {
+        return run(m, n, k, A, B, nullptr, C, false, kernel, accumulate != 0, rms_weight, flags,
+                   stream);
+    });
 }
 
 int llme_matmul_q8(size_t m, size_t n, size_t k, const float* A, const int8_t* B,
                    const float* scale, float* C, int kernel, int accumulate,
                    const float* rms_weight, unsigned flags, void* stream) {
-    return run(m, n, k, A, B, scale, C, true, kernel, accumulate != 0, rms_weight, flags, stream);
+    return llme::guarded([&]() -> int {
+        return run(m, n, k, A, B, scale, C, true, kernel, accumulate != 0, rms_weight, flags, stream);
+    });
 }
 
 const char* llme_last_error(void) { return g_error.c_str(); }
@@ -1295,15 +1325,17 @@ const char* llme_last_error(void) { return g_error.c_str(); }
 size_t llme_scratch_generation(void) { return g_generation.load(); }
 
 int llme_synchronize(void) {
-    g_error.clear();
-    cudaError_t e = cudaDeviceSynchronize();
-    if (e != cudaSuccess) return cuda_fail(e, "synchronize");
-    const unsigned dev_err =
-        read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error() |
-        read_and_clear_q8tc_error() | read_and_clear_skinny_error() | read_and_clear_attn_error() |
-        read_and_clear_f32sk_error();
-    if (dev_err) return fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up");
-    return LLME_OK;
+    return llme::guarded([&]() -> int {
+        g_error.clear();
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_fail(e, "synchronize");
+        const unsigned dev_err =
+            read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error() |
+            read_and_clear_q8tc_error() | read_and_clear_skinny_error() | read_and_clear_attn_error() |
+            read_and_clear_f32sk_error();
+        if (dev_err) return fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up");
+        return LLME_OK;
+    });
 }
 
 int llme_device_available(void) {
@@ -1320,20 +1352,23 @@ int llme_device_supported(void) {
 }
 
 int llme_device_status(void) {
-    g_error.clear();
-    cudaError_t e = cudaDeviceSynchronize();
-    if (e != cudaSuccess) return cuda_fail(e, "synchronize");
-    const unsigned dev_err =
-        read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error() |
-        read_and_clear_q8tc_error() | read_and_clear_skinny_error() | read_and_clear_attn_error() |
-        read_and_clear_f32sk_error();
-    return dev_err ? fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up") : LLME_OK;
+    return llme::guarded([&]() -> int {
+        g_error.clear();
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_fail(e, "synchronize");
+        const unsigned dev_err =
+            read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error() |
+            read_and_clear_q8tc_error() | read_and_clear_skinny_error() | read_and_clear_attn_error() |
+            read_and_clear_f32sk_error();
+        return dev_err ? fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up") : LLME_OK;
+    });
 }
 
 int llme_set_math(int math) {
     const int prev = math_mode();
     if (math != LLME_MATH_TENSOR && math != LLME_MATH_FP32) {
-        fail(LLME_E_INVALID, "llme_set_math: unknown mode " + std::to_string(math));
+        llme::guarded([&] { return fail(LLME_E_INVALID, "llme_set_math: unknown mode " +
+                                                           std::to_string(math)); });
         return -1;
     }
     g_math.store(math);
@@ -1343,39 +1378,50 @@ int llme_set_math(int math) {
 int llme_get_math(void) { return math_mode(); }
 
 int llme_alloc(void** ptr, size_t bytes) {
-    *ptr = nullptr;
-    if (bytes == 0) return LLME_OK;
-    cudaError_t e = cudaMalloc(ptr, bytes);
-    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "alloc");
+    return llme::guarded([&]() -> int {
+        if (!ptr) return fail(LLME_E_INVALID, "llme_alloc: null result pointer");
+        *ptr = nullptr;
+        if (bytes == 0) return LLME_OK;
+        cudaError_t e = cudaMalloc(ptr, bytes);
+        return e == cudaSuccess ? LLME_OK : cuda_fail(e, "alloc");
+    });
 }
 
 int llme_free(void* ptr) {
-    if (!ptr) return LLME_OK;
-    cudaError_t e = cudaFree(ptr);
-    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "free");
+    return llme::guarded([&]() -> int {
+        if (!ptr) return LLME_OK;
+        cudaError_t e = cudaFree(ptr);
+        return e == cudaSuccess ? LLME_OK : cuda_fail(e, "free");
+    });
 }
 
 int llme_copy_to_device(void* dst, const void* src, size_t bytes) {
-    if (!bytes) return LLME_OK;
-    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, cudaStreamPerThread);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamPerThread);
-    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "upload");
+    return llme::guarded([&]() -> int {
+        if (!bytes) return LLME_OK;
+        cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, cudaStreamPerThread);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamPerThread);
+        return e == cudaSuccess ? LLME_OK : cuda_fail(e, "upload");
+    });
 }
 
 int llme_copy_to_host(void* dst, const void* src, size_t bytes) {
-    if (!bytes) return LLME_OK;
-    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, cudaStreamPerThread);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamPerThread);
-    return e == cudaSuccess ? LLME_OK : cuda_fail(e, "download");
+    return llme::guarded([&]() -> int {
+        if (!bytes) return LLME_OK;
+        cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, cudaStreamPerThread);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamPerThread);
+        return e == cudaSuccess ? LLME_OK : cuda_fail(e, "download");
+    });
 }
 
 int llme_plan(size_t m, size_t n, size_t k, int is_q8, int kernel, int accumulate,
               uintptr_t a_addr, uintptr_t b_addr, uintptr_t rms_addr, int sm_count, int math,
               llme_plan_t* out) {
-    g_error.clear();
-    if (!out) return fail(LLME_E_INVALID, "llme_plan: null result pointer");
-    PlanIn in{m, n, k, is_q8 != 0, kernel, accumulate != 0, a_addr, b_addr, rms_addr, sm_count, math};
-    return make_plan(in, out);
+    return llme::guarded([&]() -> int {
+        g_error.clear();
+        if (!out) return fail(LLME_E_INVALID, "llme_plan: null result pointer");
+        PlanIn in{m, n, k, is_q8 != 0, kernel, accumulate != 0, a_addr, b_addr, rms_addr, sm_count, math};
+        return make_plan(in, out);
+    });
 }
 
 }  // extern "C"

@@ -244,46 +244,50 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(float* __r
 extern "C" {
 
 int llme_comm_unique_id(void* id) {
-    if (!id) return llme::set_error(LLME_E_INVALID, "llme_comm_unique_id: null id");
-    int st = need_nccl();
-    if (st) return st;
-    static_assert(sizeof(ncclUniqueId) == LLME_COMM_ID_BYTES, "NCCL unique id size");
-    ncclUniqueId u;
-    ncclResult_t r = nccl().getUniqueId(&u);
-    if (r != ncclSuccess) return nccl_fail(r, "get unique id");
-    std::memcpy(id, &u, sizeof(u));
-    return LLME_OK;
+    return llme::guarded([&]() -> int {
+        if (!id) return llme::set_error(LLME_E_INVALID, "llme_comm_unique_id: null id");
+        int st = need_nccl();
+        if (st) return st;
+        static_assert(sizeof(ncclUniqueId) == LLME_COMM_ID_BYTES, "NCCL unique id size");
+        ncclUniqueId u;
+        ncclResult_t r = nccl().getUniqueId(&u);
+        if (r != ncclSuccess) return nccl_fail(r, "get unique id");
+        std::memcpy(id, &u, sizeof(u));
+        return LLME_OK;
+    });
 }
 
 int llme_comm_init(llme_comm_t** out, int nranks, int rank, const void* id, double timeout_s) {
-    if (!out || !id) return llme::set_error(LLME_E_INVALID, "llme_comm_init: null pointer");
-    *out = nullptr;
-    int st = need_nccl();
-    if (st) return st;
-    if (nranks < 1 || rank < 0 || rank >= nranks)
-        return llme::set_error(LLME_E_INVALID, "llme_comm_init: rank " + std::to_string(rank) +
-                                                   " of " + std::to_string(nranks));
-    NcclApi& api = nccl();
-    ncclUniqueId u;
-    std::memcpy(&u, id, sizeof(u));
-    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
-    cfg.blocking = 0;
-    auto* c = new llme_comm;
-    c->nranks = nranks;
-    c->rank = rank;
-    ncclResult_t r = api.initRankConfig(&c->comm, nranks, u, rank, &cfg);
-    if (r != ncclSuccess && r != ncclInProgress) {
-        delete c;
-        return nccl_fail(r, "init");
-    }
-    st = wait_ready(c, timeout_s, "init");
-    if (st) {
-        if (c->comm) api.abort(c->comm);
-        delete c;
-        return st;
-    }
-    *out = c;
-    return LLME_OK;
+    return llme::guarded([&]() -> int {
+        if (!out || !id) return llme::set_error(LLME_E_INVALID, "llme_comm_init: null pointer");
+        *out = nullptr;
+        int st = need_nccl();
+        if (st) return st;
+        if (nranks < 1 || rank < 0 || rank >= nranks)
+            return llme::set_error(LLME_E_INVALID, "llme_comm_init: rank " + std::to_string(rank) +
+                                                       " of " + std::to_string(nranks));
+        NcclApi& api = nccl();
+        ncclUniqueId u;
+        std::memcpy(&u, id, sizeof(u));
+        ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+        cfg.blocking = 0;
+        auto* c = new llme_comm;
+        c->nranks = nranks;
+        c->rank = rank;
+        ncclResult_t r = api.initRankConfig(&c->comm, nranks, u, rank, &cfg);
+        if (r != ncclSuccess && r != ncclInProgress) {
+            delete c;
+            return nccl_fail(r, "init");
+        }
+        st = wait_ready(c, timeout_s, "init");
+        if (st) {
+            if (c->comm) api.abort(c->comm);
+            delete c;
+            return st;
+        }
+        *out = c;
+        return LLME_OK;
+    });
 }
 
 static void peer_release(llme_comm* c) {
@@ -295,129 +299,139 @@ static void peer_release(llme_comm* c) {
 }
 
 int llme_comm_enable_peer(llme_comm_t* c, size_t max_floats) {
-    if (!c) return llme::set_error(LLME_E_INVALID, "llme_comm_enable_peer: no communicator");
-    if (c->peer) return LLME_OK;
-    if (c->nranks > kPeerMaxRanks)
-        return llme::set_error(LLME_E_UNSUPPORTED, "llme_comm_enable_peer: more than 16 ranks");
-    const size_t slot = (max_floats + 63) / 64 * 64;
-    const size_t flags_off = 2 * slot * sizeof(float);
-    const size_t bytes = flags_off + kPeerCtas * kPeerMaxRanks * sizeof(unsigned);
-    cudaError_t e = cudaMalloc(&c->peer_buf, bytes);
-    if (e == cudaSuccess) e = cudaMemset(c->peer_buf, 0, bytes);
-    if (e == cudaSuccess) e = cudaMalloc(&c->peer_epoch, kPeerCtas * sizeof(unsigned));
-    if (e == cudaSuccess) e = cudaMemset(c->peer_epoch, 0, kPeerCtas * sizeof(unsigned));
-    cudaIpcMemHandle_t mine;
-    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mine, c->peer_buf);
-    if (e != cudaSuccess) {
-        peer_release(c);
-        return llme::set_cuda_error(e, "peer buffer");
-    }
-    // Exchange the handles over the communicator itself.
-    void* d_handles = nullptr;
-    e = cudaMalloc(&d_handles, sizeof(cudaIpcMemHandle_t) * (c->nranks + 1));
-    if (e != cudaSuccess) {
-        peer_release(c);
-        return llme::set_cuda_error(e, "peer handles");
-    }
-    char* dh = static_cast<char*>(d_handles);
-    cudaMemcpy(dh + sizeof(cudaIpcMemHandle_t) * c->nranks, &mine, sizeof(mine), cudaMemcpyHostToDevice);
-    cudaStream_t st;
-    cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
-    ncclResult_t r = nccl().allGather(dh + sizeof(cudaIpcMemHandle_t) * c->nranks, dh,
-                                      sizeof(cudaIpcMemHandle_t), ncclUint8, c->comm, st);
-    int status = LLME_OK;
-    if (r == ncclInProgress) status = wait_ready(c, kEnqueueTimeoutS, "exchange peer handles");
-    else if (r != ncclSuccess) status = nccl_fail(r, "exchange peer handles");
-    std::vector<cudaIpcMemHandle_t> all(c->nranks);
-    if (!status) {
-        cudaStreamSynchronize(st);
-        e = cudaMemcpy(all.data(), dh, sizeof(cudaIpcMemHandle_t) * c->nranks, cudaMemcpyDeviceToHost);
-        if (e != cudaSuccess) status = llme::set_cuda_error(e, "peer handles");
-    }
-    cudaStreamDestroy(st);
-    cudaFree(d_handles);
-    if (status) {
-        peer_release(c);
-        return status;
-    }
-    PeerArgs& pa = c->pargs;
-    for (int q = 0; q < c->nranks; ++q) {
-        if (q == c->rank) {
-            pa.base[q] = static_cast<float*>(c->peer_buf);
-            continue;
-        }
-        void* ptr = nullptr;
-        e = cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess);
+    return llme::guarded([&]() -> int {
+        if (!c) return llme::set_error(LLME_E_INVALID, "llme_comm_enable_peer: no communicator");
+        if (c->peer) return LLME_OK;
+        if (c->nranks > kPeerMaxRanks)
+            return llme::set_error(LLME_E_UNSUPPORTED, "llme_comm_enable_peer: more than 16 ranks");
+        const size_t slot = (max_floats + 63) / 64 * 64;
+        const size_t flags_off = 2 * slot * sizeof(float);
+        const size_t bytes = flags_off + kPeerCtas * kPeerMaxRanks * sizeof(unsigned);
+        cudaError_t e = cudaMalloc(&c->peer_buf, bytes);
+        if (e == cudaSuccess) e = cudaMemset(c->peer_buf, 0, bytes);
+        if (e == cudaSuccess) e = cudaMalloc(&c->peer_epoch, kPeerCtas * sizeof(unsigned));
+        if (e == cudaSuccess) e = cudaMemset(c->peer_epoch, 0, kPeerCtas * sizeof(unsigned));
+        cudaIpcMemHandle_t mine;
+        if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mine, c->peer_buf);
         if (e != cudaSuccess) {
             peer_release(c);
-            return llme::set_cuda_error(e, "open peer buffer");
+            return llme::set_cuda_error(e, "peer buffer");
         }
-        c->peer_opened[q] = ptr;
-        pa.base[q] = static_cast<float*>(ptr);
-    }
-    void* err = nullptr;
-    cudaGetSymbolAddress(&err, g_comm_error);
-    pa.slot_floats = slot;
-    pa.flags_off = flags_off;
-    pa.epoch = static_cast<unsigned*>(c->peer_epoch);
-    pa.err = static_cast<unsigned*>(err);
-    pa.nranks = c->nranks;
-    pa.rank = c->rank;
-    c->peer_max_floats = max_floats;
-    c->peer = true;
-    return LLME_OK;
+        // Exchange the handles over the communicator itself.
+        void* d_handles = nullptr;
+        e = cudaMalloc(&d_handles, sizeof(cudaIpcMemHandle_t) * (c->nranks + 1));
+        if (e != cudaSuccess) {
+            peer_release(c);
+            return llme::set_cuda_error(e, "peer handles");
+        }
+        char* dh = static_cast<char*>(d_handles);
+        cudaMemcpy(dh + sizeof(cudaIpcMemHandle_t) * c->nranks, &mine, sizeof(mine), cudaMemcpyHostToDevice);
+        cudaStream_t st;
+        cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+        ncclResult_t r = nccl().allGather(dh + sizeof(cudaIpcMemHandle_t) * c->nranks, dh,
+                                          sizeof(cudaIpcMemHandle_t), ncclUint8, c->comm, st);
+        int status = LLME_OK;
+        if (r == ncclInProgress) status = wait_ready(c, kEnqueueTimeoutS, "exchange peer handles");
+        else if (r != ncclSuccess) status = nccl_fail(r, "exchange peer handles");
+        std::vector<cudaIpcMemHandle_t> all(c->nranks);
+        if (!status) {
+            cudaStreamSynchronize(st);
+            e = cudaMemcpy(all.data(), dh, sizeof(cudaIpcMemHandle_t) * c->nranks, cudaMemcpyDeviceToHost);
+            if (e != cudaSuccess) status = llme::set_cuda_error(e, "peer handles");
+        }
+        cudaStreamDestroy(st);
+        cudaFree(d_handles);
+        if (status) {
+            peer_release(c);
+            return status;
+        }
+        PeerArgs& pa = c->pargs;
+        for (int q = 0; q < c->nranks; ++q) {
+            if (q == c->rank) {
+                pa.base[q] = static_cast<float*>(c->peer_buf);
+                continue;
+            }
+            void* ptr = nullptr;
+            e = cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) {
+                peer_release(c);
+                return llme::set_cuda_error(e, "open peer buffer");
+            }
+            c->peer_opened[q] = ptr;
+            pa.base[q] = static_cast<float*>(ptr);
+        }
+        void* err = nullptr;
+        cudaGetSymbolAddress(&err, g_comm_error);
+        pa.slot_floats = slot;
+        pa.flags_off = flags_off;
+        pa.epoch = static_cast<unsigned*>(c->peer_epoch);
+        pa.err = static_cast<unsigned*>(err);
+        pa.nranks = c->nranks;
+        pa.rank = c->rank;
+        c->peer_max_floats = max_floats;
+        c->peer = true;
+        return LLME_OK;
+    });
 }
 
 int llme_comm_status(void) {
-    unsigned v = 0, zero = 0;
-    cudaError_t e = cudaMemcpyFromSymbol(&v, g_comm_error, sizeof(v));
-    if (e != cudaSuccess) return llme::set_cuda_error(e, "read comm status");
-    if (v) {
-        cudaMemcpyToSymbol(g_comm_error, &zero, sizeof(zero));
-        return llme::set_error(LLME_E_TIMEOUT, "peer all-reduce: a peer did not arrive in time");
-    }
-    return LLME_OK;
+    return llme::guarded([&]() -> int {
+        unsigned v = 0, zero = 0;
+        cudaError_t e = cudaMemcpyFromSymbol(&v, g_comm_error, sizeof(v));
+        if (e != cudaSuccess) return llme::set_cuda_error(e, "read comm status");
+        if (v) {
+            cudaMemcpyToSymbol(g_comm_error, &zero, sizeof(zero));
+            return llme::set_error(LLME_E_TIMEOUT, "peer all-reduce: a peer did not arrive in time");
+        }
+        return LLME_OK;
+    });
 }
 
 int llme_comm_destroy(llme_comm_t* c) {
-    if (!c) return LLME_OK;
-    peer_release(c);
-    NcclApi& api = nccl();
-    ncclResult_t r = api.destroy(c->comm);
-    int st = LLME_OK;
-    if (r == ncclInProgress) {
-        st = wait_ready(c, kEnqueueTimeoutS, "destroy");
-    } else if (r != ncclSuccess) {
-        st = nccl_fail(r, "destroy");
-    }
-    delete c;
-    return st;
+    return llme::guarded([&]() -> int {
+        if (!c) return LLME_OK;
+        peer_release(c);
+        NcclApi& api = nccl();
+        ncclResult_t r = api.destroy(c->comm);
+        int st = LLME_OK;
+        if (r == ncclInProgress) {
+            st = wait_ready(c, kEnqueueTimeoutS, "destroy");
+        } else if (r != ncclSuccess) {
+            st = nccl_fail(r, "destroy");
+        }
+        delete c;
+        return st;
+    });
 }
 
 int llme_comm_abort(llme_comm_t* c) {
-    if (!c) return LLME_OK;
-    peer_release(c);
-    ncclResult_t r = nccl().abort(c->comm);
-    delete c;
-    return r == ncclSuccess ? LLME_OK : nccl_fail(r, "abort");
+    return llme::guarded([&]() -> int {
+        if (!c) return LLME_OK;
+        peer_release(c);
+        ncclResult_t r = nccl().abort(c->comm);
+        delete c;
+        return r == ncclSuccess ? LLME_OK : nccl_fail(r, "abort");
+    });
 }
 
 int llme_comm_size(const llme_comm_t* c) { return c ? c->nranks : 0; }
 int llme_comm_rank(const llme_comm_t* c) { return c ? c->rank : -1; }
 
 int llme_allreduce_sum_f32(float* buf, size_t count, llme_comm_t* c, void* stream_ptr) {
-    if (!c) return llme::set_error(LLME_E_INVALID, "llme_allreduce_sum_f32: no communicator");
-    if (c->nranks == 1 || count == 0) return LLME_OK;
-    if (!buf) return llme::set_error(LLME_E_INVALID, "llme_allreduce_sum_f32: null buffer");
-    cudaStream_t stream = stream_ptr ? static_cast<cudaStream_t>(stream_ptr) : cudaStreamPerThread;
-    if (c->peer && count <= c->peer_max_floats) {
-        peer_allreduce_kernel<<<kPeerCtas, kPeerThreads, 0, stream>>>(buf, count, c->pargs);
-        cudaError_t e = cudaGetLastError();
-        return e == cudaSuccess ? LLME_OK : llme::set_cuda_error(e, "launch");
-    }
-    ncclResult_t r = nccl().allReduce(buf, buf, count, ncclFloat32, ncclSum, c->comm, stream);
-    if (r == ncclInProgress) return wait_ready(c, kEnqueueTimeoutS, "all-reduce");
-    return r == ncclSuccess ? LLME_OK : nccl_fail(r, "all-reduce");
+    return llme::guarded([&]() -> int {
+        if (!c) return llme::set_error(LLME_E_INVALID, "llme_allreduce_sum_f32: no communicator");
+        if (c->nranks == 1 || count == 0) return LLME_OK;
+        if (!buf) return llme::set_error(LLME_E_INVALID, "llme_allreduce_sum_f32: null buffer");
+        cudaStream_t stream = stream_ptr ? static_cast<cudaStream_t>(stream_ptr) : cudaStreamPerThread;
+        if (c->peer && count <= c->peer_max_floats) {
+            peer_allreduce_kernel<<<kPeerCtas, kPeerThreads, 0, stream>>>(buf, count, c->pargs);
+            cudaError_t e = cudaGetLastError();
+            return e == cudaSuccess ? LLME_OK : llme::set_cuda_error(e, "launch");
+        }
+        ncclResult_t r = nccl().allReduce(buf, buf, count, ncclFloat32, ncclSum, c->comm, stream);
+        if (r == ncclInProgress) return wait_ready(c, kEnqueueTimeoutS, "all-reduce");
+        return r == ncclSuccess ? LLME_OK : nccl_fail(r, "all-reduce");
+    });
 }
 
 static int rowpar(size_t m, size_t n, size_t k_local, const float* A, const void* B,
@@ -435,15 +449,19 @@ static int rowpar(size_t m, size_t n, size_t k_local, const float* A, const void
 int llme_matmul_q8_rowpar(size_t m, size_t n, size_t k_local, const float* A_local,
                           const int8_t* B_local, const float* scale, float* C, int kernel,
                           int accumulate, unsigned flags, llme_comm_t* comm, void* stream) {
-    return rowpar(m, n, k_local, A_local, B_local, scale, C, true, kernel, accumulate, flags, comm,
-                  stream);
+    return llme::guarded([&]() -> int {
+        return rowpar(m, n, k_local, A_local, B_local, scale, C, true, kernel, accumulate, flags, comm,
+                      stream);
+    });
 }
 
 int llme_matmul_f32_rowpar(size_t m, size_t n, size_t k_local, const float* A_local,
                            const float* B_local, float* C, int kernel, int accumulate,
                            unsigned flags, llme_comm_t* comm, void* stream) {
-    return rowpar(m, n, k_local, A_local, B_local, nullptr, C, false, kernel, accumulate, flags,
-                  comm, stream);
+    return llme::guarded([&]() -> int {
+        return rowpar(m, n, k_local, A_local, B_local, nullptr, C, false, kernel, accumulate, flags,
+                      comm, stream);
+    });
 }
 
 }  // extern "C"

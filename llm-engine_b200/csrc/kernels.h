@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
+#include <exception>
+#include <new>
 #include <string>
 
 namespace llme {
@@ -13,6 +15,22 @@ namespace llme {
 // The calling thread's llme_last_error message (defined in capi.cu); return `code`.
 int set_error(int code, const std::string& msg);
 int set_cuda_error(cudaError_t e, const char* what);
+// LLME_E_HOST with a fixed message, allocating nothing (capi.cu).
+int host_failure(bool out_of_memory) noexcept;
+
+// The body of a C entry point: an exception thrown on the host (std::bad_alloc from a
+// message or a table, or anything else) becomes LLME_E_HOST instead of crossing the C
+// boundary, where it would end the calling process.
+template <typename F>
+int guarded(F&& body) noexcept {
+    try {
+        return body();
+    } catch (const std::bad_alloc&) {
+        return host_failure(true);
+    } catch (...) {
+        return host_failure(false);
+    }
+}
 // A cached 2D tensor map (no swizzle) over `rows` x `cols` elements of esz bytes, rows
 // pitch_bytes apart (capi.cu).
 int tensor_map_2d(const void* ptr, CUtensorMapDataType dtype, size_t esz, uint64_t rows,

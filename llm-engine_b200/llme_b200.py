@@ -27,7 +27,7 @@ PATHS = {0: "none", 1: "zero", 2: "naive", 3: "gemv_tma", 4: "gemv_ldg", 5: "til
 MATH_TENSOR, MATH_FP32 = 0, 1
 FLAG_WEIGHTS_STATIC = 1
 
-OK, E_INVALID, E_CUDA, E_TIMEOUT, E_UNSUPPORTED, E_NCCL = range(6)
+OK, E_INVALID, E_CUDA, E_TIMEOUT, E_UNSUPPORTED, E_NCCL, E_HOST = range(7)
 
 # cudaStreamLegacy: torch's default stream has handle 0, which the C ABI would read as
 # "per-thread default stream"; pass the legacy handle instead so both sides agree.
@@ -156,6 +156,8 @@ def _check(status: int) -> None:
         raise InvalidArgument(msg)
     if status == E_TIMEOUT:
         raise DeviceTimeout(msg)
+    if status == E_HOST:
+        raise MemoryError(msg) if "out of memory" in msg else RuntimeError(msg)
     raise CudaError(msg or f"cuda: error {status}")
 
 

@@ -393,3 +393,27 @@ def test_null_pointers_are_refused_before_any_device_work():
     assert refused(lib.llme_attention(ctypes.byref(shape), 1, None, P, P, P, P, P, 0, None))
     assert refused(lib.llme_attention(ctypes.byref(shape), 1, P, P, P, P, None, P, 0, None))
     assert lib.llme_attention(ctypes.byref(shape), 0, None, None, None, None, None, None, 0, None) == 0
+
+
+def test_status_codes_match_the_header():
+    text = open(HEADER).read()
+    codes = dict((name, int(v)) for name, v in re.findall(r"\b(LLME_(?:OK|E_\w+))\s*=\s*(\d+)", text))
+    assert codes == {"LLME_OK": L.OK, "LLME_E_INVALID": L.E_INVALID, "LLME_E_CUDA": L.E_CUDA,
+                     "LLME_E_TIMEOUT": L.E_TIMEOUT, "LLME_E_UNSUPPORTED": L.E_UNSUPPORTED,
+                     "LLME_E_NCCL": L.E_NCCL, "LLME_E_HOST": L.E_HOST}
+
+
+def test_no_exception_crosses_the_c_boundary():
+    # Every status-returning entry point runs its body under a guard that turns a host-side
+    # exception into LLME_E_HOST; the source holds one guard per such function.
+    csrc = os.path.join(REPO, "llm-engine_b200", "csrc")
+    unguarded = []
+    for name in ("capi.cu", "comm.cu", "attention.cu"):
+        src = open(os.path.join(csrc, name)).read()
+        body = src[src.index('extern "C" {'):]
+        for m in re.finditer(r"^int (llme_\w+)\([^{]*\) \{\n(.*?)^\}", body, re.S | re.M):
+            fn, text = m.group(1), m.group(2)
+            if "llme::guarded(" not in text and fn not in (
+                    "llme_set_math", "llme_device_available", "llme_device_supported"):
+                unguarded.append(fn)
+    assert unguarded == []
