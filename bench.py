@@ -15,7 +15,10 @@ replays, max over ranks. `e2e` is the same metric through the C ABI with the act
 copied in from pinned host memory and every output copied back inside the timed region.
 The weights (6.6 GB / N per GPU) are far larger than L2, so no L2 flush is needed.
 `--impl reference` times the reference's own CPU matmul_parallel (compiled from its sources
-into oracle/_ref) on a bounded sample of the chain, on the host cores.
+into oracle/_ref) on a bounded sample of the chain, on the host cores; with
+`--workload attention` or `--workload sweep` it times the reference's own GPU code for that
+path (src/cuda_attention.cu, src/cuda_matmul.cu built for sm_100a) on the same B200 and
+inputs as this library's arm.
 """
 from __future__ import annotations
 
