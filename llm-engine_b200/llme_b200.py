@@ -249,6 +249,8 @@ def quantize_q8(W):
     import torch
     if W.dtype != torch.float32 or W.dim() != 2 or not W.is_contiguous():
         raise InvalidArgument("quantize_q8: W must be a contiguous 2-D float32 tensor")
+    if W.device.type != "cuda":
+        raise InvalidArgument(f"quantize_q8: W is on {W.device}; it must be in CUDA device memory")
     k, n = W.shape
     q = torch.empty((k, n), dtype=torch.int8, device=W.device)
     scale = torch.empty(n, dtype=torch.float32, device=W.device)
@@ -393,13 +395,32 @@ def matmul(A, B, scale=None, C=None, kernel="automatic", accumulate: bool = Fals
     (n fp32, int8 only), C (m x n fp32, allocated if None). Returns C. Runs on the current
     torch stream unless `stream` is given."""
     import torch
+    if A.dim() != 2 or B.dim() != 2:
+        raise InvalidArgument("matmul: A and B must be matrices")
     m, k = A.shape
     kb, n = B.shape
     if kb != k:
         raise InvalidArgument(f"matmul_cuda: inner dimensions differ (A is {m}x{k}, B is {kb}x{n})")
-    for t in (A, B, C, scale, rms_weight):
-        if t is not None and not t.is_contiguous():
+    # Everything the kernels will read or write, checked before any pointer leaves Python: a
+    # host tensor's address or a short C would otherwise reach the GPU as a bad address.
+    f32 = (torch.float32,)
+    expect = [("A", A, f32, (m, k)), ("B", B, (torch.float32, torch.int8), (k, n)),
+              ("C", C, f32, (m, n)), ("scale", scale, f32, (n,)),
+              ("rms_weight", rms_weight, f32, (k,))]
+    for name, t, dtypes, shape in expect:
+        if t is None:
+            continue
+        if t.dtype not in dtypes:
+            raise InvalidArgument(f"matmul: {name} is {t.dtype}, expected "
+                                  + " or ".join(str(d) for d in dtypes))
+        if tuple(t.shape) != shape:
+            raise InvalidArgument(f"matmul: {name} has shape {tuple(t.shape)}, expected {shape}")
+        if not t.is_contiguous():
             raise InvalidArgument("matmul: tensors must be contiguous row-major")
+    for name, t, _, _ in expect:
+        if t is not None and (t.device.type != "cuda" or t.device != A.device):
+            raise InvalidArgument(f"matmul: {name} is on {t.device}; every tensor must be in the "
+                                  "memory of one CUDA device")
     if C is None:
         C = torch.empty((m, n), dtype=torch.float32, device=A.device)
     flags = FLAG_WEIGHTS_STATIC if weights_static else 0

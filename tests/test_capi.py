@@ -417,3 +417,31 @@ def test_no_exception_crosses_the_c_boundary():
                     "llme_set_math", "llme_device_available", "llme_device_supported"):
                 unguarded.append(fn)
     assert unguarded == []
+
+
+def test_torch_wrapper_refuses_what_the_kernels_cannot_take():
+    # Checked in Python before any pointer reaches the library: dtypes, shapes, contiguity,
+    # and residency in one CUDA device's memory (a host tensor's address on the GPU faults).
+    torch = pytest.importorskip("torch")
+    A, B = torch.zeros(3, 5), torch.zeros(5, 7)
+    q, s = torch.zeros(5, 7, dtype=torch.int8), torch.zeros(7)
+    cases = [
+        ((torch.zeros(3, 5, 2), B), {}, "matrices"),
+        ((torch.zeros(2, 3), torch.zeros(4, 2)), {}, "2x3"),
+        ((A.half(), B), {}, "A is torch.float16"),
+        ((A, B.double()), {}, "B is torch.float64"),
+        ((A, B), {"C": torch.zeros(3, 6)}, "C has shape (3, 6)"),
+        ((A, q), {"scale": torch.zeros(6)}, "scale has shape (6,)"),
+        ((A, B), {"rms_weight": torch.zeros(4)}, "rms_weight has shape (4,)"),
+        ((A, B.t().contiguous().t()), {}, "contiguous"),
+        ((A, B), {}, "CUDA device"),
+        ((A, q), {"scale": s}, "CUDA device"),
+    ]
+    for args, kw, text in cases:
+        with pytest.raises(L.InvalidArgument) as e:
+            L.matmul(*args, **kw)
+        assert text in str(e.value), (text, str(e.value))
+    with pytest.raises(L.InvalidArgument, match="CUDA device memory"):
+        L.quantize_q8(torch.zeros(4, 8))
+    with pytest.raises(L.InvalidArgument, match="2-D float32"):
+        L.quantize_q8(torch.zeros(4, 8, dtype=torch.float64))
