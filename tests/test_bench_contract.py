@@ -65,3 +65,17 @@ def test_b200_arm_refuses_without_a_b200():
     r = run("--steps", "2", "--warmup", "3")
     assert r.returncode != 0
     assert "needs an sm_100 (B200) GPU" in r.stderr
+
+
+def test_algorithmic_bytes_match_the_workload_definitions():
+    # The roofline numerators: one 4096 x 4096 int8 GEMV at m = 1 (weights + scales + A + C)
+    # and the 7B chain's 225 products (32 layers of wq, wk, wv, wo, w1, w3, w2 and the
+    # classifier), whose int8 weights alone are 6,607,077,376 bytes.
+    sys.path.insert(0, REPO)
+    import bench
+    assert bench.algorithmic_bytes(4096, 4096) == 16_826_368
+    shapes = bench.chain_shapes()
+    assert len(shapes) == 225
+    assert sum(k * n for _, k, n, _ in shapes) == 6_607_077_376
+    assert [name for name, _, _, row in shapes if row][:2] == ["wo0", "w20"]
+    assert sum(1 for *_, row in shapes if row) == 64
