@@ -97,6 +97,22 @@ def test_skinny_matches_oracle_and_emulation(m, k, n):
     np.testing.assert_array_equal(got, emulate(A, q, s))
 
 
+@pytest.mark.parametrize("outlier", [100.0, 1000.0])
+def test_skinny_outlier_activations(outlier):
+    # A few activation channels far above the rest, as in real models. The split scales each
+    # row by its maximum, so the ordinary values keep fewer of their bits; three terms still
+    # hold the decode bound (a float64 emulation of the split gives about 1e-7 here, where two
+    # terms give 2.5e-5), and the result is the kernel's arithmetic bit for bit.
+    rng = np.random.default_rng(int(outlier))
+    m, k, n = 16, 4096, 4096
+    A = uni(rng, m, k)
+    A[:, rng.integers(0, k, 8)] *= np.float32(outlier)
+    q, s = weights(rng, k, n)
+    got = run(A, q, s)
+    assert row_rel_err(got, oracle.matmul_naive_q8(A, q, s)) <= 1e-5
+    np.testing.assert_array_equal(got, emulate(A, q, s))
+
+
 @pytest.mark.parametrize("m", [2, 4, 8])
 def test_skinny_small_m_through_tiled_split(m):
     rng = np.random.default_rng(40 + m)
