@@ -67,6 +67,22 @@ def algorithmic_bytes(k, n, m=1):
     return k * n + 4 * n + 4 * m * k + 4 * m * n
 
 
+def _oracle():
+    """The checker (oracle/): used after the timed regions to compare sampled outputs with the
+    reference's arithmetic, and by the CPU-baseline legs; never inside a timed region."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle
+    return oracle
+
+
+def _row_rel_err(got, want):
+    """max over rows of ||C - C_ref||_inf / ||C_ref row||_2 (the path's error metric)."""
+    g, w = np.atleast_2d(got).astype(np.float64), np.atleast_2d(want).astype(np.float64)
+    den = np.linalg.norm(w, axis=1)
+    den = np.where(den == 0, 1.0, den)
+    return float((np.abs(g - w).max(axis=1) / den).max()) if g.size else 0.0
+
+
 # ---- clocks during the timed region (NVML, read-only) -------------------------------------
 
 class ClockSampler:
@@ -348,7 +364,8 @@ class _Null:
 
 def gemv_4096_probe(steps=200):
     """Config 0 in isolation: m = 1, 4096 x 4096 int8, back to back over 16 weight copies
-    (268 MB > 2 x L2), with and without programmatic dependent launch."""
+    (268 MB > 2 x L2), with and without programmatic dependent launch; and, where it is built,
+    the reference's own GPU matmul on the same weights and activation (reference_gpu)."""
     import torch
     import llme_b200 as L
     g = torch.Generator(device="cuda")
@@ -364,6 +381,7 @@ def gemv_4096_probe(steps=200):
     C = torch.empty(copies, DIM, device="cuda")
     stream = torch.cuda.Stream()
     h = stream.cuda_stream
+    nbytes = algorithmic_bytes(DIM, DIM)
     res = {}
     for label, flags in (("pdl", L.FLAG_WEIGHTS_STATIC), ("serial", 0)):
         def fn():
@@ -373,18 +391,112 @@ def gemv_4096_probe(steps=200):
         graph = capture(fn, stream)
         secs = time_graph(graph, steps, 5, stream, 1)
         us = secs / (steps * copies) * 1e6
-        res[label] = {"us_per_gemv": round(us, 3),
-                      "GB_s": round(algorithmic_bytes(DIM, DIM) / (us * 1e-6) / 1e9, 1)}
+        res[label] = {"us_per_gemv": round(us, 3), "GB_s": round(nbytes / (us * 1e-6) / 1e9, 1)}
         del graph
+    ref = ref_matmul_gpu()
+    if ref is not None:
+        C_ref = torch.empty(copies, DIM, device="cuda")
+
+        def calls(ok):
+            for i in range(copies):
+                ok(ref.ref_gpu_matmul_q8(1, DIM, DIM, A.data_ptr(), qs[i].data_ptr(),
+                                         ss[i].data_ptr(), C_ref[i].data_ptr(), 0, 0, None))
+        secs = time_ref_matmul_gpu(ref, calls, steps, 5)
+        us = secs / (steps * copies) * 1e6
+        torch.cuda.synchronize()
+        diff = float((C - C_ref).abs().max())
+        res["reference_gpu"] = {
+            "us_per_gemv": round(us, 3), "GB_s": round(nbytes / (us * 1e-6) / 1e9, 1),
+            "impl": "the reference's matmul_cuda (src/cuda_matmul.cu built for sm_100a), "
+                    "GpuKernel::automatic, 16 calls captured on its per-thread stream",
+            "max_abs_diff_vs_ours": float(f"{diff:.3e}"), "tolerance": 2e-5 * DIM}
     return res
 
 
-def run_sgemm(args, world, rank, local):
-    """The square SGEMM: C = A x B, fp32 N x N, A and B ~ U(-1, 1) (seed 2), through the
-    C ABI on the tcgen05 TF32 path (B read as stored, MN-major). Inputs 768 MB > L2."""
+def chain_per_call_beside_reference(chain, steps=50, warmup=5):
+    """Layer 0's seven products and the classifier, one call each (the reference's
+    CudaTransformer call pattern), on the chain's own weights and activations: this library's
+    llme_matmul_q8 against the reference's own matmul_cuda built for sm_100a, each captured
+    as one CUDA graph. None where the reference's GPU library is not built."""
     import torch
     import llme_b200 as L
-    n = args.size
+    ref = ref_matmul_gpu()
+    if ref is None:
+        return None
+    idx = list(range(7)) + [len(chain.mats) - 1]
+    outs = {"ours": torch.empty_like(chain.c_dev), "reference": torch.empty_like(chain.c_dev)}
+    nbytes = sum(algorithmic_bytes(chain.mats[i][2], chain.mats[i][3]) for i in idx)
+    stream = torch.cuda.Stream()
+    h = stream.cuda_stream
+
+    def ours():
+        for i in idx:
+            q, s, kl, nl, _ = chain.mats[i]
+            L.matmul_cuda_q8(1, nl, kl, chain.a_dev.data_ptr() + 4 * chain.a_off[i], q.data_ptr(),
+                             s.data_ptr(), outs["ours"].data_ptr() + 4 * chain.c_off[i],
+                             "automatic", False, 0, L.FLAG_WEIGHTS_STATIC, h)
+
+    def theirs(ok):
+        for i in idx:
+            q, s, kl, nl, _ = chain.mats[i]
+            ok(ref.ref_gpu_matmul_q8(1, nl, kl, chain.a_dev.data_ptr() + 4 * chain.a_off[i],
+                                     q.data_ptr(), s.data_ptr(),
+                                     outs["reference"].data_ptr() + 4 * chain.c_off[i], 0, 0,
+                                     None))
+    graph = capture(ours, stream)
+    secs_ours = time_graph(graph, steps, warmup, stream, 1)
+    del graph
+    secs_ref = time_ref_matmul_gpu(ref, theirs, steps, warmup)
+    torch.cuda.synchronize()
+    diff = max(float((outs["ours"][chain.c_off[i]:chain.c_off[i] + chain.mats[i][3]] -
+                      outs["reference"][chain.c_off[i]:chain.c_off[i] + chain.mats[i][3]])
+                     .abs().max()) for i in idx)
+    us_o, us_r = secs_ours / steps * 1e6, secs_ref / steps * 1e6
+    return {"products": "layer 0 (wq, wk, wv, wo, w1, w3, w2) + classifier, m=1, one call each",
+            "ours": {"us_per_step": round(us_o, 2), "GB_s": round(nbytes / us_o / 1e3, 1)},
+            "reference_gpu": {"us_per_step": round(us_r, 2), "GB_s": round(nbytes / us_r / 1e3, 1)},
+            "speedup": round(us_r / us_o, 2),
+            "max_abs_diff": float(f"{diff:.3e}"),
+            "impl": "the reference's matmul_cuda (src/cuda_matmul.cu built for sm_100a), "
+                    "GpuKernel::automatic, captured on its per-thread stream"}
+
+
+def chain_parity(chain, world):
+    """After the timed regions: the outputs of one grouped step (run again on the first buffer
+    set) for layer 0's seven products, the last layer's w2 and the classifier, against the
+    oracle's matmul_naive_q8 on the same int8 weights and activations, within the reference's
+    own test bound of 1e-5 * k. On several GPUs only the column-parallel products (complete
+    local slices) are compared."""
+    oracle = _oracle()
+    n = len(chain.mats)
+    pick = sorted(set([i for i in range(min(7, n))] + [max(0, n - 2), n - 1]))
+    a = chain.a_dev.cpu().numpy()
+    c = chain.c_dev.cpu().numpy()
+    worst_ratio, worst_rel, checked = 0.0, 0.0, []
+    for i in pick:
+        q, s, kl, nl, rowp = chain.mats[i]
+        if rowp and world > 1:
+            continue
+        A = a[chain.a_off[i]:chain.a_off[i] + kl][None]
+        got = c[chain.c_off[i]:chain.c_off[i] + nl][None]
+        want = oracle.matmul_naive_q8(A, q.cpu().numpy(), s.cpu().numpy())
+        worst_ratio = max(worst_ratio, float(np.abs(got.astype(np.float64) - want).max())
+                          / (1e-5 * kl))
+        worst_rel = max(worst_rel, _row_rel_err(got, want))
+        checked.append(chain.shapes[i][0])
+    return {"ok": bool(worst_ratio <= 1.0), "max_err_over_tolerance": float(f"{worst_ratio:.3e}"),
+            "row_rel_err": float(f"{worst_rel:.3e}"),
+            "tolerance": "1e-5 * k per element (the reference's tests/test_cuda.cpp bound)",
+            "products_checked": checked,
+            "against": "oracle matmul_naive_q8 on the same int8 weights and activations"}
+
+
+def sgemm_line(n, steps, warmup, world, local, check_rows=0):
+    """The square SGEMM: C = A x B, fp32 N x N, A and B ~ U(-1, 1) (seed 2), through the
+    C ABI on the tcgen05 TF32 path (B read as stored, MN-major). Inputs 768 MB > L2. With
+    check_rows > 0, that many rows of C are compared with the oracle after the timed region."""
+    import torch
+    import llme_b200 as L
     g = torch.Generator(device="cuda")
     g.manual_seed(2)
     A = torch.rand(n, n, generator=g, device="cuda") * 2 - 1
@@ -397,19 +509,19 @@ def run_sgemm(args, world, rank, local):
                                               "automatic", False, 0, L.FLAG_WEIGHTS_STATIC, h),
                     stream)
     sampler = ClockSampler(local)
-    secs = max_over_ranks(time_graph(graph, args.steps, args.warmup, stream, world, sampler), world)
+    secs = max_over_ranks(time_graph(graph, steps, warmup, stream, world, sampler), world)
+    del graph
     flops = 2.0 * n ** 3
-    tflops = flops * args.steps * world / secs / 1e12
-    bf16 = None
+    tflops = flops * steps * world / secs / 1e12
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
             bf16 = float(json.load(f)["bf16_tflops"])
-        peak, kind = bf16 / 2, "half of measured bf16 (TF32 runs at half the bf16 rate)"
+        peak, kind = bf16 / 2, "half of measured bf16 burst (TF32 runs at half the bf16 rate)"
     except Exception:
         peak, kind = 1590.0 / 2, "half of fallback bf16"
     line = {"metric": f"TF32 GEMM TFLOP/s ({n}^3, fp32 in/out)", "value": round(tflops, 1),
-            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": steps, "warmup": warmup,
+            "ms_per_step": round(secs / steps * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "tf32",
             "data": "synthetic U(-1,1)",
             "config": {"workload": "square fp32 SGEMM on the TF32 tcgen05 path (BASELINE configs[2])",
@@ -419,9 +531,30 @@ def run_sgemm(args, world, rank, local):
                          "unit": "TFLOP/s", "frac": round(tflops / world / peak, 4),
                          "peak_kind": kind, "kernel": "gemm_tf32_kernel",
                          "traffic": None},
-            "gpu_launches": 2 * args.steps, "clocks": sampler.summary()}
+            "gpu_launches": steps, "clocks": sampler.summary()}
+    if check_rows:
+        # The checker (oracle/) after the timed region: sampled rows of C against
+        # matmul_naive of those rows of A, at the TF32 path's 5e-3 row bound.
+        oracle = _oracle()
+        rng = np.random.default_rng(2)
+        rows = np.unique(np.concatenate([[0, n - 1], rng.choice(n, check_rows - 2, replace=False)]))
+        got = C[torch.from_numpy(rows).cuda()].cpu().numpy()
+        want = oracle.matmul_naive(A[torch.from_numpy(rows).cuda()].cpu().numpy(), B.cpu().numpy())
+        err = _row_rel_err(got, want)
+        line["parity"] = {"ok": bool(err <= 5e-3), "row_rel_err": float(f"{err:.3e}"),
+                          "bound": 5e-3, "rows_checked": int(rows.size),
+                          "against": "oracle matmul_naive on the sampled rows"}
+    del A, B, C
+    return line
+
+
+def run_sgemm(args, world, rank, local):
+    line = sgemm_line(args.size, args.steps, args.warmup, world, local,
+                      check_rows=0 if args.no_extras else 16)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if "parity" in line and not line["parity"]["ok"]:
+        raise SystemExit(3)
 
 
 # ---- the decode-shaped sweep ------------------------------------------------------------
@@ -840,6 +973,7 @@ class Prefill:
                     (nl, kl, A.data_ptr(), q.data_ptr(), s.data_ptr(), C.data_ptr(), 0))
         self.batches = [L.Batch(PREFILL_ROWS, prods[True])] if prods[True] else []
         self.batches.append(L.Batch(PREFILL_ROWS, prods[False]))
+        self.all_batches = self.batches
 
     def launch_grouped(self, stream_handle, comm=None, join=None):
         import llme_b200 as L
@@ -908,11 +1042,35 @@ def cpu_prefill_sample(pf, budget_s=10.0):
                                     f"{len(times)} calls"}
 
 
-def run_prefill(args, world, rank, local):
+def prefill_parity(pf, world):
+    """After the timed region: one grouped step again, then rows 0, 255 and 511 of layer 0's
+    wq, wo, w1 and w2 and the last layer's w3 (and the classifier's row) against the oracle's
+    matmul_naive_q8 on the same bytes, at the tensor-core path's 5e-3 row bound. On several
+    GPUs only the column-parallel products, whose local slices are complete, are checked."""
+    oracle = _oracle()
+    want_idx = [0, 3, 4, 6, len(pf.items) - 3, len(pf.items) - 1]
+    worst, checked = 0.0, []
+    for i in want_idx:
+        q, s, m, kl, nl, rowp, A, C = pf.items[i]
+        if rowp and world > 1:
+            continue
+        rows = [0] if m == 1 else [0, 255, m - 1]
+        A_h = A[rows].cpu().numpy()
+        got = C[rows].cpu().numpy()
+        want = oracle.matmul_naive_q8(A_h, q.cpu().numpy(), s.cpu().numpy())
+        worst = max(worst, _row_rel_err(got, want))
+        checked.append(pf.shapes[i][0])
+    return {"ok": bool(worst <= 5e-3), "row_rel_err": float(f"{worst:.3e}"), "bound": 5e-3,
+            "products_checked": checked, "rows": "0, 255, 511 (the classifier's one row)",
+            "against": "oracle matmul_naive_q8 on the same int8 weights and activations"}
+
+
+def prefill_line(world, rank, local, steps, warmup, layers, grouped=True, per_call=True,
+                 e2e=True, cpu=True, check=True):
     import torch
     import llme_b200 as L
-    L.set_math(L.MATH_TENSOR)
-    pf = Prefill(world, rank, layers=args.layers)
+    prev_math = L.set_math(L.MATH_TENSOR)
+    pf = Prefill(world, rank, layers=layers)
     stream = torch.cuda.Stream()
     h = stream.cuda_stream
     tp = comm = join = None
@@ -929,7 +1087,6 @@ def run_prefill(args, world, rank, local):
 
         def join():
             torch.cuda.current_stream().wait_stream(comm_stream)
-    grouped = args.launch == "grouped"
     if grouped:
         pf.make_batch()
         step_fn = lambda: pf.launch_grouped(h, comm, join)  # noqa: E731
@@ -937,45 +1094,47 @@ def run_prefill(args, world, rank, local):
         step_fn = lambda: pf.launch_all(h, comm, join)  # noqa: E731
     graph = capture(step_fn, stream)
     sampler = ClockSampler(local)
-    secs = max_over_ranks(time_graph(graph, args.steps, args.warmup, stream, world, sampler), world)
-    tflops = pf.flops_total * args.steps / secs / 1e12
-    per_call = None
-    if grouped:
+    secs = max_over_ranks(time_graph(graph, steps, warmup, stream, world, sampler), world)
+    tflops = pf.flops_total * steps / secs / 1e12
+    pc = None
+    if grouped and per_call:
         pc_graph = capture(lambda: pf.launch_all(h, comm, join), stream)
-        pc_secs = max_over_ranks(time_graph(pc_graph, args.steps, args.warmup, stream, world), world)
-        per_call = {"value": round(pf.flops_total * args.steps / pc_secs / 1e12, 1),
-                    "unit": "TFLOP/s", "ms_per_step": round(pc_secs / args.steps * 1e3, 4),
-                    "launches_per_step": pf.launches()}
+        pc_secs = max_over_ranks(time_graph(pc_graph, steps, warmup, stream, world), world)
+        pc = {"value": round(pf.flops_total * steps / pc_secs / 1e12, 1),
+              "unit": "TFLOP/s", "ms_per_step": round(pc_secs / steps * 1e3, 4),
+              "launches_per_step": pf.launches()}
         del pc_graph
-
-    def e2e_fn():
-        pf.h2d()
-        step_fn()
-        pf.d2h()
-    e2e_graph = capture(e2e_fn, stream)
-    e2e_secs = max_over_ranks(time_graph(e2e_graph, args.steps, args.warmup, stream, world), world)
-    e2e = {"value": round(pf.flops_total * args.steps / e2e_secs / 1e12, 1), "unit": "TFLOP/s",
-           "h2d_bytes_per_step": int(sum(t.numel() * 4 for t in pf.a_host)),
-           "d2h_bytes_per_step": int(sum(t.numel() * 4 for t in pf.c_host)),
-           "ms_per_step": round(e2e_secs / args.steps * 1e3, 4)}
+    e2e_d = None
+    if e2e:
+        def e2e_fn():
+            pf.h2d()
+            step_fn()
+            pf.d2h()
+        e2e_graph = capture(e2e_fn, stream)
+        e2e_secs = max_over_ranks(time_graph(e2e_graph, steps, warmup, stream, world), world)
+        e2e_d = {"value": round(pf.flops_total * steps / e2e_secs / 1e12, 1), "unit": "TFLOP/s",
+                 "h2d_bytes_per_step": int(sum(t.numel() * 4 for t in pf.a_host)),
+                 "d2h_bytes_per_step": int(sum(t.numel() * 4 for t in pf.c_host)),
+                 "ms_per_step": round(e2e_secs / steps * 1e3, 4)}
+        del e2e_graph
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
             peak = float(json.load(f)["bf16_tflops_sustained"])
         peak_kind = "measured bf16 sustained"
     except Exception:
         peak, peak_kind = 1400.0, "fallback bf16 sustained"
-    achieved = pf.flops_rank * args.steps / secs / 1e12
+    achieved = pf.flops_rank * steps / secs / 1e12
     launches = 2 * len(pf.batches) + 1 if grouped else pf.launches()
     line = {
         "metric": PREFILL_METRIC, "value": round(tflops, 1), "unit": "TFLOP/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
+        "steps": steps, "warmup": warmup,
+        "ms_per_step": round(secs / steps * 1e3, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8 x (int8 hi + int8 lo) -> s32",
         "data": "synthetic: N(0,0.02^2) weights (seed 4) quantised per column to int8, "
                 "U(-1,1) activations",
         "config": {"workload": "7B-shaped batched prefill, m=512, int8 weights (BASELINE "
                                "configs[4]); classifier on the last row",
-                   "layers": args.layers, "rows": PREFILL_ROWS, "products_per_step": len(pf.items),
+                   "layers": layers, "rows": PREFILL_ROWS, "products_per_step": len(pf.items),
                    "launches_per_step": launches, "flops_per_step": pf.flops_total,
                    "parallelism": f"tp{world}" if world > 1 else "single",
                    "launch": ("grouped: one split launch + one persistent tcgen05 launch over "
@@ -995,24 +1154,46 @@ def run_prefill(args, world, rank, local):
                      # bytes (weights read once) and the split's reads exactly; scaled here to
                      # the step: GEMM (W + hi/lo + C) x 1.02 + split (4mk + 2mk).
                      "traffic": int(1.02 * pf.gemm_bytes + pf.split_bytes),
-                     "traffic_source": "profiles/gemm_q8_tc_prefill.md (ratio scaled)",
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the "
+                                       "2-layer case: 1.02 x the GEMM's algorithmic bytes, "
+                                       "scaled to the step",
                      "bytes_per_step": int(pf.gemm_bytes + pf.split_bytes)},
-        "e2e": e2e, "gpu_launches": launches * args.steps, "per_call": per_call,
-        "clocks": sampler.summary(),
+        "gpu_launches": launches * steps, "clocks": sampler.summary(),
     }
-    if rank == 0 and world == 1 and not args.no_extras:
+    if e2e_d is not None:
+        line["e2e"] = e2e_d
+    if pc is not None:
+        line["per_call"] = pc
+    if check:
+        with torch.cuda.stream(stream):
+            step_fn()
+        torch.cuda.synchronize()
+        line["parity"] = prefill_parity(pf, world)
+    if cpu and rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_prefill_sample(pf)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    del graph, e2e_graph
+    del graph
     torch.cuda.synchronize()
     if grouped:
         pf.destroy_batches()
     if tp is not None:
         tp.destroy()
+    del pf
+    torch.cuda.synchronize()
+    L.set_math(prev_math)
+    return line
+
+
+def run_prefill(args, world, rank, local):
+    line = prefill_line(world, rank, local, args.steps, args.warmup, args.layers,
+                        grouped=args.launch == "grouped", cpu=not args.no_extras,
+                        check=not args.no_extras)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+    if "parity" in line and not line["parity"]["ok"]:
+        raise SystemExit(3)
 
 
 def peaks():
@@ -1193,8 +1374,9 @@ def run_ours(args):
                 # the configs[0] case measured 1.013 x its algorithmic bytes (traffic grows with
                 # the weights streamed), scaled here to this launch.
                 "traffic": int(1.013 * per_launch_bytes) if grouped else None,
-                "traffic_source": ("profiles/gemv_batch_config0_full.md (1.013 x algorithmic, "
-                                   "scaled)") if grouped else None}
+                "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the "
+                                   "grouped kernel on configs[0]: 1.013 x the algorithmic "
+                                   "bytes, scaled to this launch") if grouped else None}
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
@@ -1216,13 +1398,36 @@ def run_ours(args):
         "per_call": per_call,
         "clocks": sampler.summary(),
     }
+    # The checker after every timed region: one grouped step again, sampled outputs against
+    # the oracle (every rank takes the same collective steps).
+    if not args.no_extras:
+        chain.use_io(ios[0])
+        with torch.cuda.stream(stream):
+            step_fn()
+        torch.cuda.synchronize()
+        line["parity"] = chain_parity(chain, world)
     if rank == 0 and world == 1 and not args.no_extras and args.workload == "chain":
         line["gemv_4096x4096"] = gemv_4096_probe()
         for v in line["gemv_4096x4096"].values():
             v["frac"] = round(v["GB_s"] / peak, 4)
+        beside = chain_per_call_beside_reference(chain)
+        if beside is not None:
+            line["reference_gpu"] = beside
         line["cpu_baseline"] = cpu_baseline_sample(chain)
+        # The other two north-star targets, each its own short timed region.
+        keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "roofline",
+                "clocks", "parity", "gpu_launches")
+        sg = sgemm_line(8192, 20, 5, 1, local, check_rows=16)
+        line["sgemm_8192"] = {k: sg[k] for k in keep if k in sg} | {
+            "workload": "configs[2]: square fp32 SGEMM, N=8192, TF32 tcgen05"}
+        pre = prefill_line(1, 0, local, 20, 5, LAYERS, per_call=False, e2e=False, cpu=False,
+                           check=True)
+        line["prefill"] = {k: pre[k] for k in keep if k in pre} | {
+            "workload": "configs[4]: 7B-shaped int8 prefill, m=512, one grouped step"}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    failed = [k for k in ("parity",) if k in line and not line[k]["ok"]] + \
+        [k for k in ("sgemm_8192", "prefill") if k in line and not line[k]["parity"]["ok"]]
     # Graphs holding NCCL calls go first, then the communicator, then the process group.
     del graph, e2e_graphs
     torch.cuda.synchronize()
@@ -1233,6 +1438,8 @@ def run_ours(args):
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+    if failed:
+        raise SystemExit(f"parity failed after the timed regions: {failed}")
 
 
 def ref_gpu_attention(args, path):
@@ -1381,33 +1588,28 @@ def run_reference(args):
                f"the reference's CPU code in its own line (cpu_baseline)")
         print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
         return
-    sys.path.insert(0, os.path.join(REPO, "oracle"))
-    import oracle  # the reference arm: the reference's own CPU code
+    oracle = _oracle()  # the reference arm: the reference's own CPU code (oracle/_ref)
     kind = "reference" if oracle.Reference.available(fast=True) else "port"
-    rng = np.random.default_rng(3)
-    shapes = chain_shapes()
-    sample = shapes[:7] + shapes[-1:]
-    mats = []
-    for _, k, n, _ in sample:
-        W = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(np.float32)
-        mats.append(oracle.Reference(fast=True).quantize_q8(W) if kind == "reference"
-                    else oracle.quantize_q8(W))
-    acts = [rng.uniform(-1, 1, (1, q.shape[0])).astype(np.float32) for q, _ in mats]
-    nbytes = sum(algorithmic_bytes(q.shape[0], q.shape[1]) for q, _ in mats)
-    if kind == "reference":
-        ref = oracle.Reference(fast=True)
-        hs = [ref.qtensor(q, s) for q, s in mats]
+    shapes = chain_shapes(args.layers) if args.workload == "chain" else gemv_shapes()
+    seed = 3 if args.workload == "chain" else 0
+    t_setup = time.perf_counter()
+    ref = oracle.Reference(fast=True) if kind == "reference" else None
+    handles, acts, source = reference_chain_inputs(shapes, seed, ref, oracle)
+    setup_s = time.perf_counter() - t_setup
+    nbytes = sum(algorithmic_bytes(k, n) for (_, k, n, _) in shapes)
+    outs = [np.empty((1, n), np.float32) for (_, k, n, _) in shapes]
+    if ref is not None:
         cores = ref.threads()
 
         def step():
-            for a, hq in zip(acts, hs):
-                ref.matmul_parallel_q8(a, hq)
+            for a, hq, o in zip(acts, handles, outs):
+                ref.matmul_parallel_q8(a, hq, out=o)
     else:
         cores = oracle.default_threads()
 
         def step():
-            for a, (q, s) in zip(acts, mats):
-                oracle.matmul_parallel(a, q=q, scale=s)
+            for a, (q, s), o in zip(acts, handles, outs):
+                o[...] = oracle.matmul_parallel(a, q=q, scale=s)
     for _ in range(args.warmup):
         step()
     t0 = time.perf_counter()
@@ -1415,19 +1617,67 @@ def run_reference(args):
         step()
     secs = time.perf_counter() - t0
     value = nbytes * args.steps / secs / 1e9
-    sample_desc = (f"layer 0 (7 products) + classifier of the chain, m=1, "
-                   f"{nbytes / 1e6:.0f} MB of algorithmic bytes per step")
+    sample_desc = (f"the whole step: all {len(shapes)} products, m=1, "
+                   f"{nbytes / 1e9:.3f} GB of algorithmic bytes per step; {source}")
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(secs / args.steps * 1e3, 3), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "7B-shaped int8 decode matmul chain, m=1 (BASELINE configs[3])",
-                       "sample": sample_desc},
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: N(0,0.02^2) weights quantised per column to int8, U(-1,1) "
+                    "activations (the same bytes as this library's arm)",
+            "config": WORKLOAD_CONFIG[args.workload] | {
+                "layers": args.layers if args.workload == "chain" else None,
+                "products_per_step": len(shapes), "algorithmic_bytes_per_step": int(nbytes),
+                "parallelism": "host threads (the reference's thread pool)",
+                "isa": ref.isa() if ref is not None else "the C port, -O2"},
             "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores,
                              "kind": kind, "sample": sample_desc},
             "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+                    "d2h_bytes_per_step": 0},
+            "setup_s": round(setup_s, 1)}
     print(json.dumps(line), flush=True)
+
+
+def reference_chain_inputs(shapes, seed, ref, oracle):
+    """The chain's int8 weights and activations as the same bytes this library's arm uses:
+    each weight drawn by torch with the same generator and seed as Chain (on the GPU where one
+    is visible, as Chain draws it), copied to the host and quantised there by the reference's
+    own quantize_q8 (quant.cpp:6-28; the port where the reference is not built), on a few host
+    threads; activations drawn as Chain draws them. Returns (weights as reference-side
+    QTensors or (q, scale) pairs, activation rows, a note on where the weights came from)."""
+    import concurrent.futures as cf
+    import torch
+    cuda = torch.cuda.is_available()
+    dev = "cuda" if cuda else "cpu"
+    g = torch.Generator(device=dev)
+    quant = ref.quantize_q8 if ref is not None else oracle.quantize_q8
+    workers = max(1, min(8, os.cpu_count() or 1))
+
+    def one(W):
+        q, s = quant(W)
+        return ref.qtensor(q, s) if ref is not None else (q, s)
+    handles, futs = [None] * len(shapes), {}
+    with cf.ThreadPoolExecutor(workers) as pool:
+        for idx, (_, k, n, _) in enumerate(shapes):
+            g.manual_seed(seed * 100003 + idx)
+            W = (torch.randn(k, n, generator=g, device=dev) * 0.02).cpu().numpy()
+            futs[pool.submit(one, W)] = idx
+            if len(futs) >= 2 * workers:  # bound the fp32 copies held at once
+                done, _ = cf.wait(futs, return_when=cf.FIRST_COMPLETED)
+                for f in done:
+                    handles[futs.pop(f)] = f.result()
+        for f in cf.as_completed(list(futs)):
+            handles[futs.pop(f)] = f.result()
+    ga = torch.Generator(device="cpu")
+    ga.manual_seed(seed * 7)
+    acts = [(torch.rand(k, generator=ga) * 2 - 1).numpy().reshape(1, k) for (_, k, n, _) in shapes]
+    source = ("weights drawn by torch on the GPU exactly as the library's arm draws them, "
+              "quantised by the reference's quantize_q8" if cuda else
+              "weights drawn by torch on the host (no GPU visible: other values, the same "
+              "distribution), quantised by the reference's quantize_q8")
+    if ref is None:
+        source = source.replace("the reference's quantize_q8", "the C port of quantize_q8")
+    return handles, acts, source
 
 
 def main():

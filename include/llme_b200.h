@@ -105,23 +105,27 @@ int llme_matmul_q8(size_t m, size_t n, size_t k, const float* A, const int8_t* B
 /* Allocation-free variant of llme_matmul_q8 with LLME_KERNEL_TILED_SPLIT. It has no
  * counterpart in the reference, whose matmul_cuda grows its split-K scratch with cudaMalloc.
  *
- * For callers that must not allocate device memory while they run: code being recorded into
- * a CUDA graph (cudaMalloc is not allowed during stream capture), serving processes whose
- * allocator has reserved nearly all of HBM up front (a raw cudaMalloc would fail or fragment
- * it), and hard real-time loops that forbid allocation after start-up. The split-K partial
- * sums and tickets live in one fixed device array of LLME_NOALLOC_SCRATCH_BYTES inside the
- * library, which every GPU that loads the library holds until the process exits; the call
- * itself makes no cudaMalloc, cudaFree or other allocating call. The caller still passes A,
- * B, scale and C (same layouts and accumulate meaning as llme_matmul_q8; no RMSNorm fusion).
+ * For callers that cannot allocate device memory once they are running: a serving process
+ * whose memory pool reserved nearly all of the GPU's HBM at start-up (a cudaMalloc from inside
+ * the library would fail, or take memory the pool meant to own), a latency-bound loop that may
+ * not take cudaMalloc's device-wide synchronisation after start-up, and a plug-in inside a host
+ * runtime that owns all device memory. The split-K partial sums and tickets live in one fixed
+ * device array of LLME_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads
+ * the library holds until the process exits; the call itself makes no cudaMalloc, cudaFree or
+ * other allocating call. The caller still passes A, B, scale and C (same layouts and
+ * accumulate meaning as llme_matmul_q8; no RMSNorm fusion). It always runs the SIMT split-K
+ * tiles (fp32 FMA arithmetic), whatever llme_set_math selects for the other entry points.
  *
  * Limits and contract:
  *  - a product whose split-K plan needs more than the fixed array (partial sums of the k
  *    slices, one 64 x 64 fp32 tile per slice per output tile, plus one ticket per tile; up to
  *    4096 tickets) is rejected with LLME_E_INVALID and a message giving both sizes;
- *  - the first call on each device finds the array's device address and clears its tickets;
- *    make that first call (with the device current) before any stream capture begins;
+ *  - the first call on each device looks up the array's device address (with that device
+ *    current) and clears its tickets; make that first call before any stream capture begins.
+ *    The address is kept for the life of the process: after cudaDeviceReset on a device, do
+ *    not call the library on that device again (its grow-only scratch is lost the same way);
  *  - all calls on a device share the array and it keeps the last call's contents: calls
- *    whose kernels overlap on the GPU (other streams, concurrent graphs) race on it, so keep
+ *    whose kernels overlap on the GPU (other streams, other host threads) race on it, so keep
  *    them ordered on one stream. */
 #define LLME_NOALLOC_SCRATCH_BYTES (16u << 20)
 int llme_matmul_q8_noalloc(size_t m, size_t n, size_t k, const float* A, const int8_t* B,

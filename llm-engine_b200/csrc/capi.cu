@@ -790,8 +790,8 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
 // [partial sums: the rest]. The tickets must be zero when a launch starts; set-up clears them
 // once and every launch leaves them at zero again (the last CTA of a tile resets its ticket).
 // Partial sums are always written before they are read. Every call on a device shares this
-// one array, so two calls that overlap on the GPU (different streams, or concurrent graphs)
-// race on it.
+// one array, so two calls that overlap on the GPU (different streams or host threads) race on
+// it.
 constexpr size_t kNoAllocBytes = LLME_NOALLOC_SCRATCH_BYTES;
 constexpr size_t kNoAllocTickets = 4096;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
@@ -800,7 +800,9 @@ std::mutex g_noalloc_mu;
 unsigned char* g_noalloc_base[kMaxDevices] = {};
 
 // Once per device, with that device current: the array's device address (the host-side
-// symbol is only a stand-in, never a device pointer) and cleared tickets.
+// symbol is only a stand-in, never a device pointer) and cleared tickets. The address is kept
+// for the life of the process; a cudaDeviceReset would make it stale, which the header rules
+// out for callers.
 int noalloc_setup(int dev, cudaStream_t stream, unsigned char** base) {
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
     if (!g_noalloc_base[dev]) {

@@ -21,7 +21,35 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libllme_ref.so")
-REF_FAST_SO = os.path.join(HERE, "_ref", "libllme_ref_fast.so")
+REF_FAST_V3_SO = os.path.join(HERE, "_ref", "libllme_ref_fast.so")
+REF_FAST_V4_SO = os.path.join(HERE, "_ref", "libllme_ref_fast_v4.so")
+# The reference checkout (read-only): LLME_REFERENCE_SRC, else the directory beside this repo.
+REF_SRC = os.environ.get("LLME_REFERENCE_SRC") or os.path.join(
+    os.path.dirname(os.path.dirname(HERE)), "reference")
+
+
+def _host_has_avx512() -> bool:
+    """The x86-64-v4 level: AVX-512 F, BW, CD, DQ and VL, as the kernel reports them."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags"):
+                    flags = set(line.split(":", 1)[1].split())
+                    return {"avx512f", "avx512bw", "avx512cd", "avx512dq", "avx512vl"} <= flags
+    except OSError:
+        pass
+    return False
+
+
+def _fast_so() -> str:
+    """The timed CPU baseline: the reference's sources at -O3 for the widest vector ISA this
+    host runs (its own build uses -march=native, CMakeLists.txt:20)."""
+    if os.path.exists(REF_FAST_V4_SO) and _host_has_avx512():
+        return REF_FAST_V4_SO
+    return REF_FAST_V3_SO
+
+
+REF_FAST_SO = _fast_so()
 
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _i8p = np.ctypeslib.ndpointer(dtype=np.int8, flags="C_CONTIGUOUS")
@@ -31,7 +59,7 @@ _sz = ctypes.c_size_t
 def build() -> None:
     """Builds liboracle.so (and oracle/_ref when the reference sources are present)."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
-    if os.path.isdir("/root/reference/src"):
+    if os.path.isdir(os.path.join(REF_SRC, "src")):
         subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
 
 
@@ -137,6 +165,7 @@ class Reference:
         path = REF_FAST_SO if fast else REF_SO
         if not os.path.exists(path):
             raise FileNotFoundError(path)
+        self.path = path
         lib = ctypes.CDLL(path)
         lib.ref_last_error.restype = ctypes.c_char_p
         lib.ref_pool_threads.restype = ctypes.c_uint
@@ -169,6 +198,11 @@ class Reference:
 
     def threads(self) -> int:
         return int(self.lib.ref_pool_threads())
+
+    def isa(self) -> str:
+        """The vector ISA the loaded library was built for."""
+        return "x86-64-v4 (AVX-512)" if self.path == REF_FAST_V4_SO else (
+            "x86-64-v3 (AVX2+FMA)" if self.path == REF_FAST_V3_SO else "-O2, contraction off")
 
     def matmul_naive(self, A, B, b_rows=None):
         A, B = _c(A, np.float32), _c(B, np.float32)

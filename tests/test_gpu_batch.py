@@ -16,7 +16,9 @@ from conftest import close_to, row_rel_err
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-SHAPES = [(4096, 4096), (4096, 11008), (11008, 4096), (64, 288), (1000, 4096), (4100, 32)]
+# The chain's three weight shapes, its 4096 x 32000 classifier, and ragged ones.
+SHAPES = [(4096, 4096), (4096, 11008), (11008, 4096), (4096, 32000), (64, 288), (1000, 4096),
+          (4100, 32)]
 
 
 def make(rng, m, shapes):

@@ -95,3 +95,31 @@ def test_config2_square_1024():
     rng = np.random.default_rng(2)
     A, B = uni(rng, 1024, 1024), uni(rng, 1024, 1024)
     assert row_rel_err(run(A, B), oracle.matmul_naive(A, B)) <= 5e-3
+
+
+@pytest.mark.parametrize("n", [2048, 4096, 8192])
+def test_config2_square_sampled_rows(n):
+    """configs[2] at the sizes its TF32 target is quoted on (A, B ~ U(-1, 1), seed 2): the
+    whole N^3 product runs on the GPU; 64 rows of C (the first, the last, rows of the last
+    128-row tile and random ones) are compared with matmul_naive of those rows of A against
+    all of B, within the 5e-3 row bound, and with the float64 product of TF32 operands within
+    the fp32 accumulation noise. (The naive oracle would need minutes for the whole 8192^3.)"""
+    rng = np.random.default_rng(2)
+    A = rng.random((n, n), dtype=np.float32) * 2 - 1
+    B = rng.random((n, n), dtype=np.float32) * 2 - 1
+    assert L.plan(n, n, n, q8=False)["path_name"] == "tcgen05"
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    dC = torch.full((n, n), float("nan"), device="cuda")
+    L.matmul(dA, dB, C=dC)
+    torch.cuda.synchronize()
+    rows = np.unique(np.concatenate([[0, n - 1, n - 128, n - 65],
+                                     rng.choice(n, 60, replace=False)]))
+    got = dC[torch.from_numpy(rows).cuda()].cpu().numpy()
+    assert np.isfinite(got).all()
+    want = oracle.matmul_naive(A[rows], B)
+    err = row_rel_err(got, want)
+    ref_t = tf32_trunc(A[rows]).astype(np.float64) @ tf32_trunc(B).astype(np.float64)
+    e_t = np.abs(got - ref_t).max()
+    print(f"square {n}: row-rel {err:.2e} over {rows.size} rows; vs tf32 operands {e_t:.2e}")
+    assert err <= 5e-3, err
+    assert e_t <= 1e-5 * n

@@ -1,13 +1,18 @@
 """The allocation-free entry point, llme_matmul_q8_noalloc, against llme_matmul_q8.
 
-Some callers cannot allocate device memory while they run: code being recorded into a CUDA
-graph, serving processes whose allocator already holds nearly all of HBM, real-time loops
-that forbid allocation after start-up. For them the library offers one product whose split-K
-scratch is a fixed device array inside the library. Through the C ABI, this file checks that
-two such calls in a row match the allocating entry point running the same kernel
-(tiled_split) within the suite's tolerance, that they leave the library's grow-only scratch
-untouched (no reallocation), and that a product too large for the fixed array is refused
-with a clear message. It is collected last and needs nothing from the other test files.
+Some callers of this library cannot allocate device memory once they are running: a serving
+process whose memory pool reserved nearly all of the GPU's HBM at start-up (a cudaMalloc from
+inside the library would fail, or carve up what the pool meant to own), a latency-bound loop
+that may not take cudaMalloc's device-wide synchronisation after start-up, and a plug-in
+inside a host runtime that owns all device memory. For them the library offers one product
+whose split-K scratch is a fixed device array inside the library itself.
+
+Through the C ABI this file checks that two such calls in a row give, bit for bit, what the
+allocating entry point gives when it runs the same kernel (the SIMT split-K tiles, selected
+with LLME_MATH_FP32 and tiled_split), that both sit within the reference's 1e-5 * k of the
+oracle, that the calls leave the library's grow-only scratch untouched (no reallocation), and
+that a product too large for the fixed array is refused with a clear message. It is collected
+last and needs nothing from the other test files.
 """
 from __future__ import annotations
 
@@ -22,31 +27,42 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 
-def _case(rng, m, k, n):
+def _case(rng, m, k, n, accumulate):
     A = rng.uniform(-1, 1, (m, k)).astype(np.float32)
-    q, s = oracle.quantize_q8(rng.uniform(-1, 1, (k, n)).astype(np.float32))
+    q, s = oracle.quantize_q8((rng.standard_normal((k, n)) * 0.02).astype(np.float32))
     C0 = rng.uniform(-1, 1, (m, n)).astype(np.float32)
+    want = oracle.matmul_naive_q8(A, q, s)
+    if accumulate:
+        want = C0 + want
     dev = [torch.from_numpy(x).cuda() for x in (A, q, s, C0)]
-    return (m, k, n), dev
+    return (m, k, n, accumulate), dev, want
 
 
 def test_noalloc_matches_allocating_entry_point_twice_in_a_row():
     L.load()
     rng = np.random.default_rng(2026)
-    cases = [(_case(rng, 16, 4096, 4096), False), (_case(rng, 33, 1029, 257), True)]
+    cases = [_case(rng, 16, 4096, 4096, False), _case(rng, 33, 1029, 257, True)]
     stream = L.torch_stream_handle()
-    # The allocating entry point with the same kernel: the reference result.
-    wants = []
-    for ((m, k, n), (dA, dq, ds, dC0)), acc in cases:
-        C = dC0.clone()
-        L.matmul_cuda_q8(m, n, k, dA.data_ptr(), dq.data_ptr(), ds.data_ptr(), C.data_ptr(),
-                         "tiled_split", acc, 0, 0, stream)
-        wants.append(C)
-    torch.cuda.synchronize()
+    # The allocating entry point on the kernel the allocation-free one runs: the SIMT tiles
+    # with k split across CTAs (tiled_split in fp32 arithmetic).
+    prev = L.set_math(L.MATH_FP32)
+    try:
+        wants = []
+        for (m, k, n, acc), (dA, dq, ds, dC0), _ in cases:
+            assert L.plan(m, n, k, q8=True, kernel="tiled_split", a_addr=dA.data_ptr(),
+                          b_addr=dq.data_ptr(), math=L.MATH_FP32)["path_name"] == "tiled_simt"
+            C = dC0.clone()
+            L.matmul_cuda_q8(m, n, k, dA.data_ptr(), dq.data_ptr(), ds.data_ptr(), C.data_ptr(),
+                             "tiled_split", acc, 0, 0, stream)
+            wants.append(C)
+        torch.cuda.synchronize()
+    finally:
+        L.set_math(prev)
     generation = L.scratch_generation()
-    # Two allocation-free calls back to back on the same stream.
+    # Two allocation-free calls back to back on the same stream; the second reuses the
+    # tickets the first left behind.
     gots = []
-    for ((m, k, n), (dA, dq, ds, dC0)), acc in cases:
+    for (m, k, n, acc), (dA, dq, ds, dC0), _ in cases:
         C = dC0.clone()
         L.matmul_cuda_q8_noalloc(m, n, k, dA.data_ptr(), dq.data_ptr(), ds.data_ptr(),
                                  C.data_ptr(), acc, stream)
@@ -54,8 +70,10 @@ def test_noalloc_matches_allocating_entry_point_twice_in_a_row():
     torch.cuda.synchronize()
     L.synchronize()
     assert L.scratch_generation() == generation  # nothing was (re)allocated
-    for (((m, k, n), _), acc), got, want in zip(cases, gots, wants):
-        assert close_to(got.cpu().numpy(), want.cpu().numpy(), k, 2.0 if acc else 1.0), (m, k, n)
+    for ((m, k, n, acc), _, oracle_want), got, want in zip(cases, gots, wants):
+        g = got.cpu().numpy()
+        np.testing.assert_array_equal(g, want.cpu().numpy())
+        assert close_to(g, oracle_want, k, 2.0 if acc else 1.0), (m, k, n)
 
 
 def test_noalloc_refuses_a_product_larger_than_its_scratch():
