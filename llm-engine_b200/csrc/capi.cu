@@ -131,8 +131,10 @@ int plan_path(const PlanIn& in, llme_plan_t* p) {
             p->path = LLME_PATH_GEMV_TMA;
             p->tile_n = gemv_tma_cols(in.q8);
             strips = ceil_div(n, p->tile_n);
-            // Two CTAs per SM; slices form one cluster (at most 8), each at least two boxes deep.
-            const size_t target = 2 * static_cast<size_t>(sms);
+            // Two CTAs per SM; slices form one cluster (at most 8), each at least two boxes
+            // deep.
+            const size_t target =
+                static_cast<size_t>(gemv_call_ctas_per_sm(static_cast<int>(m))) * sms;
             slices = std::max<size_t>(
                 1, std::min({target / strips, ceil_div(k, 2 * kGemvBoxRows),
                              static_cast<size_t>(kGemvMaxCluster)}));
@@ -609,7 +611,11 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
         g.strips = p.grid_x;
         g.split = split;
         g.stream = stream;
-        g.pdl = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
+        // The TMA kernel always launches with programmatic dependent launch: before
+        // griddepcontrol.wait it reads nothing but its weights (and only with
+        // LLME_FLAG_WEIGHTS_STATIC; otherwise it merely prefetches them into L2).
+        g.weights_static = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
+        g.pdl = p.path == LLME_PATH_GEMV_TMA || g.weights_static;
         if (p.path == LLME_PATH_GEMV_TMA) {
             CUtensorMap tmB, tmA, tmW;
             st = q8 ? tensor_map(B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, n, kGemvRowBytes,

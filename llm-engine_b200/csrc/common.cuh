@@ -154,6 +154,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// Brings the box at (x, y) into L2 only (no shared memory, no barrier): a hint that is safe
+// to issue before griddepcontrol.wait, since L2 is where every write of the previous grid
+// lands and a later load still reads the current contents.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d_nohint(void* dst, const CUtensorMap* map, int x, int y,
                                                    uint64_t* bar) {
     asm volatile(

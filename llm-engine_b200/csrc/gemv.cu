@@ -48,35 +48,70 @@ constexpr int kTmaThreads = kConsumers + 32;  // + one producer warp
 constexpr int kStages = 4;
 constexpr int kBoxBytesB = kGemvRowBytes * kGemvBoxRows;  // 16 KB
 
-// Per-thread work split of one 128-byte row segment of B.
-template <int M, bool Q8>
+// Per-thread work split of one 128-byte row segment of B over `Warps` consumer warps.
+template <int M, bool Q8, int Warps = kConsumerWarps>
 struct Shape {
     static constexpr int ESZ = Q8 ? 1 : 4;
     // Columns per thread: fewer as M grows, so M x V accumulators fit 2 CTAs per SM.
     static constexpr int V = Q8 ? (M <= 2 ? 16 : (M <= 4 ? 8 : 4)) : 4;
     static constexpr int NT = kGemvRowBytes / ESZ;         // columns per CTA
     static constexpr int TPR = NT / V;                     // threads per row
-    static constexpr int RG = kConsumers / TPR;            // row groups
+    static constexpr int RG = Warps * 32 / TPR;            // row groups
     static constexpr int RPT = kGemvBoxRows / RG;          // rows per thread per box
     static_assert(TPR == 8 || TPR == 16 || TPR == 32, "row split");
     static_assert(V % 4 == 0, "packed pairs");
+    static_assert(RPT * RG == kGemvBoxRows, "rows split evenly");
 };
+
+// The per-call kernel runs two CTAs per SM, each with a ring deep enough to hold the whole
+// k-slice of the chain's 4096-deep products (6 boxes for m <= 2), requested before
+// griddepcontrol.wait; CTAs of the next call that find room start early and stage their weights
+// while this call computes, and the earliest one prefetches the next call's whole weight matrix
+// into L2 so the CTAs that start later read it from there.
+template <int M>
+constexpr int call_warps() { return kConsumerWarps; }
+template <int M>
+constexpr int call_threads() { return call_warps<M>() * 32 + 32; }
+constexpr int kCallResidentCtas = 2;
+constexpr int kCallSmemBudget = 110 * 1024;
+// Boxes a CTA prefetches into L2 beyond its ring (a sliding window).
+constexpr int kPrefetchBoxes = 8;
+// Weight matrices up to this size are prefetched into L2 whole by the first CTA of the call.
+constexpr size_t kWholePrefetchMaxBytes = size_t{48} << 20;
+constexpr uint32_t kWholePrefetchChunk = 1u << 20;
 
 template <int M, bool Q8, bool Norm>
 struct Layout {
-    static constexpr int kB = kStages * kBoxBytesB;
+    using Sh = Shape<M, Q8, call_warps<M>()>;
+    static constexpr int CW = call_warps<M>();
     static constexpr int kABox = M * kGemvBoxRows * 4;
     static constexpr int kWBox = kGemvBoxRows * 4;
+    static constexpr int kStageBytes = kBoxBytesB + kABox + (Norm ? kWBox : 0);
+    // The cluster reduction's receive area: every slice's share of the strip's sums (at most
+    // M x NT + 4 x slices floats over all senders), then their RMSNorm sums of squares.
+    static constexpr int kRecvFloats = M * Sh::NT + 4 * kGemvMaxCluster + kGemvMaxCluster * M;
+    static constexpr int kFixedBytes =
+        (Q8 ? Sh::NT * 4 : 0) + 2 * 8 * 8 + 16 + 16 + kRecvFloats * 4;
+    static constexpr int kBudget = kCallSmemBudget;
+    // Ring depth: as many stages as the budget holds (6 for m <= 2, 5 for m = 8), at most 8.
+    static constexpr int kRing = (kBudget - kFixedBytes) / kStageBytes < 8
+                                 ? (kBudget - kFixedBytes) / kStageBytes
+                                 : 8;
+    static constexpr int kB = kRing * kBoxBytesB;
     static constexpr int kOffA = kB;
-    static constexpr int kOffW = kOffA + kStages * kABox;
-    static constexpr int kOffScale = kOffW + (Norm ? kStages * kWBox : 0);  // NT floats (int8)
-    static constexpr int kOffBar = kOffScale + (Q8 ? Shape<M, Q8>::NT * 4 : 0);
-    static constexpr int kBytes = kOffBar + 2 * kStages * 8 + 16;
+    static constexpr int kOffW = kOffA + kRing * kABox;
+    static constexpr int kOffScale = kOffW + (Norm ? kRing * kWBox : 0);  // NT floats (int8)
+    static constexpr int kOffBar = kOffScale + (Q8 ? Sh::NT * 4 : 0);
+    static constexpr int kOffRedBar = kOffBar + 2 * kRing * 8;
+    static constexpr int kOffRecv = kOffRedBar + 16;
+    static constexpr int kBytes = kOffRecv + kRecvFloats * 4;
     static constexpr uint32_t kTx = kBoxBytesB + kABox + (Norm ? kWBox : 0);
     // Reduction buffers reuse the drained ring.
-    static constexpr int kRedFloats = kConsumerWarps * M * Shape<M, Q8>::NT;
-    static_assert((kRedFloats + M * Shape<M, Q8>::NT) * 4 <= kB, "reduction fits in the ring");
-    static_assert((kConsumerWarps + 2) * M * 4 <= kStages * kABox, "ss reduction fits");
+    static constexpr int kRedFloats = CW * M * Sh::NT;
+    static_assert(kRing >= 3, "ring depth");
+    static_assert(kBytes <= kBudget, "the CTA's share of the SM");
+    static_assert((kRedFloats + M * Sh::NT) * 4 <= kB, "reduction fits in the ring");
+    static_assert((CW + 2) * M * 4 <= kRing * kABox, "ss reduction fits");
 };
 
 // ---- packed f32x2 arithmetic (sm_100) ---------------------------------------------------
@@ -144,35 +179,46 @@ __device__ __forceinline__ uint32_t cluster_rank() {
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
     return r;
 }
-// Every thread of every CTA in the cluster; release/acquire orders shared-memory writes.
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                     : "memory");
-}
-// The same rendezvous with no memory ordering: only "nobody leaves yet". A release arrive
+// A cluster-wide rendezvous with no memory ordering: only "nobody leaves yet". A release arrive
 // would first wait for this CTA's global stores to be acknowledged (~1 us here).
 __device__ __forceinline__ void cluster_sync_relaxed() {
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::
                      : "memory");
 }
-__device__ __forceinline__ float4 ld_dsmem_f4(const float* local, uint32_t rank) {
+// A rendezvous split in two: arrive early (after initialising the barriers other CTAs
+// will signal), wait late (before signalling them).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
+// The shared::cluster address of this CTA's shared `local` in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(const void* local, uint32_t rank) {
     uint32_t remote;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(remote)
+    return remote;
+}
+// Asynchronous stores into another cluster CTA's shared memory, counted in bytes on that CTA's
+// mbarrier `bar` (both shared::cluster addresses).
+__device__ __forceinline__ void st_async_f4(uint32_t dst, float4 v, uint32_t bar) {
+    asm volatile(
+        "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+            dst),
+        "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void st_async_f(uint32_t dst, float v, uint32_t bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(dst),
+                 "f"(v), "r"(bar)
                  : "memory");
-    return v;
 }
-__device__ __forceinline__ float ld_dsmem_f(const float* local, uint32_t rank) {
-    uint32_t remote;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-    return v;
+// Brings `bytes` (a multiple of 16, 16-byte aligned start) of global memory into L2.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)),
+                 "r"(bytes)
+                 : "memory");
 }
-
 // Writes C for a CTA's column strip from M x NT sums that are already complete
 // (tot, shared memory) -- the kernels' common epilogue.
 // sscale: the strip's column scales already in shared memory (int8 TMA kernel), or null to
@@ -193,14 +239,17 @@ __device__ __forceinline__ void store_strip(const float* tot, const float* tot_s
 }
 
 template <int M, bool Q8, bool Norm>
-__global__ void __launch_bounds__(kTmaThreads, 2)
+__global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmW, const GemvArgs a) {
-    using S = Shape<M, Q8>;
     using L = Layout<M, Q8, Norm>;
+    using S = typename L::Sh;
+    constexpr int CW = L::CW;        // consumer warps
+    constexpr int CT = L::CW * 32;   // consumer threads
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
-    uint64_t* empty = full + kStages;
+    uint64_t* empty = full + L::kRing;
+    constexpr int R = L::kRing;  // ring depth
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int strip = blockIdx.x, slice = blockIdx.y;  // grid.y = slices = cluster size
@@ -210,17 +259,23 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
     const int nb = (k1 - k0 + kGemvBoxRows - 1) / kGemvBoxRows;
 
     if (tid == 0) GEMV_TRACE(a, 0);
-    if (tid == kConsumers) {
-        for (int s = 0; s < kStages; ++s) {
+    uint64_t* rbar = reinterpret_cast<uint64_t*>(smem + L::kOffRedBar);
+    if (tid == CT) {
+        for (int s = 0; s < R; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
+            mbar_init(&empty[s], CW);
         }
+        mbar_init(rbar, 1);
         fence_mbar_init();
         prefetch_tensormap(&tmB);
         prefetch_tensormap(&tmA);
         if (Norm) prefetch_tensormap(&tmW);
     }
     __syncthreads();
+    // The slices of a strip push their sums into each other's shared memory at the end; the
+    // rendezvous that makes every CTA's reduction barrier visible is opened here and closed
+    // only just before the first push.
+    if (a.slices > 1) cluster_arrive_relaxed();
     if (tid == 0) {
         pdl_launch_dependents();
         GEMV_TRACE(a, 1);
@@ -229,21 +284,42 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
     float* red = reinterpret_cast<float*>(smem);
     float* tot = red + L::kRedFloats;
     float* red_ss = reinterpret_cast<float*>(smem + L::kOffA);
-    float* tot_ss = red_ss + kConsumerWarps * M;
+    float* tot_ss = red_ss + CW * M;
 
-    if (warp == kConsumerWarps) {
-        // Producer. Weights first (they do not depend on the previous launch),
-        // then wait for it before loading activations.
+    if (warp == CW) {
+        // Producer. Everything before griddepcontrol.wait touches weights only: with static
+        // weights the first R boxes go straight into the ring, and in every case the next
+        // kPrefetchBoxes boxes are prefetched into L2 (a hint, safe whatever wrote them), so
+        // this CTA's weights stream from HBM while the previous launch still computes. A and
+        // the RMSNorm weight are loaded only after the wait.
         if (lane == 0) {
             const uint64_t pol = l2_evict_first_policy();
-            const int pro = min(nb, kStages);
-            for (int b = 0; b < pro; ++b) {
-                mbar_arrive_expect_tx(&full[b], L::kTx);
-                tma_load_2d(smem + b * kBoxBytesB, &tmB, col0, k0 + b * kGemvBoxRows, &full[b], pol);
-            }
+            const int pro = min(nb, R);
+            const int pf_end = min(nb, pro + kPrefetchBoxes);
+            if (a.weights_static)
+                for (int b = 0; b < pro; ++b) {
+                    mbar_arrive_expect_tx(&full[b], L::kTx);
+                    tma_load_2d(smem + b * kBoxBytesB, &tmB, col0, k0 + b * kGemvBoxRows, &full[b], pol);
+                }
+            for (int b = a.weights_static ? pro : 0; b < pf_end; ++b)
+                tma_prefetch_l2_2d(&tmB, col0, k0 + b * kGemvBoxRows);
+            // The first CTA to start brings the whole weight matrix into L2 (when it is not too
+            // large for it), so CTAs that become resident only after the previous call ends
+            // find their boxes in L2 instead of waiting on HBM.
+            const size_t wbytes = static_cast<size_t>(a.k) * a.n * S::ESZ;
+            if (blockIdx.x == 0 && blockIdx.y == 0 && wbytes <= kWholePrefetchMaxBytes)
+                for (size_t off = 0; off < wbytes; off += kWholePrefetchChunk)
+                    prefetch_l2_bulk(static_cast<const uint8_t*>(a.B) + off,
+                                     wbytes - off < kWholePrefetchChunk
+                                         ? static_cast<uint32_t>(wbytes - off)
+                                         : kWholePrefetchChunk);
             GEMV_TRACE(a, 2);
             pdl_wait();
             for (int b = 0; b < pro; ++b) {
+                if (!a.weights_static) {
+                    mbar_arrive_expect_tx(&full[b], L::kTx);
+                    tma_load_2d(smem + b * kBoxBytesB, &tmB, col0, k0 + b * kGemvBoxRows, &full[b], pol);
+                }
                 tma_load_2d_nohint(smem + L::kOffA + b * L::kABox, &tmA, k0 + b * kGemvBoxRows, 0,
                                    &full[b]);
                 if (Norm)
@@ -252,25 +328,30 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
             }
             GEMV_TRACE(a, 3);
             for (int b = pro; b < nb; ++b) {
-                const int s = b % kStages;
-                if (!mbar_wait(&empty[s], ((b / kStages) - 1) & 1, &g_gemv_error)) break;
+                const int s = b % R;
+                if (!mbar_wait(&empty[s], ((b / R) - 1) & 1, &g_gemv_error)) break;
                 mbar_arrive_expect_tx(&full[s], L::kTx);
                 const int y = k0 + b * kGemvBoxRows;
                 tma_load_2d(smem + s * kBoxBytesB, &tmB, col0, y, &full[s], pol);
                 tma_load_2d_nohint(smem + L::kOffA + s * L::kABox, &tmA, y, 0, &full[s]);
                 if (Norm) tma_load_1d(smem + L::kOffW + s * L::kWBox, &tmW, y, &full[s]);
+                if (b + kPrefetchBoxes < nb)
+                    tma_prefetch_l2_2d(&tmB, col0, k0 + (b + kPrefetchBoxes) * kGemvBoxRows);
             }
         }
         __syncwarp();
     } else {
-        // The strip's column scales are weights too: fetch them before waiting for the
-        // previous launch, so the epilogue never waits on DRAM for them.
-        if constexpr (Q8) {
-            float* sscale = reinterpret_cast<float*>(smem + L::kOffScale);
-            if (tid < S::NT) sscale[tid] = col0 + tid < a.n ? __ldg(a.scale + col0 + tid) : 0.0f;
-        }
+        // The strip's column scales are weights too: with static weights they are fetched
+        // before waiting for the previous launch, so the epilogue never waits on DRAM for them.
+        float* sscale = reinterpret_cast<float*>(smem + L::kOffScale);
+        if constexpr (Q8)
+            if (a.weights_static && tid < S::NT)
+                sscale[tid] = col0 + tid < a.n ? __ldg(a.scale + col0 + tid) : 0.0f;
         // Consumers: C is touched only after this.
         pdl_wait();
+        if constexpr (Q8)
+            if (!a.weights_static && tid < S::NT)
+                sscale[tid] = col0 + tid < a.n ? __ldg(a.scale + col0 + tid) : 0.0f;
         const int cg = tid % S::TPR, rg = tid / S::TPR;
         uint64_t acc[M][S::V / 2];
         float ss[M];
@@ -281,8 +362,8 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
             for (int j = 0; j < S::V / 2; ++j) acc[r][j] = 0ull;
         }
         for (int b = 0; b < nb; ++b) {
-            const int s = b % kStages;
-            if (!mbar_wait(&full[s], (b / kStages) & 1, &g_gemv_error)) break;
+            const int s = b % R;
+            if (!mbar_wait(&full[s], (b / R) & 1, &g_gemv_error)) break;
             if (tid == 0 && b == 0) GEMV_TRACE(a, 4);
             const uint8_t* sb = smem + s * kBoxBytesB + cg * (S::V * S::ESZ);
             const float* sa = reinterpret_cast<const float*>(smem + L::kOffA + s * L::kABox);
@@ -317,7 +398,7 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
         // Reduce the row groups: inside a warp by shuffle, then the 8 warps
         // through shared memory (the drained ring), always in the same order.
         if (tid == 0) GEMV_TRACE(a, 5);
-        named_barrier(1, kConsumers);
+        named_barrier(1, CT);
         float accf[M][S::V];
 #pragma unroll
         for (int r = 0; r < M; ++r)
@@ -346,23 +427,23 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
                 for (int r = 0; r < M; ++r) red_ss[warp * M + r] = ss[r];
             }
         }
-        named_barrier(1, kConsumers);
-        for (int e = tid; e < M * S::NT; e += kConsumers) {
+        named_barrier(1, CT);
+        for (int e = tid; e < M * S::NT; e += CT) {
             float v = 0.0f;
 #pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) v += red[w * M * S::NT + e];
+            for (int w = 0; w < CW; ++w) v += red[w * M * S::NT + e];
             tot[e] = v;
         }
         if (Norm && tid < M) {
             float v = 0.0f;
 #pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) v += red_ss[w * M + tid];
+            for (int w = 0; w < CW; ++w) v += red_ss[w * M + tid];
             tot_ss[tid] = v;
         }
         if (tid == 0) GEMV_TRACE(a, 6);
         if (a.slices == 1) {
-            named_barrier(1, kConsumers);
-            store_strip<M, S::NT, Q8, Norm>(tot, tot_ss, a, col0, tid, kConsumers,
+            named_barrier(1, CT);
+            store_strip<M, S::NT, Q8, Norm>(tot, tot_ss, a, col0, tid, CT,
                                             reinterpret_cast<const float*>(smem + L::kOffScale));
             if (tid == 0) GEMV_TRACE(a, 7);
         }
@@ -370,56 +451,57 @@ __global__ void __launch_bounds__(kTmaThreads, 2)
     if (a.slices == 1) return;
     __syncwarp();
 
-    // k split across the cluster: every CTA finishes 1/slices of the strip's
-    // columns, adding the slices' sums (read from each CTA's shared memory)
-    // in rank order; all remote loads are issued before the first add. The
-    // second barrier keeps every CTA's shared memory alive until all reads are
-    // done.
-    cluster_sync();
+    // k split across the cluster: every CTA finishes 1/slices of the strip's columns. Each
+    // slice pushes its sums for a column chunk into the owning CTA's receive area with
+    // st.async, counted on the owner's reduction barrier; the owner adds the slices in rank
+    // order. The closing rendezvous keeps every CTA alive until all pushes have landed.
+    cluster_wait();
     if (tid == 0) GEMV_TRACE(a, 8);
-    if (tid < kConsumers) {
+    if (tid < CT) {
         const uint32_t me = cluster_rank();
         constexpr int E4 = M * S::NT / 4;  // float4 chunks of the strip's sums
         const int per = (E4 + a.slices - 1) / a.slices;
-        const int e4_begin = static_cast<int>(me) * per;
-        const int e4_end = min(E4, e4_begin + per);
-        float* out4 = red;  // this CTA's drained ring: finished sums of its chunks
-        for (int e4 = e4_begin + tid; e4 < e4_end; e4 += kConsumers) {
-            float4 t[kGemvMaxCluster];
-#pragma unroll
-            for (int r = 0; r < kGemvMaxCluster; ++r)
-                if (r < a.slices) t[r] = ld_dsmem_f4(tot + 4 * e4, r);
-            float4 v = t[0];
-#pragma unroll
-            for (int r = 1; r < kGemvMaxCluster; ++r)
-                if (r < a.slices) {
-                    v.x += t[r].x;
-                    v.y += t[r].y;
-                    v.z += t[r].z;
-                    v.w += t[r].w;
-                }
-            *reinterpret_cast<float4*>(out4 + 4 * (e4 - e4_begin)) = v;
+        const int my_begin = static_cast<int>(me) * per;
+        const int my_cnt = max(0, min(E4, my_begin + per) - my_begin);
+        float* recv = reinterpret_cast<float*>(smem + L::kOffRecv);         // [slice][per * 4]
+        float* recv_ss = recv + M * S::NT + 4 * kGemvMaxCluster;             // [slice][M]
+        if (tid == 0)
+            mbar_arrive_expect_tx(rbar, static_cast<uint32_t>((a.slices - 1) *
+                                                              (my_cnt * 16 + (Norm ? M * 4 : 0))));
+        for (int e4 = tid; e4 < E4; e4 += CT) {
+            const int owner = e4 / per;
+            const float4 v = *reinterpret_cast<const float4*>(tot + 4 * e4);
+            float* dst = recv + (static_cast<int>(me) * per + (e4 - owner * per)) * 4;
+            if (owner == static_cast<int>(me))
+                *reinterpret_cast<float4*>(dst) = v;
+            else
+                st_async_f4(cluster_addr(dst, owner), v, cluster_addr(rbar, owner));
         }
-        float* ss_all = red_ss + kConsumerWarps * M + M;  // past tot_ss
         if (Norm && tid < M) {
-            float t[kGemvMaxCluster];
-#pragma unroll
-            for (int r = 0; r < kGemvMaxCluster; ++r)
-                if (r < a.slices) t[r] = ld_dsmem_f(tot_ss + tid, r);
-            float v = t[0];
-#pragma unroll
-            for (int r = 1; r < kGemvMaxCluster; ++r)
-                if (r < a.slices) v += t[r];
-            ss_all[tid] = v;
+            float* dst = recv_ss + me * M + tid;
+            for (int r = 0; r < a.slices; ++r) {
+                if (r == static_cast<int>(me))
+                    *dst = tot_ss[tid];
+                else
+                    st_async_f(cluster_addr(dst, r), tot_ss[tid], cluster_addr(rbar, r));
+            }
         }
-        named_barrier(1, kConsumers);
+        named_barrier(1, CT);
+        const bool ok = mbar_wait_cluster(rbar, 0, &g_gemv_error);
         if (tid == 0) GEMV_TRACE(a, 9);
-        for (int e = 4 * e4_begin + tid; e < 4 * e4_end; e += kConsumers) {
-            const int r = e / S::NT, col = col0 + e % S::NT;
+        const float* sc = reinterpret_cast<const float*>(smem + L::kOffScale);
+        for (int e = tid; ok && e < 4 * my_cnt; e += CT) {
+            const int eg = 4 * my_begin + e;  // element of the strip's M x NT sums
+            const int r = eg / S::NT, col = col0 + eg % S::NT;
             if (col >= a.n) continue;
-            float v = out4[e - 4 * e4_begin];
-            if constexpr (Q8) v *= reinterpret_cast<const float*>(smem + L::kOffScale)[e % S::NT];
-            if constexpr (Norm) v *= 1.0f / sqrtf(ss_all[r] / static_cast<float>(a.k) + kRmsEps);
+            float v = recv[e];
+            for (int src = 1; src < a.slices; ++src) v += recv[src * per * 4 + e];
+            if constexpr (Q8) v *= sc[eg % S::NT];
+            if constexpr (Norm) {
+                float ssum = recv_ss[r];
+                for (int src = 1; src < a.slices; ++src) ssum += recv_ss[src * M + r];
+                v *= 1.0f / sqrtf(ssum / static_cast<float>(a.k) + kRmsEps);
+            }
             float* o = a.C + static_cast<size_t>(r) * a.n + col;
             *o = a.accumulate ? *o + v : v;
         }
@@ -762,8 +844,8 @@ cudaError_t launch_tma_m(const GemvArgs& a, const CUtensorMap& tmB, const CUtens
         configured |= 1u << dev;
     }
     cudaLaunchAttribute attr[2];
-    cudaLaunchConfig_t cfg =
-        make_config(dim3(a.strips, a.slices), kTmaThreads, L::kBytes, a.stream, a.pdl, attr);
+    cudaLaunchConfig_t cfg = make_config(dim3(a.strips, a.slices), call_threads<M>(), L::kBytes,
+                                         a.stream, a.pdl, attr);
     if (a.slices > 1) {
         // The k slices of a column strip form one cluster (reduced through DSMEM).
         attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;

@@ -67,6 +67,10 @@ struct GemvArgs {
     SplitScratch split;
     cudaStream_t stream = nullptr;
     bool pdl = false;               // launch with programmatic stream serialization
+    // B and scale are not written by the launch before this one on the stream
+    // (LLME_FLAG_WEIGHTS_STATIC): the TMA kernel may then copy weights into shared memory
+    // before griddepcontrol.wait, not only prefetch them into L2.
+    bool weights_static = false;
     // Timeline tracing, used only when gemv.cu is compiled with LLME_GEMV_TRACE: 16 global
     // timer slots per CTA (entry, init, weights issued, activations issued, first data, loop
     // done, CTA sums ready, end, then the cluster reduction's steps). Null and unused in
@@ -80,6 +84,8 @@ constexpr int kGemvRowBytes = 128;
 constexpr int kGemvBoxRows = 128;
 constexpr int kGemvMaxCluster = 8;
 inline int gemv_tma_cols(bool q8) { return q8 ? kGemvRowBytes : kGemvRowBytes / 4; }
+// CTAs per SM of one per-call TMA GEMV grid.
+constexpr int gemv_call_ctas_per_sm(int) { return 2; }
 constexpr int kGemvLdgCols = 32;
 
 // Grouped GEMV: many independent int8 products of the same m (<= 8) in one persistent
