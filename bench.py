@@ -730,93 +730,96 @@ ATTN_METRIC = "decode attention GB/s (KV-cache bytes, 1 row)"
 
 def run_tp_decode(args, world, rank, local):
     """Decode tokens/s of a 7B-shaped int8 transformer (32 layers, dim 4096, 32 heads, hidden
-    11008, vocab 32000; the reference's CudaTransformer architecture, src/cuda_model.cu) split
-    over N GPUs by llm-engine_b200/tp_decode.py: heads by kv head, column-parallel wqkv / w13 /
-    classifier, row-parallel wo / w2 with the NVLink peer all-reduce fused into the residual
-    add. One step = one token at context length --context (a synthetic history in the caches),
-    captured once as a CUDA graph of C-ABI calls. Synthetic weights drawn on the device."""
+    11008, vocab 32000; the reference's CudaTransformer architecture, src/cuda_model.cu) run by
+    the library's C++ engine (llme_model_*), split over N GPUs: heads by kv head,
+    column-parallel wqkv / w13 / classifier, row-parallel wo / w2 with the NVLink peer
+    all-reduce carrying the residual add. One step = one token at context length --context (a
+    synthetic history in the caches), the engine's captured CUDA graph of the step replayed.
+    Synthetic weights drawn on the device."""
+    import time
     import torch
     import llme_b200 as L
-    from checkpoint import Config
-    from tp_decode import TPTransformer
     ctx = args.context
-    cfg = Config(DIM, HIDDEN, args.layers, 32, 32, VOCAB, ctx + 16)
+    cfg = dict(dim=DIM, hidden_dim=HIDDEN, n_layers=args.layers, n_heads=32, n_kv_heads=32,
+               vocab_size=VOCAB, seq_len=ctx + 16)
     comm = None
     if world > 1:
         import torch.distributed as dist
         uid = [L.Comm.unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         comm = L.Comm(world, rank, uid[0], timeout_s=60.0)
-        comm.enable_peer(VOCAB)  # the largest all-reduce: the logits
-    tp = TPTransformer.synthetic(cfg, world, rank, q8=True, comm=comm, seed=5)
-    g = torch.Generator(device="cuda")
-    g.manual_seed(11 + rank)
-    for lw in tp.layers:  # the keys and values of ctx earlier positions
-        lw["kc"][:ctx].uniform_(-1, 1, generator=g)
-        lw["vc"][:ctx].uniform_(-1, 1, generator=g)
-    tp.filled = ctx
-    tp.run([1], ctx)  # eager step: grows every buffer the step uses
-    graph = tp.capture_decode()
-    tp.feed_host[0], tp.feed_host[1] = ctx, 1
+        comm.enable_peer(VOCAB)  # the largest all-reduce of a decode step: the logits
+    model = L.Model.synthetic(cfg, q8=True, world=world, rank=rank, comm=comm, seed=5)
+    model.fill_history(ctx, seed=11)  # the keys and values of ctx earlier positions
+    model.decode(1, ctx)  # eager step (grows every buffer), then the step is captured
+    model.decode(1, ctx)  # one replay through the captured graph
     stream = torch.cuda.Stream()
+    h = stream.cuda_stream
+    for _ in range(args.warmup):
+        model.replay(1, h)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
     sampler = ClockSampler(local)
-    secs = max_over_ranks(time_graph(graph, args.steps, args.warmup, stream, world, sampler),
-                          world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with sampler:
+        e0.record(stream)
+        model.replay(args.steps, h)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    secs = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
     tokens_s = args.steps / secs
-    # Kernels of one token: embed; per layer wqkv, RoPE + cache, attention, wo, w13, SwiGLU,
-    # w2 (each product one launch at m = 1), with N > 1 an all-reduce after wo and w2; the
-    # classifier (+ its all-reduce).
-    launches_per_token = 1 + cfg.n_layers * (7 + (2 if world > 1 else 0)) + 1 + (1 if world > 1 else 0)
-
-    # Bytes one rank streams per token: its int8 shards + scales, its heads' KV history.
-    hs, L_ = cfg.head_size, cfg.n_layers
-    w_bytes = sum(t[0].numel() + 4 * t[1].numel() for lw in tp.layers
-                  for t in (lw["wqkv"], lw["wo"], lw["w13"], lw["w2"]))
-    w_bytes += tp.wcls[0].numel() + 4 * tp.wcls[1].numel()
-    kv_bytes = 2 * (ctx + 1) * tp.nkv * hs * 4 * L_
-    per_gpu = w_bytes + kv_bytes
+    # Kernels of one token: embed; per layer wqkv (+ RoPE + cache write in its epilogue),
+    # attention, wo, w13 (+ SwiGLU in its epilogue), w2, with N > 1 an all-reduce after wo and
+    # w2; the classifier (+ its all-reduce).
+    launches_per_token = (1 + cfg["n_layers"] * (5 + (2 if world > 1 else 0)) + 1
+                          + (1 if world > 1 else 0))
+    w_bytes, kv_per_pos = model.stream_bytes()
+    per_gpu = w_bytes + kv_per_pos * (ctx + 1)
     hbm, hbm_kind = peaks()
     achieved = per_gpu / (secs / args.steps) / 1e9
 
-    # e2e: decode() per token through the same graph -- feed copied in, logits copied out and
-    # the host waiting for them, as a caller of forward() does.
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            tp.forward(1, ctx)
-        barrier(world)
-        torch.cuda.synchronize()
-        import time
-        t0 = time.perf_counter()
-        e2e_steps = min(args.steps, 100)
-        for _ in range(e2e_steps):
-            tp.forward(1, ctx)
-        e2e_secs = max_over_ranks(time.perf_counter() - t0, world)
-    del graph
-    tp.graph = None
+    # e2e: llme_model_decode per token -- the token and position copied in, the logits copied
+    # out and the host waiting for them, as a caller sampling tokens does.
+    for _ in range(3):
+        model.decode(1, ctx)
+    barrier(world)
+    t0 = time.perf_counter()
+    e2e_steps = min(args.steps, 100)
+    for _ in range(e2e_steps):
+        model.decode(1, ctx)
+    e2e_secs = max_over_ranks(time.perf_counter() - t0, world)
     line = {"metric": f"decode tokens/s (7B-shaped int8 transformer, tensor-parallel over N GPUs, "
                       f"context {ctx})",
             "value": round(tokens_s, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 W, f32",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8 W, f32",
             "data": "synthetic: N(0,0.02^2) weights drawn on the device, quantised per column; "
                     "U(-1,1) embedding and KV history",
             "config": {"workload": "tensor-parallel transformer decode, one token per step",
-                       "layers": L_, "dim": DIM, "hidden": HIDDEN, "heads": 32, "vocab": VOCAB,
-                       "context": ctx, "parallelism": f"tp{world}",
-                       "launch": "one CUDA graph per token: embed, per layer rmsnorm+wqkv, "
-                                 "rope+cache, attention, wo+all-reduce+residual, rmsnorm+w13, "
-                                 "swiglu, w2+all-reduce+residual; classifier + all-reduce",
+                       "layers": cfg["n_layers"], "dim": DIM, "hidden": HIDDEN, "heads": 32,
+                       "vocab": VOCAB, "context": ctx, "parallelism": f"tp{world}",
+                       "engine": "the library's C++ transformer engine (llme_model_*)",
+                       "launch": "one CUDA graph per token: embed, per layer rmsnorm+wqkv with "
+                                 "RoPE and the cache write in the GEMV epilogue, attention, "
+                                 "wo (+all-reduce with the residual), rmsnorm+w13 with SwiGLU "
+                                 "in the GEMV epilogue, w2 (+all-reduce); classifier "
+                                 "(+all-reduce)",
                        "l2": f"no flush: {per_gpu / 1e9:.2f} GB per token per GPU (> L2)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_kind": hbm_kind,
-                         "kernel": "whole decode step (per GPU)", "bytes_per_token_per_gpu": per_gpu,
-                         "traffic": None},
+                         "kernel": "whole decode step (per GPU)",
+                         "bytes_per_token_per_gpu": per_gpu, "traffic": None},
             "e2e": {"value": round(e2e_steps / e2e_secs, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4 * VOCAB},
             "gpu_launches": launches_per_token * args.steps, "cpu_baseline": None,
             "cpu_baseline_note": "the reference's CPU Transformer needs a 27 GB fp32 checkpoint at "
                                  "this size; its parity is tested on small checkpoints",
             "clocks": sampler.summary()}
+    model.destroy()
+    torch.cuda.synchronize()
     if comm is not None:
         comm.destroy()
     if rank == 0:

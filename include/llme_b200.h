@@ -52,8 +52,10 @@ enum {
     LLME_E_TIMEOUT = 3,     /* a bounded device-side wait gave up (see llme_device_status) */
     LLME_E_UNSUPPORTED = 4, /* no usable sm_100 device, or a feature this build lacks */
     LLME_E_NCCL = 5,        /* NCCL error in a sharded call */
-    LLME_E_HOST = 6         /* host side: memory exhausted or an internal error; no
+    LLME_E_HOST = 6,        /* host side: memory exhausted or an internal error; no
                                exception ever crosses this interface */
+    LLME_E_RANGE = 7        /* a token or position outside the model's range:
+                               std::out_of_range in the reference (its check_feed) */
 };
 
 /* ---- kernel choice: GpuKernel, cuda_matmul.h:66-72 ---------------------------------- */
@@ -198,9 +200,10 @@ int llme_attention(const llme_attention_shape* s, size_t rows, const int* pos_de
                    float* scratch, int kernel, void* stream);
 
 /* ---- decode-step helpers (the transformer's elementwise steps, one rank's heads) ------------ *
- * The steps of a decoder layer around the matmuls and the attention (the reference's
- * src/cuda_model.cu:22-75 kernels and src/model.cpp:171-184 RoPE tables), for the
- * tensor-parallel transformer: a rank holds nq query heads and nkv kv heads, and a qkv row is
+ * The steps of a decoder layer around the matmuls and the attention for the transformer
+ * engine below (what the reference's CudaTransformer computes between its matmuls,
+ * src/cuda_model.cu:22-75, and its RoPE tables, src/model.cpp:171-184), used for steps wider
+ * than the GEMV's fused epilogues: a rank holds nq query heads and nkv kv heads, and a qkv row is
  * [q: nq * head_size | k: nkv * head_size | v: nkv * head_size]. Positions and token ids are
  * read from device memory, feed[0] = the first position, feed[1 .. n] = the tokens, so one
  * captured graph serves every position. All asynchronous on `stream` (NULL: per-thread
@@ -215,7 +218,8 @@ int llme_embed_rows(size_t n, size_t dim, const int* feed, const float* table, f
 int llme_rope_cache(size_t n, int nq, int nkv, int head_size, const int* feed, const float* cos,
                     const float* sin, float* qkv, float* key_cache, float* value_cache,
                     void* stream);
-/* hb[r][c] = silu(gu[r][c]) * gu[r][hidden + c] for r < n, c < hidden (SwiGLU, gate | up). */
+/* hb[r][c] = silu(gu[r][2c]) * gu[r][2c + 1] for r < n, c < hidden (SwiGLU over interleaved
+ * (gate, up) pairs, the layout the transformer engine keeps w13's columns in). */
 int llme_swiglu(size_t n, size_t hidden, const float* gu, float* hb, void* stream);
 /* Host: the RoPE angle tables (seq_len x head_size / 2 each) with the reference's float
  * expressions, cos[p][j] = cos(p / 10000^(2j / head_size)). */
@@ -304,6 +308,85 @@ int llme_matmul_q8_rowpar(size_t m, size_t n, size_t k_local, const float* A_loc
 int llme_matmul_f32_rowpar(size_t m, size_t n, size_t k_local, const float* A_local,
                            const float* B_local, float* C, int kernel, int accumulate,
                            unsigned flags, llme_comm_t* comm, void* stream);
+
+/* ---- the transformer engine (the reference's CudaTransformer, optionally tensor-parallel) -- *
+ * The reference's Llama-architecture model (src/model.h; its GPU form CudaTransformer,
+ * src/cuda_model.cu:164-270) run by this library from C++: every matmul through the kernels
+ * above, attention through llme_attention, one model object per GPU.
+ *   world = 1: the whole model on the current GPU.
+ *   world > 1: rank `rank` holds a slice of every layer: attention heads split by kv head
+ *     (kv heads [rank * n_kv / world, ...) and the query heads that read them, so RoPE, the
+ *     KV cache and attention stay local); wqkv, w13 and the classifier column-parallel (this
+ *     rank's q, k, v / gate, up / vocabulary columns); wo and w2 row-parallel (the rows that
+ *     multiply this rank's heads / hidden units), each followed by one sum all-reduce of the
+ *     residual stream with the residual add folded in (rank 0 adds it before the sum). int8
+ *     weights are quantised per column over the whole matrix, as the reference's quantize_q8
+ *     does, so every rank's int8 values are exactly the reference's. With a communicator
+ *     (llme_comm_init) the all-reduces run on it; without one, llme_model_group_forward runs
+ *     `world` rank models held by one process on one GPU and sums their partials in rank order
+ *     (the all-reduce's arithmetic), so the decomposition is testable on one device.
+ * A step of at most 8 tokens fuses RoPE with the KV-cache write into the wqkv product and
+ * SwiGLU into the w13 product (the GEMV epilogue; w13's gate and up columns are kept
+ * interleaved in pairs for it); wider steps run them as separate kernels.
+ * Positions follow the reference (its check_feed, src/model.cpp:165-177): tokens in
+ * [0, vocab), pos + n <= seq_len, pos <= the number of positions already cached; otherwise
+ * LLME_E_RANGE. Every call below runs on the model's own stream and returns when the logits
+ * (vocab floats, host memory; the whole vocabulary on every rank) are written. */
+typedef struct {
+    int dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len;
+} llme_model_config;
+typedef struct llme_model llme_model_t;
+
+/* Loads a llama2.c checkpoint (the reference's load_checkpoint, src/model.cpp:113-163: the
+ * same header and size checks and error texts; LLME_E_INVALID) onto the current GPU; q8:
+ * int8 projections. world > 1 without `comm` builds a rank for llme_model_group_forward. */
+int llme_model_load(const char* checkpoint, int q8, int world, int rank, llme_comm_t* comm,
+                    llme_model_t** model);
+/* A model of cfg's shape with weights drawn on the device (projections N(0, 0.02^2),
+ * embedding U(-1, 1), unit RMSNorm weights), each rank drawing only its own slices: for
+ * benchmarks at sizes no host checkpoint is needed for. */
+int llme_model_synthetic(const llme_model_config* cfg, int q8, int world, int rank,
+                         llme_comm_t* comm, unsigned long long seed, llme_model_t** model);
+int llme_model_get_config(const llme_model_t* model, llme_model_config* cfg);
+/* Host only (no GPU): the checkpoint's header and size checks of llme_model_load, and its
+ * configuration. */
+int llme_checkpoint_config(const char* checkpoint, llme_model_config* cfg);
+/* Host only: rank `rank`'s slice of a model split over `world` ranks -- query heads
+ * [q0, q0 + nq), kv heads [kv0, kv0 + nkv), hidden units [h0, h0 + hc), vocabulary
+ * [v0, v0 + vc) (hidden units and vocabulary in contiguous blocks, the first total % world
+ * ranks one larger). LLME_E_INVALID when the kv heads do not split evenly. */
+typedef struct {
+    int q0, nq, kv0, nkv;
+    size_t h0, hc, v0, vc;
+} llme_model_slice;
+int llme_model_partition(const llme_model_config* cfg, int world, int rank, llme_model_slice* out);
+/* This rank's slice: query heads, kv heads, hidden units, vocabulary entries. */
+int llme_model_local(const llme_model_t* model, int* q_heads, int* kv_heads, int* hidden,
+                     int* vocab);
+/* Device bytes this rank streams per decoded token: its projection weights (+ scales) and,
+ * per cached position, its keys and values. */
+int llme_model_stream_bytes(const llme_model_t* model, size_t* weight_bytes,
+                            size_t* kv_bytes_per_position);
+/* Feeds tokens[0..n) at positions [pos, pos + n); logits of the last one. */
+int llme_model_forward(llme_model_t* model, const int* tokens, size_t n, size_t pos,
+                       float* logits);
+/* One token through the decode step captured as a CUDA graph (captured after an eager first
+ * step, and again whenever a longer step has reallocated the buffers it reads or the
+ * library's scratch generation moved, as the reference's CudaTransformer re-captures). */
+int llme_model_decode(llme_model_t* model, int token, size_t pos, float* logits);
+/* How many times the decode graph has been captured (0 before the first llme_model_decode). */
+size_t llme_model_captures(const llme_model_t* model);
+/* Benchmark helpers: fill the first `positions` cache rows of every layer with U(-1, 1) and
+ * count them as cached; replay the captured decode step `times` times on `stream` (its last
+ * token and position, asynchronously, logits left in device memory). */
+int llme_model_fill_history(llme_model_t* model, size_t positions, unsigned long long seed);
+int llme_model_replay(llme_model_t* model, size_t times, void* stream);
+/* One forward over `world` rank models on the current GPU (built with world > 1 and no
+ * communicator, ranks 0..world-1 in order), their partial results summed in rank order at
+ * every reduction point; rank 0's logits. */
+int llme_model_group_forward(llme_model_t* const* ranks, int world, const int* tokens, size_t n,
+                             size_t pos, float* logits);
+int llme_model_destroy(llme_model_t* model);
 
 /* ---- host-side planning, exposed so the dispatch logic can be tested without a GPU -------- */
 enum {

@@ -27,7 +27,7 @@ INCLUDE = os.path.join(REPO, "include")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "lib")
 
-CUDA_SOURCES = ["capi.cu", "gemv.cu", "gemm_simt.cu", "gemm_tc.cu", "gemm_q8_tc.cu", "gemm_q8_skinny.cu", "gemm_f32_skinny.cu", "quant.cu", "decode_ops.cu", "attention.cu", "comm.cu"]
+CUDA_SOURCES = ["capi.cu", "gemv.cu", "gemm_simt.cu", "gemm_tc.cu", "gemm_q8_tc.cu", "gemm_q8_skinny.cu", "gemm_f32_skinny.cu", "quant.cu", "decode_ops.cu", "attention.cu", "comm.cu", "model.cu"]
 CXX_SHIM = "cuda_matmul.cpp"
 LIB_NAME = "libllme_b200.so"
 CXX_LIB_NAME = "libllme_b200_cxx.so"

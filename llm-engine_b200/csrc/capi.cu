@@ -541,7 +541,8 @@ bool missing_pointer(size_t m, size_t n, size_t k, const float* A, const void* B
 }
 
 int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float* scale, float* C,
-        bool q8, int kernel, bool accumulate, const float* rms, unsigned flags, void* stream_ptr) {
+        bool q8, int kernel, bool accumulate, const float* rms, unsigned flags, void* stream_ptr,
+        const GemvEpilogue* epi = nullptr) {
     g_error.clear();
     if (missing_pointer(m, n, k, A, B, scale, C, q8, accumulate))
         return fail(LLME_E_INVALID, "matmul_cuda: null pointer " + shapes(m, n, k));
@@ -565,6 +566,11 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
     llme_plan_t p;
     st = make_plan(in, &p);
     if (st) return st;
+    // A fused epilogue exists only in the TMA GEMV, works on column pairs and writes plainly.
+    if (epi && epi->kind != kEpiStore &&
+        (p.path != LLME_PATH_GEMV_TMA || n % 2 != 0 || accumulate))
+        return fail(LLME_E_UNSUPPORTED, "matmul: fused epilogue needs the TMA GEMV path, an even n "
+                                        "and no accumulation " + shapes(m, n, k));
     if (p.path == LLME_PATH_NONE) return LLME_OK;
     if (p.path == LLME_PATH_ZERO) {
         cudaError_t e = cudaMemsetAsync(C, 0, m * n * sizeof(float), stream);
@@ -615,6 +621,7 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
         // griddepcontrol.wait it reads nothing but its weights (and only with
         // LLME_FLAG_WEIGHTS_STATIC; otherwise it merely prefetches them into L2).
         g.weights_static = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
+        if (epi) g.epi = *epi;
         g.pdl = p.path == LLME_PATH_GEMV_TMA || g.weights_static;
         if (p.path == LLME_PATH_GEMV_TMA) {
             CUtensorMap tmB, tmA, tmW;
@@ -1186,6 +1193,21 @@ int run_product(size_t m, size_t n, size_t k, const float* A, const void* B, con
                 void* stream) {
     return run(m, n, k, A, B, scale, C, q8, kernel, accumulate, rms, flags, stream);
 }
+int run_product_epilogue(size_t m, size_t n, size_t k, const float* A, const void* B,
+                         const float* scale, float* C, bool q8, const float* rms, unsigned flags,
+                         void* stream, const GemvEpilogue& epi) {
+    return run(m, n, k, A, B, scale, C, q8, LLME_KERNEL_AUTOMATIC, false, rms, flags, stream, &epi);
+}
+int plan_product(size_t m, size_t n, size_t k, bool q8, const void* A, const void* B,
+                 const float* rms, llme_plan_t* p) {
+    int dev = 0, sms = 0;
+    int st = current_device(&dev);
+    if (!st) st = device_sms(dev, &sms);
+    if (st) return st;
+    PlanIn in{m, n, k, q8, LLME_KERNEL_AUTOMATIC, false, reinterpret_cast<uintptr_t>(A),
+              reinterpret_cast<uintptr_t>(B), reinterpret_cast<uintptr_t>(rms), sms, math_mode()};
+    return make_plan(in, p);
+}
 }  // namespace llme
 
 extern "C" {
@@ -1340,7 +1362,7 @@ int llme_synchronize(void) {
         const unsigned dev_err =
             read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error() |
             read_and_clear_q8tc_error() | read_and_clear_skinny_error() | read_and_clear_attn_error() |
-            read_and_clear_f32sk_error();
+            read_and_clear_f32sk_error() | read_and_clear_ops_error();
         if (dev_err) return fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up");
         return LLME_OK;
     });
@@ -1367,7 +1389,7 @@ int llme_device_status(void) {
         const unsigned dev_err =
             read_and_clear_gemv_error() | read_and_clear_tiled_error() | read_and_clear_tc_error() |
             read_and_clear_q8tc_error() | read_and_clear_skinny_error() | read_and_clear_attn_error() |
-            read_and_clear_f32sk_error();
+            read_and_clear_f32sk_error() | read_and_clear_ops_error();
         return dev_err ? fail(LLME_E_TIMEOUT, "device: a bounded wait in a kernel gave up") : LLME_OK;
     });
 }

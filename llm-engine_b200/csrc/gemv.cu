@@ -219,6 +219,38 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) 
                  "r"(bytes)
                  : "memory");
 }
+// The fused epilogues (GemvEpilogue): a finished pair of adjacent output columns (col even)
+// of row r, already scaled.
+__device__ __forceinline__ void epilogue_pair(const GemvArgs& a, int r, int col, float v0, float v1) {
+    const GemvEpilogue& e = a.epi;
+    if (e.kind == kEpiSwiglu) {
+        const float sig = 1.0f / (1.0f + expf(-v0));
+        e.out[static_cast<size_t>(r) * (a.n / 2) + col / 2] = v0 * sig * v1;
+        return;
+    }
+    // kEpiRopeCache
+    const int hs = e.head_size, head = col / hs;
+    const int pos = e.feed[0] + r;
+    const size_t kvd = static_cast<size_t>(e.nkv) * hs;
+    const int qd = e.nq * hs;
+    if (head < e.nq + e.nkv) {
+        const int j = (col % hs) / 2;
+        const float c = e.cos[static_cast<size_t>(pos) * (hs / 2) + j];
+        const float sn = e.sin[static_cast<size_t>(pos) * (hs / 2) + j];
+        const float r0 = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, sn));
+        const float r1 = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, c));
+        v0 = r0;
+        v1 = r1;
+        if (head >= e.nq)
+            *reinterpret_cast<float2*>(e.key_cache + static_cast<size_t>(pos) * kvd + (col - qd)) =
+                make_float2(v0, v1);
+    } else {
+        *reinterpret_cast<float2*>(e.value_cache + static_cast<size_t>(pos) * kvd +
+                                   (col - qd - static_cast<int>(kvd))) = make_float2(v0, v1);
+    }
+    *reinterpret_cast<float2*>(a.C + static_cast<size_t>(r) * a.n + col) = make_float2(v0, v1);
+}
+
 // Writes C for a CTA's column strip from M x NT sums that are already complete
 // (tot, shared memory) -- the kernels' common epilogue.
 // sscale: the strip's column scales already in shared memory (int8 TMA kernel), or null to
@@ -227,6 +259,24 @@ template <int M, int NT, bool Q8, bool Norm>
 __device__ __forceinline__ void store_strip(const float* tot, const float* tot_ss, const GemvArgs& a,
                                             int col0, int tid, int nthreads,
                                             const float* sscale = nullptr) {
+    if (a.epi.kind != kEpiStore) {
+        for (int e = 2 * tid; e < M * NT; e += 2 * nthreads) {
+            const int r = e / NT, col = col0 + e % NT;
+            if (col >= a.n) continue;
+            float v0 = tot[e], v1 = tot[e + 1];
+            if constexpr (Q8) {
+                v0 *= sscale ? sscale[e % NT] : __ldg(a.scale + col);
+                v1 *= sscale ? sscale[e % NT + 1] : __ldg(a.scale + col + 1);
+            }
+            if constexpr (Norm) {
+                const float inv = 1.0f / sqrtf(tot_ss[r] / static_cast<float>(a.k) + kRmsEps);
+                v0 *= inv;
+                v1 *= inv;
+            }
+            epilogue_pair(a, r, col, v0, v1);
+        }
+        return;
+    }
     for (int e = tid; e < M * NT; e += nthreads) {
         const int r = e / NT, col = col0 + e % NT;
         if (col >= a.n) continue;
@@ -490,7 +540,31 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
         const bool ok = mbar_wait_cluster(rbar, 0, &g_gemv_error);
         if (tid == 0) GEMV_TRACE(a, 9);
         const float* sc = reinterpret_cast<const float*>(smem + L::kOffScale);
-        for (int e = tid; ok && e < 4 * my_cnt; e += CT) {
+        // Fused epilogues work on pairs of columns; chunks start at multiples of four
+        // elements, so a pair never straddles two owners.
+        for (int e = 2 * tid; a.epi.kind != kEpiStore && ok && e < 4 * my_cnt; e += 2 * CT) {
+            const int eg = 4 * my_begin + e;
+            const int r = eg / S::NT, col = col0 + eg % S::NT;
+            if (col >= a.n) continue;
+            float v0 = recv[e], v1 = recv[e + 1];
+            for (int src = 1; src < a.slices; ++src) {
+                v0 += recv[src * per * 4 + e];
+                v1 += recv[src * per * 4 + e + 1];
+            }
+            if constexpr (Q8) {
+                v0 *= sc[eg % S::NT];
+                v1 *= sc[eg % S::NT + 1];
+            }
+            if constexpr (Norm) {
+                float ssum = recv_ss[r];
+                for (int src = 1; src < a.slices; ++src) ssum += recv_ss[src * M + r];
+                const float inv = 1.0f / sqrtf(ssum / static_cast<float>(a.k) + kRmsEps);
+                v0 *= inv;
+                v1 *= inv;
+            }
+            epilogue_pair(a, r, col, v0, v1);
+        }
+        for (int e = tid; a.epi.kind == kEpiStore && ok && e < 4 * my_cnt; e += CT) {
             const int eg = 4 * my_begin + e;  // element of the strip's M x NT sums
             const int r = eg / S::NT, col = col0 + eg % S::NT;
             if (col >= a.n) continue;

@@ -10,6 +10,8 @@
 #include <new>
 #include <string>
 
+#include "llme_b200.h"
+
 namespace llme {
 
 // The calling thread's llme_last_error message (defined in capi.cu); return `code`.
@@ -52,7 +54,30 @@ struct SplitScratch {
     unsigned* counters = nullptr; // one per tile, zero between launches
 };
 
+// What the per-call TMA GEMV (m <= 8) does with a finished pair of adjacent output columns
+// (2c, 2c + 1) of row r instead of writing C as is; the decode step of the transformer engine
+// fuses its elementwise work here.
+enum GemvEpilogueKind { kEpiStore = 0, kEpiRopeCache = 1, kEpiSwiglu = 2 };
+struct GemvEpilogue {
+    int kind = kEpiStore;
+    // kEpiRopeCache: C's columns are [q: nq heads | k: nkv heads | v: nkv heads] of head_size
+    // floats. q and k pairs are rotated by the angle of the pair's index within its head at
+    // row r's position feed[0] + r (cos / sin: rows of head_size / 2 per position) and written
+    // to C; k and v pairs are also written to the caches (rows of nkv * head_size floats) at
+    // that position.
+    int nq = 0, nkv = 0, head_size = 0;
+    const int* feed = nullptr;
+    const float* cos = nullptr;
+    const float* sin = nullptr;
+    float* key_cache = nullptr;
+    float* value_cache = nullptr;
+    // kEpiSwiglu: C's columns hold (gate, up) of hidden unit c at 2c and 2c + 1; instead of C,
+    // out[r][c] = silu(gate) * up (rows of n / 2 floats).
+    float* out = nullptr;
+};
+
 struct GemvArgs {
+    GemvEpilogue epi;
     int m = 0, n = 0, k = 0;
     const float* A = nullptr;
     const void* B = nullptr;        // int8 or fp32, k x n
@@ -296,8 +321,25 @@ cudaError_t launch_embed_rows(int n, int dim, const int* feed, const float* tabl
 cudaError_t launch_rope_cache(int n, int nq, int nkv, int head_size, const int* feed,
                               const float* cos_t, const float* sin_t, float* qkv, float* key_cache,
                               float* value_cache, cudaStream_t stream);
+// SwiGLU over interleaved (gate, up) column pairs: hb[r][c] = silu(gu[r][2c]) * gu[r][2c + 1].
 cudaError_t launch_swiglu(int n, int hidden, const float* gu, float* hb, cudaStream_t stream);
 void rope_tables(size_t seq_len, size_t head_size, float* cos_out, float* sin_out);
+// bufs_dev: a device array of `ranks` buffer pointers; every buffer becomes the rank-order sum.
+cudaError_t launch_rank_sum(float* const* bufs_dev, int ranks, size_t count, cudaStream_t stream);
+// Synthetic weights drawn on the device from (seed, element index): N(0, stddev^2), U(lo, hi).
+cudaError_t launch_fill_normal(float* out, size_t count, uint64_t seed, float stddev,
+                               cudaStream_t stream);
+cudaError_t launch_fill_uniform(float* out, size_t count, uint64_t seed, float lo, float hi,
+                                cudaStream_t stream);
+unsigned read_and_clear_ops_error();
+
+// A product with a fused GEMV epilogue (m <= 8 on the TMA GEMV path only; LLME_E_UNSUPPORTED
+// before any launch otherwise), and the plan llme_matmul_* would follow for a product.
+int run_product_epilogue(size_t m, size_t n, size_t k, const float* A, const void* B,
+                         const float* scale, float* C, bool q8, const float* rms, unsigned flags,
+                         void* stream, const GemvEpilogue& epi);
+int plan_product(size_t m, size_t n, size_t k, bool q8, const void* A, const void* B,
+                 const float* rms, llme_plan_t* p);
 
 // out = rmsnorm(A) * w per row (eps 1e-5), m rows of k.
 cudaError_t launch_rmsnorm_rows(int m, int k, const float* A, const float* w, float* out,

@@ -27,7 +27,7 @@ PATHS = {0: "none", 1: "zero", 2: "naive", 3: "gemv_tma", 4: "gemv_ldg", 5: "til
 MATH_TENSOR, MATH_FP32 = 0, 1
 FLAG_WEIGHTS_STATIC = 1
 
-OK, E_INVALID, E_CUDA, E_TIMEOUT, E_UNSUPPORTED, E_NCCL, E_HOST = range(7)
+OK, E_INVALID, E_CUDA, E_TIMEOUT, E_UNSUPPORTED, E_NCCL, E_HOST, E_RANGE = range(8)
 
 # cudaStreamLegacy: torch's default stream has handle 0, which the C ABI would read as
 # "per-thread default stream"; pass the legacy handle instead so both sides agree.
@@ -69,6 +69,25 @@ class Q8Product(ctypes.Structure):
                 ("accumulate", ctypes.c_int)]
 
 
+class ModelConfig(ctypes.Structure):
+    """llme_model_config: the llama2.c header fields."""
+    _fields_ = [(f, ctypes.c_int) for f in ("dim", "hidden_dim", "n_layers", "n_heads",
+                                            "n_kv_heads", "vocab_size", "seq_len")]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+class ModelSlice(ctypes.Structure):
+    """llme_model_slice: one rank's heads, hidden units and vocabulary."""
+    _fields_ = [("q0", ctypes.c_int), ("nq", ctypes.c_int), ("kv0", ctypes.c_int),
+                ("nkv", ctypes.c_int), ("h0", ctypes.c_size_t), ("hc", ctypes.c_size_t),
+                ("v0", ctypes.c_size_t), ("vc", ctypes.c_size_t)]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
 _lib = None
 
 
@@ -102,6 +121,29 @@ def load() -> ctypes.CDLL:
     lib.llme_rope_cache.argtypes = [sz, i, i, i, vp, vp, vp, vp, vp, vp, vp]
     lib.llme_swiglu.argtypes = [sz, sz, vp, vp, vp]
     lib.llme_rope_tables.argtypes = [sz, sz, vp, vp]
+    mp, ip = ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)
+    cfgp = ctypes.POINTER(ModelConfig)
+    lib.llme_model_load.argtypes = [ctypes.c_char_p, i, i, i, vp, ctypes.POINTER(vp)]
+    lib.llme_model_synthetic.argtypes = [cfgp, i, i, i, vp, ctypes.c_ulonglong, ctypes.POINTER(vp)]
+    lib.llme_checkpoint_config.argtypes = [ctypes.c_char_p, cfgp]
+    lib.llme_model_partition.argtypes = [cfgp, i, i, ctypes.POINTER(ModelSlice)]
+    lib.llme_model_get_config.argtypes = [mp, cfgp]
+    lib.llme_model_local.argtypes = [mp, ip, ip, ip, ip]
+    lib.llme_model_stream_bytes.argtypes = [mp, ctypes.POINTER(sz), ctypes.POINTER(sz)]
+    lib.llme_model_forward.argtypes = [mp, vp, sz, sz, vp]
+    lib.llme_model_decode.argtypes = [mp, i, sz, vp]
+    lib.llme_model_captures.argtypes = [mp]
+    lib.llme_model_captures.restype = sz
+    lib.llme_model_fill_history.argtypes = [mp, sz, ctypes.c_ulonglong]
+    lib.llme_model_replay.argtypes = [mp, sz, vp]
+    lib.llme_model_group_forward.argtypes = [ctypes.POINTER(vp), i, vp, sz, sz, vp]
+    lib.llme_model_destroy.argtypes = [mp]
+    for f in ("llme_model_load", "llme_model_synthetic", "llme_checkpoint_config",
+              "llme_model_partition", "llme_model_get_config", "llme_model_local",
+              "llme_model_stream_bytes", "llme_model_forward", "llme_model_decode",
+              "llme_model_fill_history", "llme_model_replay", "llme_model_group_forward",
+              "llme_model_destroy"):
+        getattr(lib, f).restype = i
     for f in ("llme_embed_rows", "llme_rope_cache", "llme_swiglu", "llme_rope_tables"):
         getattr(lib, f).restype = i
     lib.llme_batch_q8_create.argtypes = [ctypes.POINTER(vp), sz, sz, ctypes.POINTER(Q8Product)]
@@ -158,6 +200,8 @@ def _check(status: int) -> None:
         raise DeviceTimeout(msg)
     if status == E_HOST:
         raise MemoryError(msg) if "out of memory" in msg else RuntimeError(msg)
+    if status == E_RANGE:
+        raise IndexError(msg)
     raise CudaError(msg or f"cuda: error {status}")
 
 
@@ -435,3 +479,115 @@ def matmul(A, B, scale=None, C=None, kernel="automatic", accumulate: bool = Fals
         matmul_cuda_f32(m, n, k, A.data_ptr(), B.data_ptr(), C.data_ptr(), kernel, accumulate,
                         rms, flags, h)
     return C
+
+
+# ---- the transformer engine (C++, model.cu) ----------------------------------------------------
+
+def _config(cfg) -> "ModelConfig":
+    if isinstance(cfg, ModelConfig):
+        return cfg
+    if isinstance(cfg, dict):
+        return ModelConfig(**cfg)
+    return ModelConfig(*cfg)
+
+
+def checkpoint_config(path: str) -> dict:
+    """The header and size checks of llme_model_load on the host (no GPU); the configuration."""
+    c = ModelConfig()
+    _check(load().llme_checkpoint_config(path.encode(), ctypes.byref(c)))
+    return c.as_dict()
+
+
+def model_partition(cfg, world: int, rank: int) -> dict:
+    """Rank `rank`'s query heads, kv heads, hidden units and vocabulary (host only)."""
+    out = ModelSlice()
+    _check(load().llme_model_partition(ctypes.byref(_config(cfg)), world, rank, ctypes.byref(out)))
+    return out.as_dict()
+
+
+class Model:
+    """One rank (or the whole) of the reference's transformer on the current GPU, run by the
+    library's C++ engine (llme_model_*). forward()/decode() return the last row's logits as a
+    numpy array (the whole vocabulary on every rank)."""
+
+    def __init__(self, handle: int):
+        self.handle = handle
+        c = ModelConfig()
+        _check(load().llme_model_get_config(handle, ctypes.byref(c)))
+        self.config = c.as_dict()
+        nq, nkv, hc, vc = (ctypes.c_int() for _ in range(4))
+        _check(load().llme_model_local(handle, ctypes.byref(nq), ctypes.byref(nkv),
+                                       ctypes.byref(hc), ctypes.byref(vc)))
+        self.local = {"q_heads": nq.value, "kv_heads": nkv.value, "hidden": hc.value,
+                      "vocab": vc.value}
+
+    @classmethod
+    def load(cls, path: str, q8: bool = False, world: int = 1, rank: int = 0, comm=None):
+        h = ctypes.c_void_p()
+        _check(load().llme_model_load(path.encode(), int(bool(q8)), world, rank,
+                                      comm.handle if comm is not None else None, ctypes.byref(h)))
+        return cls(h.value)
+
+    @classmethod
+    def synthetic(cls, cfg, q8: bool = True, world: int = 1, rank: int = 0, comm=None,
+                  seed: int = 0):
+        h = ctypes.c_void_p()
+        _check(load().llme_model_synthetic(ctypes.byref(_config(cfg)), int(bool(q8)), world, rank,
+                                           comm.handle if comm is not None else None, seed,
+                                           ctypes.byref(h)))
+        return cls(h.value)
+
+    def _logits(self):
+        import numpy as np
+        return np.zeros(self.config["vocab_size"], np.float32)
+
+    def forward(self, tokens, pos: int):
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        out = self._logits()
+        _check(load().llme_model_forward(self.handle, t.ctypes.data, t.size, pos,
+                                          out.ctypes.data))
+        return out
+
+    def decode(self, token: int, pos: int):
+        out = self._logits()
+        _check(load().llme_model_decode(self.handle, int(token), pos, out.ctypes.data))
+        return out
+
+    @property
+    def captures(self) -> int:
+        return int(load().llme_model_captures(self.handle))
+
+    def stream_bytes(self) -> tuple[int, int]:
+        w, kv = ctypes.c_size_t(), ctypes.c_size_t()
+        _check(load().llme_model_stream_bytes(self.handle, ctypes.byref(w), ctypes.byref(kv)))
+        return w.value, kv.value
+
+    def fill_history(self, positions: int, seed: int = 0) -> None:
+        _check(load().llme_model_fill_history(self.handle, positions, seed))
+
+    def replay(self, times: int, stream: int | None = None) -> None:
+        _check(load().llme_model_replay(self.handle, times, stream or None))
+
+    @staticmethod
+    def group_forward(models, tokens, pos: int):
+        """One forward over emulated ranks (Models built with world > 1 and no communicator,
+        ranks 0..world-1); their partials summed in rank order. Rank 0's logits."""
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        arr = (ctypes.c_void_p * len(models))(*[m.handle for m in models])
+        out = models[0]._logits()
+        _check(load().llme_model_group_forward(arr, len(models), t.ctypes.data, t.size, pos,
+                                                out.ctypes.data))
+        return out
+
+    def destroy(self) -> None:
+        if self.handle:
+            _check(load().llme_model_destroy(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass

@@ -400,7 +400,7 @@ def test_status_codes_match_the_header():
     codes = dict((name, int(v)) for name, v in re.findall(r"\b(LLME_(?:OK|E_\w+))\s*=\s*(\d+)", text))
     assert codes == {"LLME_OK": L.OK, "LLME_E_INVALID": L.E_INVALID, "LLME_E_CUDA": L.E_CUDA,
                      "LLME_E_TIMEOUT": L.E_TIMEOUT, "LLME_E_UNSUPPORTED": L.E_UNSUPPORTED,
-                     "LLME_E_NCCL": L.E_NCCL, "LLME_E_HOST": L.E_HOST}
+                     "LLME_E_NCCL": L.E_NCCL, "LLME_E_HOST": L.E_HOST, "LLME_E_RANGE": L.E_RANGE}
 
 
 def test_no_exception_crosses_the_c_boundary():
@@ -408,7 +408,7 @@ def test_no_exception_crosses_the_c_boundary():
     # exception into LLME_E_HOST; the source holds one guard per such function.
     csrc = os.path.join(REPO, "llm-engine_b200", "csrc")
     unguarded = []
-    for name in ("capi.cu", "comm.cu", "attention.cu"):
+    for name in ("capi.cu", "comm.cu", "attention.cu", "model.cu"):
         src = open(os.path.join(csrc, name)).read()
         body = src[src.index('extern "C" {'):]
         for m in re.finditer(r"^int (llme_\w+)\([^{]*\) \{\n(.*?)^\}", body, re.S | re.M):

@@ -1,8 +1,9 @@
-"""llm-engine_b200/checkpoint.py against the reference's own load_checkpoint (src/model.cpp:
-113-169, compiled into oracle/_ref/libref_model.so) on corrupted llama2.c files: header
-fields set to zero, negative or inconsistent values, truncated or over-long files, a missing
-file. Both loaders must accept the same files and reject the others with the same message.
-No GPU."""
+"""The transformer engine's C++ checkpoint reader (llme_checkpoint_config: the header and size
+checks llme_model_load makes, llm-engine_b200/csrc/model.cu) against the reference's own
+load_checkpoint (src/model.cpp:113-163, compiled into oracle/_ref/libref_model.so) on corrupted
+llama2.c files: header fields set to zero, negative or inconsistent values, truncated or
+over-long files, a missing file. Both readers must accept the same files and reject the others
+with the same message. No GPU."""
 from __future__ import annotations
 
 import os
@@ -12,7 +13,7 @@ import pytest
 from hypothesis import given, settings, strategies as st
 
 import oracle
-from checkpoint import load_checkpoint
+import llme_b200 as L
 from model_fixture import make_model, write_checkpoint
 
 pytestmark = pytest.mark.skipif(not oracle.RefModel.available(), reason="reference model not built")
@@ -20,9 +21,9 @@ pytestmark = pytest.mark.skipif(not oracle.RefModel.available(), reason="referen
 
 def outcome_ours(path):
     try:
-        load_checkpoint(path)
+        L.checkpoint_config(path)
         return "ok"
-    except RuntimeError as e:
+    except L.InvalidArgument as e:
         return str(e)
 
 

@@ -1,15 +1,20 @@
-"""The tensor-parallel transformer (llm-engine_b200/tp_decode.py) against the reference's own CPU
-Transformer (src/model.cpp, built into oracle/_ref) on the same llama2.c checkpoint and token
-stream: token-by-token decoding, then a prefill continuing the cache, fp32 and int8 weights.
+"""The transformer engine (the library's C++ llme_model_*, llm-engine_b200/csrc/model.cu) against
+the reference's own CPU Transformer (src/model.cpp, built into oracle/_ref) on the same llama2.c
+checkpoint and token stream: token-by-token decoding, prefills continuing the cache (three
+tokens: the fused GEMV epilogues; nine tokens: the separate RoPE and SwiGLU kernels), fp32 and
+int8 weights.
 
 * one rank: every step's logits within the reference model test's tolerance
   (tests/test_cuda_model.cpp:30, 1e-4, here relative to the largest logit);
-* 2 and 4 ranks emulated in one process on one GPU: each rank holds only its heads, hidden
-  slice and vocabulary slice; the test sums the yielded buffers over ranks in rank order, as
-  the all-reduce does -- the decomposition must reproduce the unsharded model;
+* 2 and 4 ranks emulated in one process on one GPU (llme_model_group_forward): each rank holds
+  only its heads, hidden slice and vocabulary slice, and the partials are summed in rank order
+  at every reduction point, as the all-reduce does -- the decomposition must reproduce the
+  unsharded model;
+* the one-token step captured as a CUDA graph and replayed at later and rewound positions,
+  and captured again after a longer prefill reallocated its buffers;
 * 2 GPUs (skipped with fewer): one process per GPU, the library's communicator with its
-  NVLink peer all-reduce fused into the residual add; both ranks must end with the same
-  logits. Child processes keep NVLS off (NCCL_NVLS_ENABLE=0).
+  NVLink peer all-reduce; both ranks must end with the same logits. Child processes keep NVLS
+  off (NCCL_NVLS_ENABLE=0).
 """
 from __future__ import annotations
 
@@ -23,9 +28,7 @@ import pytest
 
 import oracle
 import llme_b200 as L
-from checkpoint import load_checkpoint
 from model_fixture import make_model, write_checkpoint
-from tp_decode import TPTransformer
 
 torch = pytest.importorskip("torch")
 pytestmark = [pytest.mark.gpu,
@@ -33,8 +36,10 @@ pytestmark = [pytest.mark.gpu,
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 ENV = dict(os.environ, NCCL_NVLS_ENABLE="0")
-# token-by-token over the first positions, then a prefill of the next three, then one more
-STREAM = [([5], 0), ([17], 1), ([2], 2), ([44], 3), ([9], 4), ([31, 0, 12], 5), ([7], 8)]
+# token-by-token over the first positions, a prefill of the next three, one more token, then a
+# nine-token prefill that rewinds to position 4
+STREAM = [([5], 0), ([17], 1), ([2], 2), ([44], 3), ([9], 4), ([31, 0, 12], 5), ([7], 8),
+          ([3, 1, 4, 1, 5, 9, 2, 6, 5], 4)]
 MODELS = {"gqa": dict(dim=64, hidden=96, layers=2, heads=8, kv_heads=4, vocab=50, seq_len=16),
           "mha": dict(dim=64, hidden=80, layers=2, heads=4, kv_heads=4, vocab=53, seq_len=16)}
 
@@ -56,31 +61,14 @@ def checkpoint(tmp_path, name, seed=7):
     return p
 
 
-def emulated_run(shards, tokens, pos):
-    """One pass over shards that stand for the ranks of one model: at every reduction point
-    the yielded buffers are summed in rank order and the sum written back to each."""
-    gens = [s.steps(tokens, pos) for s in shards]
-    while True:
-        bufs = [next(g, None) for g in gens]
-        if all(b is None for b in bufs):
-            break
-        assert all(b is not None for b in bufs), "ranks disagree on the reduction points"
-        total = bufs[0].clone()
-        for b in bufs[1:]:
-            total += b
-        for b in bufs:
-            b.copy_(total)
-    return shards[0].logits.cpu().numpy()
-
-
 @pytest.mark.parametrize("q8", [False, True])
 @pytest.mark.parametrize("name", ["gqa", "mha"])
 def test_one_rank_matches_the_reference_model(tmp_path, name, q8):
     p = checkpoint(tmp_path, name)
     ref = oracle.RefModel(p, q8)
-    tp = TPTransformer(load_checkpoint(p), q8=q8)
+    model = L.Model.load(p, q8=q8)
     for tokens, pos in STREAM:
-        got, want = tp.run(tokens, pos), ref.run(tokens, pos)
+        got, want = model.forward(tokens, pos), ref.run(tokens, pos)
         assert close(got, want), (tokens, pos, float(np.abs(got - want).max()))
 
 
@@ -89,60 +77,83 @@ def test_one_rank_matches_the_reference_model(tmp_path, name, q8):
 def test_emulated_ranks_match_the_reference_model(tmp_path, world, q8):
     p = checkpoint(tmp_path, "gqa", seed=8)
     ref = oracle.RefModel(p, q8)
-    ck = load_checkpoint(p)
-    shards = [TPTransformer(ck, world=world, rank=r, q8=q8) for r in range(world)]
-    assert sum(s.nq for s in shards) == ck.config.n_heads
-    assert all(s.hc < ck.config.hidden_dim for s in shards)
+    ranks = [L.Model.load(p, q8=q8, world=world, rank=r) for r in range(world)]
+    cfg = ranks[0].config
+    assert sum(r.local["q_heads"] for r in ranks) == cfg["n_heads"]
+    assert sum(r.local["hidden"] for r in ranks) == cfg["hidden_dim"]
+    assert sum(r.local["vocab"] for r in ranks) == cfg["vocab_size"]
     for tokens, pos in STREAM:
-        got, want = emulated_run(shards, tokens, pos), ref.run(tokens, pos)
+        got, want = L.Model.group_forward(ranks, tokens, pos), ref.run(tokens, pos)
         assert close(got, want), (world, tokens, pos, float(np.abs(got - want).max()))
+    with pytest.raises(L.InvalidArgument):
+        ranks[1].forward([1], 0)  # a rank without a communicator runs only in its group
 
 
 @pytest.mark.parametrize("q8", [False, True])
 def test_graph_decode_matches_the_reference_model(tmp_path, q8):
-    # The one-token step captured once (after an eager step) and replayed at later positions,
+    # The one-token step runs eagerly once and is captured, then replayed at later positions,
     # including a rewind that overwrites a cached position, as the reference's graph serves
     # every position (src/cuda_model.cu:190-220).
     p = checkpoint(tmp_path, "gqa", seed=10)
     ref = oracle.RefModel(p, q8)
-    tp = TPTransformer(load_checkpoint(p), q8=q8)
-    assert close(tp.run([3], 0), ref.run([3], 0))
-    tp.capture_decode()
-    for token, pos in [(8, 1), (21, 2), (4, 3), (40, 2), (6, 3), (11, 4)]:
-        got, want = tp.forward(token, pos), ref.run([token], pos)
+    model = L.Model.load(p, q8=q8)
+    assert model.captures == 0
+    for token, pos in [(3, 0), (8, 1), (21, 2), (4, 3), (40, 2), (6, 3), (11, 4)]:
+        got, want = model.decode(token, pos), ref.run([token], pos)
         assert close(got, want), (token, pos, float(np.abs(got - want).max()))
+        assert model.captures == 1
+    model.replay(3)  # more replays of the last step on the current stream
+    torch.cuda.synchronize()
+    L.device_status()
 
 
 @pytest.mark.parametrize("q8", [False, True])
 def test_graph_recaptured_after_a_longer_prefill(tmp_path, q8):
-    # A prefill longer than any run before replaces the activation buffers the graph points
-    # at; the next decode() sees the generation move and captures again, as the reference's
-    # CudaTransformer does (src/cuda_model.cu:175-177, 196-227).
+    # A prefill longer than any step before replaces the activation buffers the graph points
+    # at; the next decode sees the buffers' generation move and captures again, as the
+    # reference's CudaTransformer does (src/cuda_model.cu:175-177, 196-227).
     p = checkpoint(tmp_path, "mha", seed=12)
     ref = oracle.RefModel(p, q8)
-    tp = TPTransformer(load_checkpoint(p), q8=q8)
-    assert close(tp.run([3], 0), ref.run([3], 0))
-    tp.capture_decode()
-    captured = tp.graph_generation
-    assert close(tp.forward(8, 1), ref.run([8], 1))
-    assert tp.graph_generation == captured
-    assert close(tp.prefill([4, 9, 1, 30], 2), ref.run([4, 9, 1, 30], 2))
-    assert tp.buffers_generation() != captured
+    model = L.Model.load(p, q8=q8)
+    assert close(model.decode(3, 0), ref.run([3], 0))
+    assert close(model.decode(8, 1), ref.run([8], 1))
+    assert model.captures == 1
+    assert close(model.forward([4, 9, 1, 30], 2), ref.run([4, 9, 1, 30], 2))
     for token, pos in [(5, 6), (12, 7), (2, 8)]:
-        got, want = tp.forward(token, pos), ref.run([token], pos)
+        got, want = model.decode(token, pos), ref.run([token], pos)
         assert close(got, want), (token, pos, float(np.abs(got - want).max()))
-    assert tp.graph_generation == tp.buffers_generation() != captured
+    assert model.captures == 2
 
 
 def test_positions_are_checked(tmp_path):
-    tp = TPTransformer(load_checkpoint(checkpoint(tmp_path, "gqa")))
+    model = L.Model.load(checkpoint(tmp_path, "gqa"))
     with pytest.raises(IndexError):
-        tp.run([1], 3)          # skips cached positions
+        model.forward([1], 3)          # skips cached positions
     with pytest.raises(IndexError):
-        tp.run([50], 0)         # outside the vocabulary
-    tp.run([1], 0)
+        model.forward([50], 0)         # outside the vocabulary
     with pytest.raises(IndexError):
-        tp.run([1] * 16, 1)     # past seq_len
+        model.decode(-1, 0)
+    model.forward([1], 0)
+    with pytest.raises(IndexError):
+        model.forward([1] * 16, 1)     # past seq_len
+    with pytest.raises(L.InvalidArgument):
+        model.forward([], 0)
+
+
+def test_synthetic_model_runs_and_repeats():
+    # The benchmark's model: weights drawn on the device, a cache history filled, one token
+    # decoded twice at the same position gives the same logits bit for bit (eager, then the
+    # captured graph).
+    cfg = dict(dim=256, hidden_dim=512, n_layers=2, n_heads=4, n_kv_heads=2, vocab_size=1000,
+               seq_len=64)
+    model = L.Model.synthetic(cfg, q8=True, seed=3)
+    model.fill_history(40, seed=1)
+    a = model.decode(7, 40)
+    b = model.decode(7, 40)
+    assert np.isfinite(a).all() and np.abs(a).max() > 0
+    np.testing.assert_array_equal(a, b)
+    w, kv = model.stream_bytes()
+    assert w > 2 * 256 * 256 and kv == 2 * 2 * 2 * 64 * 4
 
 
 WORKER = r"""
@@ -151,8 +162,6 @@ import numpy as np
 sys.path.insert(0, "llm-engine_b200"); sys.path.insert(0, "tests")
 import torch, torch.distributed as dist
 import llme_b200 as L
-from checkpoint import load_checkpoint
-from tp_decode import TPTransformer
 rank, world, port, ckpt, q8, out = (int(sys.argv[1]), int(sys.argv[2]), int(sys.argv[3]),
                                     sys.argv[4], sys.argv[5] == "1", sys.argv[6])
 torch.cuda.set_device(rank)
@@ -162,12 +171,14 @@ uid = [L.Comm.unique_id() if rank == 0 else None]
 dist.broadcast_object_list(uid, src=0)
 comm = L.Comm(world, rank, uid[0], timeout_s=60.0)
 comm.enable_peer(1 << 16)
-tp = TPTransformer(load_checkpoint(ckpt), world=world, rank=rank, q8=q8, comm=comm)
+model = L.Model.load(ckpt, q8=q8, world=world, rank=rank, comm=comm)
 stream = eval(sys.argv[7])
 for i, (tokens, pos) in enumerate(stream):
-    np.save(f"{out}/logits_{i}_{rank}.npy", tp.run(tokens, pos))
+    np.save(f"{out}/logits_{i}_{rank}.npy", model.forward(tokens, pos))
+np.save(f"{out}/decode_{rank}.npy", np.stack([model.decode(t, p) for t, p in [(4, 13), (9, 14)]]))
 torch.cuda.synchronize()
 L.Comm.status()
+model.destroy()
 comm.destroy()
 dist.destroy_process_group()
 print("OK", rank)
@@ -195,3 +206,7 @@ def test_two_gpus_match_the_reference_model(tmp_path, q8):
         got = [np.load(tmp_path / f"logits_{i}_{r}.npy") for r in range(world)]
         np.testing.assert_array_equal(got[0], got[1])
         assert close(got[0], want), (tokens, pos, float(np.abs(got[0] - want).max()))
+    dec = [np.load(tmp_path / f"decode_{r}.npy") for r in range(world)]
+    np.testing.assert_array_equal(dec[0], dec[1])
+    for j, (t, p_) in enumerate([(4, 13), (9, 14)]):
+        assert close(dec[0][j], ref.run([t], p_))

@@ -1,7 +1,9 @@
-"""Host side of the tensor-parallel transformer (no GPU): the checkpoint loader against the
-llama2.c layout the reference reads (src/model.cpp:113-169), the RoPE tables against the
-reference's own (rope_tables, model.cpp:171-184, compiled into oracle/_ref), the head / hidden
-partition, and the reference CPU Transformer that the GPU tests use as their oracle."""
+"""Host side of the transformer engine (no GPU): the C++ checkpoint reader's header and size
+rules (llme_checkpoint_config, the same checks llme_model_load makes) on files the reference
+reads, the RoPE tables against the reference's own (rope_tables, model.cpp:171-184, compiled
+into oracle/_ref), the tensor-parallel partition of heads, hidden units and vocabulary, the
+reference CPU Transformer that the GPU tests use as their oracle, and the argument checks of
+the decode-step kernels."""
 from __future__ import annotations
 
 import numpy as np
@@ -9,47 +11,33 @@ import pytest
 
 import oracle
 import llme_b200 as L
-from checkpoint import load_checkpoint
 from model_fixture import make_model, write_checkpoint
-from tp_decode import head_partition, shard_layer
 
 
-def test_loader_concatenates_and_transposes_like_the_reference(tmp_path):
+def test_checkpoint_config_reads_the_header(tmp_path):
     m = make_model(dim=32, hidden=48, layers=2, heads=4, kv_heads=2, vocab=20, seq_len=8, seed=3)
     p = str(tmp_path / "m.bin")
     write_checkpoint(m, p)
-    ck = load_checkpoint(p)
-    c = ck.config
-    assert (c.dim, c.hidden_dim, c.n_layers, c.n_heads, c.n_kv_heads, c.vocab_size, c.seq_len) == \
-        (32, 48, 2, 4, 2, 20, 8)
-    assert c.head_size == 8 and c.kv_dim == 16
-    for l, lw in enumerate(ck.layers):
-        np.testing.assert_array_equal(lw.wqkv, np.concatenate([m["wq"][l].T, m["wk"][l].T,
-                                                               m["wv"][l].T], axis=1))
-        np.testing.assert_array_equal(lw.w13, np.concatenate([m["w1"][l].T, m["w3"][l].T], axis=1))
-        np.testing.assert_array_equal(lw.wo, m["wo"][l].T)
-        np.testing.assert_array_equal(lw.w2, m["w2"][l].T)
-        np.testing.assert_array_equal(lw.rms_att, m["rms_att"][l])
-    np.testing.assert_array_equal(ck.wcls, m["wcls"].T)
-    np.testing.assert_array_equal(ck.token_embedding, m["emb"])
+    assert L.checkpoint_config(p) == dict(dim=32, hidden_dim=48, n_layers=2, n_heads=4,
+                                          n_kv_heads=2, vocab_size=20, seq_len=8)
     ms = make_model(dim=32, hidden=48, layers=1, heads=4, kv_heads=4, vocab=20, seq_len=8,
                     shared=True, seed=4)
-    write_checkpoint(ms, p)
-    np.testing.assert_array_equal(load_checkpoint(p).wcls, ms["emb"].T)
+    write_checkpoint(ms, p)  # classifier shared with the embedding: vocab stored positive
+    assert L.checkpoint_config(p)["vocab_size"] == 20
 
 
-def test_loader_rejects_what_the_reference_rejects(tmp_path):
+def test_checkpoint_reader_rejects_what_the_reference_rejects(tmp_path):
     m = make_model(dim=32, hidden=48, layers=1, heads=4, kv_heads=2, vocab=20, seq_len=8)
     p = str(tmp_path / "m.bin")
     write_checkpoint(m, p, drop_bytes=4)
-    with pytest.raises(RuntimeError, match="header implies"):
-        load_checkpoint(p)
+    with pytest.raises(L.InvalidArgument, match="header implies"):
+        L.checkpoint_config(p)
     bad = dict(m, heads=3)  # 32 does not split into 3 heads
     write_checkpoint(bad, p)
-    with pytest.raises(RuntimeError, match="even-sized heads"):
-        load_checkpoint(p)
-    with pytest.raises(RuntimeError, match="cannot open"):
-        load_checkpoint(str(tmp_path / "missing.bin"))
+    with pytest.raises(L.InvalidArgument, match="even-sized heads"):
+        L.checkpoint_config(p)
+    with pytest.raises(L.InvalidArgument, match="cannot open"):
+        L.checkpoint_config(str(tmp_path / "missing.bin"))
 
 
 @pytest.mark.skipif(not oracle.RefModel.available(), reason="reference model not built here")
@@ -61,53 +49,44 @@ def test_rope_tables_match_the_reference_bit_for_bit(seq_len, dim, heads):
     np.testing.assert_array_equal(sin, rs)
 
 
-@pytest.mark.parametrize("world", [1, 2, 4])
-def test_shards_reassemble_the_layer(world, tmp_path):
-    # Column shards cover every q / k / v / gate / up column once; row-parallel partial
-    # products sum to the unsharded product (numpy, float64).
-    m = make_model(dim=64, hidden=96, layers=1, heads=8, kv_heads=4, vocab=50, seq_len=8, seed=5)
-    p = str(tmp_path / "m.bin")
-    write_checkpoint(m, p)
-    ck = load_checkpoint(p)
-    cfg, lw = ck.config, ck.layers[0]
-    rng = np.random.default_rng(1)
-    x = rng.uniform(-1, 1, (3, cfg.dim))
-    qkv_full = x @ lw.wqkv.astype(np.float64)
-    att = rng.uniform(-1, 1, (3, cfg.dim))
-    hb = rng.uniform(-1, 1, (3, cfg.hidden_dim))
-    hs, D, KV, H = cfg.head_size, cfg.dim, cfg.kv_dim, cfg.hidden_dim
-    wo_sum = np.zeros((3, D))
-    w2_sum = np.zeros((3, D))
-    seen_q, seen_kv, seen_h = [], [], []
+@pytest.mark.parametrize("cfg", [
+    dict(dim=64, hidden_dim=96, n_layers=1, n_heads=8, n_kv_heads=4, vocab_size=50, seq_len=8),
+    dict(dim=4096, hidden_dim=11008, n_layers=32, n_heads=32, n_kv_heads=32, vocab_size=32000,
+         seq_len=2048),
+    dict(dim=4096, hidden_dim=14336, n_layers=32, n_heads=32, n_kv_heads=8, vocab_size=128256,
+         seq_len=8192)])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_partition_covers_every_head_unit_and_token_once(cfg, world):
+    if cfg["n_kv_heads"] % world:
+        with pytest.raises(L.InvalidArgument, match="do not split"):
+            L.model_partition(cfg, world, 0)
+        return
+    group = cfg["n_heads"] // cfg["n_kv_heads"]
+    q, kv, hid, voc = [], [], [], []
     for r in range(world):
-        q0, nq, kv0, nkv = head_partition(cfg.n_heads, cfg.n_kv_heads, world, r)
-        assert nq == nkv * (cfg.n_heads // cfg.n_kv_heads)
-        sh = shard_layer(lw, cfg, world, r)
-        local = x @ sh["wqkv"].astype(np.float64)
-        np.testing.assert_allclose(local[:, :nq * hs], qkv_full[:, q0 * hs:(q0 + nq) * hs])
-        np.testing.assert_allclose(local[:, nq * hs:(nq + nkv) * hs],
-                                   qkv_full[:, D + kv0 * hs:D + (kv0 + nkv) * hs])
-        np.testing.assert_allclose(local[:, (nq + nkv) * hs:],
-                                   qkv_full[:, D + KV + kv0 * hs:D + KV + (kv0 + nkv) * hs])
-        r0, rc = sh["wo_rows"]
-        wo_sum += att[:, r0:r0 + rc] @ lw.wo[r0:r0 + rc].astype(np.float64)
-        h0, hc = sh["w2_rows"]
-        assert sh["w13"].shape == (D, 2 * hc)
-        np.testing.assert_array_equal(sh["w13"][:, :hc], lw.w13[:, h0:h0 + hc])
-        np.testing.assert_array_equal(sh["w13"][:, hc:], lw.w13[:, H + h0:H + h0 + hc])
-        w2_sum += hb[:, h0:h0 + hc] @ lw.w2[h0:h0 + hc].astype(np.float64)
-        seen_q += list(range(q0, q0 + nq))
-        seen_kv += list(range(kv0, kv0 + nkv))
-        seen_h += list(range(h0, h0 + hc))
-    assert seen_q == list(range(cfg.n_heads)) and seen_kv == list(range(cfg.n_kv_heads))
-    assert seen_h == list(range(H))
-    np.testing.assert_allclose(wo_sum, att @ lw.wo.astype(np.float64), rtol=1e-12, atol=1e-12)
-    np.testing.assert_allclose(w2_sum, hb @ lw.w2.astype(np.float64), rtol=1e-12, atol=1e-12)
+        s = L.model_partition(cfg, world, r)
+        assert s["nq"] == s["nkv"] * group and s["q0"] == s["kv0"] * group
+        q += list(range(s["q0"], s["q0"] + s["nq"]))
+        kv += list(range(s["kv0"], s["kv0"] + s["nkv"]))
+        hid += list(range(s["h0"], s["h0"] + s["hc"]))
+        voc.append((s["v0"], s["vc"]))
+        # contiguous blocks, sizes differing by at most one
+        assert abs(s["hc"] - cfg["hidden_dim"] / world) < 1
+        assert abs(s["vc"] - cfg["vocab_size"] / world) < 1
+    assert q == list(range(cfg["n_heads"])) and kv == list(range(cfg["n_kv_heads"]))
+    assert hid == list(range(cfg["hidden_dim"]))
+    assert [v0 for v0, _ in voc] == list(np.cumsum([0] + [vc for _, vc in voc[:-1]]))
+    assert sum(vc for _, vc in voc) == cfg["vocab_size"]
 
 
-def test_kv_heads_must_split_evenly():
+def test_partition_rejects_bad_configurations():
+    good = dict(dim=64, hidden_dim=96, n_layers=1, n_heads=8, n_kv_heads=4, vocab_size=50,
+                seq_len=8)
+    for bad in (dict(good, n_heads=6), dict(good, n_kv_heads=3), dict(good, dim=0)):
+        with pytest.raises(L.InvalidArgument):
+            L.model_partition(bad, 1, 0)
     with pytest.raises(L.InvalidArgument):
-        head_partition(8, 2, 4, 0)
+        L.model_partition(good, 2, 2)
 
 
 @pytest.mark.skipif(not oracle.RefModel.available(), reason="reference model not built here")
