@@ -824,6 +824,9 @@ def run_tp_decode(args, world, rank, local):
         comm.destroy()
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
 
 
 def attention_case_inputs(torch, g, heads, kvh, hs, T):
