@@ -223,4 +223,21 @@ __device__ __forceinline__ void s8x4_to_f32(uint32_t w, float (&x)[4]) {
 // RMSNorm's eps, as the reference's ops.h / cuda_util.cuh.
 constexpr float kRmsEps = 1e-5f;
 
+// The int8 digits of y (|y| <= 127 up to one rounding) in base 256:
+// y ~ t0 + t1 / 256 + t2 / 65536. Each residual times 256 is exact in fp32 (y - rint(y) is a
+// multiple of y's unit in the last place, at most 1/2 in size). A second digit that rounds to
+// +128 (y - t0 = 1/2 with t0 rounded to even below y) carries one into t0 and becomes -128,
+// so every digit fits int8 and the error stays at most 2^-16 (2^-17 unless the last digit
+// is clamped to 127).
+__device__ __forceinline__ void int8_digits(float y, int& t0, int& t1, int& t2) {
+    const float f0 = fminf(fmaxf(rintf(y), -127.0f), 127.0f);
+    const float r1 = (y - f0) * 256.0f;  // [-128, 128]
+    const float g1 = rintf(r1);
+    const float f2 = fminf(fmaxf(rintf((r1 - g1) * 256.0f), -128.0f), 127.0f);
+    const int carry = g1 > 127.0f ? 1 : 0;
+    t0 = static_cast<int>(f0) + carry;
+    t1 = static_cast<int>(g1) - 256 * carry;
+    t2 = static_cast<int>(f2);
+}
+
 }  // namespace llme

@@ -429,15 +429,11 @@ struct SplitRow {
         const float x = norm ? a * inv_rms * g : a;
         float y = pre == 1.0f ? x * q : (x * pre) * q;
         if (!(fabsf(y) <= 128.0f)) y = 0.0f;  // non-finite rows: the row scale is NaN
-        const float t0 = fminf(fmaxf(rintf(y), -127.0f), 127.0f);
-        const float r1 = (y - t0) * 256.0f;
-        const float t1 = fminf(fmaxf(rintf(r1), -127.0f), 127.0f);
-        *o0 = static_cast<int8_t>(static_cast<int>(t0));
-        *o1 = static_cast<int8_t>(static_cast<int>(t1));
-        if (three) {
-            const float t2 = fminf(fmaxf(rintf((r1 - t1) * 256.0f), -127.0f), 127.0f);
-            *o2 = static_cast<int8_t>(static_cast<int>(t2));
-        }
+        int t0, t1, t2;
+        int8_digits(y, t0, t1, t2);  // two terms: the first two digits
+        *o0 = static_cast<int8_t>(t0);
+        *o1 = static_cast<int8_t>(t1);
+        if (three) *o2 = static_cast<int8_t>(t2);
     }
     __device__ __forceinline__ void split4(float4 v, float4 g, int8_t* p0, int8_t* p1,
                                            int8_t* p2) const {

@@ -69,3 +69,15 @@ def row_rel_err(got: np.ndarray, want: np.ndarray) -> float:
     den = np.linalg.norm(w, axis=1)
     den = np.where(den == 0, 1.0, den)
     return float((num / den).max()) if g.size else 0.0
+
+
+def int8_digits(y: np.ndarray):
+    """The kernels' int8 digits of y = x * (127 / max|x|) in base 256, computed in fp32 as the
+    device does: y ~ t0 + t1 / 256 + t2 / 65536, a second digit of +128 carried into t0."""
+    y = np.asarray(y, dtype=np.float32)
+    t0 = np.clip(np.rint(y), -127, 127).astype(np.float32)
+    r1 = ((y - t0) * np.float32(256)).astype(np.float32)
+    g1 = np.rint(r1).astype(np.float32)
+    t2 = np.clip(np.rint(((r1 - g1) * np.float32(256)).astype(np.float32)), -128, 127)
+    carry = (g1 > 127).astype(np.float32)
+    return t0 + carry, g1 - np.float32(256) * carry, t2.astype(np.float32)

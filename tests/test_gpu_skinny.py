@@ -14,7 +14,7 @@ import pytest
 
 import oracle
 import llme_b200 as L
-from conftest import row_rel_err
+from conftest import int8_digits, row_rel_err
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -34,12 +34,9 @@ def split3(A):
     amax = np.abs(A).max(axis=1).astype(np.float32)
     q = (np.float32(127.0) / amax).astype(np.float32)
     y = (A * q[:, None]).astype(np.float32)
-    t0 = np.clip(np.rint(y), -127, 127).astype(np.float32)
-    r1 = ((y - t0) * np.float32(256)).astype(np.float32)
-    t1 = np.clip(np.rint(r1), -127, 127).astype(np.float32)
-    t2 = np.clip(np.rint(((r1 - t1) * np.float32(256)).astype(np.float32)), -127, 127)
+    t0, t1, t2 = int8_digits(y)
     s = (amax / np.float32(127.0)).astype(np.float32)
-    return t0, t1, t2.astype(np.float32), s
+    return t0, t1, t2, s
 
 
 def emulate(A, q8, scale, C0=None):
@@ -111,6 +108,21 @@ def test_skinny_outlier_activations(outlier):
     got = run(A, q, s)
     assert row_rel_err(got, oracle.matmul_naive_q8(A, q, s)) <= 1e-5
     np.testing.assert_array_equal(got, emulate(A, q, s))
+
+
+def test_skinny_half_way_digits():
+    # Rows whose scale is exactly 1 (max |x| = 127) and whose other values lie half way between
+    # integers: the first digit rounds to even, the remainder is exactly 1/2, and the second
+    # digit is carried (+128 -> first digit + 1, second digit -128). The three digits then
+    # hold every value exactly, so the result is the oracle's within fp32 rounding.
+    rng = np.random.default_rng(77)
+    m, k, n = 12, 4096, 2048
+    A = (rng.integers(-126, 126, (m, k)) + 0.5).astype(np.float32)
+    A[:, 0] = 127.0
+    q, s = weights(rng, k, n)
+    got = run(A, q, s)
+    np.testing.assert_array_equal(got, emulate(A, q, s))
+    assert row_rel_err(got, oracle.matmul_naive_q8(A, q, s)) <= 1e-6
 
 
 @pytest.mark.parametrize("m", [2, 4, 8])

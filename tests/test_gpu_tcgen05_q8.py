@@ -21,7 +21,7 @@ import pytest
 
 import oracle
 import llme_b200 as L
-from conftest import row_rel_err
+from conftest import int8_digits, row_rel_err
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -37,14 +37,13 @@ def weights(rng, k, n):
 
 def split_rows(A):
     """The split pass for rows without RMSNorm, as the kernel computes it in fp32:
-    s = max|x| / 127, y = x * (127 / max|x|), hi = rint(y), lo = rint((y - hi) * 256)."""
+    s = max|x| / 127, y = x * (127 / max|x|), hi and lo the first two int8 digits of y."""
     A = A.astype(np.float32)
     amax = np.abs(A).max(axis=1).astype(np.float32)
     assert (amax > 1e-30).all()
     q = (np.float32(127.0) / amax).astype(np.float32)
     y = (A * q[:, None]).astype(np.float32)
-    hi = np.clip(np.rint(y), -127, 127).astype(np.float32)
-    lo = np.clip(np.rint(((y - hi) * np.float32(256)).astype(np.float32)), -127, 127)
+    hi, lo, _ = int8_digits(y)
     s = (amax / np.float32(127.0)).astype(np.float32)
     return hi.astype(np.int64), lo.astype(np.int64), s
 
