@@ -518,6 +518,9 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
         if (tid == 0)
             mbar_arrive_expect_tx(rbar, static_cast<uint32_t>((a.slices - 1) *
                                                               (my_cnt * 16 + (Norm ? M * 4 : 0))));
+        // tot was written by other consumer threads (element e by thread e % CT); the cluster
+        // wait above orders nothing inside this CTA.
+        named_barrier(1, CT);
         for (int e4 = tid; e4 < E4; e4 += CT) {
             const int owner = e4 / per;
             const float4 v = *reinterpret_cast<const float4*>(tot + 4 * e4);

@@ -212,6 +212,29 @@ def test_scratch_settles_after_one_pass():
     assert L.scratch_generation() == gen
 
 
+@pytest.mark.parametrize("m,k", [(8, 5504), (6, 5504), (5, 5504), (8, 2816), (7, 11008)])
+def test_cluster_reduction_with_a_short_last_slice(m, k):
+    # k slices of a column strip reduced across their cluster while the last, one-box slice
+    # finishes long before the others: every CTA's sums must be complete before it sends
+    # them (a missing barrier there once let a few owners read half-written values). Repeated
+    # calls, since the failure depended on timing.
+    rng = np.random.default_rng(70 + m + k)
+    n = 4096
+    q, s = oracle.quantize_q8((rng.standard_normal((k, n)) * 0.02).astype(np.float32))
+    dq, ds = dev(q), dev(s)
+    assert L.plan(m, n, k, q8=True)["slices"] > 1
+    runs = []
+    for _ in range(8):
+        A = uni(rng, m, k)
+        C = torch.full((m, n), float("nan"), device="cuda")
+        L.matmul(dev(A), dq, scale=ds, C=C, weights_static=True)
+        runs.append((A, C))
+    torch.cuda.synchronize()
+    for A, C in runs:
+        got, want = C.cpu().numpy(), oracle.matmul_naive_q8(A, q, s)
+        assert close_to(got, want, k), (m, k, int((np.abs(got - want) > 1e-5 * k).sum()))
+
+
 def test_programmatic_launch_gives_identical_bits():
     rng = np.random.default_rng(21)
     A = uni(rng, 2, 4096)
