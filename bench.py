@@ -771,9 +771,11 @@ def run_tp_decode(args, world, rank, local):
     secs = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
     tokens_s = args.steps / secs
     # Kernels of one token: embed; per layer wqkv (+ RoPE + cache write in its epilogue),
-    # attention, wo, w13 (+ SwiGLU in its epilogue), w2, with N > 1 an all-reduce after wo and
-    # w2; the classifier (+ its all-reduce).
-    launches_per_token = (1 + cfg["n_layers"] * (5 + (2 if world > 1 else 0)) + 1
+    # attention, wo, w13 (+ SwiGLU in its epilogue), w2; the classifier (+ its all-reduce at
+    # N > 1). At N > 1 the sums after wo and w2 run inside those GEMVs when every rank's shard
+    # has the same size (hidden % N == 0), else as two more all-reduce launches per layer.
+    separate_sums = world > 1 and cfg["hidden_dim"] % world != 0
+    launches_per_token = (1 + cfg["n_layers"] * (5 + (2 if separate_sums else 0)) + 1
                           + (1 if world > 1 else 0))
     w_bytes, kv_per_pos = model.stream_bytes()
     per_gpu = w_bytes + kv_per_pos * (ctx + 1)
@@ -804,9 +806,11 @@ def run_tp_decode(args, world, rank, local):
                        "engine": "the library's C++ transformer engine (llme_model_*)",
                        "launch": "one CUDA graph per token: embed, per layer rmsnorm+wqkv with "
                                  "RoPE and the cache write in the GEMV epilogue, attention, "
-                                 "wo (+all-reduce with the residual), rmsnorm+w13 with SwiGLU "
-                                 "in the GEMV epilogue, w2 (+all-reduce); classifier "
-                                 "(+all-reduce)",
+                                 "wo with the residual, rmsnorm+w13 with SwiGLU in the GEMV "
+                                 "epilogue, w2 with the residual; classifier. At N > 1 the rank "
+                                 "sums of wo and w2 run inside their GEMVs (each CTA exchanges "
+                                 "its columns with the same CTA of every rank over NVLink); "
+                                 "the classifier's logits are summed by the peer all-reduce",
                        "l2": f"no flush: {per_gpu / 1e9:.2f} GB per token per GPU (> L2)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_kind": hbm_kind,

@@ -87,7 +87,15 @@ enum {
     /* B and scale are not written by the launch that precedes this one on the stream, so the
        kernel may start streaming them before that launch finishes (programmatic dependent
        launch). True for model weights; not assumed by default. */
-    LLME_FLAG_WEIGHTS_STATIC = 1u << 0
+    LLME_FLAG_WEIGHTS_STATIC = 1u << 0,
+    /* Row-parallel products (llme_matmul_*_rowpar): every rank calls with the same m, n and
+       k_local and with equally aligned pointers, so every rank's product follows the same
+       plan. With a peer-enabled communicator (llme_comm_enable_peer) of 2 to 8 ranks, m <= 8
+       and the automatic kernel, the sum over the ranks is then taken inside the product's
+       GEMV: each CTA sends its finished columns to the same CTA of every rank over NVLink and
+       writes the rank-ordered sum, with no separate all-reduce launch. Ranks that break the
+       promise get LLME_E_TIMEOUT from llme_comm_status (bounded waits), not a hang. */
+    LLME_FLAG_SAME_SHARDS = 1u << 1
 };
 
 /* matmul_cuda(m, n, k, A, const float* B, C, kernel, fusion): cuda_matmul.h:97-99.

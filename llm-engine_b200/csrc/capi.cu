@@ -566,11 +566,19 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
     llme_plan_t p;
     st = make_plan(in, &p);
     if (st) return st;
-    // A fused epilogue exists only in the TMA GEMV, works on column pairs and writes plainly.
-    if (epi && epi->kind != kEpiStore &&
-        (p.path != LLME_PATH_GEMV_TMA || n % 2 != 0 || accumulate))
+    // A fused epilogue exists only in the TMA GEMV. The elementwise ones work on column pairs
+    // and write plainly; the peer sum needs every CTA of the grid resident at once (each waits
+    // for the same CTA of every rank) and a flag slot per CTA.
+    if (epi && epi->kind == kEpiPeerSum) {
+        if (p.path != LLME_PATH_GEMV_TMA ||
+            static_cast<long>(p.grid_x) * p.grid_y > std::min(epi->peer.units, 2 * sms))
+            return fail(LLME_E_UNSUPPORTED, "matmul: the in-kernel rank sum needs the TMA GEMV path "
+                                            "with one resident grid " + shapes(m, n, k));
+    } else if (epi && epi->kind != kEpiStore &&
+               (p.path != LLME_PATH_GEMV_TMA || n % 2 != 0 || accumulate)) {
         return fail(LLME_E_UNSUPPORTED, "matmul: fused epilogue needs the TMA GEMV path, an even n "
                                         "and no accumulation " + shapes(m, n, k));
+    }
     if (p.path == LLME_PATH_NONE) return LLME_OK;
     if (p.path == LLME_PATH_ZERO) {
         cudaError_t e = cudaMemsetAsync(C, 0, m * n * sizeof(float), stream);
@@ -1195,8 +1203,9 @@ int run_product(size_t m, size_t n, size_t k, const float* A, const void* B, con
 }
 int run_product_epilogue(size_t m, size_t n, size_t k, const float* A, const void* B,
                          const float* scale, float* C, bool q8, const float* rms, unsigned flags,
-                         void* stream, const GemvEpilogue& epi) {
-    return run(m, n, k, A, B, scale, C, q8, LLME_KERNEL_AUTOMATIC, false, rms, flags, stream, &epi);
+                         void* stream, const GemvEpilogue& epi, bool accumulate) {
+    return run(m, n, k, A, B, scale, C, q8, LLME_KERNEL_AUTOMATIC, accumulate, rms, flags, stream,
+               &epi);
 }
 int plan_product(size_t m, size_t n, size_t k, bool q8, const void* A, const void* B,
                  const float* rms, llme_plan_t* p) {

@@ -50,6 +50,10 @@ struct llme_comm {
     void* peer_epoch = nullptr;
     void* peer_opened[kPeerMaxRanks] = {};
     PeerArgs pargs{};
+    // The GEMV's in-kernel rank sum (kEpiPeerSum): receive areas behind the all-reduce's in the
+    // same shared buffer, one epoch counter per CTA slot.
+    void* push_epoch = nullptr;
+    llme::PeerSum push{};
 };
 
 namespace {
@@ -129,15 +133,6 @@ constexpr double kEnqueueTimeoutS = 60.0;
 
 __device__ unsigned int g_comm_error;
 
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
 // One-shot all-reduce over NVLink peer memory, in place on `data` (count floats, identical
 // on every rank). CTA b owns elements [b*chunk, (b+1)*chunk): it copies them into slot
 // (epoch & 1) of this rank's symmetric buffer, raises its flag on every rank, waits (bounded)
@@ -173,12 +168,12 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(float* __r
     __syncthreads();
     if (tid < p.nranks) {
         unsigned* flags = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(p.base[tid]) + p.flags_off);
-        st_release_sys(flags + b * kPeerMaxRanks + p.rank, e);
+        llme::st_release_sys(flags + b * kPeerMaxRanks + p.rank, e);
         const unsigned* my_flags =
             reinterpret_cast<const unsigned*>(reinterpret_cast<char*>(p.base[p.rank]) + p.flags_off);
         const unsigned* f = my_flags + b * kPeerMaxRanks + tid;
         const unsigned long long t0 = llme::global_timer_ns();
-        for (uint32_t i = 0; ld_acquire_sys(f) < e; ++i) {
+        for (uint32_t i = 0; llme::ld_acquire_sys(f) < e; ++i) {
             if ((i & 255) == 255 && llme::global_timer_ns() - t0 > llme::kWaitLimitNs) {
                 atomicExch(p.err, static_cast<unsigned>(LLME_E_TIMEOUT));
                 s_ok = 0;
@@ -241,6 +236,18 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(float* __r
 
 }  // namespace
 
+namespace llme {
+int comm_peer_sum(llme_comm_t* c, GemvEpilogue* epi) {
+    if (!c || !c->peer || c->push.world < 2)
+        return set_error(LLME_E_UNSUPPORTED, "in-kernel rank sum: no peer-enabled communicator of "
+                                             "2 to 8 ranks");
+    *epi = GemvEpilogue{};
+    epi->kind = kEpiPeerSum;
+    epi->peer = c->push;
+    return LLME_OK;
+}
+}  // namespace llme
+
 extern "C" {
 
 int llme_comm_unique_id(void* id) {
@@ -295,6 +302,9 @@ static void peer_release(llme_comm* c) {
         if (c->peer_opened[r]) cudaIpcCloseMemHandle(c->peer_opened[r]);
     if (c->peer_buf) cudaFree(c->peer_buf);
     if (c->peer_epoch) cudaFree(c->peer_epoch);
+    if (c->push_epoch) cudaFree(c->push_epoch);
+    c->peer_buf = c->peer_epoch = c->push_epoch = nullptr;
+    c->push = llme::PeerSum{};
     c->peer = false;
 }
 
@@ -306,11 +316,28 @@ int llme_comm_enable_peer(llme_comm_t* c, size_t max_floats) {
             return llme::set_error(LLME_E_UNSUPPORTED, "llme_comm_enable_peer: more than 16 ranks");
         const size_t slot = (max_floats + 63) / 64 * 64;
         const size_t flags_off = 2 * slot * sizeof(float);
-        const size_t bytes = flags_off + kPeerCtas * kPeerMaxRanks * sizeof(unsigned);
+        const size_t ar_bytes = flags_off + kPeerCtas * kPeerMaxRanks * sizeof(unsigned);
+        // The GEMV's in-kernel rank sum: per slot, per CTA of a resident grid (two per SM),
+        // per source rank, the values a CTA owns (at most 8 rows x 128 columns); then a flag
+        // per CTA and source rank.
+        int dev = 0, sms = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int units = 2 * (sms > 0 ? sms : 148);
+        const int unit_floats = 8 * 128;
+        const bool push = c->nranks <= llme::kPeerSumMaxRanks;
+        const size_t push_off = (ar_bytes + 255) / 256 * 256;
+        const size_t push_flags_off =
+            2 * static_cast<size_t>(units) * c->nranks * unit_floats * sizeof(float);
+        const size_t bytes =
+            push ? push_off + push_flags_off + static_cast<size_t>(units) * llme::kPeerFlagStride * sizeof(unsigned)
+                 : ar_bytes;
         cudaError_t e = cudaMalloc(&c->peer_buf, bytes);
         if (e == cudaSuccess) e = cudaMemset(c->peer_buf, 0, bytes);
         if (e == cudaSuccess) e = cudaMalloc(&c->peer_epoch, kPeerCtas * sizeof(unsigned));
         if (e == cudaSuccess) e = cudaMemset(c->peer_epoch, 0, kPeerCtas * sizeof(unsigned));
+        if (e == cudaSuccess && push) e = cudaMalloc(&c->push_epoch, units * sizeof(unsigned));
+        if (e == cudaSuccess && push) e = cudaMemset(c->push_epoch, 0, units * sizeof(unsigned));
         cudaIpcMemHandle_t mine;
         if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mine, c->peer_buf);
         if (e != cudaSuccess) {
@@ -368,6 +395,18 @@ int llme_comm_enable_peer(llme_comm_t* c, size_t max_floats) {
         pa.err = static_cast<unsigned*>(err);
         pa.nranks = c->nranks;
         pa.rank = c->rank;
+        if (push) {
+            llme::PeerSum& ps = c->push;
+            for (int q = 0; q < c->nranks; ++q)
+                ps.base[q] = reinterpret_cast<float*>(reinterpret_cast<char*>(pa.base[q]) + push_off);
+            ps.flags_off = push_flags_off;
+            ps.units = units;
+            ps.unit_floats = unit_floats;
+            ps.epoch = static_cast<unsigned*>(c->push_epoch);
+            ps.err = pa.err;
+            ps.world = c->nranks;
+            ps.rank = c->rank;
+        }
         c->peer_max_floats = max_floats;
         c->peer = true;
         return LLME_OK;
@@ -440,7 +479,17 @@ static int rowpar(size_t m, size_t n, size_t k_local, const float* A, const void
     if (!c) return llme::set_error(LLME_E_INVALID, "row-parallel product: no communicator");
     // Only rank 0 adds the existing C, so after the sum it is counted once.
     const bool acc = accumulate != 0 && c->rank == 0;
-    int st = llme::run_product(m, n, k_local, A, B, scale, C, q8, kernel, acc, nullptr, flags,
+    const unsigned kflags = flags & ~static_cast<unsigned>(LLME_FLAG_SAME_SHARDS);
+    if ((flags & LLME_FLAG_SAME_SHARDS) && c->nranks > 1 && kernel == LLME_KERNEL_AUTOMATIC) {
+        // Every rank runs the same plan: the sum is taken inside the GEMV when it takes it.
+        llme::GemvEpilogue epi;
+        if (llme::comm_peer_sum(c, &epi) == LLME_OK) {
+            const int st = llme::run_product_epilogue(m, n, k_local, A, B, scale, C, q8, nullptr,
+                                                      kflags, stream, epi, acc);
+            if (st != LLME_E_UNSUPPORTED) return st;
+        }
+    }
+    int st = llme::run_product(m, n, k_local, A, B, scale, C, q8, kernel, acc, nullptr, kflags,
                                stream);
     if (st) return st;
     return llme_allreduce_sum_f32(C, m * n, c, stream);

@@ -220,6 +220,17 @@ __device__ __forceinline__ void s8x4_to_f32(uint32_t w, float (&x)[4]) {
     x[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - kBias;
 }
 
+// System-scope acquire load and release store of a 32-bit flag (cross-GPU handshakes over
+// peer memory).
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // RMSNorm's eps, as the reference's ops.h / cuda_util.cuh.
 constexpr float kRmsEps = 1e-5f;
 

@@ -251,6 +251,68 @@ __device__ __forceinline__ void epilogue_pair(const GemvArgs& a, int r, int col,
     *reinterpret_cast<float2*>(a.C + static_cast<size_t>(r) * a.n + col) = make_float2(v0, v1);
 }
 
+// ---- kEpiPeerSum: the row-parallel sum over the ranks, inside the GEMV ----------------------
+
+__device__ __forceinline__ float* peer_region(const PeerSum& p, int q, unsigned slot, int unit, int src) {
+    return p.base[q] + ((static_cast<size_t>(slot) * p.units + unit) * p.world + src) * p.unit_floats;
+}
+__device__ __forceinline__ unsigned* peer_flag(const PeerSum& p, int q, int unit, int src) {
+    return reinterpret_cast<unsigned*>(reinterpret_cast<char*>(p.base[q]) + p.flags_off) +
+           static_cast<size_t>(unit) * kPeerFlagStride + src;
+}
+
+// The `count` values this CTA owns, exchanged with the same CTA of every rank and summed in
+// rank order into C. value(e) is owned element e's finished value (partial, scaled), where(e,
+// r, col) its place in C (col >= n: padding, skipped). Every one of the nthreads consumer
+// threads calls this; `state` is two words of this CTA's shared memory.
+template <typename Value, typename Where>
+__device__ __forceinline__ void peer_sum_store(const GemvArgs& a, int count, Value value, Where where,
+                                               unsigned* state, int tid, int nthreads) {
+    const PeerSum& p = a.epi.peer;
+    const int unit = blockIdx.y * gridDim.x + blockIdx.x;
+    if (tid == 0) {
+        const unsigned e = __ldcg(p.epoch + unit) + 1;
+        p.epoch[unit] = e;
+        state[0] = e;
+        state[1] = 1;
+    }
+    named_barrier(1, nthreads);
+    const unsigned epoch = state[0];
+    const unsigned slot = epoch & 1u;
+    for (int e = tid; e < count; e += nthreads) {
+        int r, col;
+        where(e, r, col);
+        if (col >= a.n) continue;
+        float v = value(e);
+        if (a.accumulate) v += a.C[static_cast<size_t>(r) * a.n + col];
+        for (int q = 0; q < p.world; ++q) peer_region(p, q, slot, unit, p.rank)[e] = v;
+    }
+    __threadfence_system();
+    named_barrier(1, nthreads);
+    if (tid < p.world) {
+        st_release_sys(peer_flag(p, tid, unit, p.rank), epoch);
+        const unsigned* f = peer_flag(p, p.rank, unit, tid);
+        const unsigned long long t0 = global_timer_ns();
+        for (uint32_t i = 0; ld_acquire_sys(f) < epoch; ++i) {
+            if ((i & 255) == 255 && global_timer_ns() - t0 > kWaitLimitNs) {
+                atomicExch(p.err, static_cast<unsigned>(LLME_E_TIMEOUT));
+                state[1] = 0;
+                break;
+            }
+        }
+    }
+    named_barrier(1, nthreads);
+    if (!state[1]) return;
+    for (int e = tid; e < count; e += nthreads) {
+        int r, col;
+        where(e, r, col);
+        if (col >= a.n) continue;
+        float v = __ldcg(peer_region(p, p.rank, slot, unit, 0) + e);
+        for (int src = 1; src < p.world; ++src) v += __ldcg(peer_region(p, p.rank, slot, unit, src) + e);
+        a.C[static_cast<size_t>(r) * a.n + col] = v;
+    }
+}
+
 // Writes C for a CTA's column strip from M x NT sums that are already complete
 // (tot, shared memory) -- the kernels' common epilogue.
 // sscale: the strip's column scales already in shared memory (int8 TMA kernel), or null to
@@ -258,7 +320,22 @@ __device__ __forceinline__ void epilogue_pair(const GemvArgs& a, int r, int col,
 template <int M, int NT, bool Q8, bool Norm>
 __device__ __forceinline__ void store_strip(const float* tot, const float* tot_ss, const GemvArgs& a,
                                             int col0, int tid, int nthreads,
-                                            const float* sscale = nullptr) {
+                                            const float* sscale = nullptr,
+                                            unsigned* peer_state = nullptr) {
+    if (a.epi.kind == kEpiPeerSum && peer_state) {
+        auto value = [&](int e) {
+            float v = tot[e];
+            if constexpr (Q8) v *= sscale ? sscale[e % NT] : __ldg(a.scale + col0 + e % NT);
+            if constexpr (Norm) v *= 1.0f / sqrtf(tot_ss[e / NT] / static_cast<float>(a.k) + kRmsEps);
+            return v;
+        };
+        auto where = [&](int e, int& r, int& col) {
+            r = e / NT;
+            col = col0 + e % NT;
+        };
+        peer_sum_store(a, M * NT, value, where, peer_state, tid, nthreads);
+        return;
+    }
     if (a.epi.kind != kEpiStore) {
         for (int e = 2 * tid; e < M * NT; e += 2 * nthreads) {
             const int r = e / NT, col = col0 + e % NT;
@@ -494,7 +571,8 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
         if (a.slices == 1) {
             named_barrier(1, CT);
             store_strip<M, S::NT, Q8, Norm>(tot, tot_ss, a, col0, tid, CT,
-                                            reinterpret_cast<const float*>(smem + L::kOffScale));
+                                            reinterpret_cast<const float*>(smem + L::kOffScale),
+                                            reinterpret_cast<unsigned*>(smem + L::kOffRedBar + 8));
             if (tid == 0) GEMV_TRACE(a, 7);
         }
     }
@@ -543,9 +621,34 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
         const bool ok = mbar_wait_cluster(rbar, 0, &g_gemv_error);
         if (tid == 0) GEMV_TRACE(a, 9);
         const float* sc = reinterpret_cast<const float*>(smem + L::kOffScale);
+        if (a.epi.kind == kEpiPeerSum) {
+            // Every consumer thread takes part (the exchange has barriers), also when the
+            // cluster reduction gave up (the error word is set; the values are then not used).
+            auto value = [&](int e) {
+                const int eg = 4 * my_begin + e;
+                float v = recv[e];
+                for (int src = 1; src < a.slices; ++src) v += recv[src * per * 4 + e];
+                if constexpr (Q8) v *= sc[eg % S::NT];
+                if constexpr (Norm) {
+                    const int r = eg / S::NT;
+                    float ssum = recv_ss[r];
+                    for (int src = 1; src < a.slices; ++src) ssum += recv_ss[src * M + r];
+                    v *= 1.0f / sqrtf(ssum / static_cast<float>(a.k) + kRmsEps);
+                }
+                return ok ? v : 0.0f;
+            };
+            auto where = [&](int e, int& r, int& col) {
+                const int eg = 4 * my_begin + e;
+                r = eg / S::NT;
+                col = col0 + eg % S::NT;
+            };
+            peer_sum_store(a, 4 * my_cnt, value, where,
+                           reinterpret_cast<unsigned*>(smem + L::kOffRedBar + 8), tid, CT);
+        }
         // Fused epilogues work on pairs of columns; chunks start at multiples of four
         // elements, so a pair never straddles two owners.
-        for (int e = 2 * tid; a.epi.kind != kEpiStore && ok && e < 4 * my_cnt; e += 2 * CT) {
+        for (int e = 2 * tid; a.epi.kind != kEpiStore && a.epi.kind != kEpiPeerSum && ok &&
+                              e < 4 * my_cnt; e += 2 * CT) {
             const int eg = 4 * my_begin + e;
             const int r = eg / S::NT, col = col0 + eg % S::NT;
             if (col >= a.n) continue;

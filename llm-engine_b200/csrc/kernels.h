@@ -57,7 +57,29 @@ struct SplitScratch {
 // What the per-call TMA GEMV (m <= 8) does with a finished pair of adjacent output columns
 // (2c, 2c + 1) of row r instead of writing C as is; the decode step of the transformer engine
 // fuses its elementwise work here.
-enum GemvEpilogueKind { kEpiStore = 0, kEpiRopeCache = 1, kEpiSwiglu = 2 };
+enum GemvEpilogueKind { kEpiStore = 0, kEpiRopeCache = 1, kEpiSwiglu = 2, kEpiPeerSum = 3 };
+
+// kEpiPeerSum: the tensor-parallel sum of a row-parallel product taken inside the GEMV. Every
+// rank runs the same plan, so CTA u owns the same output elements on every rank. CTA u pushes
+// its finished values (its partial, plus C on the rank that accumulates) into region
+// (slot, u, this rank) of every rank's receive area with plain peer stores, raises flag
+// (u, this rank) there with a release store, waits (bounded) until flag (u, src) of its own
+// area reaches the call's epoch for every src, and writes the sum over src = 0, 1, ... to C --
+// the same bits on every rank. A per-CTA epoch in device memory picks the slot (epoch & 1),
+// so back-to-back calls and CUDA-graph replays never overwrite a region a peer is still
+// reading: a rank reaches epoch e + 2 of CTA u only after every peer raised e + 1 there.
+constexpr int kPeerSumMaxRanks = 8;
+constexpr int kPeerFlagStride = 16;   // flags per unit (one per source rank, up to 16 ranks)
+struct PeerSum {
+    float* base[kPeerSumMaxRanks] = {};  // every rank's receive area, this rank's included
+    size_t flags_off = 0;                // bytes from a receive area to its flags
+    int units = 0;                       // CTAs a call may have (grid x * grid y)
+    int unit_floats = 0;                 // values a CTA owns at most
+    unsigned* epoch = nullptr;           // `units` counters, this rank's memory
+    unsigned* err = nullptr;             // device error word (LLME_E_TIMEOUT)
+    int world = 0, rank = 0;
+};
+
 struct GemvEpilogue {
     int kind = kEpiStore;
     // kEpiRopeCache: C's columns are [q: nq heads | k: nkv heads | v: nkv heads] of head_size
@@ -74,6 +96,7 @@ struct GemvEpilogue {
     // kEpiSwiglu: C's columns hold (gate, up) of hidden unit c at 2c and 2c + 1; instead of C,
     // out[r][c] = silu(gate) * up (rows of n / 2 floats).
     float* out = nullptr;
+    PeerSum peer;  // kEpiPeerSum
 };
 
 struct GemvArgs {
@@ -337,7 +360,10 @@ unsigned read_and_clear_ops_error();
 // before any launch otherwise), and the plan llme_matmul_* would follow for a product.
 int run_product_epilogue(size_t m, size_t n, size_t k, const float* A, const void* B,
                          const float* scale, float* C, bool q8, const float* rms, unsigned flags,
-                         void* stream, const GemvEpilogue& epi);
+                         void* stream, const GemvEpilogue& epi, bool accumulate = false);
+// Fills epi with kEpiPeerSum over the communicator's receive areas (comm.cu); LLME_E_UNSUPPORTED
+// without a peer-enabled communicator of at most kPeerSumMaxRanks ranks.
+int comm_peer_sum(llme_comm_t* comm, GemvEpilogue* epi);
 int plan_product(size_t m, size_t n, size_t k, bool q8, const void* A, const void* B,
                  const float* rms, llme_plan_t* p);
 

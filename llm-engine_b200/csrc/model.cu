@@ -6,9 +6,12 @@
 // must sum partial results: per layer, (1) RMSNorm + wqkv, RoPE + KV-cache write, attention,
 // wo into the residual stream; (2) RMSNorm + w13, SwiGLU, w2 into the residual stream; then
 // (3) RMSNorm + classifier into the logits. After each segment the residual stream (or the
-// logits) is summed over the ranks: by the communicator's all-reduce (NCCL or the NVLink peer
-// all-reduce), or, for ranks emulated in one process, by a rank-order sum on the device. Rank 0
-// adds the residual before the sum (accumulate), the others contribute their partial only.
+// logits) is summed over the ranks: inside the wo / w2 GEMV itself when the ranks' shards are
+// equal and the communicator has peer receive areas (each CTA exchanges its finished columns
+// with the same CTA of every rank over NVLink), else by the communicator's all-reduce (NCCL or
+// the NVLink peer all-reduce), or, for ranks emulated in one process, by a rank-order sum on
+// the device. Rank 0 adds the residual before the sum (accumulate), the others contribute
+// their partial only.
 // At most 8 tokens per step: RoPE + cache write and SwiGLU are the GEMV's epilogues; wider
 // steps run the separate kernels of decode_ops.cu. The one-token step is captured as a CUDA
 // graph reading its token and position from device memory, so one graph serves every
@@ -283,6 +286,25 @@ int product_fused(llme_model& m, size_t rows, const Proj& w, const float* A, flo
                                       LLME_FLAG_WEIGHTS_STATIC, s, epi);
 }
 
+// A row-parallel product (wo, w2) whose sum over the ranks is taken inside the GEMV when every
+// rank's shard has the same size (so every rank follows the same plan) and the communicator has
+// its peer receive areas; *summed tells the caller to skip the separate all-reduce. Otherwise
+// the plain product (rank 0 adds the residual), summed by the caller.
+int rowpar_product(llme_model& m, size_t rows, const Proj& w, const float* A, float* C, bool lead,
+                   bool equal_shards, cudaStream_t s, bool* summed) {
+    *summed = false;
+    llme::GemvEpilogue epi;
+    if (m.world > 1 && m.comm && equal_shards && llme::comm_peer_sum(m.comm, &epi) == LLME_OK) {
+        const int st = llme::run_product_epilogue(rows, w.n, w.k, A, w.w, w.scale, C, m.q8, nullptr,
+                                                  LLME_FLAG_WEIGHTS_STATIC, s, epi, lead);
+        if (st != LLME_E_UNSUPPORTED) {
+            *summed = st == LLME_OK;
+            return st;
+        }
+    }
+    return product(m, rows, w, A, C, lead, nullptr, s);
+}
+
 int segments(const llme_model& m) { return 2 * m.cfg.n_layers + 1; }
 
 // The buffer summed over the ranks after segment `seg`.
@@ -296,8 +318,9 @@ void reduction_buffer(const llme_model& m, int seg, size_t n, float** buf, size_
     }
 }
 
-int run_segment(llme_model& m, int seg, size_t n, cudaStream_t s) {
+int run_segment(llme_model& m, int seg, size_t n, cudaStream_t s, bool* summed) {
     const int D = m.cfg.dim;
+    *summed = false;
     const bool lead = m.rank == 0;  // adds the residual before the sum
     if (seg == segments(m) - 1) {
         int st = cu(cudaMemsetAsync(m.logits, 0, m.cfg.vocab_size * sizeof(float), s), "model: logits");
@@ -327,7 +350,8 @@ int run_segment(llme_model& m, int seg, size_t n, cudaStream_t s) {
         if (!st)
             st = llme_attention(&m.shape, n, m.feed, m.qkv, L.kc, L.vc, m.att, m.scratch,
                                 LLME_ATTN_AUTOMATIC, s);
-        if (!st) st = product(m, n, L.wo, m.att, m.x, lead, nullptr, s);
+        // Heads split evenly over the ranks, so wo's shards are always the same size.
+        if (!st) st = rowpar_product(m, n, L.wo, m.att, m.x, lead, true, s, summed);
         return st;
     }
     llme::GemvEpilogue swiglu;
@@ -336,7 +360,8 @@ int run_segment(llme_model& m, int seg, size_t n, cudaStream_t s) {
     st = product_fused(m, n, L.w13, m.x, m.gu, L.rms_ffn, swiglu, s, &fused);
     if (!st && !fused)
         st = cu(llme::launch_swiglu(static_cast<int>(n), static_cast<int>(m.hc), m.gu, m.hb, s), "model: swiglu");
-    if (!st) st = product(m, n, L.w2, m.hb, m.x, lead, nullptr, s);
+    if (!st)
+        st = rowpar_product(m, n, L.w2, m.hb, m.x, lead, m.cfg.hidden_dim % m.world == 0, s, summed);
     return st;
 }
 
@@ -345,8 +370,9 @@ int enqueue_step(llme_model& m, size_t n, cudaStream_t s) {
     int st = cu(cudaMemcpyAsync(m.feed, m.feed_host, (n + 1) * sizeof(int), cudaMemcpyHostToDevice, s),
                 "model: feed");
     for (int seg = 0; !st && seg < segments(m); ++seg) {
-        st = run_segment(m, seg, n, s);
-        if (!st && m.world > 1) {
+        bool summed = false;
+        st = run_segment(m, seg, n, s, &summed);
+        if (!st && m.world > 1 && !summed) {
             float* buf;
             size_t count;
             reduction_buffer(m, seg, n, &buf, &count);
@@ -458,7 +484,8 @@ int group_forward(llme_model* const* r, int world, const int* tokens, size_t n, 
         st = cu(cudaMemcpyAsync(r[i]->feed, r[i]->feed_host, (n + 1) * sizeof(int), cudaMemcpyHostToDevice, s),
                 "group: feed");
     for (int seg = 0; !st && seg < segments(m0); ++seg) {
-        for (int i = 0; !st && i < world; ++i) st = run_segment(*r[i], seg, n, s);
+        bool summed = false;  // group ranks have no communicator: always summed here
+        for (int i = 0; !st && i < world; ++i) st = run_segment(*r[i], seg, n, s, &summed);
         if (st) break;
         const bool last = seg == segments(m0) - 1;
         st = cu(llme::launch_rank_sum(m0.group_bufs + (last ? 8 : 0), world,

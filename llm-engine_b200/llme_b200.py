@@ -26,6 +26,7 @@ PATHS = {0: "none", 1: "zero", 2: "naive", 3: "gemv_tma", 4: "gemv_ldg", 5: "til
          9: "tcgen05_f32_skinny"}
 MATH_TENSOR, MATH_FP32 = 0, 1
 FLAG_WEIGHTS_STATIC = 1
+FLAG_SAME_SHARDS = 2
 
 OK, E_INVALID, E_CUDA, E_TIMEOUT, E_UNSUPPORTED, E_NCCL, E_HOST, E_RANGE = range(8)
 

@@ -5,7 +5,9 @@
 * On two GPUs (skipped with fewer): the library's NVLink peer all-reduce, six calls back to
   back with exactly known sums; column-parallel products on n-shards and row-parallel products
   on k-shards (llme_matmul_q8_rowpar, all-reduce inside, residual added once), through the C
-  ABI, against the oracle on the unsharded weights.
+  ABI, against the oracle on the unsharded weights; with equal shards (LLME_FLAG_SAME_SHARDS)
+  the rank sum taken inside the GEMV, bit for bit the separate all-reduce's result on every
+  rank, over repeated back-to-back calls.
 Child processes keep NVLS off (NCCL_NVLS_ENABLE=0), as failure tests on this pool require.
 """
 from __future__ import annotations
@@ -55,6 +57,7 @@ sys.path.insert(0, "llm-engine_b200"); sys.path.insert(0, "oracle")
 import torch, torch.distributed as dist
 import llme_b200 as L, shard, oracle
 rank, world, port, out = int(sys.argv[1]), int(sys.argv[2]), int(sys.argv[3]), sys.argv[4]
+SAME_SHARDS = eval(sys.argv[5])
 torch.cuda.set_device(rank)
 dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                         world_size=world, timeout=datetime.timedelta(seconds=60))
@@ -94,12 +97,40 @@ for (m, k, n) in [(1, 4096, 4096), (4, 11008, 4096), (8, 1024, 2048), (130, 512,
     torch.cuda.synchronize()
     np.save(f"{out}/col_{m}_{rank}.npy", Cc.cpu().numpy())
     np.save(f"{out}/row_{m}_{rank}.npy", Cr.cpu().numpy())
+# Row-parallel products with every rank's shard the same size (FLAG_SAME_SHARDS): the sum over
+# the ranks runs inside the GEMV. Several calls back to back with no host sync (both slots of
+# every CTA reused), each against the separate-all-reduce path on the same inputs.
+fused = {}
+for it in range(3):
+    for (m, k, n) in SAME_SHARDS:
+        A = rng.uniform(-1, 1, (m, k)).astype(np.float32) + it
+        q, s = oracle.quantize_q8((rng.standard_normal((k, n)) * 0.02).astype(np.float32))
+        C0 = rng.uniform(-1, 1, (m, n)).astype(np.float32)
+        Ar, qr = shard.activation_columns(A, world, rank), shard.row_shard(q, world, rank)
+        dAr, dqr, ds = dev(Ar), dev(qr), dev(s)
+        Cf, Cs = dev(C0), dev(C0)
+        for C, fl in ((Cf, L.FLAG_SAME_SHARDS | L.FLAG_WEIGHTS_STATIC), (Cs, L.FLAG_WEIGHTS_STATIC)):
+            comm.matmul_q8_rowpar(m, n, Ar.shape[1], dAr.data_ptr(), dqr.data_ptr(), ds.data_ptr(),
+                                  C.data_ptr(), accumulate=True, flags=fl,
+                                  stream=L.torch_stream_handle())
+        fused[(it, m, k, n)] = (Cf, Cs, dAr, dqr, ds)
+torch.cuda.synchronize()
+L.Comm.status()
+for (it, m, k, n), (Cf, Cs, *_) in fused.items():
+    np.save(f"{out}/fused_{it}_{m}_{k}_{rank}.npy", Cf.cpu().numpy())
+    np.save(f"{out}/sep_{it}_{m}_{k}_{rank}.npy", Cs.cpu().numpy())
 L.synchronize()
 L.Comm.status()
 comm.destroy()
 dist.destroy_process_group()
 print("OK", rank)
 """
+
+
+# (m, k, n) of the row-parallel products with equal shards (k splits evenly over 2 ranks): the
+# 7B decode's wo and w2, several rows, one k slice per strip (a 2 x 128-row k shard).
+SAME_SHARDS = [(1, 4096, 4096), (1, 11008, 4096), (4, 4096, 4096), (8, 11008, 4096),
+               (2, 256, 8192), (3, 2048, 1040)]
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
@@ -109,8 +140,9 @@ def test_tensor_parallel_products_on_two_gpus(tmp_path):
         sk.bind(("127.0.0.1", 0))
         port = sk.getsockname()[1]
     procs = [subprocess.Popen([sys.executable, "-c", TP_WORKER, str(r), str(world), str(port),
-                               str(tmp_path)], cwd=REPO, env=ENV, stdout=subprocess.PIPE,
-                              stderr=subprocess.STDOUT, text=True) for r in range(world)]
+                               str(tmp_path), repr(SAME_SHARDS)], cwd=REPO, env=ENV,
+                              stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+             for r in range(world)]
     outs = [p.communicate(timeout=300)[0] for p in procs]
     for p, o in zip(procs, outs):
         assert p.returncode == 0 and "OK" in o, o[-3000:]
@@ -125,3 +157,27 @@ def test_tensor_parallel_products_on_two_gpus(tmp_path):
         assert close_to(cols, full, k), m
         for r in range(world):
             assert close_to(np.load(tmp_path / f"row_{m}_{r}.npy"), C0 + full, k, 2.0), (m, r)
+    # The in-kernel rank sum adds the same values in the same order as the separate all-reduce,
+    # so both give the same bits, on every rank, and match the oracle.
+    report = []
+    for it in range(3):
+        for (m, k, n) in SAME_SHARDS:
+            A = rng.uniform(-1, 1, (m, k)).astype(np.float32) + it
+            q, s = oracle.quantize_q8((rng.standard_normal((k, n)) * 0.02).astype(np.float32))
+            C0 = rng.uniform(-1, 1, (m, n)).astype(np.float32)
+            want = C0 + oracle.matmul_naive_q8(A, q, s)
+            got = [np.load(tmp_path / f"fused_{it}_{m}_{k}_{r}.npy") for r in range(world)]
+            sep = [np.load(tmp_path / f"sep_{it}_{m}_{k}_{r}.npy") for r in range(world)]
+            bad = []
+            for r in range(world):
+                if not np.array_equal(got[r], sep[0], equal_nan=True):
+                    diff = np.argwhere(~((got[r] == sep[0]) | (np.isnan(got[r]) & np.isnan(sep[0]))))
+                    bad.append(f"rank {r}: {len(diff)} differ from the separate sum, first at "
+                               f"{diff[0].tolist()}")
+                for name, x in (("fused", got[r]), ("separate", sep[r])):
+                    if not close_to(x, want, k, 2.0):
+                        bad.append(f"{name} rank {r}: {int(np.isnan(x).sum())} NaN, "
+                                   f"{int((np.abs(x - want) > 2e-5 * k).sum())} off the oracle")
+            if bad:
+                report.append(f"it {it} (m, k, n) = {(m, k, n)}: " + "; ".join(bad))
+    assert not report, "\n".join(report)
