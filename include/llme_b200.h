@@ -317,6 +317,18 @@ int llme_matmul_f32_rowpar(size_t m, size_t n, size_t k_local, const float* A_lo
                            const float* B_local, float* C, int kernel, int accumulate,
                            unsigned flags, llme_comm_t* comm, void* stream);
 
+/* llme_batch_run for row-parallel products (m = 1..8) with the sum over the ranks taken inside
+ * the launch, the multi-GPU form of the grouped step. Every rank creates its batch from
+ * products of the same shapes in the same order (equal shards, equally aligned pointers), so
+ * every rank's CTA c runs the same units; CTA c sends each unit's finished columns to every
+ * rank over NVLink (plain peer stores into the communicator's receive areas), waits once for
+ * the other ranks' CTA c and writes the rank-ordered sums to C. No separate all-reduce launch.
+ * A product's accumulate applies as given: set it on one rank only to add C once. Needs a
+ * peer-enabled communicator (llme_comm_enable_peer) of 2 to 8 ranks; LLME_E_UNSUPPORTED for an
+ * m >= 128 batch or a batch whose busiest CTA's values exceed the receive area (4096 floats).
+ * A rank that breaks the same-shapes promise gets LLME_E_TIMEOUT from llme_comm_status. */
+int llme_batch_run_rowpar(llme_batch_t* batch, llme_comm_t* comm, unsigned flags, void* stream);
+
 /* ---- the transformer engine (the reference's CudaTransformer, optionally tensor-parallel) -- *
  * The reference's Llama-architecture model (src/model.h; its GPU form CudaTransformer,
  * src/cuda_model.cu:164-270) run by this library from C++: every matmul through the kernels

@@ -899,6 +899,7 @@ struct llme_batch {
     int dev = 0;
     void* dmem = nullptr;
     llme::BatchArgs args;
+    size_t max_cta_units = 0;  // units of the busiest CTA (the rank sum's per-CTA area)
     // Tensor-core batches (m >= 128): the grouped tcgen05 launch and its split-row scratch.
     bool tc = false;
     llme::Q8TcBatchArgs targs;
@@ -977,9 +978,11 @@ int batch_create_tc(llme_batch_t** out, size_t m, size_t count, const llme_q8_pr
     const auto per_cta = lpt_assign(work, grid);
     std::vector<uint2> table;
     std::vector<int> cta_begin(grid + 1, 0);
+    size_t max_cta_units = 0;
     for (int c = 0; c < grid; ++c) {
         cta_begin[c] = static_cast<int>(table.size());
         for (size_t u : per_cta[c]) table.push_back(units[u]);
+        max_cta_units = std::max(max_cta_units, per_cta[c].size());
     }
     cta_begin[grid] = static_cast<int>(table.size());
 
@@ -1130,9 +1133,11 @@ int batch_create(llme_batch_t** out, size_t m, size_t count, const llme_q8_produ
     const auto per_cta = lpt_assign(unit_bytes, grid);
     std::vector<unsigned> table;
     std::vector<int> cta_begin(grid + 1, 0);
+    size_t max_cta_units = 0;
     for (int c = 0; c < grid; ++c) {
         cta_begin[c] = static_cast<int>(table.size());
         for (size_t u : per_cta[c]) table.push_back(units[u]);
+        max_cta_units = std::max(max_cta_units, per_cta[c].size());
     }
     cta_begin[grid] = static_cast<int>(table.size());
     // [maps B][maps A][items][unit table], each part 128-byte aligned.
@@ -1164,6 +1169,7 @@ int batch_create(llme_batch_t** out, size_t m, size_t count, const llme_q8_produ
         delete b;
         return cuda_fail(e, "upload batch");
     }
+    b->max_cta_units = max_cta_units;
     BatchArgs& a = b->args;
     a.m = static_cast<int>(m);
     a.units = static_cast<int>(table.size());
@@ -1323,6 +1329,34 @@ int llme_batch_run(llme_batch_t* b, unsigned flags, void* stream) {
         BatchArgs a = b->args;
         a.stream = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
         a.pdl = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
+        cudaError_t e = launch_gemv_batch(a);
+        return e == cudaSuccess ? LLME_OK : cuda_fail(e, "launch");
+    });
+}
+
+int llme_batch_run_rowpar(llme_batch_t* b, llme_comm_t* comm, unsigned flags, void* stream) {
+    return llme::guarded([&]() -> int {
+        g_error.clear();
+        if (!b) return fail(LLME_E_INVALID, "llme_batch_run_rowpar: null batch");
+        int dev = 0;
+        int st = current_device(&dev);
+        if (st) return st;
+        if (dev != b->dev)
+            return fail(LLME_E_INVALID, "llme_batch_run_rowpar: batch belongs to another device");
+        if (b->tc) return fail(LLME_E_UNSUPPORTED, "llme_batch_run_rowpar: m >= 128 batch");
+        GemvEpilogue epi;
+        st = comm_peer_sum(comm, &epi);
+        if (st) return st;
+        BatchArgs a = b->args;
+        const size_t floats = b->max_cta_units * static_cast<size_t>(a.m) * gemv_tma_cols(true);
+        if (a.grid > epi.peer.units || floats > static_cast<size_t>(epi.peer.unit_floats))
+            return fail(LLME_E_UNSUPPORTED, "llme_batch_run_rowpar: a CTA's " + std::to_string(floats) +
+                                                " values exceed the receive area's " +
+                                                std::to_string(epi.peer.unit_floats));
+        a.stream = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
+        a.pdl = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
+        a.peer_sum = true;
+        a.peer = epi.peer;
         cudaError_t e = launch_gemv_batch(a);
         return e == cudaSuccess ? LLME_OK : cuda_fail(e, "launch");
     });

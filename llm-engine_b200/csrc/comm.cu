@@ -317,14 +317,15 @@ int llme_comm_enable_peer(llme_comm_t* c, size_t max_floats) {
         const size_t slot = (max_floats + 63) / 64 * 64;
         const size_t flags_off = 2 * slot * sizeof(float);
         const size_t ar_bytes = flags_off + kPeerCtas * kPeerMaxRanks * sizeof(unsigned);
-        // The GEMV's in-kernel rank sum: per slot, per CTA of a resident grid (two per SM),
-        // per source rank, the values a CTA owns (at most 8 rows x 128 columns); then a flag
-        // per CTA and source rank.
+        // The GEMVs' in-kernel rank sum: per slot, per CTA of a resident grid (two per SM),
+        // per source rank, the values a CTA owns (a per-call GEMV CTA at most 8 rows x 128
+        // columns, a grouped CTA its units' strips, up to 4096 floats); then a flag per CTA
+        // and source rank.
         int dev = 0, sms = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         const int units = 2 * (sms > 0 ? sms : 148);
-        const int unit_floats = 8 * 128;
+        const int unit_floats = 4096;
         const bool push = c->nranks <= llme::kPeerSumMaxRanks;
         const size_t push_off = (ar_bytes + 255) / 256 * 256;
         const size_t push_flags_off =

@@ -825,7 +825,8 @@ struct BatchLayout {
     static constexpr int kRedFloats = kConsumerWarps * M * S::NT;
     static constexpr int kOffTot = kOffRed + kRedFloats * 4;
     static constexpr int kOffBar = kOffTot + M * S::NT * 4;
-    static constexpr int kBytes = kOffBar + 2 * kStages * 8 + 16;
+    static constexpr int kOffPeer = kOffBar + 2 * kStages * 8 + 16;  // the rank sum's epoch, ok
+    static constexpr int kBytes = kOffPeer + 16;
     static constexpr uint32_t kTx = kBoxBytesB + kABox;
 };
 
@@ -909,8 +910,20 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_batch_kernel(const BatchA
     pdl_wait();
     const int cg = tid % S::TPR, rg = tid / S::TPR;
     int b = 0;
+    const int u_begin = __ldg(a.cta_begin + blockIdx.x);
     const int u_end = __ldg(a.cta_begin + blockIdx.x + 1);
-    for (int u = __ldg(a.cta_begin + blockIdx.x); u < u_end; ++u) {
+    unsigned* peer_state = reinterpret_cast<unsigned*>(smem + L::kOffPeer);
+    const int c = blockIdx.x;
+    if (a.peer_sum && u_begin < u_end) {
+        if (tid == 0) {
+            const unsigned e = __ldcg(a.peer.epoch + c) + 1;
+            a.peer.epoch[c] = e;
+            peer_state[0] = e;
+            peer_state[1] = 1;
+        }
+        named_barrier(1, kConsumers);
+    }
+    for (int u = u_begin; u < u_end; ++u) {
         const unsigned code = __ldg(a.unit_table + u);
         const int item = static_cast<int>(code >> 16), strip = static_cast<int>(code & 0xFFFFu);
         const BatchItem it = a.items[item];
@@ -984,10 +997,54 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_batch_kernel(const BatchA
             if (col < it.n) {
                 v *= sc;
                 float* o = it.C + static_cast<size_t>(r) * it.n + col;
-                *o = it.accumulate ? *o + v : v;
+                if (a.peer_sum) {
+                    if (it.accumulate) v += *o;
+                    const size_t at = static_cast<size_t>(u - u_begin) * M * S::NT + e;
+                    const unsigned slot = peer_state[0] & 1u;
+                    for (int q = 0; q < a.peer.world; ++q)
+                        peer_region(a.peer, q, slot, c, a.peer.rank)[at] = v;
+                } else {
+                    *o = it.accumulate ? *o + v : v;
+                }
             }
         }
         named_barrier(1, kConsumers);  // red is rewritten by the next unit
+    }
+    if (!a.peer_sum || u_begin >= u_end) return;
+
+    // Every unit pushed: one flag per rank, one bounded wait, then the rank-ordered sums.
+    const PeerSum& p = a.peer;
+    const unsigned epoch = peer_state[0], slot = epoch & 1u;
+    __threadfence_system();
+    named_barrier(1, kConsumers);
+    if (tid < p.world) {
+        st_release_sys(peer_flag(p, tid, c, p.rank), epoch);
+        const unsigned* f = peer_flag(p, p.rank, c, tid);
+        const unsigned long long t0 = global_timer_ns();
+        for (uint32_t i = 0; ld_acquire_sys(f) < epoch; ++i) {
+            if ((i & 255) == 255 && global_timer_ns() - t0 > kWaitLimitNs) {
+                atomicExch(p.err, static_cast<unsigned>(LLME_E_TIMEOUT));
+                peer_state[1] = 0;
+                break;
+            }
+        }
+    }
+    named_barrier(1, kConsumers);
+    if (!peer_state[1]) return;
+    for (int u = u_begin; u < u_end; ++u) {
+        const unsigned code = __ldg(a.unit_table + u);
+        const BatchItem& it = a.items[code >> 16];
+        const int col0 = static_cast<int>(code & 0xFFFFu) * S::NT;
+        const int n = it.n;
+        float* C = it.C;
+        for (int e = tid; e < M * S::NT; e += kConsumers) {
+            const int r = e / S::NT, col = col0 + e % S::NT;
+            if (col >= n) continue;
+            const size_t at = static_cast<size_t>(u - u_begin) * M * S::NT + e;
+            float v = __ldcg(peer_region(p, p.rank, slot, c, 0) + at);
+            for (int src = 1; src < p.world; ++src) v += __ldcg(peer_region(p, p.rank, slot, c, src) + at);
+            C[static_cast<size_t>(r) * n + col] = v;
+        }
     }
 }
 

@@ -159,6 +159,14 @@ struct BatchArgs {
     int grid = 0;
     cudaStream_t stream = nullptr;
     bool pdl = false;
+    // The row-parallel sum over the ranks inside the launch (llme_batch_run_rowpar): every
+    // rank runs the same batch, so CTA c owns the same units everywhere. CTA c pushes each
+    // unit's finished strip into its region of every rank's receive area as it goes (unit j of
+    // the CTA at j x m x 128 floats), raises one flag per rank after its last unit, waits once
+    // and writes the rank-ordered sums -- the same slots, flags and epochs as the per-call
+    // GEMV's kEpiPeerSum, indexed by CTA.
+    bool peer_sum = false;
+    PeerSum peer;
 };
 cudaError_t launch_gemv_batch(const BatchArgs& a);
 int gemv_batch_ctas_per_sm();

@@ -150,7 +150,8 @@ def load() -> ctypes.CDLL:
     lib.llme_batch_q8_create.argtypes = [ctypes.POINTER(vp), sz, sz, ctypes.POINTER(Q8Product)]
     lib.llme_batch_run.argtypes = [vp, u, vp]
     lib.llme_batch_destroy.argtypes = [vp]
-    for f in ("llme_batch_q8_create", "llme_batch_run", "llme_batch_destroy"):
+    lib.llme_batch_run_rowpar.argtypes = [vp, vp, u, vp]
+    for f in ("llme_batch_q8_create", "llme_batch_run", "llme_batch_destroy", "llme_batch_run_rowpar"):
         getattr(lib, f).restype = i
     lib.llme_comm_unique_id.argtypes = [ctypes.c_char_p]
     lib.llme_comm_init.argtypes = [ctypes.POINTER(vp), i, i, ctypes.c_char_p, ctypes.c_double]
@@ -324,6 +325,11 @@ class Batch:
 
     def run(self, flags: int = 0, stream: int | None = None) -> None:
         _check(load().llme_batch_run(self.handle, flags, stream or None))
+
+    def run_rowpar(self, comm, flags: int = 0, stream: int | None = None) -> None:
+        """The batch with the sum over the ranks taken inside the launch (row-parallel products,
+        every rank running a batch of the same shapes)."""
+        _check(load().llme_batch_run_rowpar(self.handle, comm.handle, flags, stream or None))
 
     def destroy(self) -> None:
         if self.handle:

@@ -7,7 +7,9 @@
   on k-shards (llme_matmul_q8_rowpar, all-reduce inside, residual added once), through the C
   ABI, against the oracle on the unsharded weights; with equal shards (LLME_FLAG_SAME_SHARDS)
   the rank sum taken inside the GEMV, bit for bit the separate all-reduce's result on every
-  rank, over repeated back-to-back calls.
+  rank, over repeated back-to-back calls; and a grouped row-parallel batch with the rank sum
+  inside its launch (llme_batch_run_rowpar), against the plain batch + all-reduce and the
+  oracle.
 Child processes keep NVLS off (NCCL_NVLS_ENABLE=0), as failure tests on this pool require.
 """
 from __future__ import annotations
@@ -58,6 +60,7 @@ import torch, torch.distributed as dist
 import llme_b200 as L, shard, oracle
 rank, world, port, out = int(sys.argv[1]), int(sys.argv[2]), int(sys.argv[3]), sys.argv[4]
 SAME_SHARDS = eval(sys.argv[5])
+BATCH = eval(sys.argv[6])
 torch.cuda.set_device(rank)
 dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                         world_size=world, timeout=datetime.timedelta(seconds=60))
@@ -119,6 +122,39 @@ L.Comm.status()
 for (it, m, k, n), (Cf, Cs, *_) in fused.items():
     np.save(f"{out}/fused_{it}_{m}_{k}_{rank}.npy", Cf.cpu().numpy())
     np.save(f"{out}/sep_{it}_{m}_{k}_{rank}.npy", Cs.cpu().numpy())
+# A row-parallel batch (equal shards) with the sum over the ranks inside the launch, against
+# the same batch run plainly and summed by the peer all-reduce; rank 0 adds C0 (accumulate).
+prods = []
+for (k, n) in BATCH:
+    A = rng.uniform(-1, 1, (1, k)).astype(np.float32)
+    q, s = oracle.quantize_q8((rng.standard_normal((k, n)) * 0.02).astype(np.float32))
+    prods.append((dev(shard.activation_columns(A, world, rank)), dev(shard.row_shard(q, world, rank)),
+                  dev(s), k // world, n))
+C0 = [rng.uniform(-1, 1, (1, n)).astype(np.float32) for (_, n) in BATCH]
+offs = np.cumsum([0] + [(n + 3) // 4 * 4 for (_, n) in BATCH])
+Cf = torch.zeros(int(offs[-1]), device="cuda")
+Cs = torch.zeros(int(offs[-1]), device="cuda")
+acc = 1 if rank == 0 else 0
+def batch(C):
+    return L.Batch(1, [(n, kl, a.data_ptr(), b.data_ptr(), sc.data_ptr(), C.data_ptr() + 4 * int(o), acc)
+                       for (a, b, sc, kl, n), o in zip(prods, offs[:-1])])
+bf, bs = batch(Cf), batch(Cs)
+h = L.torch_stream_handle()
+runs = []
+for it in range(3):
+    for C in (Cf, Cs):
+        for (kk, n), o, c0 in zip(BATCH, offs[:-1], C0):
+            C[int(o):int(o) + n].copy_(torch.from_numpy(c0[0]))
+    bf.run_rowpar(comm, L.FLAG_WEIGHTS_STATIC, h)
+    bs.run(L.FLAG_WEIGHTS_STATIC, h)
+    comm.allreduce_sum_f32(Cs.data_ptr(), Cs.numel(), stream=h)
+    runs.append((Cf.clone(), Cs.clone()))
+torch.cuda.synchronize()
+L.Comm.status()
+for it, (f, sp) in enumerate(runs):
+    np.save(f"{out}/batchf_{it}_{rank}.npy", f.cpu().numpy())
+    np.save(f"{out}/batchs_{it}_{rank}.npy", sp.cpu().numpy())
+bf.destroy(); bs.destroy()
 L.synchronize()
 L.Comm.status()
 comm.destroy()
@@ -131,6 +167,9 @@ print("OK", rank)
 # 7B decode's wo and w2, several rows, one k slice per strip (a 2 x 128-row k shard).
 SAME_SHARDS = [(1, 4096, 4096), (1, 11008, 4096), (4, 4096, 4096), (8, 11008, 4096),
                (2, 256, 8192), (3, 2048, 1040)]
+# (k, n) of a grouped row-parallel step: the decode's wo / w2 shapes and enough small products
+# that CTAs run several units each.
+BATCH = [(4096, 4096), (11008, 4096), (2048, 1040)] + [(256, 2048)] * 24
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
@@ -140,7 +179,7 @@ def test_tensor_parallel_products_on_two_gpus(tmp_path):
         sk.bind(("127.0.0.1", 0))
         port = sk.getsockname()[1]
     procs = [subprocess.Popen([sys.executable, "-c", TP_WORKER, str(r), str(world), str(port),
-                               str(tmp_path), repr(SAME_SHARDS)], cwd=REPO, env=ENV,
+                               str(tmp_path), repr(SAME_SHARDS), repr(BATCH)], cwd=REPO, env=ENV,
                               stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
              for r in range(world)]
     outs = [p.communicate(timeout=300)[0] for p in procs]
@@ -180,4 +219,24 @@ def test_tensor_parallel_products_on_two_gpus(tmp_path):
                                    f"{int((np.abs(x - want) > 2e-5 * k).sum())} off the oracle")
             if bad:
                 report.append(f"it {it} (m, k, n) = {(m, k, n)}: " + "; ".join(bad))
+    # The grouped row-parallel step: the in-launch sum equals the plain batch + all-reduce bit
+    # for bit on both ranks, and the oracle on the unsharded products (C0 added once).
+    want = []
+    for (k, n) in BATCH:
+        A = rng.uniform(-1, 1, (1, k)).astype(np.float32)
+        q, s = oracle.quantize_q8((rng.standard_normal((k, n)) * 0.02).astype(np.float32))
+        want.append(oracle.matmul_naive_q8(A, q, s))
+    C0 = [rng.uniform(-1, 1, (1, n)).astype(np.float32) for (_, n) in BATCH]
+    offs = np.cumsum([0] + [(n + 3) // 4 * 4 for (_, n) in BATCH])
+    for it in range(3):
+        f = [np.load(tmp_path / f"batchf_{it}_{r}.npy") for r in range(world)]
+        sp = np.load(tmp_path / f"batchs_{it}_0.npy")
+        for r in range(world):
+            if not np.array_equal(f[r], sp):
+                report.append(f"batch it {it} rank {r}: {int((f[r] != sp).sum())} differ from the "
+                              "plain batch + all-reduce")
+        for (k, n), o, w, c0 in zip(BATCH, offs[:-1], want, C0):
+            got = f[0][int(o):int(o) + n][None, :]
+            if not close_to(got, c0 + w, k, 2.0):
+                report.append(f"batch it {it} (k, n) = {(k, n)}: off the oracle")
     assert not report, "\n".join(report)
