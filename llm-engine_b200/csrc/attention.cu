@@ -15,7 +15,8 @@
 // two-level tree: the CTA completing a group of 64 chunks' ticket merges that group in chunk
 // order, the CTA completing the (head group, row)'s ticket merges the groups in group order --
 // deterministic, no second launch, tickets reset for the next call. Chunks are sized for
-// about two to three CTAs per SM; the grid is sized for seq_len and the context length is
+// about three CTAs per SM (a tensor-parallel rank's 16 or 8 heads get shorter chunks in one
+// wave); the grid is sized for seq_len and the context length is
 // read from device memory, so a graph captured once serves every position; chunks past the
 // context exit at once.
 //
@@ -40,7 +41,7 @@ __device__ unsigned int g_attn_error;
 
 constexpr int kAttnThreads = 256;
 constexpr int kMinChunk = 64;               // positions per split CTA, at least
-constexpr int kTargetCtas = 296;            // split CTAs a single row aims for (2 per SM)
+constexpr int kTargetCtas = 444;            // split CTAs a single row aims for (3 per SM)
 // A split CTA's shared memory, at most: three CTAs per SM, so some load while others compute
 // (measured on B200: 7B MHA decode 41 us against 47 us with two larger CTAs per SM).
 constexpr size_t kSplitSmemBudget = 72 * 1024;
