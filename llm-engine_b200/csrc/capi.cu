@@ -1349,10 +1349,10 @@ int llme_batch_run_rowpar(llme_batch_t* b, llme_comm_t* comm, unsigned flags, vo
         if (st) return st;
         BatchArgs a = b->args;
         const size_t floats = b->max_cta_units * static_cast<size_t>(a.m) * gemv_tma_cols(true);
-        if (a.grid > epi.peer.units || floats > static_cast<size_t>(epi.peer.unit_floats))
+        if (a.grid > epi.peer.units || floats > static_cast<size_t>(epi.peer.unit_words))
             return fail(LLME_E_UNSUPPORTED, "llme_batch_run_rowpar: a CTA's " + std::to_string(floats) +
                                                 " values exceed the receive area's " +
-                                                std::to_string(epi.peer.unit_floats));
+                                                std::to_string(epi.peer.unit_words));
         a.stream = stream ? static_cast<cudaStream_t>(stream) : cudaStreamPerThread;
         a.pdl = (flags & LLME_FLAG_WEIGHTS_STATIC) != 0;
         a.peer_sum = true;

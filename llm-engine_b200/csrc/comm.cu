@@ -318,21 +318,18 @@ int llme_comm_enable_peer(llme_comm_t* c, size_t max_floats) {
         const size_t flags_off = 2 * slot * sizeof(float);
         const size_t ar_bytes = flags_off + kPeerCtas * kPeerMaxRanks * sizeof(unsigned);
         // The GEMVs' in-kernel rank sum: per slot, per CTA of a resident grid (two per SM),
-        // per source rank, the values a CTA owns (a per-call GEMV CTA at most 8 rows x 128
-        // columns, a grouped CTA its units' strips, up to 4096 floats); then a flag per CTA
-        // and source rank.
+        // per source rank, the epoch-tagged 64-bit words of the values a CTA owns (a per-call
+        // GEMV CTA at most 8 rows x 128 columns, a grouped CTA its units' strips, up to 2048).
         int dev = 0, sms = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         const int units = 2 * (sms > 0 ? sms : 148);
-        const int unit_floats = 4096;
+        const int unit_words = 2048;
         const bool push = c->nranks <= llme::kPeerSumMaxRanks;
         const size_t push_off = (ar_bytes + 255) / 256 * 256;
-        const size_t push_flags_off =
-            2 * static_cast<size_t>(units) * c->nranks * unit_floats * sizeof(float);
-        const size_t bytes =
-            push ? push_off + push_flags_off + static_cast<size_t>(units) * llme::kPeerFlagStride * sizeof(unsigned)
-                 : ar_bytes;
+        const size_t push_bytes =
+            2 * static_cast<size_t>(units) * c->nranks * unit_words * sizeof(unsigned long long);
+        const size_t bytes = push ? push_off + push_bytes : ar_bytes;
         cudaError_t e = cudaMalloc(&c->peer_buf, bytes);
         if (e == cudaSuccess) e = cudaMemset(c->peer_buf, 0, bytes);
         if (e == cudaSuccess) e = cudaMalloc(&c->peer_epoch, kPeerCtas * sizeof(unsigned));
@@ -399,10 +396,10 @@ int llme_comm_enable_peer(llme_comm_t* c, size_t max_floats) {
         if (push) {
             llme::PeerSum& ps = c->push;
             for (int q = 0; q < c->nranks; ++q)
-                ps.base[q] = reinterpret_cast<float*>(reinterpret_cast<char*>(pa.base[q]) + push_off);
-            ps.flags_off = push_flags_off;
+                ps.base[q] = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(pa.base[q]) +
+                                                                   push_off);
             ps.units = units;
-            ps.unit_floats = unit_floats;
+            ps.unit_words = unit_words;
             ps.epoch = static_cast<unsigned*>(c->push_epoch);
             ps.err = pa.err;
             ps.world = c->nranks;

@@ -231,6 +231,37 @@ __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// A 64-bit word written and read as one access at system scope: a value and its tag that
+// cross NVLink together.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Reads the tagged word at p once its tag (high 32 bits) equals `tag`, returning the value
+// (low 32 bits as a float); after kWaitLimitNs sets *err and returns 0.
+__device__ __forceinline__ float wait_tagged(const unsigned long long* p, unsigned tag,
+                                             unsigned* err) {
+    unsigned long long w = ld_relaxed_sys_u64(p);
+    if (static_cast<unsigned>(w >> 32) == tag) return __uint_as_float(static_cast<unsigned>(w));
+    const unsigned long long t0 = global_timer_ns();
+    for (uint32_t i = 0;; ++i) {
+        w = ld_relaxed_sys_u64(p);
+        if (static_cast<unsigned>(w >> 32) == tag) return __uint_as_float(static_cast<unsigned>(w));
+        if ((i & 255) == 255 && global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicExch(err, static_cast<unsigned>(LLME_E_TIMEOUT));
+            return 0.0f;
+        }
+    }
+}
+__device__ __forceinline__ unsigned long long tagged(float v, unsigned tag) {
+    return (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+}
+
 // RMSNorm's eps, as the reference's ops.h / cuda_util.cuh.
 constexpr float kRmsEps = 1e-5f;
 

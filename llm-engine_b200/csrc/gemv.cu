@@ -253,18 +253,16 @@ __device__ __forceinline__ void epilogue_pair(const GemvArgs& a, int r, int col,
 
 // ---- kEpiPeerSum: the row-parallel sum over the ranks, inside the GEMV ----------------------
 
-__device__ __forceinline__ float* peer_region(const PeerSum& p, int q, unsigned slot, int unit, int src) {
-    return p.base[q] + ((static_cast<size_t>(slot) * p.units + unit) * p.world + src) * p.unit_floats;
-}
-__device__ __forceinline__ unsigned* peer_flag(const PeerSum& p, int q, int unit, int src) {
-    return reinterpret_cast<unsigned*>(reinterpret_cast<char*>(p.base[q]) + p.flags_off) +
-           static_cast<size_t>(unit) * kPeerFlagStride + src;
+__device__ __forceinline__ unsigned long long* peer_region(const PeerSum& p, int q, unsigned slot,
+                                                           int unit, int src) {
+    return p.base[q] + ((static_cast<size_t>(slot) * p.units + unit) * p.world + src) * p.unit_words;
 }
 
 // The `count` values this CTA owns, exchanged with the same CTA of every rank and summed in
 // rank order into C. value(e) is owned element e's finished value (partial, scaled), where(e,
 // r, col) its place in C (col >= n: padding, skipped). Every one of the nthreads consumer
-// threads calls this; `state` is two words of this CTA's shared memory.
+// threads calls this; `state` is a word of this CTA's shared memory. A thread reads back only
+// the elements it wrote, so after the epoch is known no barrier is needed.
 template <typename Value, typename Where>
 __device__ __forceinline__ void peer_sum_store(const GemvArgs& a, int count, Value value, Where where,
                                                unsigned* state, int tid, int nthreads) {
@@ -274,7 +272,6 @@ __device__ __forceinline__ void peer_sum_store(const GemvArgs& a, int count, Val
         const unsigned e = __ldcg(p.epoch + unit) + 1;
         p.epoch[unit] = e;
         state[0] = e;
-        state[1] = 1;
     }
     named_barrier(1, nthreads);
     const unsigned epoch = state[0];
@@ -284,31 +281,18 @@ __device__ __forceinline__ void peer_sum_store(const GemvArgs& a, int count, Val
         where(e, r, col);
         if (col >= a.n) continue;
         float v = value(e);
-        if (a.accumulate) v += a.C[static_cast<size_t>(r) * a.n + col];
-        for (int q = 0; q < p.world; ++q) peer_region(p, q, slot, unit, p.rank)[e] = v;
+        float* o = a.C + static_cast<size_t>(r) * a.n + col;
+        if (a.accumulate) v += *o;
+        const unsigned long long w = tagged(v, epoch);
+        for (int q = 0; q < p.world; ++q) st_relaxed_sys_u64(peer_region(p, q, slot, unit, p.rank) + e, w);
     }
-    __threadfence_system();
-    named_barrier(1, nthreads);
-    if (tid < p.world) {
-        st_release_sys(peer_flag(p, tid, unit, p.rank), epoch);
-        const unsigned* f = peer_flag(p, p.rank, unit, tid);
-        const unsigned long long t0 = global_timer_ns();
-        for (uint32_t i = 0; ld_acquire_sys(f) < epoch; ++i) {
-            if ((i & 255) == 255 && global_timer_ns() - t0 > kWaitLimitNs) {
-                atomicExch(p.err, static_cast<unsigned>(LLME_E_TIMEOUT));
-                state[1] = 0;
-                break;
-            }
-        }
-    }
-    named_barrier(1, nthreads);
-    if (!state[1]) return;
     for (int e = tid; e < count; e += nthreads) {
         int r, col;
         where(e, r, col);
         if (col >= a.n) continue;
-        float v = __ldcg(peer_region(p, p.rank, slot, unit, 0) + e);
-        for (int src = 1; src < p.world; ++src) v += __ldcg(peer_region(p, p.rank, slot, unit, src) + e);
+        float v = wait_tagged(peer_region(p, p.rank, slot, unit, 0) + e, epoch, p.err);
+        for (int src = 1; src < p.world; ++src)
+            v += wait_tagged(peer_region(p, p.rank, slot, unit, src) + e, epoch, p.err);
         a.C[static_cast<size_t>(r) * a.n + col] = v;
     }
 }
@@ -919,7 +903,6 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_batch_kernel(const BatchA
             const unsigned e = __ldcg(a.peer.epoch + c) + 1;
             a.peer.epoch[c] = e;
             peer_state[0] = e;
-            peer_state[1] = 1;
         }
         named_barrier(1, kConsumers);
     }
@@ -1000,9 +983,10 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_batch_kernel(const BatchA
                 if (a.peer_sum) {
                     if (it.accumulate) v += *o;
                     const size_t at = static_cast<size_t>(u - u_begin) * M * S::NT + e;
-                    const unsigned slot = peer_state[0] & 1u;
+                    const unsigned epoch = peer_state[0];
+                    const unsigned long long w = tagged(v, epoch);
                     for (int q = 0; q < a.peer.world; ++q)
-                        peer_region(a.peer, q, slot, c, a.peer.rank)[at] = v;
+                        st_relaxed_sys_u64(peer_region(a.peer, q, epoch & 1u, c, a.peer.rank) + at, w);
                 } else {
                     *o = it.accumulate ? *o + v : v;
                 }
@@ -1012,25 +996,10 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_batch_kernel(const BatchA
     }
     if (!a.peer_sum || u_begin >= u_end) return;
 
-    // Every unit pushed: one flag per rank, one bounded wait, then the rank-ordered sums.
+    // Every unit written: each thread reads back the ranks' words of the elements it wrote, in
+    // rank order, and writes the sums.
     const PeerSum& p = a.peer;
     const unsigned epoch = peer_state[0], slot = epoch & 1u;
-    __threadfence_system();
-    named_barrier(1, kConsumers);
-    if (tid < p.world) {
-        st_release_sys(peer_flag(p, tid, c, p.rank), epoch);
-        const unsigned* f = peer_flag(p, p.rank, c, tid);
-        const unsigned long long t0 = global_timer_ns();
-        for (uint32_t i = 0; ld_acquire_sys(f) < epoch; ++i) {
-            if ((i & 255) == 255 && global_timer_ns() - t0 > kWaitLimitNs) {
-                atomicExch(p.err, static_cast<unsigned>(LLME_E_TIMEOUT));
-                peer_state[1] = 0;
-                break;
-            }
-        }
-    }
-    named_barrier(1, kConsumers);
-    if (!peer_state[1]) return;
     for (int u = u_begin; u < u_end; ++u) {
         const unsigned code = __ldg(a.unit_table + u);
         const BatchItem& it = a.items[code >> 16];
@@ -1041,8 +1010,9 @@ __global__ void __launch_bounds__(kTmaThreads, 2) gemv_batch_kernel(const BatchA
             const int r = e / S::NT, col = col0 + e % S::NT;
             if (col >= n) continue;
             const size_t at = static_cast<size_t>(u - u_begin) * M * S::NT + e;
-            float v = __ldcg(peer_region(p, p.rank, slot, c, 0) + at);
-            for (int src = 1; src < p.world; ++src) v += __ldcg(peer_region(p, p.rank, slot, c, src) + at);
+            float v = wait_tagged(peer_region(p, p.rank, slot, c, 0) + at, epoch, p.err);
+            for (int src = 1; src < p.world; ++src)
+                v += wait_tagged(peer_region(p, p.rank, slot, c, src) + at, epoch, p.err);
             C[static_cast<size_t>(r) * n + col] = v;
         }
     }

@@ -60,21 +60,22 @@ struct SplitScratch {
 enum GemvEpilogueKind { kEpiStore = 0, kEpiRopeCache = 1, kEpiSwiglu = 2, kEpiPeerSum = 3 };
 
 // kEpiPeerSum: the tensor-parallel sum of a row-parallel product taken inside the GEMV. Every
-// rank runs the same plan, so CTA u owns the same output elements on every rank. CTA u pushes
-// its finished values (its partial, plus C on the rank that accumulates) into region
-// (slot, u, this rank) of every rank's receive area with plain peer stores, raises flag
-// (u, this rank) there with a release store, waits (bounded) until flag (u, src) of its own
-// area reaches the call's epoch for every src, and writes the sum over src = 0, 1, ... to C --
-// the same bits on every rank. A per-CTA epoch in device memory picks the slot (epoch & 1),
-// so back-to-back calls and CUDA-graph replays never overwrite a region a peer is still
-// reading: a rank reaches epoch e + 2 of CTA u only after every peer raised e + 1 there.
+// rank runs the same plan, so CTA u owns the same output elements on every rank. CTA u writes
+// each finished value (its partial, plus C on the rank that accumulates) into region
+// (slot, u, this rank) of every rank's receive area as one 64-bit word, the value's bits
+// tagged with the call's epoch (a single relaxed system-scope store, so the value and its
+// tag land together: no fence and no separate flag). The thread that owns an element then
+// polls (bounded) region (slot, u, src) of its own area until src's word carries the epoch,
+// for src = 0, 1, ..., and writes the sum in that order to C -- the same bits on every rank.
+// A per-CTA epoch in device memory picks the slot (epoch & 1), so back-to-back calls and
+// CUDA-graph replays never overwrite a word a peer has not read yet: a rank writes epoch
+// e + 2 of CTA u only after reading every peer's e + 1 there, written after that peer's
+// kernel of epoch e (which read e) had finished.
 constexpr int kPeerSumMaxRanks = 8;
-constexpr int kPeerFlagStride = 16;   // flags per unit (one per source rank, up to 16 ranks)
 struct PeerSum {
-    float* base[kPeerSumMaxRanks] = {};  // every rank's receive area, this rank's included
-    size_t flags_off = 0;                // bytes from a receive area to its flags
+    unsigned long long* base[kPeerSumMaxRanks] = {};  // every rank's receive area (own too)
     int units = 0;                       // CTAs a call may have (grid x * grid y)
-    int unit_floats = 0;                 // values a CTA owns at most
+    int unit_words = 0;                  // values a CTA owns at most
     unsigned* epoch = nullptr;           // `units` counters, this rank's memory
     unsigned* err = nullptr;             // device error word (LLME_E_TIMEOUT)
     int world = 0, rank = 0;
@@ -160,11 +161,11 @@ struct BatchArgs {
     cudaStream_t stream = nullptr;
     bool pdl = false;
     // The row-parallel sum over the ranks inside the launch (llme_batch_run_rowpar): every
-    // rank runs the same batch, so CTA c owns the same units everywhere. CTA c pushes each
-    // unit's finished strip into its region of every rank's receive area as it goes (unit j of
-    // the CTA at j x m x 128 floats), raises one flag per rank after its last unit, waits once
-    // and writes the rank-ordered sums -- the same slots, flags and epochs as the per-call
-    // GEMV's kEpiPeerSum, indexed by CTA.
+    // rank runs the same batch, so CTA c owns the same units everywhere. CTA c writes each
+    // unit's finished strip, epoch-tagged, into its region of every rank's receive area as it
+    // goes (unit j of the CTA at j x m x 128 words), and after its last unit reads the ranks'
+    // words back in rank order and writes the sums -- the same slots, tags and epochs as the
+    // per-call GEMV's kEpiPeerSum, indexed by CTA.
     bool peer_sum = false;
     PeerSum peer;
 };
