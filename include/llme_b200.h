@@ -293,9 +293,12 @@ int llme_comm_rank(const llme_comm_t* comm);
 
 /* Switches llme_allreduce_sum_f32 (up to max_floats values) from NCCL to the library's own
  * one-shot all-reduce over NVLink peer memory: a symmetric buffer per rank shared through CUDA
- * IPC (handles exchanged once over this communicator; collective: every rank calls it), per-CTA
- * arrival flags with bounded waits, and sums taken in rank order, so every rank gets the same
- * bits. Plain peer loads and stores only. Call before capturing graphs. */
+ * IPC (handles exchanged once over this communicator; collective: every rank calls it); every
+ * rank writes its values into every rank's buffer as epoch-tagged 64-bit words and sums the
+ * words it receives in rank order once their tags match (bounded waits), so every rank gets
+ * the same bits. Plain peer stores and local loads only. Also sets up the receive areas of the
+ * in-kernel rank sums (LLME_FLAG_SAME_SHARDS, llme_batch_run_rowpar). Call before capturing
+ * graphs. */
 int llme_comm_enable_peer(llme_comm_t* comm, size_t max_floats);
 
 /* Reads and clears the peer all-reduce's device error word: LLME_E_TIMEOUT if a peer did not

@@ -27,12 +27,11 @@ constexpr int kPeerCtas = 64;
 constexpr int kPeerThreads = 256;
 
 // Device-side view of the peer all-reduce: every rank's symmetric buffer mapped into this
-// process (own included), laid out as [2 slots x max_floats floats][flags: kPeerCtas x
-// kPeerMaxRanks u32], plus this rank's per-CTA call counters.
+// process (own included), laid out as [2 slots][nranks sources][slot_words] epoch-tagged
+// 64-bit words, plus this rank's per-CTA call counters.
 struct PeerArgs {
-    float* base[kPeerMaxRanks];
-    size_t slot_floats;
-    size_t flags_off;  // bytes from base to the flags
+    unsigned long long* base[kPeerMaxRanks];
+    size_t slot_words;
     unsigned* epoch;   // kPeerCtas counters (local memory)
     unsigned* err;     // device error word
     int nranks, rank;
@@ -134,102 +133,38 @@ constexpr double kEnqueueTimeoutS = 60.0;
 __device__ unsigned int g_comm_error;
 
 // One-shot all-reduce over NVLink peer memory, in place on `data` (count floats, identical
-// on every rank). CTA b owns elements [b*chunk, (b+1)*chunk): it copies them into slot
-// (epoch & 1) of this rank's symmetric buffer, raises its flag on every rank, waits (bounded)
-// for the same CTA of every rank to do the same, then sums the slots of ranks 0..n-1 in that
-// order -- so every rank gets the same bits. Two slots and monotonic per-CTA epochs make
-// back-to-back calls (and CUDA-graph replays) safe: a rank can only reuse a slot after every
-// peer has started the following call, i.e. finished reading it.
+// on every rank). CTA b owns elements [b*chunk, (b+1)*chunk). Each thread writes its elements
+// into source row `rank` of slot (epoch & 1) of every rank's buffer as 64-bit words, the value's
+// bits tagged with the call's epoch (one relaxed system-scope store: value and tag cross NVLink
+// together), then reads the same elements back from its own buffer, source by source in rank
+// order, each once its tag matches (bounded wait), and stores the sum -- so every rank gets the
+// same bits, with no fence, flag or remote read. Two slots and monotonic per-CTA epochs make
+// back-to-back calls (and CUDA-graph replays) safe: a rank writes epoch e + 2 of CTA b only
+// after reading every peer's e + 1, written after that peer's kernel of epoch e had finished.
 __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(float* __restrict__ data,
                                                                         size_t count,
                                                                         const PeerArgs p) {
     __shared__ unsigned s_epoch;
-    __shared__ int s_ok;
     const int b = blockIdx.x, tid = threadIdx.x;
     if (tid == 0) {
         s_epoch = p.epoch[b] + 1;
         p.epoch[b] = s_epoch;
-        s_ok = 1;
     }
     __syncthreads();
     const unsigned e = s_epoch;
     const size_t chunk = ((count + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
     const size_t lo = min(count, b * chunk), hi = min(count, lo + chunk);
-    const size_t slot = (e & 1u) * p.slot_floats;
-    float* mine = p.base[p.rank] + slot;
-    // lo is a multiple of 4 and slots are 64-float aligned; data is 16-byte aligned when
-    // vec (checked by the host), so float4 moves cover [lo, lo + 4 * n4).
-    const bool vec = (reinterpret_cast<uintptr_t>(data) & 15) == 0;
-    const size_t n4 = vec ? (hi - lo) / 4 : 0;
-    for (size_t i = tid; i < n4; i += kPeerThreads)
-        reinterpret_cast<float4*>(mine + lo)[i] = reinterpret_cast<const float4*>(data + lo)[i];
-    for (size_t i = lo + 4 * n4 + tid; i < hi; i += kPeerThreads) mine[i] = data[i];
-    __threadfence_system();
-    __syncthreads();
-    if (tid < p.nranks) {
-        unsigned* flags = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(p.base[tid]) + p.flags_off);
-        llme::st_release_sys(flags + b * kPeerMaxRanks + p.rank, e);
-        const unsigned* my_flags =
-            reinterpret_cast<const unsigned*>(reinterpret_cast<char*>(p.base[p.rank]) + p.flags_off);
-        const unsigned* f = my_flags + b * kPeerMaxRanks + tid;
-        const unsigned long long t0 = llme::global_timer_ns();
-        for (uint32_t i = 0; llme::ld_acquire_sys(f) < e; ++i) {
-            if ((i & 255) == 255 && llme::global_timer_ns() - t0 > llme::kWaitLimitNs) {
-                atomicExch(p.err, static_cast<unsigned>(LLME_E_TIMEOUT));
-                s_ok = 0;
-                break;
-            }
-        }
+    const size_t row = p.slot_words;                        // words of one source row
+    const size_t slot = (e & 1u) * static_cast<size_t>(p.nranks) * row;
+    for (size_t i = lo + tid; i < hi; i += kPeerThreads) {
+        const unsigned long long w = llme::tagged(data[i], e);
+        for (int q = 0; q < p.nranks; ++q)
+            llme::st_relaxed_sys_u64(p.base[q] + slot + static_cast<size_t>(p.rank) * row + i, w);
     }
-    __syncthreads();
-    if (!s_ok) return;
-    // Every rank's value of a float4 is requested before the first add (8 ranks at most in
-    // flight per vector, two vectors per step), then summed in rank order.
-    constexpr int kMaxR = 8;
-    if (p.nranks <= kMaxR) {
-        for (size_t i = tid; i < n4; i += 2 * kPeerThreads) {
-            const size_t i2 = i + kPeerThreads;
-            float4 t[2][kMaxR];
-#pragma unroll
-            for (int r = 0; r < kMaxR; ++r) {
-                if (r < p.nranks) {
-                    const float4* src = reinterpret_cast<const float4*>(p.base[r] + slot + lo);
-                    t[0][r] = __ldcg(src + i);
-                    if (i2 < n4) t[1][r] = __ldcg(src + i2);
-                }
-            }
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                if (h == 1 && i2 >= n4) break;
-                float4 v = t[h][0];
-#pragma unroll
-                for (int r = 1; r < kMaxR; ++r) {
-                    if (r < p.nranks) {
-                        v.x += t[h][r].x;
-                        v.y += t[h][r].y;
-                        v.z += t[h][r].z;
-                        v.w += t[h][r].w;
-                    }
-                }
-                reinterpret_cast<float4*>(data + lo)[h ? i2 : i] = v;
-            }
-        }
-    } else {
-        for (size_t i = tid; i < n4; i += kPeerThreads) {
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int r = 0; r < p.nranks; ++r) {
-                const float4 t = __ldcg(reinterpret_cast<const float4*>(p.base[r] + slot + lo) + i);
-                v.x += t.x;
-                v.y += t.y;
-                v.z += t.z;
-                v.w += t.w;
-            }
-            reinterpret_cast<float4*>(data + lo)[i] = v;
-        }
-    }
-    for (size_t i = lo + 4 * n4 + tid; i < hi; i += kPeerThreads) {
-        float v = 0.0f;
-        for (int r = 0; r < p.nranks; ++r) v += __ldcg(p.base[r] + slot + i);
+    for (size_t i = lo + tid; i < hi; i += kPeerThreads) {
+        const unsigned long long* mine = p.base[p.rank] + slot + i;
+        float v = llme::wait_tagged(mine, e, p.err);
+        for (int r = 1; r < p.nranks; ++r) v += llme::wait_tagged(mine + static_cast<size_t>(r) * row, e, p.err);
         data[i] = v;
     }
 }
@@ -315,8 +250,7 @@ int llme_comm_enable_peer(llme_comm_t* c, size_t max_floats) {
         if (c->nranks > kPeerMaxRanks)
             return llme::set_error(LLME_E_UNSUPPORTED, "llme_comm_enable_peer: more than 16 ranks");
         const size_t slot = (max_floats + 63) / 64 * 64;
-        const size_t flags_off = 2 * slot * sizeof(float);
-        const size_t ar_bytes = flags_off + kPeerCtas * kPeerMaxRanks * sizeof(unsigned);
+        const size_t ar_bytes = 2 * static_cast<size_t>(c->nranks) * slot * sizeof(unsigned long long);
         // The GEMVs' in-kernel rank sum: per slot, per CTA of a resident grid (two per SM),
         // per source rank, the epoch-tagged 64-bit words of the values a CTA owns (a per-call
         // GEMV CTA at most 8 rows x 128 columns, a grouped CTA its units' strips, up to 2048).
@@ -373,7 +307,7 @@ int llme_comm_enable_peer(llme_comm_t* c, size_t max_floats) {
         PeerArgs& pa = c->pargs;
         for (int q = 0; q < c->nranks; ++q) {
             if (q == c->rank) {
-                pa.base[q] = static_cast<float*>(c->peer_buf);
+                pa.base[q] = static_cast<unsigned long long*>(c->peer_buf);
                 continue;
             }
             void* ptr = nullptr;
@@ -383,12 +317,11 @@ int llme_comm_enable_peer(llme_comm_t* c, size_t max_floats) {
                 return llme::set_cuda_error(e, "open peer buffer");
             }
             c->peer_opened[q] = ptr;
-            pa.base[q] = static_cast<float*>(ptr);
+            pa.base[q] = static_cast<unsigned long long*>(ptr);
         }
         void* err = nullptr;
         cudaGetSymbolAddress(&err, g_comm_error);
-        pa.slot_floats = slot;
-        pa.flags_off = flags_off;
+        pa.slot_words = slot;
         pa.epoch = static_cast<unsigned*>(c->peer_epoch);
         pa.err = static_cast<unsigned*>(err);
         pa.nranks = c->nranks;
