@@ -156,6 +156,10 @@ __global__ void __launch_bounds__(kAttnThreads)
 
     const int hg = blockIdx.x, i = blockIdx.y, s = blockIdx.z, splits = gridDim.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // The next launch (a product staging its static weights) may become resident once every
+    // CTA of this grid has started; it reads this kernel's output only after its own
+    // griddepcontrol.wait, which waits for this whole grid to finish.
+    if (tid == 0) pdl_launch_dependents();
     pdl_wait();  // q, the caches and the position come from earlier launches
     const int n_ctx = *a.pos + i + 1;
     const int chunk = chunk_size(n_ctx, splits);
@@ -403,6 +407,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_single_kernel(AttnArgs a) {
     const int hs = a.head_size;
     const int h = blockIdx.x, i = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) pdl_launch_dependents();  // as in the split kernel
     pdl_wait();
     const int n_ctx = *a.pos + i + 1;
     const int kv_off = (h / a.group) * hs;
