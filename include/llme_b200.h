@@ -423,8 +423,8 @@ enum {
     LLME_PATH_TCGEN05_Q8 = 7,  /* tcgen05/TMEM tensor-core GEMM, int8 weights (kind::i8 on a
                                   two-term int8 split of the activation rows) */
     LLME_PATH_TCGEN05_SKINNY = 8, /* decode-shaped int8 products on tcgen05: three-term split
-                                     (fp32-decode accuracy), k split across CTAs, exact int64
-                                     sums */
+                                     (fp32-decode accuracy), k slices reduced in a
+                                     thread-block cluster as exact int64 sums */
     LLME_PATH_TCGEN05_F32_SKINNY = 9  /* decode-shaped fp32 products on tcgen05 in three TF32
                                          terms (fp32-decode accuracy), k slices reduced in a
                                          thread-block cluster */

@@ -206,17 +206,16 @@ int plan_path(const PlanIn& in, llme_plan_t* p) {
         const size_t units = static_cast<size_t>(p->grid_x) * p->grid_y;
         const size_t nkb = ceil_div(k, size_t{128});
         const size_t target = static_cast<size_t>(skinny_ctas_per_sm(t)) * sms;
-        // k slices: as many as keep every CTA resident in one wave, each at least 4 blocks deep.
-        size_t slices = std::max<size_t>(1, std::min(target / units, ceil_div(nkb, size_t{4})));
+        // k slices (one cluster, at most 8): as many as keep every CTA resident in one wave,
+        // each at least 4 blocks deep.
+        size_t slices = std::max<size_t>(
+            1, std::min({target / units, ceil_div(nkb, size_t{4}), size_t{8}}));
         const size_t span_blocks = ceil_div(nkb, slices);
         slices = ceil_div(nkb, span_blocks);
         p->slices = static_cast<int>(slices);
+        p->cluster = static_cast<int>(slices);
         p->span = static_cast<int>(span_blocks * 128);
         p->operand_bytes = skinny_operand_bytes(m, k);
-        if (slices > 1) {
-            p->counter_slots = units;
-            p->split_bytes = m * n * sizeof(long long);
-        }
         return LLME_OK;
     }
     // Decode-shaped fp32 products on tcgen05 in three TF32 terms (the fp32 decode path's
@@ -324,11 +323,6 @@ struct DeviceState {
     size_t partial_cap = 0;
     Scratch norm;
     Scratch operand;  // split activation rows (int8 tensor-core GEMMs) or B^T (TF32 GEMM)
-    // Skinny tcgen05 GEMM: [tickets: skinny_counters x u32][int64 sums], zero between launches
-    // (zeroed when it grows; each launch leaves it zero).
-    Scratch skinny;
-    size_t skinny_counters = 0;
-    size_t skinny_accum_bytes = 0;
 };
 
 std::mutex g_dev_mu;
@@ -404,36 +398,6 @@ int ensure_buffer(Scratch& b, size_t bytes, float** out) {
 }
 
 int ensure_norm(int dev, size_t bytes, float** out) { return ensure_buffer(g_dev[dev].norm, bytes, out); }
-
-// The skinny GEMM's zeroed tickets and int64 accumulators; both regions grow to the largest
-// size seen, the whole buffer is zeroed when it grows, and every launch leaves it zero.
-int ensure_skinny(int dev, size_t counters, size_t accum_bytes, cudaStream_t stream,
-                  unsigned** ctr, long long** acc) {
-    DeviceState& d = g_dev[dev];
-    const size_t want_c = std::max(counters, d.skinny_counters);
-    const size_t want_a = std::max(round_up(accum_bytes, 256), d.skinny_accum_bytes);
-    if (!d.skinny.ptr || want_c > d.skinny_counters || want_a > d.skinny_accum_bytes) {
-        if (d.skinny.ptr) {
-            cudaError_t e = cudaFree(d.skinny.ptr);
-            if (e != cudaSuccess) return cuda_fail(e, "free scratch");
-            d.skinny.ptr = nullptr;
-            d.skinny.cap = d.skinny_counters = d.skinny_accum_bytes = 0;
-        }
-        const size_t bytes = round_up(want_c * sizeof(unsigned), 256) + want_a;
-        cudaError_t e = cudaMalloc(&d.skinny.ptr, bytes);
-        if (e != cudaSuccess) return cuda_fail(e, "alloc scratch");
-        d.skinny.cap = bytes;
-        d.skinny_counters = want_c;
-        d.skinny_accum_bytes = want_a;
-        e = cudaMemsetAsync(d.skinny.ptr, 0, bytes, stream);
-        if (e != cudaSuccess) return cuda_fail(e, "zero scratch");
-        g_generation.fetch_add(1);
-    }
-    *ctr = static_cast<unsigned*>(d.skinny.ptr);
-    *acc = reinterpret_cast<long long*>(static_cast<char*>(d.skinny.ptr) +
-                                        round_up(d.skinny_counters * sizeof(unsigned), 256));
-    return LLME_OK;
-}
 
 // ---- TMA descriptors -------------------------------------------------------------------
 
@@ -714,10 +678,6 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
         float* rs = reinterpret_cast<float*>(t2 + plane);
         const size_t kp = q8tc_pitch(k);
         SkinnyArgs t;
-        if (p.slices > 1) {
-            st = ensure_skinny(dev, p.counter_slots, p.split_bytes, stream, &t.counters, &t.accum);
-            if (st) return st;
-        }
         e = launch_split_rows(static_cast<int>(m), static_cast<int>(k), static_cast<int>(kp), A,
                               rms, t0, t1, t2, rs, stream, true);
         if (e != cudaSuccess) return cuda_fail(e, "launch");

@@ -16,12 +16,13 @@
 //     M=128 N=3T K=32 MMA with exact s32 sums in TMEM;
 //   * the epilogue combines the three sums of an output exactly in 64 bits,
 //         S = (S0 << 16) + (S1 << 8) + S2,
-//     and, when k is split over several CTAs, adds S into an int64 accumulator in global
-//     memory (red.global.add.u64). Integer addition is exact and associative, so the result
-//     does not depend on the order in which slices arrive: bit-for-bit repeatable with no
-//     fixed-order reduction. The CTA that brings the tile's ticket to the slice count writes
-//     C = fl(fl(S * 2^-16) * fl(s_row * scale_col)) (+ C) and clears the accumulators and the
-//     ticket for the next launch.
+//     and writes C = fl(fl(S * 2^-16) * fl(s_row * scale_col)) (+ C);
+//   * when k is split, the k slices of a column tile form one thread-block cluster (grid z,
+//     at most 8 CTAs): each CTA parks its T x 128 int64 sums in its drained stage ring and,
+//     after a cluster barrier, CTA r adds rows r, r + slices, ... of every slice's sums
+//     through distributed shared memory and writes those rows of C. Integer addition is
+//     exact, so C is the same bits whatever the slice count; there is no global scratch, no
+//     atomic and no ticket, and every CTA of the cluster converts its share of the tile.
 //
 // With LLME_FLAG_WEIGHTS_STATIC the producer issues the weight loads of its first stages
 // before griddepcontrol.wait, so they stream while the split pass (the previous launch) runs.
@@ -49,6 +50,7 @@ struct SkGeo {
     static constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
     static constexpr int kN = kTerms * T;                     // 48 / 96 / 192
     static constexpr uint32_t kTmemCols = kN <= 64 ? 64 : kN <= 128 ? 128 : 256;
+    static_assert(T * SW * 8 <= kStages * kStageBytes, "int64 partial tile in the drained ring");
 };
 
 __device__ __forceinline__ void mma_i8_skinny(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
@@ -64,6 +66,15 @@ __device__ __forceinline__ void mma_i8_skinny(uint32_t tmem_d, uint64_t adesc, u
 constexpr uint32_t idesc_skinny(int M, int N) {
     return (2u << 4) | (1u << 7) | (1u << 10) | (1u << 15) |
            (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+__device__ __forceinline__ longlong2 ld_cluster_s64x2(const long long* local, uint32_t rank) {
+    longlong2 v;
+    asm volatile("ld.shared::cluster.v2.s64 {%0, %1}, [%2];"
+                 : "=l"(v.x), "=l"(v.y)
+                 : "r"(tc::map_to_cta(smem_u32(local), rank))
+                 : "memory");
+    return v;
 }
 
 __device__ __forceinline__ float finish64(long long s, float rs, float sc) {
@@ -108,7 +119,6 @@ __global__ void __launch_bounds__(kSkThreads)
     uint64_t* empty = full + kStages;
     uint64_t* done = empty + kStages;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-    int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c0 = blockIdx.x * SW;      // first output column
@@ -183,14 +193,15 @@ __global__ void __launch_bounds__(kSkThreads)
         }
     } else {
         const int q = warp & 3;  // TMEM lane quadrant
-        const int col = c0 + q * 32 + lane;
+        const int lc = q * 32 + lane;  // column within the tile
+        const int col = c0 + lc;
         const bool col_ok = col < a.n;
         pdl_wait();              // C and the row scales come after the kernels before this one
-        const bool ok = mbar_wait(done, 0, &g_skinny_error);
+        const bool ok = mbar_wait(done, 0, &g_skinny_error) && nk > 0;
         tc::fence_after_sync();
         const float sc = col_ok ? a.scale[col] : 0.0f;
         const uint32_t base = tmem + (static_cast<uint32_t>(q * 32) << 16);
-        const bool split = a.slices > 1;
+        long long* part = reinterpret_cast<long long*>(smem);  // the ring, drained by `done`
 #pragma unroll 1
         for (int c = 0; c < T / 16; ++c) {
             __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
@@ -198,57 +209,72 @@ __global__ void __launch_bounds__(kSkThreads)
             tc::tmem_ld_32x32b_x16(base + c * 16, s0);
             tc::tmem_ld_32x32b_x16(base + T + c * 16, s1);
             tc::tmem_ld_32x32b_x16(base + 2 * T + c * 16, s2);
-            if (!ok || nk == 0) continue;
-            const int row0 = r0 + c * 16;
             long long S[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-                S[j] = (static_cast<long long>(static_cast<int>(s0[j])) << 16) +
-                       (static_cast<long long>(static_cast<int>(s1[j])) << 8) +
-                       static_cast<long long>(static_cast<int>(s2[j]));
-            if (split) {
+                S[j] = ok ? (static_cast<long long>(static_cast<int>(s0[j])) << 16) +
+                                (static_cast<long long>(static_cast<int>(s1[j])) << 8) +
+                                static_cast<long long>(static_cast<int>(s2[j]))
+                          : 0;
+            if (a.slices > 1) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    if (row0 + j < a.m && col_ok)
-                        atomicAdd(reinterpret_cast<unsigned long long*>(a.accum) +
-                                      static_cast<size_t>(row0 + j) * a.n + col,
-                                  static_cast<unsigned long long>(S[j]));
-            } else {
-                store_rows(a, row0, col, col_ok, sc, S);
+                for (int j = 0; j < 16; ++j) part[(c * 16 + j) * SW + lc] = S[j];
+            } else if (ok) {
+                store_rows(a, r0 + c * 16, col, col_ok, sc, S);
             }
         }
-        if (split) {
-            // Ticket: the CTA that completes the tile's count converts its sums.
-            __threadfence();
-            named_barrier(1, 128);
-            if (threadIdx.x == 64) {
-                const unsigned tile = blockIdx.y * gridDim.x + blockIdx.x;
-                const unsigned t = atomicAdd(a.counters + tile, 1u);
-                *last_flag = (t == static_cast<unsigned>(a.slices) - 1) ? 1 : 0;
-            }
-            named_barrier(1, 128);
-            if (*last_flag) {
-                __threadfence();
-                unsigned long long* acc = reinterpret_cast<unsigned long long*>(a.accum);
+    }
+    if (a.slices > 1) {
+        // Every CTA's sums are parked; CTA `me` of the cluster adds rows me, me + slices, ... of
+        // all of them. Thread t of warps 2-5 takes the column pair 2 (t % 64) of every second
+        // such row, two rows' loads from every slice in flight.
+        __syncwarp();
+        tc::pair_sync();
+        if (warp >= 2) {
+            const int t = threadIdx.x - 64;
+            const int cp = (t & 63) * 2;
+            const int col = c0 + cp;
+            const bool col_ok = col < a.n;  // n % 16 == 0: both columns of the pair or neither
+            const float sc0 = col_ok ? a.scale[col] : 0.0f;
+            const float sc1 = col_ok ? a.scale[col + 1] : 0.0f;
+            const long long* part = reinterpret_cast<const long long*>(smem);
+            const int slices = a.slices;
+            const int me = static_cast<int>(tc::cluster_rank());
+            const int nrows = (T - me + slices - 1) / slices;
 #pragma unroll 1
-                for (int row0 = r0; row0 < r0 + T; row0 += 16) {
-                    // All 16 sums in flight before any store (loads and stores may alias).
-                    long long S[16];
+            for (int j0 = t >> 6; j0 < nrows; j0 += 4) {
+                longlong2 v[2][8];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        S[j] = row0 + j < a.m && col_ok
-                                   ? static_cast<long long>(
-                                         __ldcg(acc + static_cast<size_t>(row0 + j) * a.n + col))
-                                   : 0;
+                for (int u = 0; u < 2; ++u) {
+                    const int row = me + slices * (j0 + 2 * u);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        if (row0 + j < a.m && col_ok)
-                            acc[static_cast<size_t>(row0 + j) * a.n + col] = 0ull;
-                    store_rows(a, row0, col, col_ok, sc, S);
+                    for (int r = 0; r < 8; ++r)
+                        v[u][r] = j0 + 2 * u < nrows && r < slices
+                                      ? ld_cluster_s64x2(part + row * SW + cp, r)
+                                      : make_longlong2(0, 0);
                 }
-                if (threadIdx.x == 64) a.counters[blockIdx.y * gridDim.x + blockIdx.x] = 0u;
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int grow = r0 + me + slices * (j0 + 2 * u);
+                    if (j0 + 2 * u >= nrows || grow >= a.m || !col_ok) continue;
+                    long long s0 = v[u][0].x, s1 = v[u][0].y;
+#pragma unroll
+                    for (int r = 1; r < 8; ++r) {
+                        s0 += v[u][r].x;  // zero beyond the slice count
+                        s1 += v[u][r].y;
+                    }
+                    const float rs = a.row_scale[grow];
+                    float* dst = a.C + static_cast<size_t>(grow) * a.n + col;
+                    const float o0 = a.accumulate ? dst[0] : 0.0f;
+                    const float o1 = a.accumulate ? dst[1] : 0.0f;
+                    const float v0 = finish64(s0, rs, sc0), v1 = finish64(s1, rs, sc1);
+                    dst[0] = a.accumulate ? __fadd_rn(o0, v0) : v0;
+                    dst[1] = a.accumulate ? __fadd_rn(o1, v1) : v1;
+                }
             }
         }
+        __syncwarp();
+        tc::pair_sync();  // no CTA leaves while another may still read its sums
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -277,11 +303,15 @@ cudaError_t launch_t(const SkinnyArgs& a, const CUtensorMap& tmW, const CUtensor
     cfg.blockDim = dim3(kSkThreads);
     cfg.dynamicSmemBytes = SkGeo<T>::kSmemBytes;
     cfg.stream = a.stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = a.slices;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, gemm_q8_skinny_kernel<T>, tmW, t0, t1, t2, a);
 }
 
@@ -293,6 +323,7 @@ int skinny_ctas_per_sm(int t) { return t >= 64 ? 1 : 2; }
 cudaError_t launch_gemm_q8_skinny(const SkinnyArgs& a, const CUtensorMap& tmW,
                                   const CUtensorMap& t0, const CUtensorMap& t1,
                                   const CUtensorMap& t2) {
+    if (a.slices < 1 || a.slices > 8) return cudaErrorInvalidValue;  // one portable cluster
     switch (a.rows_per_tile) {
         case 16: return launch_t<16>(a, tmW, t0, t1, t2);
         case 32: return launch_t<32>(a, tmW, t0, t1, t2);

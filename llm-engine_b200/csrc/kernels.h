@@ -278,20 +278,17 @@ cudaError_t launch_gemm_q8_tc(const Q8TcArgs& a, const CUtensorMap& tmHi, const 
 unsigned read_and_clear_q8tc_error();
 
 // Decode-shaped int8 products on tcgen05 (gemm_q8_skinny.cu): three-term split rows, one CTA
-// per (128-column, rows_per_tile-row) tile and k-slice; slices > 1 add exact int64 sums into
-// `accum` (m x n, zero between launches) and the last CTA of a tile (per `counters`, zero
-// between launches) writes C.
+// per (128-column, rows_per_tile-row) tile and k-slice; the k slices of a tile form one
+// thread-block cluster (at most 8) and add their exact int64 sums through DSMEM.
 struct SkinnyArgs {
     int m = 0, n = 0, k = 0;
     const float* scale = nullptr;
     const float* row_scale = nullptr;
     float* C = nullptr;
-    long long* accum = nullptr;
-    unsigned* counters = nullptr;
     bool accumulate = false;
     bool weights_static = false;  // weight loads may start before the previous launch ends
     int rows_per_tile = 16;       // 16, 32 or 64
-    int slices = 1;
+    int slices = 1;               // grid z = cluster size, at most 8
     int span_blocks = 0;          // 128-deep k blocks per slice
     cudaStream_t stream = nullptr;
 };

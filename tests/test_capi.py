@@ -204,7 +204,8 @@ def test_tcgen05_skinny_plan():
     assert p["path_name"] == "tcgen05_skinny" and p["kernel"] == 3       # -> tiled_split
     assert (p["tile_m"], p["tile_n"], p["grid_x"], p["grid_y"]) == (16, 128, 32, 1)
     assert p["slices"] == 8 and p["span"] == 512                          # 256 CTAs
-    assert p["counter_slots"] == 32 and p["split_bytes"] == 16 * 4096 * 8
+    assert p["cluster"] == 8                    # the k slices of a tile are one cluster
+    assert p["counter_slots"] == 0 and p["split_bytes"] == 0              # no scratch
     assert p["operand_bytes"] == 3 * 16 * 4096 + 16 * 4
     p = L.plan(64, 4096, 4096, q8=True)
     assert p["tile_m"] == 64 and p["slices"] == 4 and p["grid_x"] * p["slices"] <= 148

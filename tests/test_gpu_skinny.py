@@ -1,11 +1,13 @@
 """Decode-shaped int8 products on the tensor cores (LLME_PATH_TCGEN05_SKINNY): activation rows
-split into three int8 terms, kind::i8 MMAs, k split across CTAs with exact int64 sums.
+split into three int8 terms, kind::i8 MMAs, the k slices of a tile one thread-block cluster
+adding exact int64 sums through distributed shared memory.
 
 Held to the decode path's accuracy bound: max over rows of
 ||C - C_ref||_inf / ||C_ref row||_2 <= 1e-5 against the oracle (matmul_naive on the dequantised
 weights, tests/test_quant.cpp:57-79); bit for bit against a numpy restatement of the kernel's
-own arithmetic for rows without RMSNorm; repeats bit-identical whatever order the k slices'
-atomic adds arrive in; and the decode sweep's int8 shapes (m = 16, 64 x 4096^2) at full size.
+own arithmetic for rows without RMSNorm, at every cluster size from 1 to 8 that the shapes
+below reach (integer sums: the same bits whatever the slice count); repeats bit-identical; and
+the decode sweep's int8 shapes (m = 16, 64 x 4096^2) at full size.
 """
 from __future__ import annotations
 

@@ -84,7 +84,7 @@ def test_every_plan_covers_c_and_k_within_limits(m, n, k, q8, kernel, accumulate
     if path == "tcgen05_skinny":
         assert q8 and n % 16 == 0 and kernel in ("tiled", "tiled_split")
         assert span % 128 == 0 and p["operand_bytes"] > 0
-        assert p["split_bytes"] == (8 * m * n if s > 1 else 0)
+        assert s <= 8 and p["cluster"] == s and p["split_bytes"] == 0
     if path == "tcgen05_f32_skinny":
         assert not q8 and n % 4 == 0 and k % 4 == 0 and kernel in ("tiled", "tiled_split")
         assert rms or a_addr % 16 == 0
