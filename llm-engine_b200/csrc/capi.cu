@@ -121,39 +121,55 @@ int plan_path(const PlanIn& in, llme_plan_t* p) {
     const bool has_rms = in.rms_addr != 0;
     const int sms = in.sms > 0 ? in.sms : 148;
 
-    if (kernel == LLME_KERNEL_SKINNY) {
-        const size_t esz = in.q8 ? 1 : 4;
-        const bool tma = in.b_addr % 16 == 0 && (n * esz) % 16 == 0 && in.a_addr % 16 == 0 &&
-                         k % 4 == 0 && (!has_rms || in.rms_addr % 16 == 0);
-        p->tile_m = static_cast<int>(m);
-        size_t strips, slices, span;
-        if (tma) {
-            p->path = LLME_PATH_GEMV_TMA;
-            p->tile_n = gemv_tma_cols(in.q8);
-            strips = ceil_div(n, p->tile_n);
-            // Two CTAs per SM; slices form one cluster (at most 8), each at least two boxes
-            // deep.
-            const size_t target =
-                static_cast<size_t>(gemv_call_ctas_per_sm(static_cast<int>(m))) * sms;
-            slices = std::max<size_t>(
-                1, std::min({target / strips, ceil_div(k, 2 * kGemvBoxRows),
-                             static_cast<size_t>(kGemvMaxCluster)}));
-            span = round_up(ceil_div(k, slices), kGemvBoxRows);
-        } else {
-            p->path = LLME_PATH_GEMV_LDG;
-            p->tile_n = kGemvLdgCols;
-            strips = ceil_div(n, p->tile_n);
-            const size_t target = 8 * static_cast<size_t>(sms);
-            slices = std::max<size_t>(1, std::min(target / strips, ceil_div(k, 256)));
-            span = ceil_div(k, slices);
-        }
+    // Operands the TMA GEMV can stream: 16-byte aligned rows and starts.
+    const bool gemv_tma = in.b_addr % 16 == 0 && (n * (in.q8 ? 1 : 4)) % 16 == 0 &&
+                          in.a_addr % 16 == 0 && k % 4 == 0 && (!has_rms || in.rms_addr % 16 == 0);
+    // The TMA GEMV's grid: two CTAs per SM; the k slices of a column strip form one cluster (at
+    // most 8), each at least two boxes deep.
+    auto plan_gemv_tma = [&](int rows) {
+        p->path = LLME_PATH_GEMV_TMA;
+        p->tile_m = rows;
+        p->tile_n = gemv_tma_cols(in.q8);
+        const size_t strips = ceil_div(n, p->tile_n);
+        const size_t target = static_cast<size_t>(gemv_call_ctas_per_sm(rows)) * sms;
+        size_t slices = std::max<size_t>(
+            1, std::min({target / strips, ceil_div(k, 2 * kGemvBoxRows),
+                         static_cast<size_t>(kGemvMaxCluster)}));
+        const size_t span = round_up(ceil_div(k, slices), kGemvBoxRows);
         slices = ceil_div(k, span);
         p->grid_x = static_cast<int>(strips);
         p->grid_y = static_cast<int>(slices);
         p->slices = static_cast<int>(slices);
         p->span = static_cast<int>(span);
-        p->cluster = p->path == LLME_PATH_GEMV_TMA ? static_cast<int>(slices) : 1;
-        if (slices > 1 && p->path == LLME_PATH_GEMV_LDG) {
+        p->cluster = static_cast<int>(slices);
+        return LLME_OK;
+    };
+
+    if (kernel == LLME_KERNEL_SKINNY && gemv_tma) return plan_gemv_tma(static_cast<int>(m));
+    // fp32 B with 9..16 rows (tiled_split, or tiled) in LLME_MATH_FP32: the TMA GEMV at 16
+    // rows, exact fp32 arithmetic (33 us for 16 x 4096^2 against 126 on the SIMT tiles). In
+    // tensor math the three-term TF32 kernel below is faster (19 us).
+    if (!in.q8 && in.math == LLME_MATH_FP32 && m > kSkinnyMaxRows &&
+        m <= static_cast<size_t>(kGemvWideRows) && gemv_tma &&
+        (kernel == LLME_KERNEL_TILED_SPLIT || kernel == LLME_KERNEL_TILED))
+        return plan_gemv_tma(kGemvWideRows);
+
+    if (kernel == LLME_KERNEL_SKINNY) {
+        // Ragged rows or unaligned pointers: the plain-load GEMV.
+        p->path = LLME_PATH_GEMV_LDG;
+        p->tile_m = static_cast<int>(m);
+        p->tile_n = kGemvLdgCols;
+        const size_t strips = ceil_div(n, p->tile_n);
+        const size_t target = 8 * static_cast<size_t>(sms);
+        size_t slices = std::max<size_t>(1, std::min(target / strips, ceil_div(k, 256)));
+        const size_t span = ceil_div(k, slices);
+        slices = ceil_div(k, span);
+        p->grid_x = static_cast<int>(strips);
+        p->grid_y = static_cast<int>(slices);
+        p->slices = static_cast<int>(slices);
+        p->span = static_cast<int>(span);
+        p->cluster = 1;
+        if (slices > 1) {
             // The plain-load kernel reduces its slices through global scratch.
             p->counter_slots = strips;
             p->split_bytes = strips * slices * (m * p->tile_n + m) * sizeof(float);
@@ -602,8 +618,9 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
                     : tensor_map(B, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k, n, kGemvRowBytes / 4,
                                  kGemvBoxRows, &tmB);
             if (st) return st;
+            // The box is the kernel's row count (16 for 9..16 fp32 rows: zero fill past m).
             st = tensor_map(A, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, k, kGemvBoxRows,
-                            static_cast<uint32_t>(m), &tmA);
+                            static_cast<uint32_t>(p.tile_m), &tmA);
             if (st) return st;
             if (rms) {
                 st = tensor_map(rms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 0, k, kGemvBoxRows, 1,

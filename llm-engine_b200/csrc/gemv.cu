@@ -1,5 +1,5 @@
-// Weight-streaming GEMV / skinny GEMM for decode-shaped products (m <= 8):
-// C (+)= [rmsnorm(A)] x B, B fp32 or int8 k x n row-major with column scales.
+// Weight-streaming GEMV / skinny GEMM for decode-shaped products (m <= 8, and fp32 B up to
+// 16 rows): C (+)= [rmsnorm(A)] x B, B fp32 or int8 k x n row-major with column scales.
 //
 // The reference's counterpart is sgemm_skinny + sum_slices
 // (src/cuda_matmul.cu:189-254, launched by run_skinny :365-397). This design
@@ -27,6 +27,12 @@
 //    k rows while it streams, multiplies A by the norm weight in the loop, and
 //    the final per-row 1/sqrt(mean + eps) multiplies the reduced sums -- no
 //    pre-pass and no second read of A.
+//  * fp32 B with 9..16 rows (one M = 16 instantiation; A rows past m arrive as the
+//    TMA's zero fill and their outputs are not stored) keeps 16 x 2 outputs per
+//    thread and pairs each output's accumulator over even and odd k instead of
+//    over columns: a 16-byte load of A gives two k pairs of one row, used as they
+//    are by fma.rn.f32x2 against the column's k pairs of B, so A needs no
+//    repacking and each A load feeds four packed FMAs.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -52,14 +58,19 @@ constexpr int kBoxBytesB = kGemvRowBytes * kGemvBoxRows;  // 16 KB
 template <int M, bool Q8, int Warps = kConsumerWarps>
 struct Shape {
     static constexpr int ESZ = Q8 ? 1 : 4;
+    // fp32 B past 8 rows: accumulators paired over k (two columns per thread, four
+    // consecutive k rows at a time) instead of over columns.
+    static constexpr bool KQ = !Q8 && M > 8;
     // Columns per thread: fewer as M grows, so M x V accumulators fit 2 CTAs per SM.
-    static constexpr int V = Q8 ? (M <= 2 ? 16 : (M <= 4 ? 8 : 4)) : 4;
+    static constexpr int V = Q8 ? (M <= 2 ? 16 : (M <= 4 ? 8 : 4)) : (KQ ? 2 : 4);
+    static constexpr int ACC = KQ ? V : V / 2;              // 64-bit accumulators per row
     static constexpr int NT = kGemvRowBytes / ESZ;         // columns per CTA
     static constexpr int TPR = NT / V;                     // threads per row
     static constexpr int RG = Warps * 32 / TPR;            // row groups
     static constexpr int RPT = kGemvBoxRows / RG;          // rows per thread per box
+    static constexpr int QPT = RPT / 4;                    // k-quad form: quads per thread
     static_assert(TPR == 8 || TPR == 16 || TPR == 32, "row split");
-    static_assert(V % 4 == 0, "packed pairs");
+    static_assert(KQ ? (V == 2 && M <= 16 && RPT % 4 == 0) : V % 4 == 0, "packed pairs");
     static_assert(RPT * RG == kGemvBoxRows, "rows split evenly");
 };
 
@@ -279,7 +290,7 @@ __device__ __forceinline__ void peer_sum_store(const GemvArgs& a, int count, Val
     for (int e = tid; e < count; e += nthreads) {
         int r, col;
         where(e, r, col);
-        if (col >= a.n) continue;
+        if (col >= a.n || r >= a.m) continue;  // past n, or a zero-filled row past m
         float v = value(e);
         float* o = a.C + static_cast<size_t>(r) * a.n + col;
         if (a.accumulate) v += *o;
@@ -289,7 +300,7 @@ __device__ __forceinline__ void peer_sum_store(const GemvArgs& a, int count, Val
     for (int e = tid; e < count; e += nthreads) {
         int r, col;
         where(e, r, col);
-        if (col >= a.n) continue;
+        if (col >= a.n || r >= a.m) continue;  // past n, or a zero-filled row past m
         float v = wait_tagged(peer_region(p, p.rank, slot, unit, 0) + e, epoch, p.err);
         for (int src = 1; src < p.world; ++src)
             v += wait_tagged(peer_region(p, p.rank, slot, unit, src) + e, epoch, p.err);
@@ -323,7 +334,7 @@ __device__ __forceinline__ void store_strip(const float* tot, const float* tot_s
     if (a.epi.kind != kEpiStore) {
         for (int e = 2 * tid; e < M * NT; e += 2 * nthreads) {
             const int r = e / NT, col = col0 + e % NT;
-            if (col >= a.n) continue;
+            if (col >= a.n || r >= a.m) continue;  // past n, or a zero-filled row past m
             float v0 = tot[e], v1 = tot[e + 1];
             if constexpr (Q8) {
                 v0 *= sscale ? sscale[e % NT] : __ldg(a.scale + col);
@@ -340,7 +351,7 @@ __device__ __forceinline__ void store_strip(const float* tot, const float* tot_s
     }
     for (int e = tid; e < M * NT; e += nthreads) {
         const int r = e / NT, col = col0 + e % NT;
-        if (col >= a.n) continue;
+        if (col >= a.n || r >= a.m) continue;  // past n, or a zero-filled row past m
         float v = tot[e];
         if constexpr (Q8) v *= sscale ? sscale[e % NT] : __ldg(a.scale + col);
         if constexpr (Norm) v *= 1.0f / sqrtf(tot_ss[r] / static_cast<float>(a.k) + kRmsEps);
@@ -464,13 +475,16 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
             if (!a.weights_static && tid < S::NT)
                 sscale[tid] = col0 + tid < a.n ? __ldg(a.scale + col0 + tid) : 0.0f;
         const int cg = tid % S::TPR, rg = tid / S::TPR;
-        uint64_t acc[M][S::V / 2];
+        uint64_t acc[M][S::ACC];
         float ss[M];
+        // k-quad form: this thread's share of the sums of squares, all for row tid / 16.
+        float row_ss = 0.0f;
+        static_assert(!(S::KQ && Norm) || CT == 16 * M, "k-quad RMSNorm: 16 threads per row");
 #pragma unroll
         for (int r = 0; r < M; ++r) {
             ss[r] = 0.0f;
 #pragma unroll
-            for (int j = 0; j < S::V / 2; ++j) acc[r][j] = 0ull;
+            for (int j = 0; j < S::ACC; ++j) acc[r][j] = 0ull;
         }
         for (int b = 0; b < nb; ++b) {
             const int s = b % R;
@@ -479,27 +493,71 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
             const uint8_t* sb = smem + s * kBoxBytesB + cg * (S::V * S::ESZ);
             const float* sa = reinterpret_cast<const float*>(smem + L::kOffA + s * L::kABox);
             const float* sw = reinterpret_cast<const float*>(smem + L::kOffW + s * L::kWBox);
-#pragma unroll
-            for (int i = 0; i < S::RPT; ++i) {
-                const int row = rg + i * S::RG;
-                float av[M];
-#pragma unroll
-                for (int r = 0; r < M; ++r) av[r] = sa[r * kGemvBoxRows + row];
+            if constexpr (S::KQ) {
                 if constexpr (Norm) {
-                    const float w = sw[row];
+                    // The stage's A box is normalised in place before anyone reads it: thread
+                    // tid takes row tid / 16, k 4 (tid % 16) .. + 3 and the four 64 further
+                    // (conflict-free), adds their squares and multiplies them by the weight.
+                    float* q = const_cast<float*>(sa) + (tid >> 4) * kGemvBoxRows + 4 * (tid & 15);
+                    const float* wk = sw + 4 * (tid & 15);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        float4 u = *reinterpret_cast<const float4*>(q + 64 * h);
+                        const float4 w = *reinterpret_cast<const float4*>(wk + 64 * h);
+                        row_ss = fmaf(u.x, u.x, fmaf(u.y, u.y, fmaf(u.z, u.z, fmaf(u.w, u.w, row_ss))));
+                        u.x *= w.x;
+                        u.y *= w.y;
+                        u.z *= w.z;
+                        u.w *= w.w;
+                        *reinterpret_cast<float4*>(q + 64 * h) = u;
+                    }
+                    named_barrier(2, CT);
+                }
+                // Quads q = rg, rg + RG, ...: k rows 4q .. 4q + 3, columns 2 cg, 2 cg + 1.
+#pragma unroll 1
+                for (int i = 0; i < S::QPT; ++i) {
+                    const int k4 = 4 * (rg + i * S::RG);
+                    float2 bv[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        bv[j] = *reinterpret_cast<const float2*>(sb + (k4 + j) * kGemvRowBytes);
+                    // One column's (k, k + 1) and (k + 2, k + 3) pairs of B.
+                    const uint64_t c0lo = pack2(bv[0].x, bv[1].x), c0hi = pack2(bv[2].x, bv[3].x);
+                    const uint64_t c1lo = pack2(bv[0].y, bv[1].y), c1hi = pack2(bv[2].y, bv[3].y);
 #pragma unroll
                     for (int r = 0; r < M; ++r) {
-                        ss[r] = fmaf(av[r], av[r], ss[r]);
-                        av[r] *= w;
+                        const ulonglong2 aq =
+                            *reinterpret_cast<const ulonglong2*>(sa + r * kGemvBoxRows + k4);
+                        const uint64_t alo = aq.x, ahi = aq.y;
+                        acc[r][0] = fma2(alo, c0lo, acc[r][0]);
+                        acc[r][1] = fma2(alo, c1lo, acc[r][1]);
+                        acc[r][0] = fma2(ahi, c0hi, acc[r][0]);
+                        acc[r][1] = fma2(ahi, c1hi, acc[r][1]);
                     }
                 }
-                uint64_t x[S::V / 2];
-                load_pairs<Q8, S::V>(sb + row * kGemvRowBytes, x);
+            } else {
 #pragma unroll
-                for (int r = 0; r < M; ++r) {
-                    const uint64_t a2 = pack2(av[r], av[r]);
+                for (int i = 0; i < S::RPT; ++i) {
+                    const int row = rg + i * S::RG;
+                    float av[M];
 #pragma unroll
-                    for (int j = 0; j < S::V / 2; ++j) acc[r][j] = fma2(a2, x[j], acc[r][j]);
+                    for (int r = 0; r < M; ++r) av[r] = sa[r * kGemvBoxRows + row];
+                    if constexpr (Norm) {
+                        const float w = sw[row];
+#pragma unroll
+                        for (int r = 0; r < M; ++r) {
+                            ss[r] = fmaf(av[r], av[r], ss[r]);
+                            av[r] *= w;
+                        }
+                    }
+                    uint64_t x[S::V / 2];
+                    load_pairs<Q8, S::V>(sb + row * kGemvRowBytes, x);
+#pragma unroll
+                    for (int r = 0; r < M; ++r) {
+                        const uint64_t a2 = pack2(av[r], av[r]);
+#pragma unroll
+                        for (int j = 0; j < S::V / 2; ++j) acc[r][j] = fma2(a2, x[j], acc[r][j]);
+                    }
                 }
             }
             __syncwarp();
@@ -512,14 +570,33 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
         named_barrier(1, CT);
         float accf[M][S::V];
 #pragma unroll
-        for (int r = 0; r < M; ++r)
+        for (int r = 0; r < M; ++r) {
+            if constexpr (S::KQ) {
+                // Even-k and odd-k sums of each output.
 #pragma unroll
-            for (int j = 0; j < S::V / 2; ++j) unpack2(acc[r][j], accf[r][2 * j], accf[r][2 * j + 1]);
+                for (int j = 0; j < S::V; ++j) {
+                    float lo, hi;
+                    unpack2(acc[r][j], lo, hi);
+                    accf[r][j] = lo + hi;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < S::V / 2; ++j)
+                    unpack2(acc[r][j], accf[r][2 * j], accf[r][2 * j + 1]);
+            }
+        }
+        if constexpr (S::KQ && Norm) {
+            // The row's 16 threads are one half-warp: its total is the row's whole sum of
+            // squares over this CTA's k (the ring is drained: the barrier above).
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) row_ss += __shfl_xor_sync(0xffffffffu, row_ss, off);
+            if ((tid & 15) == 0) tot_ss[tid >> 4] = row_ss;
+        }
 #pragma unroll
         for (int off = S::TPR; off < 32; off <<= 1) {
 #pragma unroll
             for (int r = 0; r < M; ++r) {
-                ss[r] += __shfl_xor_sync(0xffffffffu, ss[r], off);
+                if constexpr (Norm && !S::KQ) ss[r] += __shfl_xor_sync(0xffffffffu, ss[r], off);
 #pragma unroll
                 for (int j = 0; j < S::V; ++j) accf[r][j] += __shfl_xor_sync(0xffffffffu, accf[r][j], off);
             }
@@ -527,13 +604,18 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
         if (lane < S::TPR) {
 #pragma unroll
             for (int r = 0; r < M; ++r) {
-                float4* dst = reinterpret_cast<float4*>(red + (warp * M + r) * S::NT + cg * S::V);
+                float* dst = red + (warp * M + r) * S::NT + cg * S::V;
+                if constexpr (S::V % 4 == 0) {
 #pragma unroll
-                for (int j = 0; j < S::V / 4; ++j)
-                    dst[j] = make_float4(accf[r][4 * j], accf[r][4 * j + 1], accf[r][4 * j + 2],
-                                         accf[r][4 * j + 3]);
+                    for (int j = 0; j < S::V / 4; ++j)
+                        reinterpret_cast<float4*>(dst)[j] =
+                            make_float4(accf[r][4 * j], accf[r][4 * j + 1], accf[r][4 * j + 2],
+                                        accf[r][4 * j + 3]);
+                } else {
+                    *reinterpret_cast<float2*>(dst) = make_float2(accf[r][0], accf[r][1]);
+                }
             }
-            if (Norm && cg == 0) {
+            if (Norm && !S::KQ && cg == 0) {
 #pragma unroll
                 for (int r = 0; r < M; ++r) red_ss[warp * M + r] = ss[r];
             }
@@ -545,7 +627,7 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
             for (int w = 0; w < CW; ++w) v += red[w * M * S::NT + e];
             tot[e] = v;
         }
-        if (Norm && tid < M) {
+        if (Norm && !S::KQ && tid < M) {
             float v = 0.0f;
 #pragma unroll
             for (int w = 0; w < CW; ++w) v += red_ss[w * M + tid];
@@ -635,7 +717,7 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
                               e < 4 * my_cnt; e += 2 * CT) {
             const int eg = 4 * my_begin + e;
             const int r = eg / S::NT, col = col0 + eg % S::NT;
-            if (col >= a.n) continue;
+            if (col >= a.n || r >= a.m) continue;  // past n, or a zero-filled row past m
             float v0 = recv[e], v1 = recv[e + 1];
             for (int src = 1; src < a.slices; ++src) {
                 v0 += recv[src * per * 4 + e];
@@ -657,7 +739,7 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
         for (int e = tid; a.epi.kind == kEpiStore && ok && e < 4 * my_cnt; e += CT) {
             const int eg = 4 * my_begin + e;  // element of the strip's M x NT sums
             const int r = eg / S::NT, col = col0 + eg % S::NT;
-            if (col >= a.n) continue;
+            if (col >= a.n || r >= a.m) continue;  // past n, or a zero-filled row past m
             float v = recv[e];
             for (int src = 1; src < a.slices; ++src) v += recv[src * per * 4 + e];
             if constexpr (Q8) v *= sc[eg % S::NT];
@@ -1077,7 +1159,11 @@ cudaError_t launch_tma_rows(const GemvArgs& a, const CUtensorMap& tmB, const CUt
         case 6: return launch_tma_m<6, Q8, Norm>(a, tmB, tmA, tmW);
         case 7: return launch_tma_m<7, Q8, Norm>(a, tmB, tmA, tmW);
         case 8: return launch_tma_m<8, Q8, Norm>(a, tmB, tmA, tmW);
-        default: return cudaErrorInvalidValue;
+        default:
+            // fp32 B, 9..16 rows: one 16-row instantiation (its A map's box is 16 rows).
+            if constexpr (!Q8)
+                if (a.m > 8 && a.m <= kGemvWideRows) return launch_tma_m<kGemvWideRows, false, Norm>(a, tmB, tmA, tmW);
+            return cudaErrorInvalidValue;
     }
 }
 

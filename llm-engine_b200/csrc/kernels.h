@@ -132,6 +132,9 @@ struct GemvArgs {
 constexpr int kGemvRowBytes = 128;
 constexpr int kGemvBoxRows = 128;
 constexpr int kGemvMaxCluster = 8;
+// fp32 B: the TMA GEMV also takes 9..16 rows, as one 16-row instantiation whose A box is
+// 16 rows (the rows past m arrive as zero fill and are not stored).
+constexpr int kGemvWideRows = 16;
 inline int gemv_tma_cols(bool q8) { return q8 ? kGemvRowBytes : kGemvRowBytes / 4; }
 // CTAs per SM of one per-call TMA GEMV grid.
 constexpr int gemv_call_ctas_per_sm(int) { return 2; }

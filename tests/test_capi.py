@@ -243,6 +243,26 @@ def test_tcgen05_f32_skinny_plan():
     p = L.plan(24, 1028, 512, q8=False, a_addr=260, rms_addr=256)
     assert p["path_name"] == "tcgen05_f32_skinny" and p["rms_prepass"] == 1
     assert L.plan(24, 1028, 512, q8=False, a_addr=260)["path_name"] == "tiled_simt"
+
+
+def test_fp32_gemv_up_to_16_rows_plan():
+    # fp32 weights with 9..16 rows (automatic -> tiled_split, or tiled) in fp32 arithmetic: the
+    # TMA GEMV at 16 rows instead of the SIMT tiles. Tensor math keeps the TF32 kernel.
+    F = L.MATH_FP32
+    for m in (9, 12, 16):
+        p = L.plan(m, 4096, 4096, q8=False, math=F)
+        assert p["path_name"] == "gemv_tma" and p["kernel"] == 3
+        assert (p["tile_m"], p["tile_n"], p["grid_x"]) == (16, 32, 128)
+        assert p["slices"] == 2 and p["cluster"] == 2 and p["span"] == 2048   # 256 CTAs
+        assert p["split_bytes"] == 0 and p["norm_bytes"] == 0 and p["rms_prepass"] == 0
+        assert L.plan(m, 4096, 4096, q8=False)["path_name"] == "tcgen05_f32_skinny"
+    assert L.plan(12, 4096, 4096, q8=False, kernel="tiled", math=F)["path_name"] == "gemv_tma"
+    assert L.plan(12, 4096, 4096, q8=False, rms_addr=256, math=F)["path_name"] == "gemv_tma"
+    assert L.plan(17, 4096, 4096, q8=False, math=F)["path_name"] == "tiled_simt"
+    assert L.plan(16, 4096, 4096, q8=True, math=F)["path_name"] == "tiled_simt"   # int8 W
+    # Operands the TMA cannot stream: the SIMT tiles, as before.
+    assert L.plan(12, 4096, 4096, q8=False, a_addr=260, math=F)["path_name"] == "tiled_simt"
+    assert L.plan(12, 4096, 4098, q8=False, math=F)["path_name"] == "tiled_simt"  # k % 4
     assert L.plan(24, 1030, 512, q8=False)["path_name"] == "tiled_simt"   # n % 4
     assert L.plan(24, 1028, 514, q8=False)["path_name"] == "tiled_simt"   # k % 4
     assert L.plan(24, 1028, 512, q8=False, b_addr=8)["path_name"] == "tiled_simt"

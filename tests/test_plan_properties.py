@@ -65,8 +65,13 @@ def test_every_plan_covers_c_and_k_within_limits(m, n, k, q8, kernel, accumulate
         assert math == L.MATH_TENSOR
     if path in TMA_PATHS:
         assert b_addr % 16 == 0
-    if path in ("gemv_tma", "gemv_ldg"):
+    if path == "gemv_ldg":
         assert m <= 8 and kernel == "skinny"
+    if path == "gemv_tma":
+        # m <= 8 through skinny; fp32 B with 9..16 rows through tiled_split (automatic) or
+        # tiled, in fp32 arithmetic.
+        assert (m <= 8 and kernel == "skinny") or (not q8 and 9 <= m <= 16 and math == L.MATH_FP32
+                                                   and kernel in ("tiled", "tiled_split"))
     if path == "gemv_tma":
         assert a_addr % 16 == 0 and k % 4 == 0 and (n * (1 if q8 else 4)) % 16 == 0
         assert rms == 0 or rms % 16 == 0
@@ -98,7 +103,8 @@ def test_every_plan_covers_c_and_k_within_limits(m, n, k, q8, kernel, accumulate
     else:
         assert p["grid_x"] * p["tile_n"] >= n
         if path in ("gemv_tma", "gemv_ldg"):
-            assert p["tile_m"] == m        # every row in one CTA; grid y holds the k slices
+            # every row in one CTA (16 for fp32 B past 8 rows); grid y holds the k slices
+            assert p["tile_m"] == (m if m <= 8 else 16)
         else:
             assert p["grid_y"] * p["tile_m"] >= m
     # scratch is asked for only when the path uses it, and the normalised copy of A only
