@@ -11,10 +11,12 @@
 // The chunk's softmax is kept unnormalised (max m, sum l of exp(score - m)) and the
 // exp-weighted sum of values o is formed with one thread per (head, float4 of the head) and
 // position slots. A context that fits one chunk is normalised and written directly;
-// otherwise each CTA writes (o, m, l) to scratch and the partials are merged in a fixed
-// two-level tree: the CTA completing a group of 64 chunks' ticket merges that group in chunk
-// order, the CTA completing the (head group, row)'s ticket merges the groups in group order --
-// deterministic, no second launch, tickets reset for the next call. Chunks are sized for
+// otherwise each CTA writes (o, m, l) to scratch and leaves. The merge is a second launch
+// (programmatic dependent launch: it becomes resident while the chunks run and waits for
+// them), parallel over (head, row, 32 of the head's dimensions): M = max m_c, the chunk
+// weights w_c = exp(m_c - M) and L = sum w_c l_c, then O = sum w_c o_c in chunk order
+// (deterministic), out = O / L; no CTA of the split launch waits on a ticket or merges a
+// group of chunks alone. Chunks are sized for
 // about three CTAs per SM (a tensor-parallel rank's 16 or 8 heads get shorter chunks in one
 // wave); the grid is sized for seq_len and the context length is
 // read from device memory, so a graph captured once serves every position; chunks past the
@@ -59,79 +61,92 @@ __host__ __device__ inline int chunk_size(int n_ctx, int splits) {
     return (c + kBoxRows - 1) / kBoxRows * kBoxRows;
 }
 
-constexpr int kMergeGroup = 64;             // chunks merged by one CTA at the first level
+constexpr int kMergeDims4 = 8;    // float4s of a head's dimensions per merge CTA (32 floats)
+constexpr int kMergeSlots = kAttnThreads / kMergeDims4;  // chunk slots per float4
 
-// Combines partials c0 .. c0 + cnt - 1 (of `stride` per head) of the G heads starting at
-// head_row, in that order: per head (a warp each) M = max m_c, w_c = exp(m_c - M) and
-// L = sum w_c l_c into res[g] = (M, L); then O = sum w_c o_c, `slots` threads per (head,
-// float4) with eight independent loads in flight, added in slot order into red[0 .. pairs).
-// Other CTAs' partials are read through L2 (__ldcg): this SM's L1 may hold stale lines.
-template <int G>
-__device__ void merge_partials(const float2* ml_src, const float4* o_src, size_t head_row,
-                               int stride, int c0, int cnt, int hs4, int pairs, int slots,
-                               float* wts, float2* res, float4* red) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int g = warp; g < G; g += kAttnThreads / 32) {
-        const size_t b = (head_row + g) * stride + c0;
-        float m = -INFINITY;
-        for (int c = lane; c < cnt; c += 32) m = fmaxf(m, __ldcg(&ml_src[b + c]).x);
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float l = 0.0f;
-        for (int c = lane; c < cnt; c += 32) {
-            const float2 p = __ldcg(&ml_src[b + c]);
-            const float w = expf(p.x - m);
-            wts[g * cnt + c] = w;
-            l += w * p.y;
-        }
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        if (lane == 0) res[g] = make_float2(m, l);
-    }
+// out[i][h][d] = sum_c w_c o_c[d] / L over the chunks c < n of (head h, row i): one CTA per
+// (head, row, kMergeDims4 float4s of the head). Launched after the split kernel with
+// programmatic dependent launch; the partials are read through L2 (__ldcg) after the wait.
+__global__ void __launch_bounds__(kAttnThreads) attn_merge_kernel(AttnArgs a, int splits) {
+    extern __shared__ __align__(16) float wts[];  // splits weights, then kAttnThreads float4s
+    __shared__ float red_s[kAttnThreads / 32];
+    const int h = blockIdx.x, i = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int hs4 = a.head_size / 4;
+    if (tid == 0) pdl_launch_dependents();
+    pdl_wait();  // the chunks' partials come from the split launch
+    const int n_ctx = *a.pos + i + 1;
+    const int chunk = chunk_size(n_ctx, splits);
+    const int n = (n_ctx + chunk - 1) / chunk;
+    if (n == 1) return;  // the split kernel normalised and wrote this row itself
+    const size_t rb = static_cast<size_t>(i) * a.scratch_row;
+    const float2* ml = a.part_ml + rb / 2 + static_cast<size_t>(h) * splits;
+    // M = max m_c, then w_c = exp(m_c - M) and L = sum w_c l_c (block reductions, fixed order).
+    float m = -INFINITY;
+    for (int c = tid; c < n; c += kAttnThreads) m = fmaxf(m, __ldcg(&ml[c]).x);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red_s[warp] = m;
     __syncthreads();
-    for (int base = 0; base < pairs; base += kAttnThreads) {
-        const int j = base + tid % (slots > 1 ? pairs : kAttnThreads);
-        const int r = slots > 1 ? tid / pairs : 0;
-        if (j < pairs && r < slots) {
-            const int g = j / hs4, d4 = j % hs4;
-            const float4* po = o_src + ((head_row + g) * stride + c0) * hs4 + d4;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            int c = r;
-            for (; c + 7 * slots < cnt; c += 8 * slots) {
-                float4 o[8];
+    m = red_s[0];
+    for (int w = 1; w < kAttnThreads / 32; ++w) m = fmaxf(m, red_s[w]);
+    float l = 0.0f;
+    for (int c = tid; c < n; c += kAttnThreads) {
+        const float2 p = __ldcg(&ml[c]);
+        const float w = expf(p.x - m);
+        wts[c] = w;
+        l += w * p.y;
+    }
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    __syncthreads();  // every thread has read red_s's maxima before it is rewritten
+    if (lane == 0) red_s[warp] = l;
+    __syncthreads();
+    l = red_s[0];
+    for (int w = 1; w < kAttnThreads / 32; ++w) l += red_s[w];
+    // O for float4 d4 of this CTA's slice: slot r takes chunks r, r + kMergeSlots, ...
+    const int d4 = blockIdx.z * kMergeDims4 + tid % kMergeDims4, r = tid / kMergeDims4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (d4 < hs4) {
+        const float4* po = reinterpret_cast<const float4*>(a.part_o + rb) +
+                           static_cast<size_t>(h) * splits * hs4 + d4;
+        int c = r;
+        for (; c + 3 * kMergeSlots < n; c += 4 * kMergeSlots) {
+            float4 o[4];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) o[u] = __ldcg(po + static_cast<size_t>(c + u * slots) * hs4);
+            for (int u = 0; u < 4; ++u) o[u] = __ldcg(po + static_cast<size_t>(c + u * kMergeSlots) * hs4);
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const float w = wts[g * cnt + c + u * slots];
-                    acc.x += w * o[u].x;
-                    acc.y += w * o[u].y;
-                    acc.z += w * o[u].z;
-                    acc.w += w * o[u].w;
-                }
+            for (int u = 0; u < 4; ++u) {
+                const float w = wts[c + u * kMergeSlots];
+                acc.x += w * o[u].x;
+                acc.y += w * o[u].y;
+                acc.z += w * o[u].z;
+                acc.w += w * o[u].w;
             }
-            for (; c < cnt; c += slots) {
-                const float4 o = __ldcg(po + static_cast<size_t>(c) * hs4);
-                const float w = wts[g * cnt + c];
-                acc.x += w * o.x;
-                acc.y += w * o.y;
-                acc.z += w * o.z;
-                acc.w += w * o.w;
-            }
-            red[r * pairs + j] = acc;
+        }
+        for (; c < n; c += kMergeSlots) {
+            const float4 o = __ldcg(po + static_cast<size_t>(c) * hs4);
+            const float w = wts[c];
+            acc.x += w * o.x;
+            acc.y += w * o.y;
+            acc.z += w * o.z;
+            acc.w += w * o.w;
         }
     }
+    float4* slot_sum = reinterpret_cast<float4*>(wts + (splits + 3) / 4 * 4);
+    slot_sum[tid] = acc;
     __syncthreads();
-    for (int j = tid; j < pairs; j += kAttnThreads) {
-        float4 acc = red[j];
-        for (int r = 1; r < slots; ++r) {
-            const float4 x = red[r * pairs + j];
-            acc.x += x.x;
-            acc.y += x.y;
-            acc.z += x.z;
-            acc.w += x.w;
+    if (r == 0 && d4 < hs4) {
+        float4 o = slot_sum[tid];
+        for (int q = 1; q < kMergeSlots; ++q) {  // slots in order
+            const float4 x = slot_sum[q * kMergeDims4 + tid];
+            o.x += x.x;
+            o.y += x.y;
+            o.z += x.z;
+            o.w += x.w;
         }
-        red[j] = acc;
+        const float inv = 1.0f / l;
+        reinterpret_cast<float4*>(a.out + static_cast<size_t>(i) * a.out_stride +
+                                  static_cast<size_t>(h) * a.head_size)[d4] =
+            make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
     }
-    __syncthreads();
 }
 
 // The G queries of one lane: float4 number sub + j * lpp of each head, j < QV.
@@ -152,7 +167,6 @@ __global__ void __launch_bounds__(kAttnThreads)
     float4* red = reinterpret_cast<float4*>(sc + G * cap4);  // slots x G x hs4
     __shared__ uint64_t bar[2];
     __shared__ float2 ml[G];
-    __shared__ int last;
 
     const int hg = blockIdx.x, i = blockIdx.y, s = blockIdx.z, splits = gridDim.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -297,15 +311,11 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
     __syncthreads();
 
-    // This row's block of the scratch: [tickets | chunk partials | group partials], at a
-    // stride that depends on the shape only, so calls of any row count leave every row's
-    // tickets where the next call looks for them.
+    // This row's block of the scratch: [chunk partials o | chunk (m, l)], at a stride that
+    // depends on the shape only; the merge launch reads them.
     const size_t rb = static_cast<size_t>(i) * a.scratch_row;
     float* part_o = a.part_o + rb;
     float2* part_ml = a.part_ml + rb / 2;
-    float* part2_o = a.part2_o + rb;
-    float2* part2_ml = a.part2_ml + rb / 2;
-    const size_t head_row = h0;  // first head of the group within the row's block
     for (int j = tid; j < pairs; j += kAttnThreads) {
         const int g = j / hs4, d4 = j % hs4;
         float4 o = red[j];
@@ -322,61 +332,10 @@ __global__ void __launch_bounds__(kAttnThreads)
                                       static_cast<size_t>(h0 + g) * hs)[d4] =
                 make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
         } else {
-            reinterpret_cast<float4*>(part_o)[((head_row + g) * splits + s) * hs4 + d4] = o;
+            reinterpret_cast<float4*>(part_o)[(static_cast<size_t>(h0 + g) * splits + s) * hs4 + d4] = o;
         }
     }
-    if (n == 1) return;
-    if (tid < G) part_ml[(head_row + tid) * splits + s] = ml[tid];
-
-    // Merge, two levels deep, fixed order (deterministic): chunks in groups of kMergeGroup, the
-    // CTA that completes a group's ticket merges it into a group partial; the CTA that
-    // completes the (head group, row)'s ticket merges the group partials into the output.
-    const int ngroups = (n + kMergeGroup - 1) / kMergeGroup;
-    const int max_groups = (splits + kMergeGroup - 1) / kMergeGroup;
-    const int grp = s / kMergeGroup, c0 = grp * kMergeGroup;
-    const int cnt = min(kMergeGroup, n - c0);
-    unsigned* tickets = a.counters + rb + static_cast<size_t>(hg) * (max_groups + 1);
-    float* wts = reinterpret_cast<float*>(red + slots * pairs);  // G x max(kMergeGroup, groups)
-    // G x (M, L), 16-byte aligned after the weights
-    float2* res = reinterpret_cast<float2*>(wts + (G * max(kMergeGroup, max_groups) + 3) / 4 * 4);
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        last = atomicAdd(&tickets[1 + grp], 1u) == static_cast<unsigned>(cnt - 1);
-        if (last) tickets[1 + grp] = 0;  // ready for the next call
-    }
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    merge_partials<G>(part_ml, reinterpret_cast<const float4*>(part_o), head_row, splits, c0,
-                      cnt, hs4, pairs, slots, wts, res, red);
-    if (ngroups > 1) {
-        // Publish the group partial, then the last group's CTA merges the groups.
-        for (int j = tid; j < pairs; j += kAttnThreads) {
-            const int g = j / hs4, d4 = j % hs4;
-            reinterpret_cast<float4*>(part2_o)[((head_row + g) * max_groups + grp) * hs4 + d4] = red[j];
-        }
-        if (tid < G) part2_ml[(head_row + tid) * max_groups + grp] = res[tid];
-        __threadfence();
-        __syncthreads();
-        if (tid == 0) {
-            last = atomicAdd(&tickets[0], 1u) == static_cast<unsigned>(ngroups - 1);
-            if (last) tickets[0] = 0;
-        }
-        __syncthreads();
-        if (!last) return;
-        __threadfence();
-        merge_partials<G>(part2_ml, reinterpret_cast<const float4*>(part2_o), head_row,
-                          max_groups, 0, ngroups, hs4, pairs, slots, wts, res, red);
-    }
-    for (int j = tid; j < pairs; j += kAttnThreads) {
-        const int g = j / hs4, d4 = j % hs4;
-        const float4 o = red[j];
-        const float inv = 1.0f / res[g].y;
-        reinterpret_cast<float4*>(a.out + static_cast<size_t>(i) * a.out_stride +
-                                  static_cast<size_t>(h0 + g) * hs)[d4] =
-            make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
-    }
+    if (n > 1 && tid < G) part_ml[static_cast<size_t>(h0 + tid) * splits + s] = ml[tid];
 }
 
 __device__ __forceinline__ float block_max(float v, float* red) {
@@ -481,16 +440,19 @@ struct SplitGeo {
     size_t smem;
 };
 
-// K and V chunks, the queries, the scores, the slot sums and the merge's chunk weights.
-size_t split_smem_bytes(const llme_attention_shape& s, int cap, int splits) {
+// K and V chunks, the queries, the scores and the slot sums.
+size_t split_smem_bytes(const llme_attention_shape& s, int cap) {
     const size_t G = heads_per_block(s), hs = s.head_size, hs4 = hs / 4;
     const size_t cap4 = (static_cast<size_t>(cap) + 3) / 4 * 4;
     const size_t pairs = G * hs4;
     const size_t slots = std::max<size_t>(1, kAttnThreads / pairs);
-    const size_t groups = (static_cast<size_t>(splits) + kMergeGroup - 1) / kMergeGroup;
-    const size_t wts = (G * std::max<size_t>(kMergeGroup, groups) + 3) / 4 * 4;
     return (2 * static_cast<size_t>(cap) * hs + G * hs + G * cap4) * sizeof(float) +
-           slots * pairs * 16 + (wts + 2 * G) * sizeof(float) + 128;  // + alignment slack
+           slots * pairs * 16 + 128;  // + alignment slack
+}
+
+// The merge launch: the chunk weights, then one float4 per thread.
+size_t merge_smem_bytes(int splits) {
+    return (static_cast<size_t>(splits) + 3) / 4 * 4 * sizeof(float) + kAttnThreads * 16;
 }
 
 // Splits: enough for one row to give about kTargetCtas CTAs, no chunk below kMinChunk
@@ -501,11 +463,11 @@ SplitGeo split_geo(const llme_attention_shape& s) {
     const int most = std::max(1, (s.seq_len + kMinChunk - 1) / kMinChunk);
     int splits = std::min(most, std::max(1, (kTargetCtas + groups - 1) / groups));
     int cap = chunk_size(s.seq_len, splits);
-    while (split_smem_bytes(s, cap, splits) > kSplitSmemBudget && cap > kMinChunk) {
+    while (split_smem_bytes(s, cap) > kSplitSmemBudget && cap > kMinChunk) {
         ++splits;
         cap = chunk_size(s.seq_len, splits);
     }
-    return {splits, cap, split_smem_bytes(s, cap, splits)};
+    return {splits, cap, split_smem_bytes(s, cap)};
 }
 
 size_t single_smem_bytes(const llme_attention_shape& s) {
@@ -527,27 +489,21 @@ int resolve(const llme_attention_shape& s, int kernel, size_t rows) {
 }
 
 // Scratch (floats): one block per row, at a stride that depends on the shape only --
-// [tickets: per head group one second-level ticket and one per chunk group | chunk partials o
-// | chunk (m, l) | group partials o | group (m, l)], each part 16-byte aligned. Offsets are
-// within a row's block; a call with fewer rows uses a prefix of the blocks, so every row's
-// tickets sit in the same place whatever the row count (each call leaves them at zero).
+// [chunk partials o | chunk (m, l)], each part 16-byte aligned. Offsets are within a row's
+// block; a call with fewer rows uses a prefix of the blocks. Every partial is written before
+// the merge reads it, so the scratch needs no initial contents.
 struct ScratchLayout {
-    size_t counters, o, ml, o2, ml2, row;
+    size_t o, ml, row;
 };
 
 ScratchLayout scratch_layout(const llme_attention_shape& s) {
     const SplitGeo g = split_geo(s);
-    const size_t heads = static_cast<size_t>(s.n_heads);
-    const size_t chunks = heads * static_cast<size_t>(g.splits);
-    const size_t groups = (static_cast<size_t>(g.splits) + kMergeGroup - 1) / kMergeGroup;
+    const size_t chunks = static_cast<size_t>(s.n_heads) * static_cast<size_t>(g.splits);
     auto up4 = [](size_t x) { return (x + 3) / 4 * 4; };
     ScratchLayout l{};
-    l.counters = 0;
-    l.o = up4(static_cast<size_t>(s.n_heads / heads_per_block(s)) * (groups + 1));
+    l.o = 0;
     l.ml = l.o + up4(chunks * static_cast<size_t>(s.head_size));
-    l.o2 = l.ml + up4(2 * chunks);
-    l.ml2 = l.o2 + up4(heads * groups * static_cast<size_t>(s.head_size));
-    l.row = l.ml2 + up4(2 * heads * groups);
+    l.row = l.ml + up4(2 * chunks);
     return l;
 }
 
@@ -597,6 +553,30 @@ cudaError_t launch_split(const CUtensorMap& tmK, const CUtensorMap& tmV, const A
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, attn_split_kernel<G, QV>, tmK, tmV, a);
+}
+
+// The merge of the chunks' partials: one CTA per (head, row, 32 dimensions of the head).
+cudaError_t launch_merge(const AttnArgs& a, size_t rows, int splits, cudaStream_t stream) {
+    const size_t smem = merge_smem_bytes(splits);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(attn_merge_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kAttnSmemAttr);
+        if (e != cudaSuccess) return e;
+    }
+    const int hs4 = a.head_size / 4;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(a.n_heads), static_cast<unsigned>(rows),
+                       static_cast<unsigned>((hs4 + kMergeDims4 - 1) / kMergeDims4));
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, attn_merge_kernel, a, splits);
 }
 
 template <int G>
@@ -699,9 +679,6 @@ int llme_attention(const llme_attention_shape* s, size_t rows, const int* pos_de
             a.chunk_cap = g.cap;
             a.part_o = scratch + l.o;
             a.part_ml = reinterpret_cast<float2*>(scratch + l.ml);
-            a.part2_o = scratch + l.o2;
-            a.part2_ml = reinterpret_cast<float2*>(scratch + l.ml2);
-            a.counters = reinterpret_cast<unsigned*>(scratch + l.counters);
             a.scratch_row = l.row;
             const int G = heads_per_block(*s);
             const dim3 grid(static_cast<unsigned>(s->n_heads / G), static_cast<unsigned>(rows),
@@ -726,6 +703,7 @@ int llme_attention(const llme_attention_shape* s, size_t rows, const int* pos_de
                 case 2: e = launch_split_g<2>(tmK, tmV, a, grid, g.smem, stream); break;
                 default: e = launch_split_g<1>(tmK, tmV, a, grid, g.smem, stream); break;
             }
+            if (e == cudaSuccess && g.splits > 1) e = launch_merge(a, rows, g.splits, stream);
         }
         return e == cudaSuccess ? LLME_OK : set_cuda_error(e, "attention");
     });

@@ -303,7 +303,7 @@ cudaError_t launch_gemm_q8_skinny(const SkinnyArgs& a, const CUtensorMap& tmW,
 unsigned read_and_clear_skinny_error();
 
 // Causal decode attention (attention.cu). The split kernel's scratch: partial o (rows x
-// heads x splits x head_size), (m, l) pairs, tickets per (row, head group).
+// heads x splits x head_size) and (m, l) pairs, merged by a second launch.
 struct AttnArgs {
     int n_heads = 0, head_size = 0, group = 1, chunk_cap = 0;
     bool boxes = false;  // keys and values by 2D TMA boxes (head_size <= 256), else row copies
@@ -315,9 +315,6 @@ struct AttnArgs {
     float* out = nullptr;
     float* part_o = nullptr;
     float2* part_ml = nullptr;
-    float* part2_o = nullptr;     // group partials (the merge's second level)
-    float2* part2_ml = nullptr;
-    unsigned* counters = nullptr;
     size_t scratch_row = 0;       // floats between rows' scratch blocks (the pointers: row 0)
 };
 unsigned read_and_clear_attn_error();

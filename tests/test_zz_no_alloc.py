@@ -10,9 +10,10 @@ whose split-K scratch is a fixed device array inside the library itself.
 Through the C ABI this file checks that two such calls in a row give, bit for bit, what the
 allocating entry point gives when it runs the same kernel (the SIMT split-K tiles, selected
 with LLME_MATH_FP32 and tiled_split), that both sit within the reference's 1e-5 * k of the
-oracle, that the calls leave the library's grow-only scratch untouched (no reallocation), and
-that a product too large for the fixed array is refused with a clear message. It is collected
-last and needs nothing from the other test files.
+oracle, that the calls leave the library's grow-only scratch untouched (no reallocation), that
+calls captured in a CUDA graph replay correctly with new inputs, and that a product too large
+for the fixed array is refused with a clear message. It is collected last and needs nothing
+from the other test files.
 """
 from __future__ import annotations
 
@@ -74,6 +75,43 @@ def test_noalloc_matches_allocating_entry_point_twice_in_a_row():
         g = got.cpu().numpy()
         np.testing.assert_array_equal(g, want.cpu().numpy())
         assert close_to(g, oracle_want, k, 2.0 if acc else 1.0), (m, k, n)
+
+
+def test_noalloc_calls_replay_from_a_cuda_graph():
+    # The callers this entry point is for record graphs: two calls captured once (the second
+    # accumulating, so it starts from tickets the first left at zero) are replayed with new
+    # inputs copied into the captured buffers; every replay matches the oracle and nothing is
+    # allocated.
+    L.load()
+    rng = np.random.default_rng(77)
+    m, k, n = 16, 2048, 1024
+    q, s = oracle.quantize_q8((rng.standard_normal((k, n)) * 0.02).astype(np.float32))
+    dA = torch.zeros(m, k, device="cuda")
+    dq, ds = torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda()
+    dC1 = torch.zeros(m, n, device="cuda")
+    dC2 = torch.zeros(m, n, device="cuda")
+    args = (m, n, k, dA.data_ptr(), dq.data_ptr(), ds.data_ptr())
+    L.matmul_cuda_q8_noalloc(*args, dC1.data_ptr(), False, L.torch_stream_handle())  # set-up
+    torch.cuda.synchronize()
+    generation = L.scratch_generation()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        st = L.torch_stream_handle()
+        L.matmul_cuda_q8_noalloc(*args, dC1.data_ptr(), False, st)
+        L.matmul_cuda_q8_noalloc(*args, dC2.data_ptr(), True, st)
+    for _ in range(3):
+        A = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+        C0 = rng.uniform(-1, 1, (m, n)).astype(np.float32)
+        dA.copy_(torch.from_numpy(A))
+        dC2.copy_(torch.from_numpy(C0))
+        graph.replay()
+        torch.cuda.synchronize()
+        want = oracle.matmul_naive_q8(A, q, s)
+        assert close_to(dC1.cpu().numpy(), want, k)
+        assert close_to(dC2.cpu().numpy(), C0 + want, k, 2.0)
+    del graph
+    L.synchronize()
+    assert L.scratch_generation() == generation
 
 
 def test_noalloc_refuses_a_product_larger_than_its_scratch():
