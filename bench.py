@@ -780,8 +780,15 @@ def run_tp_decode(args, world, rank, local):
     # N > 1). At N > 1 the sums after wo and w2 run inside those GEMVs when every rank's shard
     # has the same size (hidden % N == 0), else as two more all-reduce launches per layer.
     separate_sums = world > 1 and cfg["hidden_dim"] % world != 0
-    launches_per_token = (1 + cfg["n_layers"] * (5 + (2 if separate_sums else 0)) + 1
-                          + (1 if world > 1 else 0))
+    # the attention: its split kernel, and the merge launch when the context spans chunks (the
+    # engine's per-rank shape: this rank's heads over the qkv row it writes)
+    part = L.model_partition(cfg, world, rank)
+    hs = cfg["dim"] // cfg["n_heads"]
+    attn_launches = L.attention_launches(L.AttentionShape(
+        part["nq"], part["nkv"], hs, cfg["seq_len"], (part["nq"] + 2 * part["nkv"]) * hs,
+        part["nkv"] * hs, part["nq"] * hs), 1)
+    launches_per_token = (1 + cfg["n_layers"] * (4 + attn_launches + (2 if separate_sums else 0))
+                          + 1 + (1 if world > 1 else 0))
     w_bytes, kv_per_pos = model.stream_bytes()
     per_gpu = w_bytes + kv_per_pos * (ctx + 1)
     hbm, hbm_kind = peaks()
@@ -908,7 +915,9 @@ def run_attention(args, world, rank, local):
             "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(value / hbm, 4), "peak_kind": hbm_kind,
                          "kernel": "attn_split_kernel", "traffic": None},
-            "gpu_launches": len(ATTN_CASES) * ATTN_LAYERS * args.steps,
+            "gpu_launches": sum(L.attention_launches(L.AttentionShape(
+                h, kvh, hs, T, h * hs + 2 * kvh * hs, kvh * hs, h * hs), 1)
+                for _, h, kvh, hs, T in ATTN_CASES) * ATTN_LAYERS * args.steps,
             "clocks": sampler.summary()}
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -199,10 +199,14 @@ enum { LLME_ATTN_AUTOMATIC = 0, LLME_ATTN_SINGLE_BLOCK = 1, LLME_ATTN_SPLIT = 2 
 int llme_attention_check(const llme_attention_shape* s, int kernel);
 /* Floats of scratch llme_attention needs for up to `rows` rows (0 for single_block). */
 size_t llme_attention_scratch_floats(const llme_attention_shape* s, size_t rows, int kernel);
+/* Kernels one llme_attention call with these arguments enqueues on its stream: 1, or 2 when the
+ * split path may divide a context into chunks (their partials are then merged by a second
+ * launch); 0 when the arguments are invalid. Host only. */
+size_t llme_attention_launches(const llme_attention_shape* s, size_t rows, int kernel);
 /* out[i][h * head_size + d] = sum over t <= *pos_dev + i of softmax_t(q_i,h . k_t / sqrt(hs))
  * v_t[d], kv head h / (n_heads / n_kv_heads); the position is read from device memory.
- * scratch: zero-filled before its first use, left ready by every call. Asynchronous on
- * `stream` (NULL: per-thread default stream); deterministic bit for bit. */
+ * scratch: needs no initial contents (every chunk partial is written before it is read).
+ * Asynchronous on `stream` (NULL: per-thread default stream); deterministic bit for bit. */
 int llme_attention(const llme_attention_shape* s, size_t rows, const int* pos_dev,
                    const float* q, const float* key_cache, const float* value_cache, float* out,
                    float* scratch, int kernel, void* stream);

@@ -623,6 +623,18 @@ size_t llme_attention_scratch_floats(const llme_attention_shape* s, size_t rows,
     return scratch_layout(*s).row * rows;
 }
 
+size_t llme_attention_launches(const llme_attention_shape* s, size_t rows, int kernel) {
+    try {
+        if (!s || rows == 0 || check(*s, kernel) != LLME_OK) return 0;
+        kernel = resolve(*s, kernel, rows);
+        if (check(*s, kernel) != LLME_OK) return 0;
+        if (kernel == LLME_ATTN_SINGLE_BLOCK) return 1;
+        return split_geo(*s).splits > 1 ? 2 : 1;
+    } catch (...) {
+        return 0;
+    }
+}
+
 int llme_attention(const llme_attention_shape* s, size_t rows, const int* pos_dev, const float* q,
                    const float* key_cache, const float* value_cache, float* out, float* scratch,
                    int kernel, void* stream_ptr) {

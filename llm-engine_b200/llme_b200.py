@@ -116,6 +116,8 @@ def load() -> ctypes.CDLL:
     lib.llme_attention_check.argtypes = [ctypes.POINTER(AttentionShape), i]
     lib.llme_attention_scratch_floats.argtypes = [ctypes.POINTER(AttentionShape), sz, i]
     lib.llme_attention_scratch_floats.restype = sz
+    lib.llme_attention_launches.argtypes = [ctypes.POINTER(AttentionShape), sz, i]
+    lib.llme_attention_launches.restype = sz
     lib.llme_attention.argtypes = [ctypes.POINTER(AttentionShape), sz, vp, vp, vp, vp, vp, vp, i,
                                    vp]
     lib.llme_embed_rows.argtypes = [sz, sz, vp, vp, vp, vp]
@@ -246,6 +248,11 @@ def attention_check(shape: AttentionShape, kernel="automatic") -> None:
 
 def attention_scratch_floats(shape: AttentionShape, rows: int, kernel="automatic") -> int:
     return load().llme_attention_scratch_floats(ctypes.byref(shape), rows, ATTN_KERNELS[kernel])
+
+
+def attention_launches(shape: AttentionShape, rows: int, kernel="automatic") -> int:
+    """Kernels one attention call enqueues (1, or 2 with the split path's merge); 0: invalid."""
+    return load().llme_attention_launches(ctypes.byref(shape), rows, ATTN_KERNELS[kernel])
 
 
 def attention(shape: AttentionShape, rows: int, pos_dev: int, q: int, k_cache: int, v_cache: int,

@@ -315,6 +315,20 @@ def test_math_mode_roundtrip():
         L.set_math(5)
 
 
+def test_attention_launch_counts():
+    # Kernels one call enqueues (host only): the split kernel, plus the merge launch when the
+    # context may span chunks; single_block is one launch; invalid arguments give 0.
+    S = L.AttentionShape
+    mha = S(32, 32, 128, 4096, 3 * 4096, 4096, 4096)
+    assert L.attention_launches(mha, 1) == 2
+    assert L.attention_launches(S(4, 1, 128, 20000, 768, 128, 512), 1) == 2
+    assert L.attention_launches(S(4, 1, 128, 64, 768, 128, 512), 1) == 1     # one chunk
+    assert L.attention_launches(S(32, 32, 128, 100, 3 * 4096, 4096, 4096), 20) == 1  # single
+    assert L.attention_launches(S(32, 32, 128, 100, 3 * 4096, 4096, 4096), 20, "split") == 2
+    assert L.attention_launches(mha, 0) == 0
+    assert L.attention_launches(S(6, 4, 8, 64, 96, 32, 48), 1) == 0          # 6 heads / 4 kv
+
+
 def test_attention_check_rules():
     # The reference's attention_check rules (src/cuda_attention.cu:306-325), host only.
     S = L.AttentionShape
