@@ -454,7 +454,9 @@ typedef struct {
 /* The plan llme_matmul_f32 (is_q8 == 0) or llme_matmul_q8 (is_q8 == 1) would follow on a
  * device with `sm_count` SMs, for A, B and the RMSNorm weight at the given device addresses
  * (rms_addr 0 = no RMSNorm). No GPU is touched. Returns LLME_E_INVALID (with the same
- * message) where the call would. */
+ * message) where the call would. One difference: a GEMV's k slices form thread-block clusters,
+ * and on a device the calls take the driver's count of clusters it can hold at once where this
+ * function assumes 2 x sm_count / (cluster size); the device may then use fewer slices. */
 int llme_plan(size_t m, size_t n, size_t k, int is_q8, int kernel, int accumulate,
               uintptr_t a_addr, uintptr_t b_addr, uintptr_t rms_addr, int sm_count, int math,
               llme_plan_t* out);

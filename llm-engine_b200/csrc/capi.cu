@@ -73,6 +73,9 @@ struct PlanIn {
     uintptr_t a_addr, b_addr, rms_addr;
     int sms;
     int math;
+    // The device's capacity for per-call GEMV clusters of 1..kGemvMaxCluster CTAs (entry c - 1),
+    // or null: host-only plans then take 2 x SMs / c.
+    const int* gemv_clusters = nullptr;
 };
 
 // The int8 tcgen05 GEMM on CTA pairs (one M=256 MMA over two SMs, 256-column tiles) only when
@@ -124,23 +127,26 @@ int plan_path(const PlanIn& in, llme_plan_t* p) {
     // Operands the TMA GEMV can stream: 16-byte aligned rows and starts.
     const bool gemv_tma = in.b_addr % 16 == 0 && (n * (in.q8 ? 1 : 4)) % 16 == 0 &&
                           in.a_addr % 16 == 0 && k % 4 == 0 && (!has_rms || in.rms_addr % 16 == 0);
-    // The TMA GEMV's grid: up to two CTAs per SM; the k slices of a column strip form one
-    // cluster (at most 8), each at least two boxes deep. Past half as many strips as SMs, the
-    // slices are just enough for one CTA per SM (ceil(SMs / strips): 2 up to one strip per SM,
-    // then 1): measured on the 7B wqkv (96 strips, 50 MB) 13.95 us per call at 2 slices against
-    // 18.08 at 3, and the decode step 428 against 406 tokens/s.
+    // The TMA GEMV's grid: two CTAs per SM; the k slices of a column strip form one cluster (at
+    // most 8), each at least two boxes deep, and every cluster must be resident at once: the
+    // device holds fewer clusters than 2 x SMs / c when they do not pack every GPC (B200, c = 1..8:
+    // 296, 148, 93, 71, 56, 45, 37, 33), and a cluster that waits for a second wave doubles the
+    // call (the 7B wqkv, 96 strips: 18.08 us at 3 slices, 13.95 at 2; the 86-strip w1 fits at 3).
     auto plan_gemv_tma = [&](int rows) {
         p->path = LLME_PATH_GEMV_TMA;
         p->tile_m = rows;
         p->tile_n = gemv_tma_cols(in.q8);
         const size_t strips = ceil_div(n, p->tile_n);
         const size_t target = static_cast<size_t>(gemv_call_ctas_per_sm(rows)) * sms;
-        const size_t by_grid = 2 * strips > static_cast<size_t>(sms)
-                                   ? ceil_div(static_cast<size_t>(sms), strips)
-                                   : target / strips;
         size_t slices = std::max<size_t>(
-            1, std::min({by_grid, ceil_div(k, 2 * kGemvBoxRows),
+            1, std::min({target / strips, ceil_div(k, 2 * kGemvBoxRows),
                          static_cast<size_t>(kGemvMaxCluster)}));
+        auto capacity = [&](size_t c) {
+            return in.gemv_clusters && in.gemv_clusters[c - 1] > 0
+                       ? static_cast<size_t>(in.gemv_clusters[c - 1])
+                       : target / c;
+        };
+        while (slices > 1 && strips > capacity(slices)) --slices;
         const size_t span = round_up(ceil_div(k, slices), kGemvBoxRows);
         slices = ceil_div(k, span);
         p->grid_x = static_cast<int>(strips);
@@ -345,6 +351,8 @@ struct DeviceState {
     size_t partial_cap = 0;
     Scratch norm;
     Scratch operand;  // split activation rows (int8 tensor-core GEMMs) or B^T (TF32 GEMM)
+    // Per-call GEMV cluster capacity by cluster size (0: not queried yet).
+    int gemv_clusters[kGemvMaxCluster] = {};
 };
 
 std::mutex g_dev_mu;
@@ -355,6 +363,26 @@ int current_device(int* dev) {
     if (e != cudaSuccess) return cuda_fail(e, "get device");
     if (*dev < 0 || *dev >= kMaxDevices) return fail(LLME_E_UNSUPPORTED, "device index too large");
     return LLME_OK;
+}
+
+// The device's capacity for per-call GEMV clusters of 1..kGemvMaxCluster CTAs, queried once
+// (the current device must be `dev`); null when the driver does not answer.
+const int* device_gemv_clusters(int dev) {
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    DeviceState& d = g_dev[dev];
+    if (d.gemv_clusters[0] == 0) {
+        int t[kGemvMaxCluster];
+        for (int c = 1; c <= kGemvMaxCluster; ++c) {
+            t[c - 1] = gemv_max_active_clusters(c);
+            if (t[c - 1] <= 0) {
+                cudaGetLastError();  // a refused query leaves no sticky error
+                return nullptr;
+            }
+        }
+        std::copy(t, t + kGemvMaxCluster, d.gemv_clusters);
+    }
+    return d.gemv_clusters;
 }
 
 int device_sms(int dev, int* sms) {
@@ -538,6 +566,7 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
     if (st) return st;
     st = device_sms(dev, &sms);
     if (st) return st;
+    const int* gemv_clusters = device_gemv_clusters(dev);
     PlanIn in{m,
               n,
               k,
@@ -549,6 +578,7 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
               reinterpret_cast<uintptr_t>(rms),
               sms,
               math_mode()};
+    in.gemv_clusters = gemv_clusters;
     llme_plan_t p;
     st = make_plan(in, &p);
     if (st) return st;
@@ -1204,6 +1234,7 @@ int plan_product(size_t m, size_t n, size_t k, bool q8, const void* A, const voi
     if (st) return st;
     PlanIn in{m, n, k, q8, LLME_KERNEL_AUTOMATIC, false, reinterpret_cast<uintptr_t>(A),
               reinterpret_cast<uintptr_t>(B), reinterpret_cast<uintptr_t>(rms), sms, math_mode()};
+    in.gemv_clusters = device_gemv_clusters(dev);
     return make_plan(in, p);
 }
 }  // namespace llme

@@ -1147,6 +1147,34 @@ cudaError_t launch_tma_m(const GemvArgs& a, const CUtensorMap& tmB, const CUtens
     return cudaLaunchKernelEx(&cfg, kern, tmB, tmA, tmW, a);
 }
 
+}  // namespace
+
+// Clusters of `cluster` CTAs of the per-call TMA GEMV the current device holds at once. Every
+// per-call instantiation has the same launch shape (call_threads, at most kCallSmemBudget of
+// shared memory, two CTAs per SM), so the largest stands for all.
+int gemv_max_active_clusters(int cluster) {
+    auto kern = gemv_tma_kernel<1, true, false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kCallSmemBudget);
+    if (e != cudaSuccess) return -1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, static_cast<unsigned>(cluster));
+    cfg.blockDim = dim3(call_threads<1>());
+    cfg.dynamicSmemBytes = kCallSmemBudget;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = static_cast<unsigned>(cluster);
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    return e == cudaSuccess ? n : -1;
+}
+
+namespace {
+
 template <bool Q8, bool Norm>
 cudaError_t launch_tma_rows(const GemvArgs& a, const CUtensorMap& tmB, const CUtensorMap& tmA,
                             const CUtensorMap& tmW) {

@@ -138,6 +138,9 @@ constexpr int kGemvWideRows = 16;
 inline int gemv_tma_cols(bool q8) { return q8 ? kGemvRowBytes : kGemvRowBytes / 4; }
 // CTAs per SM of one per-call TMA GEMV grid.
 constexpr int gemv_call_ctas_per_sm(int) { return 2; }
+// Clusters of `cluster` per-call TMA GEMV CTAs the current device holds at once (the driver's
+// occupancy answer; below 2 x SMs / cluster when clusters do not pack every GPC); -1 on error.
+int gemv_max_active_clusters(int cluster);
 constexpr int kGemvLdgCols = 32;
 
 // Grouped GEMV: many independent int8 products of the same m (<= 8) in one persistent
