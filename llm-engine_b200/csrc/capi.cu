@@ -161,10 +161,15 @@ int plan_path(const PlanIn& in, llme_plan_t* p) {
     // fp32 B with 9..16 rows (tiled_split, or tiled) in LLME_MATH_FP32: the TMA GEMV at 16
     // rows, exact fp32 arithmetic (33 us for 16 x 4096^2 against 126 on the SIMT tiles). In
     // tensor math the three-term TF32 kernel below is faster (19 us).
+    // RMSNorm runs as the separate row pass here (the 16-row kernel has no fused norm).
     if (!in.q8 && in.math == LLME_MATH_FP32 && m > kSkinnyMaxRows &&
         m <= static_cast<size_t>(kGemvWideRows) && gemv_tma &&
-        (kernel == LLME_KERNEL_TILED_SPLIT || kernel == LLME_KERNEL_TILED))
-        return plan_gemv_tma(kGemvWideRows);
+        (kernel == LLME_KERNEL_TILED_SPLIT || kernel == LLME_KERNEL_TILED)) {
+        plan_gemv_tma(kGemvWideRows);
+        p->rms_prepass = has_rms ? 1 : 0;
+        if (has_rms) p->norm_bytes = m * k * sizeof(float);
+        return LLME_OK;
+    }
 
     if (kernel == LLME_KERNEL_SKINNY) {
         // Ragged rows or unaligned pointers: the plain-load GEMV.
@@ -629,10 +634,11 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
         g.m = static_cast<int>(m);
         g.n = static_cast<int>(n);
         g.k = static_cast<int>(k);
-        g.A = A;
+        // RMSNorm fused in the kernel, or (16-row fp32 GEMV) already applied by the row pass.
+        g.A = a_in;
         g.B = B;
         g.scale = scale;
-        g.rms = rms;
+        g.rms = p.rms_prepass ? nullptr : rms;
         g.C = C;
         g.q8 = q8;
         g.accumulate = accumulate;
@@ -655,11 +661,11 @@ int run(size_t m, size_t n, size_t k, const float* A, const void* B, const float
                                  kGemvBoxRows, &tmB);
             if (st) return st;
             // The box is the kernel's row count (16 for 9..16 fp32 rows: zero fill past m).
-            st = tensor_map(A, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, k, kGemvBoxRows,
+            st = tensor_map(g.A, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, m, k, kGemvBoxRows,
                             static_cast<uint32_t>(p.tile_m), &tmA);
             if (st) return st;
-            if (rms) {
-                st = tensor_map(rms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 0, k, kGemvBoxRows, 1,
+            if (g.rms) {
+                st = tensor_map(g.rms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 0, k, kGemvBoxRows, 1,
                                 &tmW);
                 if (st) return st;
             } else {

@@ -32,7 +32,8 @@
 //    thread and pairs each output's accumulator over even and odd k instead of
 //    over columns: a 16-byte load of A gives two k pairs of one row, used as they
 //    are by fma.rn.f32x2 against the column's k pairs of B, so A needs no
-//    repacking and each A load feeds four packed FMAs.
+//    repacking and each A load feeds four packed FMAs. It has no fused RMSNorm
+//    (the caller's row pass normalises A first).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -477,9 +478,7 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
         const int cg = tid % S::TPR, rg = tid / S::TPR;
         uint64_t acc[M][S::ACC];
         float ss[M];
-        // k-quad form: this thread's share of the sums of squares, all for row tid / 16.
-        float row_ss = 0.0f;
-        static_assert(!(S::KQ && Norm) || CT == 16 * M, "k-quad RMSNorm: 16 threads per row");
+        static_assert(!(S::KQ && Norm), "the k-quad form has no fused RMSNorm");
 #pragma unroll
         for (int r = 0; r < M; ++r) {
             ss[r] = 0.0f;
@@ -494,25 +493,6 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
             const float* sa = reinterpret_cast<const float*>(smem + L::kOffA + s * L::kABox);
             const float* sw = reinterpret_cast<const float*>(smem + L::kOffW + s * L::kWBox);
             if constexpr (S::KQ) {
-                if constexpr (Norm) {
-                    // The stage's A box is normalised in place before anyone reads it: thread
-                    // tid takes row tid / 16, k 4 (tid % 16) .. + 3 and the four 64 further
-                    // (conflict-free), adds their squares and multiplies them by the weight.
-                    float* q = const_cast<float*>(sa) + (tid >> 4) * kGemvBoxRows + 4 * (tid & 15);
-                    const float* wk = sw + 4 * (tid & 15);
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        float4 u = *reinterpret_cast<const float4*>(q + 64 * h);
-                        const float4 w = *reinterpret_cast<const float4*>(wk + 64 * h);
-                        row_ss = fmaf(u.x, u.x, fmaf(u.y, u.y, fmaf(u.z, u.z, fmaf(u.w, u.w, row_ss))));
-                        u.x *= w.x;
-                        u.y *= w.y;
-                        u.z *= w.z;
-                        u.w *= w.w;
-                        *reinterpret_cast<float4*>(q + 64 * h) = u;
-                    }
-                    named_barrier(2, CT);
-                }
                 // Quads q = rg, rg + RG, ...: k rows 4q .. 4q + 3, columns 2 cg, 2 cg + 1.
 #pragma unroll 1
                 for (int i = 0; i < S::QPT; ++i) {
@@ -585,18 +565,11 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
                     unpack2(acc[r][j], accf[r][2 * j], accf[r][2 * j + 1]);
             }
         }
-        if constexpr (S::KQ && Norm) {
-            // The row's 16 threads are one half-warp: its total is the row's whole sum of
-            // squares over this CTA's k (the ring is drained: the barrier above).
-#pragma unroll
-            for (int off = 8; off > 0; off >>= 1) row_ss += __shfl_xor_sync(0xffffffffu, row_ss, off);
-            if ((tid & 15) == 0) tot_ss[tid >> 4] = row_ss;
-        }
 #pragma unroll
         for (int off = S::TPR; off < 32; off <<= 1) {
 #pragma unroll
             for (int r = 0; r < M; ++r) {
-                if constexpr (Norm && !S::KQ) ss[r] += __shfl_xor_sync(0xffffffffu, ss[r], off);
+                if constexpr (Norm) ss[r] += __shfl_xor_sync(0xffffffffu, ss[r], off);
 #pragma unroll
                 for (int j = 0; j < S::V; ++j) accf[r][j] += __shfl_xor_sync(0xffffffffu, accf[r][j], off);
             }
@@ -615,7 +588,7 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
                     *reinterpret_cast<float2*>(dst) = make_float2(accf[r][0], accf[r][1]);
                 }
             }
-            if (Norm && !S::KQ && cg == 0) {
+            if (Norm && cg == 0) {
 #pragma unroll
                 for (int r = 0; r < M; ++r) red_ss[warp * M + r] = ss[r];
             }
@@ -627,7 +600,7 @@ __global__ void __launch_bounds__(call_threads<M>(), kCallResidentCtas)
             for (int w = 0; w < CW; ++w) v += red[w * M * S::NT + e];
             tot[e] = v;
         }
-        if (Norm && !S::KQ && tid < M) {
+        if (Norm && tid < M) {
             float v = 0.0f;
 #pragma unroll
             for (int w = 0; w < CW; ++w) v += red_ss[w * M + tid];
@@ -1188,9 +1161,10 @@ cudaError_t launch_tma_rows(const GemvArgs& a, const CUtensorMap& tmB, const CUt
         case 7: return launch_tma_m<7, Q8, Norm>(a, tmB, tmA, tmW);
         case 8: return launch_tma_m<8, Q8, Norm>(a, tmB, tmA, tmW);
         default:
-            // fp32 B, 9..16 rows: one 16-row instantiation (its A map's box is 16 rows).
-            if constexpr (!Q8)
-                if (a.m > 8 && a.m <= kGemvWideRows) return launch_tma_m<kGemvWideRows, false, Norm>(a, tmB, tmA, tmW);
+            // fp32 B, 9..16 rows, no fused RMSNorm: one 16-row instantiation (its A map's box
+            // is 16 rows).
+            if constexpr (!Q8 && !Norm)
+                if (a.m > 8 && a.m <= kGemvWideRows) return launch_tma_m<kGemvWideRows, false, false>(a, tmB, tmA, tmW);
             return cudaErrorInvalidValue;
     }
 }

@@ -258,7 +258,9 @@ def test_fp32_gemv_up_to_16_rows_plan():
         assert p["split_bytes"] == 0 and p["norm_bytes"] == 0 and p["rms_prepass"] == 0
         assert L.plan(m, 4096, 4096, q8=False)["path_name"] == "tcgen05_f32_skinny"
     assert L.plan(12, 4096, 4096, q8=False, kernel="tiled", math=F)["path_name"] == "gemv_tma"
-    assert L.plan(12, 4096, 4096, q8=False, rms_addr=256, math=F)["path_name"] == "gemv_tma"
+    p = L.plan(12, 4096, 4096, q8=False, rms_addr=256, math=F)   # RMSNorm by the row pass
+    assert p["path_name"] == "gemv_tma" and p["rms_prepass"] == 1
+    assert p["norm_bytes"] == 12 * 4096 * 4
     assert L.plan(17, 4096, 4096, q8=False, math=F)["path_name"] == "tiled_simt"
     assert L.plan(16, 4096, 4096, q8=True, math=F)["path_name"] == "tiled_simt"   # int8 W
     # Operands the TMA cannot stream: the SIMT tiles, as before.

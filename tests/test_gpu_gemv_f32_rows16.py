@@ -1,8 +1,8 @@
 """fp32-weight products with 9..16 rows in fp32 arithmetic (LLME_MATH_FP32) on the TMA GEMV
 (LLME_PATH_GEMV_TMA at 16 rows): exact fp32 FMA arithmetic with each output's accumulator
 paired over even and odd k, the rows past m read as the TMA's zero fill and never stored, the k
-slices of a column strip reduced in one thread-block cluster, RMSNorm applied to each stage's A
-box in place.
+slices of a column strip reduced in one thread-block cluster; RMSNorm by the library's row pass
+before the GEMV.
 
 The reference runs these shapes on sgemm_tiled<64,4,Split,float> (tiled_split,
 src/cuda_matmul.cu:71-125, 352-363). Held to the decode path's accuracy bound, max over rows of
@@ -84,8 +84,8 @@ def test_rows16_matches_oracle(m, k, n):
 
 @pytest.mark.parametrize("m,k,n", [(12, 3000, 1536), (16, 4096, 4096), (9, 256, 260)])
 def test_rows16_fusion(m, k, n):
-    # MatmulFusion{accumulate, rms_weight} (tests/test_cuda.cpp:190-212): the RMSNorm is
-    # applied inside the kernel, one slice or a cluster of them.
+    # MatmulFusion{accumulate, rms_weight} (tests/test_cuda.cpp:190-212): the RMSNorm row
+    # pass, then the GEMV over one slice or a cluster of them.
     rng = np.random.default_rng(8 + m + k)
     A, C0, w, W = uni(rng, m, k), uni(rng, m, n), uni(rng, k), weights(rng, k, n)
     got = run(A, W, C0=C0, accumulate=True, spare_rows=2)
