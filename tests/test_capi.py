@@ -332,6 +332,17 @@ def test_attention_launch_counts():
     assert L.attention_launches(S(6, 4, 8, 64, 96, 32, 48), 1) == 0          # 6 heads / 4 kv
 
 
+def test_attention_scratch_is_the_chunk_partials():
+    # One block per row: every chunk's partial o (head_size floats) and its (m, l) pair, each
+    # part a whole number of float4s -- nothing else (the merge is a second launch, so there
+    # are no tickets or group partials).
+    S = L.AttentionShape
+    mha = S(32, 32, 128, 4096, 3 * 4096, 4096, 4096)      # 64 chunks of 64 positions
+    chunks = 32 * 64
+    assert L.attention_scratch_floats(mha, 1, "split") == chunks * 128 + 2 * chunks
+    assert L.attention_scratch_floats(mha, 3, "split") == 3 * (chunks * 128 + 2 * chunks)
+
+
 def test_attention_check_rules():
     # The reference's attention_check rules (src/cuda_attention.cu:306-325), host only.
     S = L.AttentionShape
