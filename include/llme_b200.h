@@ -460,6 +460,16 @@ typedef struct {
 int llme_plan(size_t m, size_t n, size_t k, int is_q8, int kernel, int accumulate,
               uintptr_t a_addr, uintptr_t b_addr, uintptr_t rms_addr, int sm_count, int math,
               llme_plan_t* out);
+/* llme_plan for a device that holds gemv_clusters[c - 1] GEMV clusters of c CTAs at once
+ * (c = 1..8, as llme_gemv_cluster_capacity reports; NULL: as llme_plan), so an offline plan
+ * matches the one the calls take on that device. No GPU is touched. */
+int llme_plan_clusters(size_t m, size_t n, size_t k, int is_q8, int kernel, int accumulate,
+                       uintptr_t a_addr, uintptr_t b_addr, uintptr_t rms_addr, int sm_count,
+                       int math, const int* gemv_clusters, llme_plan_t* out);
+/* The current device's capacity for the weight-streaming GEMV's thread-block clusters:
+ * out[c - 1] = clusters of c CTAs it holds at once, c = 1..8 (the driver's occupancy
+ * answer, two CTAs per SM; below 2 x SMs / c where clusters do not pack every GPC). */
+int llme_gemv_cluster_capacity(int* out);
 
 #ifdef __cplusplus
 }

@@ -1510,10 +1510,34 @@ int llme_plan(size_t m, size_t n, size_t k, int is_q8, int kernel, int accumulat
               uintptr_t a_addr, uintptr_t b_addr, uintptr_t rms_addr, int sm_count, int math,
               llme_plan_t* out) {
     return llme::guarded([&]() -> int {
+        return llme_plan_clusters(m, n, k, is_q8, kernel, accumulate, a_addr, b_addr, rms_addr,
+                                  sm_count, math, nullptr, out);
+    });
+}
+
+int llme_plan_clusters(size_t m, size_t n, size_t k, int is_q8, int kernel, int accumulate,
+                       uintptr_t a_addr, uintptr_t b_addr, uintptr_t rms_addr, int sm_count,
+                       int math, const int* gemv_clusters, llme_plan_t* out) {
+    return llme::guarded([&]() -> int {
         g_error.clear();
         if (!out) return fail(LLME_E_INVALID, "llme_plan: null result pointer");
         PlanIn in{m, n, k, is_q8 != 0, kernel, accumulate != 0, a_addr, b_addr, rms_addr, sm_count, math};
+        in.gemv_clusters = gemv_clusters;
         return make_plan(in, out);
+    });
+}
+
+int llme_gemv_cluster_capacity(int* out) {
+    return llme::guarded([&]() -> int {
+        g_error.clear();
+        if (!out) return fail(LLME_E_INVALID, "llme_gemv_cluster_capacity: null result pointer");
+        int dev = 0;
+        int st = current_device(&dev);
+        if (st) return st;
+        const int* t = device_gemv_clusters(dev);
+        if (!t) return fail(LLME_E_UNSUPPORTED, "llme_gemv_cluster_capacity: the driver gave no answer");
+        std::copy(t, t + kGemvMaxCluster, out);
+        return LLME_OK;
     });
 }
 

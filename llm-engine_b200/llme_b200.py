@@ -180,6 +180,12 @@ def load() -> ctypes.CDLL:
     lib.llme_plan.argtypes = [sz, sz, sz, i, i, i, ctypes.c_size_t, ctypes.c_size_t,
                               ctypes.c_size_t, i, i, ctypes.POINTER(Plan)]
     lib.llme_plan.restype = i
+    lib.llme_plan_clusters.argtypes = [sz, sz, sz, i, i, i, ctypes.c_size_t, ctypes.c_size_t,
+                                       ctypes.c_size_t, i, i, ctypes.POINTER(ctypes.c_int),
+                                       ctypes.POINTER(Plan)]
+    lib.llme_plan_clusters.restype = i
+    lib.llme_gemv_cluster_capacity.argtypes = [ctypes.POINTER(ctypes.c_int)]
+    lib.llme_gemv_cluster_capacity.restype = i
     lib.llme_alloc.argtypes = [ctypes.POINTER(vp), sz]
     lib.llme_free.argtypes = [vp]
     lib.llme_copy_to_device.argtypes = [vp, vp, sz]
@@ -400,12 +406,26 @@ class Comm:
 
 def plan(m: int, n: int, k: int, q8: bool, kernel="automatic", accumulate: bool = False,
          a_addr: int = 256, b_addr: int = 256, rms_addr: int = 0, sm_count: int = 148,
-         math: int = MATH_TENSOR) -> dict:
-    """The dispatch decision for a call, computed on the host only (no GPU needed)."""
+         math: int = MATH_TENSOR, gemv_clusters=None) -> dict:
+    """The dispatch decision for a call, computed on the host only (no GPU needed).
+    gemv_clusters: a device's GEMV cluster capacity (8 counts, gemv_cluster_capacity());
+    None models it as 2 x sm_count / cluster size."""
     p = Plan()
-    _check(load().llme_plan(m, n, k, int(bool(q8)), _kernel_id(kernel), int(bool(accumulate)),
-                            a_addr, b_addr, rms_addr, sm_count, math, ctypes.byref(p)))
+    args = (m, n, k, int(bool(q8)), _kernel_id(kernel), int(bool(accumulate)), a_addr, b_addr,
+            rms_addr, sm_count, math)
+    if gemv_clusters is None:
+        _check(load().llme_plan(*args, ctypes.byref(p)))
+    else:
+        table = (ctypes.c_int * 8)(*gemv_clusters)
+        _check(load().llme_plan_clusters(*args, table, ctypes.byref(p)))
     return p.as_dict()
+
+
+def gemv_cluster_capacity() -> list:
+    """The current device's capacity for GEMV clusters of 1..8 CTAs (needs a GPU)."""
+    out = (ctypes.c_int * 8)()
+    _check(load().llme_gemv_cluster_capacity(out))
+    return list(out)
 
 
 def scratch_generation() -> int:

@@ -175,6 +175,24 @@ def test_decode_shapes_fill_the_gpu():
         assert 0.8 * 296 <= p["grid_x"] * p["grid_y"] <= 296, (n, k, p)
 
 
+def test_gemv_slices_fit_the_device_cluster_capacity():
+    # The k slices of a strip form one cluster, and every cluster must be resident at once.
+    # B200's measured capacity (clusters of 1..8 CTAs at two CTAs per SM) is below 296 / c.
+    b200 = [296, 148, 93, 71, 56, 45, 37, 33]
+    # the 7B wqkv: 96 strips; the model would take 3 slices, the device holds 93 clusters of 3
+    assert L.plan(1, 12288, 4096, q8=True)["grid_y"] == 3
+    p = L.plan(1, 12288, 4096, q8=True, gemv_clusters=b200)
+    assert p["grid_y"] == 2 and p["cluster"] == 2 and p["span"] == 2048
+    # the 86-strip w1 fits at 3; 32 strips fit at 8 (33 clusters)
+    assert L.plan(1, 11008, 4096, q8=True, gemv_clusters=b200)["grid_y"] == 3
+    assert L.plan(1, 4096, 4096, q8=True, gemv_clusters=b200)["grid_y"] == 8
+    # one fewer cluster of 8 than strips: 7 slices, k still covered exactly once
+    p = L.plan(1, 4096, 4096, q8=True, gemv_clusters=b200[:7] + [31])
+    assert p["grid_y"] == 7 and (p["slices"] - 1) * p["span"] < 4096 <= p["slices"] * p["span"]
+    # a table with no answer for a size falls back to the model
+    assert L.plan(1, 12288, 4096, q8=True, gemv_clusters=[0] * 8)["grid_y"] == 3
+
+
 def test_tcgen05_path_choice():
     # TF32 tensor cores for m >= 128 with TMA-addressable fp32 operands, in tensor math only.
     assert L.plan(128, 4096, 4096, q8=False)["path_name"] == "tcgen05"
