@@ -76,9 +76,10 @@ enum {
        (and tiled_split): three TF32 terms (fp32 B) or three int8 activation terms (int8 B),
        the fp32 decode path's bound of 1e-5. m <= 8: the fp32-FMA GEMV. Default. */
     LLME_MATH_TENSOR = 0,
-    /* fp32-faithful: every product with m >= 9 runs on the SIMT tiles with fp32 FMA, as the
-       reference's kernels do (the GEMV is fp32 FMA in both modes). Selected at load time by
-       LLME_B200_MATH=fp32 in the environment. */
+    /* fp32-faithful: every product with m >= 9 runs in fp32 FMA, as the reference's kernels
+       do: fp32 B with 9..16 rows on the 16-row GEMV, the rest on the SIMT tiles (the GEMV is
+       fp32 FMA in both modes). Selected at load time by LLME_B200_MATH=fp32 in the
+       environment. */
     LLME_MATH_FP32 = 1
 };
 
@@ -420,7 +421,8 @@ enum {
     LLME_PATH_NONE = 0,        /* nothing to launch (m == 0 or n == 0) */
     LLME_PATH_ZERO = 1,        /* k == 0: memset of C */
     LLME_PATH_NAIVE = 2,
-    LLME_PATH_GEMV_TMA = 3,    /* weight-streaming GEMV, TMA ring (aligned B, m <= 8) */
+    LLME_PATH_GEMV_TMA = 3,    /* weight-streaming GEMV, TMA ring (aligned B, m <= 8; fp32 B
+                                  up to 16 rows in LLME_MATH_FP32) */
     LLME_PATH_GEMV_LDG = 4,    /* weight-streaming GEMV, plain loads (ragged B) */
     LLME_PATH_TILED_SIMT = 5,  /* fp32 SIMT tiles, k split across CTAs */
     LLME_PATH_TCGEN05 = 6,     /* tcgen05/TMEM tensor-core GEMM, TF32 (fp32 weights) */

@@ -54,7 +54,7 @@ struct SplitScratch {
     unsigned* counters = nullptr; // one per tile, zero between launches
 };
 
-// What the per-call TMA GEMV (m <= 8) does with a finished pair of adjacent output columns
+// What the per-call TMA GEMV (m <= 8, or 16) does with a finished pair of adjacent output columns
 // (2c, 2c + 1) of row r instead of writing C as is; the decode step of the transformer engine
 // fuses its elementwise work here.
 enum GemvEpilogueKind { kEpiStore = 0, kEpiRopeCache = 1, kEpiSwiglu = 2, kEpiPeerSum = 3 };
@@ -365,7 +365,7 @@ cudaError_t launch_fill_uniform(float* out, size_t count, uint64_t seed, float l
                                 cudaStream_t stream);
 unsigned read_and_clear_ops_error();
 
-// A product with a fused GEMV epilogue (m <= 8 on the TMA GEMV path only; LLME_E_UNSUPPORTED
+// A product with a fused GEMV epilogue (the TMA GEMV path only; LLME_E_UNSUPPORTED
 // before any launch otherwise), and the plan llme_matmul_* would follow for a product.
 int run_product_epilogue(size_t m, size_t n, size_t k, const float* A, const void* B,
                          const float* scale, float* C, bool q8, const float* rms, unsigned flags,
