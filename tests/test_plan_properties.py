@@ -114,3 +114,34 @@ def test_every_plan_covers_c_and_k_within_limits(m, n, k, q8, kernel, accumulate
         assert rms and p["norm_bytes"] == 4 * m * k
     else:
         assert p["norm_bytes"] == 0
+
+
+@settings(max_examples=1500, deadline=None)
+@given(n=dims(), k=dims(), q8=st.booleans(), m=st.integers(1, 8),
+       sms=st.sampled_from([148, 132, 20]),
+       shrink=st.lists(st.floats(0.3, 1.0), min_size=8, max_size=8))
+def test_gemv_clusters_fit_the_device_capacity(n, k, q8, m, sms, shrink):
+    # For any device capacity table (clusters of c CTAs it holds at once, at most the model's
+    # 2 x SMs / c and not growing with c), the GEMV's k slices leave every cluster resident
+    # at once and still cover k exactly once; the device never takes more slices than the
+    # model would.
+    model = [2 * sms // c for c in range(1, 9)]
+    table, prev = [], None
+    for c in range(8):
+        v = max(1, int(model[c] * shrink[c]))
+        v = min(v, prev) if prev is not None else v
+        table.append(v)
+        prev = v
+    kw = dict(q8=q8, kernel="skinny", sm_count=sms)
+    try:
+        base = L.plan(m, n, k, **kw)
+    except L.InvalidArgument:
+        return
+    if base["path_name"] != "gemv_tma":
+        return
+    p = L.plan(m, n, k, gemv_clusters=table, **kw)
+    s, span = p["slices"], p["span"]
+    assert p["path_name"] == "gemv_tma" and p["grid_x"] == base["grid_x"]
+    assert s == 1 or p["grid_x"] <= table[s - 1], (table, p)
+    assert (s - 1) * span < k <= s * span and span % 128 == 0
+    assert p["cluster"] == s and s <= base["slices"]
